@@ -1,0 +1,222 @@
+"""Per-op CPU restatements (torch fp32 on the CPU). Test infrastructure only.
+
+Every function names the reference code it restates. Values cross op
+boundaries in the dtypes the reference stores (bf16 activations, fp8 e4m3
+codes with fp32 scales), so roundings happen where the reference's do.
+Scales are returned group-major, (width / 128, rows), as the kernels
+write them.
+"""
+
+import torch
+
+GROUP = 128
+FP8_MAX = 448.0
+
+
+def _to_bf16(x):
+    return x.to(torch.bfloat16)
+
+
+def _to_fp8(x):
+    return x.to(torch.float8_e4m3fn)
+
+
+# Every narrowing conversion goes through these two hooks: round to nearest
+# even, as the compiled kernels (cvt.rn) do. The golden-vector test swaps in
+# the conversions of the Triton interpreter that produced the vectors.
+CONVERT = {"bf16": _to_bf16, "fp8": _to_fp8}
+
+
+def to_bf16(x):
+    return CONVERT["bf16"](x)
+
+
+def to_fp8(x):
+    return CONVERT["fp8"](x)
+
+
+def bf16(x):
+    """Round fp32 to bf16 and back (round to nearest even)."""
+    return to_bf16(x).to(torch.float32)
+
+
+def quant_groups(y):
+    """1x128 fp8 quantisation of fp32 rows.
+
+    The per-group quantiser shared by vLLM's per_token_group_quant_fp8 and
+    Quail's fused Triton kernels (quail/backends/quail/executor/
+    attention.py:315-323, 348-355, 461-469): scale = max(amax, 1e-10) / 448,
+    q = clamp(y / scale, -448, 448) cast to e4m3 (nearest even).
+    Returns (codes float8_e4m3fn [rows, width], scales f32 [width/128, rows]).
+    """
+    rows, width = y.shape
+    g = y.reshape(rows, width // GROUP, GROUP)
+    amax = g.abs().amax(dim=2)
+    scale = torch.clamp(amax, min=1e-10) / FP8_MAX
+    q = torch.clamp(g / scale[:, :, None], -FP8_MAX, FP8_MAX)
+    return to_fp8(q.reshape(rows, width)), scale.t().contiguous()
+
+
+def dequant(codes, scales):
+    """fp32 values of fp8 codes with group-major scales."""
+    rows, width = codes.shape
+    s = scales.t().reshape(rows, width // GROUP, 1)
+    return (codes.to(torch.float32).reshape(rows, width // GROUP, GROUP) * s).reshape(rows, width)
+
+
+def rms_norm_bf16(x, w, eps):
+    """vLLM rms_norm on bf16 rows (vllm/ir/ops/layernorm.py rms_norm):
+    fp32 variance, x * rsqrt(var + eps) rounded to bf16, times the bf16
+    weight, rounded to bf16."""
+    x = x.to(torch.float32)
+    var = x.pow(2).mean(dim=-1, keepdim=True)
+    y = bf16(x * (1.0 / torch.sqrt(var + eps)))
+    return bf16(y * w.to(torch.float32))
+
+
+def embed_rmsnorm_quant(ids, embed, w, eps):
+    """Layer 0: embedding gather, vLLM rms_norm, per-group quant
+    (models/qwen3.py:51, 55-57; attention.py:143-151, 763-766)."""
+    residual = embed[ids]
+    q, s = quant_groups(rms_norm_bf16(residual, w, eps))
+    return residual, q, s
+
+
+def add_rmsnorm_quant(hidden, residual, w, eps):
+    """Triton add_rms_norm_quant (attention.py:326-359): x = hidden +
+    residual in fp32; residual stored as bf16(x); y = x * rstd * w in fp32
+    from the unrounded x; per-group quant. Returns (new residual, q, s)."""
+    x = hidden.to(torch.float32) + residual.to(torch.float32)
+    ms = (x * x).sum(dim=-1, keepdim=True) / x.shape[-1]
+    rstd = 1.0 / torch.sqrt(ms + eps)
+    y = x * rstd * w.to(torch.float32)
+    q, s = quant_groups(y)
+    return to_bf16(x), q, s
+
+
+def silu_mul_quant(gate_up):
+    """Triton silu_mul_quant (attention.py:301-323): y = g * sigmoid(g) * u
+    in fp32 from the bf16 halves; per-group quant."""
+    half = gate_up.shape[1] // 2
+    g = gate_up[:, :half].to(torch.float32)
+    u = gate_up[:, half:].to(torch.float32)
+    y = g * (1.0 / (1.0 + torch.exp(-g))) * u
+    return quant_groups(y)
+
+
+def gemm_fp8_bs(a_codes, a_scales, w_codes, w_scales):
+    """DeepGEMM fp8_gemm_nt as Quail calls it (attention.py:129-141):
+    per 128-deep K block an fp32 partial product of the fp8 codes, scaled
+    by a_scale[kb, m] * w_scale[n/128, kb] and accumulated in fp32 in K
+    order; bf16 output. a_scales is group-major (K/128, M)."""
+    m, k = a_codes.shape
+    n = w_codes.shape[0]
+    kb = k // GROUP
+    a = a_codes.to(torch.float32).reshape(m, kb, GROUP).permute(1, 0, 2)
+    w = w_codes.to(torch.float32).reshape(n, kb, GROUP).permute(1, 2, 0)
+    acc = torch.zeros(m, n, dtype=torch.float32)
+    ws = w_scales.to(torch.float32).repeat_interleave(GROUP, dim=0)  # [n, kb]
+    for b in range(kb):
+        partial = a[b] @ w[b]
+        acc = acc + partial * (a_scales[b][:, None] * ws[:, b][None, :])
+    return to_bf16(acc)
+
+
+def qk_norm_rope(qkv, positions, cos_sin, q_w, k_w, eps, n_q, n_kv, head_dim=128):
+    """Triton qk_norm_rope (attention.py:363-409): per-head RMSNorm of q
+    and k in fp32, times the weight, neox rotary with cos | sin of the bf16
+    cache row; bf16 outputs. Also returns v, the raw slice (qwen3.py:63-64)."""
+    rows = qkv.shape[0]
+    half = head_dim // 2
+    cs = cos_sin[positions].to(torch.float32)
+    cos, sin = cs[:, None, :half], cs[:, None, half:]
+
+    def norm_rope(x, w, heads):
+        x = x.reshape(rows, heads, head_dim).to(torch.float32)
+        a, b = x[..., :half], x[..., half:]
+        ms = ((a * a).sum(-1, keepdim=True) + (b * b).sum(-1, keepdim=True)) / head_dim
+        rstd = 1.0 / torch.sqrt(ms + eps)
+        wf = w.to(torch.float32)
+        a = a * rstd * wf[:half]
+        b = b * rstd * wf[half:]
+        out = torch.cat((a * cos - b * sin, b * cos + a * sin), dim=-1)
+        return to_bf16(out).reshape(rows, heads * head_dim)
+
+    qw = n_q * head_dim
+    kw = n_kv * head_dim
+    q = norm_rope(qkv[:, :qw], q_w, n_q)
+    k = norm_rope(qkv[:, qw:qw + kw], k_w, n_kv)
+    v = qkv[:, qw + kw:qw + 2 * kw].contiguous()
+    return q, k, v
+
+
+def attend(q, k, v, scale, mask=None):
+    """Exact softmax attention in fp32 for one query head group.
+
+    q [nq, d], k/v [nk, d] (bf16 values); mask [nq, nk] True = visible.
+    Returns (out bf16 [nq, d], lse f32 [nq]) with lse the natural
+    log-sum-exp of the scaled scores, FlashAttention's softmax_lse
+    (attention.py:802-818, return_softmax_lse=True)."""
+    s = (q.to(torch.float32) @ k.to(torch.float32).t()) * scale
+    if mask is not None:
+        s = s.masked_fill(~mask, float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)
+    p = torch.exp(s - lse[:, None])
+    out = p @ v.to(torch.float32)
+    return to_bf16(out), lse
+
+
+def attention_heads(q, k, v, n_q, n_kv, scale, mask=None, head_dim=128):
+    """attend() over every query head with grouped KV heads.
+
+    q [nq, n_q*d]; k, v [nk, n_kv*d]. Returns (out bf16 [nq, n_q*d],
+    lse f32 [nq, n_q])."""
+    nq, nk = q.shape[0], k.shape[0]
+    qh = q.reshape(nq, n_q, head_dim)
+    kh = k.reshape(nk, n_kv, head_dim)
+    vh = v.reshape(nk, n_kv, head_dim)
+    group = n_q // n_kv
+    outs, lses = [], []
+    for h in range(n_q):
+        o, l = attend(qh[:, h], kh[:, h // group], vh[:, h // group], scale, mask)
+        outs.append(o)
+        lses.append(l)
+    return torch.stack(outs, dim=1).reshape(nq, n_q * head_dim), torch.stack(lses, dim=1)
+
+
+def merge_attn_quant(out_a, lse_a, out_b, lse_b, source, n_q, head_dim=128):
+    """Triton merge_attn_quant (attention.py:432-473): w = bf16(sigmoid(
+    lse_b - lse_a)); merged = bf16(a + (b - a) * w); rows with source < 0
+    keep a; per-head (128-column) quantisation. out_b/lse_b are indexed by
+    source. Returns (q, scales)."""
+    rows = out_a.shape[0]
+    a = out_a.to(torch.float32).reshape(rows, n_q, head_dim)
+    has_b = source >= 0
+    safe = torch.clamp(source, min=0).long()
+    b = out_b.to(torch.float32).reshape(-1, n_q, head_dim)[safe]
+    lb = lse_b[safe]
+    w = bf16(1.0 / (1.0 + torch.exp(-(lb - lse_a))))
+    merged = bf16(a + (b - a) * w[:, :, None])
+    y = torch.where(has_b[:, None, None], merged, a)
+    return quant_groups(y.reshape(rows, n_q * head_dim))
+
+
+def final_norm(hidden, residual, finals, w, eps):
+    """index_select of the answer rows + vLLM fused_add_rms_norm
+    (models/qwen3.py:72-77; vllm/ir/ops/layernorm.py fused_add_rms_norm):
+    x = hidden + residual in fp32, rstd from the unrounded x,
+    bf16(bf16(x * rstd) * w)."""
+    x = hidden[finals].to(torch.float32) + residual[finals].to(torch.float32)
+    var = x.pow(2).mean(dim=-1, keepdim=True)
+    y = bf16(x * (1.0 / torch.sqrt(var + eps)))
+    return to_bf16(y * w.to(torch.float32))
+
+
+def answer_margin(normed, ans_w, true_cols, false_cols):
+    """AnswerRows.logits + AsyncAnswers.submit (readout.py:45-49, 70-80):
+    bf16 scores of the retained head rows (fp32 accumulate), max per class,
+    margin = t - f, bit = t > f."""
+    scores = bf16(normed.to(torch.float32) @ ans_w.to(torch.float32).t())
+    t = scores[:, list(true_cols)].amax(dim=1)
+    f = scores[:, list(false_cols)].amax(dim=1)
+    return t - f, (t > f).to(torch.uint8)

@@ -1,0 +1,450 @@
+// FP8 e4m3 block-scaled GEMM on tcgen05 tensor cores (sm_100a).
+//
+//   out[m, n] = bf16( sum_kb P_kb[m, n] * a_scale[kb, m] * w_scale[n / 128, kb] )
+//   P_kb[m, n] = sum_{k in block kb} a[m, k] * w[n, k]        (128-wide K blocks)
+//
+// The scales are arbitrary fp32 values (1x128 for activations, 128x128 for
+// weights), so they cannot ride on the MX block-scale hardware path (UE8M0
+// only); each 128-deep K block is accumulated by the tensor cores into its
+// own TMEM buffer and promoted into fp32 registers by the epilogue warps with
+// that block's scales, while the tensor cores fill the other buffer.
+//
+// Persistent kernel, one block per SM, 18 warps:
+//   warp 0      TMA producer: A [128 x 128] and W [BN x 128] tiles into a
+//               4-stage shared-memory ring (128-byte swizzle), one mbarrier
+//               transaction per stage;
+//   warp 1      allocates TMEM (2 x BN columns) and issues tcgen05.mma
+//               (M=128, N=BN, K=32, kind::f8f6f4) from one thread;
+//   warps 2-17  epilogue: warp w reads TMEM lanes 32*(w%4).. (its rows) and
+//               columns (w-2)/4 * BN/4 .. (its slice), scales and accumulates.
+// No cluster launch and no TMA multicast: every block loads its own tiles.
+// Every mbarrier wait is bounded (about one second); a wait that gives up
+// sets a status bit, makes the other roles stop, drains the copies and MMAs
+// in flight and frees TMEM before the block exits.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace {
+
+using namespace qb;
+
+constexpr int BM = 128;
+constexpr int BK = 128;
+constexpr int STAGES = 4;
+constexpr int EPI_WARPS = 16;
+constexpr int NUM_THREADS = (2 + EPI_WARPS) * 32;
+constexpr uint64_t TIMEOUT_NS = 1000000000ull;
+
+template <int BN>
+struct Cfg {
+    static constexpr int A_BYTES = BM * BK;
+    static constexpr int B_BYTES = BN * BK;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int TMEM_COLS = 2 * BN;  // two accumulator buffers
+    static constexpr int SLICE = BN / 4;      // columns per epilogue warp
+    static constexpr int BAR_BYTES = 256;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+    // instruction descriptor: D f32, A/B e4m3, both K-major, N, M=128
+    static constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) |
+                                      ((uint32_t)(BM >> 4) << 24);
+};
+
+struct Barriers {
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    uint64_t tmem_full[2];
+    uint64_t tmem_empty[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for the phase with the given parity; false when it gave up (timeout
+// or another role aborted), after which the caller stops its loop.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          uint32_t* status, uint32_t bit) {
+    const uint32_t addr = smem_u32(bar);
+    if (mbar_try_wait(addr, parity)) return true;
+    const uint64_t start = globaltimer();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(addr, parity)) return true;
+        if ((it & 255u) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer() - start > TIMEOUT_NS) {
+                atomicOr(status, bit);
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), version 1 (sm_100), base offset 0.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void mma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// 16 consecutive 32-bit columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
+                   const __grid_constant__ CUtensorMap map_b, const float* __restrict__ a_scale,
+                   int64_t a_scale_ld, const float* __restrict__ w_scale, bf16* __restrict__ out,
+                   int M, int N, int K, uint32_t* status) {
+    using C = Cfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    // SWIZZLE_128B tiles need 1024-byte aligned shared memory
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+    Barriers* bars = reinterpret_cast<Barriers*>(smem + STAGES * C::STAGE_BYTES);
+    volatile int* abort_flag = &bars->abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int num_n = N / BN;
+    const int num_m = (M + BM - 1) / BM;
+    const int total = num_m * num_n;
+    const int n_kb = K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&bars->full[s], 1);
+            mbar_init(&bars->empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars->tmem_full[b], 1);
+            mbar_init(&bars->tmem_empty[b], EPI_WARPS);
+        }
+        mbar_init(&bars->drain, 1);
+        bars->abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&bars->tmem_base)),
+                     "r"(C::TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = bars->tmem_base;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a))
+                         : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b))
+                         : "memory");
+            int it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+                const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
+                for (int kb = 0; kb < n_kb; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    const uint32_t round = (uint32_t)(it / STAGES);
+                    if (!mbar_wait(&bars->empty[s], (round & 1u) ^ 1u, abort_flag, status,
+                                   STATUS_GEMM_PRODUCER)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* sa = smem + s * C::STAGE_BYTES;
+                    mbar_arrive_expect_tx(&bars->full[s], C::STAGE_BYTES);
+                    tma_load_2d(smem_u32(sa), &map_a, kb * BK, m0, &bars->full[s]);
+                    tma_load_2d(smem_u32(sa + C::A_BYTES), &map_b, kb * BK, n0, &bars->full[s]);
+                }
+            }
+            // no copy may still be landing when the block exits: wait for the
+            // last load issued on each stage
+            for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j) {
+                const int s = j % STAGES;
+                if (!mbar_try_wait(smem_u32(&bars->full[s]), (uint32_t)(j / STAGES) & 1u)) {
+                    int flag = 0;
+                    mbar_wait(&bars->full[s], (uint32_t)(j / STAGES) & 1u, &flag, status,
+                              STATUS_GEMM_DRAIN);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            int it = 0, acc_it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+                for (int kb = 0; kb < n_kb; ++kb, ++it, ++acc_it) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait(&bars->full[s], (uint32_t)(it / STAGES) & 1u, abort_flag,
+                                   status, STATUS_GEMM_MMA)) {
+                        ok = false;
+                        break;
+                    }
+                    const int buf = acc_it & 1;
+                    const uint32_t use = (uint32_t)(acc_it >> 1);
+                    if (!mbar_wait(&bars->tmem_empty[buf], (use & 1u) ^ 1u, abort_flag, status,
+                                   STATUS_GEMM_MMA)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+                    const uint64_t adesc = sw128_desc(sa);
+                    const uint64_t bdesc = sw128_desc(sa + C::A_BYTES);
+                    const uint32_t d = tmem_base + (uint32_t)(buf * BN);
+#pragma unroll
+                    for (int k = 0; k < BK / 32; ++k)  // 32 bytes of K per MMA
+                        mma_f8(d, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), C::IDESC,
+                               k > 0 ? 1u : 0u);
+                    mma_commit(&bars->empty[s]);
+                    mma_commit(&bars->tmem_full[buf]);
+                }
+            }
+            // every MMA issued must finish before TMEM is freed
+            mma_commit(&bars->drain);
+            int flag = 0;
+            mbar_wait(&bars->drain, 0, &flag, status, STATUS_GEMM_DRAIN);
+        }
+    } else {
+        // ---------------- epilogue: promote, accumulate, store ----------------
+        const int ew = warp - 2;
+        const int quarter = warp & 3;          // TMEM lanes this warp may access
+        const int col0 = (ew >> 2) * C::SLICE; // its column slice
+        const int row_in_tile = quarter * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+        int acc_it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+            const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
+            const int m = m0 + row_in_tile;
+            const bool valid = m < M;
+            const float* ws_row = w_scale + (int64_t)((n0 + col0) / 128) * n_kb;
+            float acc[C::SLICE];
+#pragma unroll
+            for (int j = 0; j < C::SLICE; ++j) acc[j] = 0.0f;
+            float as_next = valid ? a_scale[m] : 0.0f;
+            float ws_next = ws_row[0];
+            for (int kb = 0; kb < n_kb; ++kb, ++acc_it) {
+                const float sc = as_next * ws_next;
+                if (kb + 1 < n_kb) {
+                    as_next = valid ? a_scale[(int64_t)(kb + 1) * a_scale_ld + m] : 0.0f;
+                    ws_next = ws_row[kb + 1];
+                }
+                const int buf = acc_it & 1;
+                if (!mbar_wait(&bars->tmem_full[buf], (uint32_t)(acc_it >> 1) & 1u, abort_flag,
+                               status, STATUS_GEMM_EPILOGUE)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t taddr = tmem_base + lane_addr + (uint32_t)(buf * BN + col0);
+#pragma unroll
+                for (int c = 0; c < C::SLICE; c += 16) {
+                    float v[16];
+                    tmem_ld16(taddr + (uint32_t)c, v);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) acc[c + j] = fmaf(v[j], sc, acc[c + j]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->tmem_empty[buf]);
+            }
+            if (!ok) break;
+            if (valid) {
+                bf16* dst = out + (int64_t)m * N + n0 + col0;
+#pragma unroll
+                for (int j = 0; j < C::SLICE; j += 8)
+                    *reinterpret_cast<uint4*>(dst + j) = float_to_bf16x8(acc + j);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(C::TMEM_COLS)
+                     : "memory");
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (fn == nullptr) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return nullptr;
+        fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 2-D K-major fp8 tensor map: rows x k bytes, box box_rows x 128, 128B swizzle.
+int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, int box_rows) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = get_encoder();
+    if (!enc) {
+        set_error("qb_gemm_fp8_bs: cuTensorMapEncodeTiled unavailable");
+        return QB_ERR_CUDA;
+    }
+    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)k};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("qb_gemm_fp8_bs: cuTensorMapEncodeTiled failed (%d)", (int)r);
+        return QB_ERR_CUDA;
+    }
+    return QB_OK;
+}
+
+int sm_count() {
+    static int count[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (count[dev] == 0) {
+        int c = 0;
+        cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
+        count[dev] = c > 0 ? c : 148;
+    }
+    return count[dev];
+}
+
+template <int BN>
+int launch(const void* a, const float* a_scale, int64_t a_scale_ld, const void* w,
+           const float* w_scale, void* out, int64_t m, int64_t n, int64_t k, cudaStream_t stream) {
+    using C = Cfg<BN>;
+    CUtensorMap map_a, map_b;
+    int st = make_map(&map_a, a, m, k, BM);
+    if (st) return st;
+    st = make_map(&map_b, w, n, k, BN);
+    if (st) return st;
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_fp8_bs_kernel<BN>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        if (e != cudaSuccess) return launch_status("qb_gemm_fp8_bs: smem attribute");
+        attr[dev] = true;
+    }
+    uint32_t* status = device_status_ptr();
+    if (!status) return launch_status("qb_gemm_fp8_bs: status word");
+    const int64_t tiles = ((m + BM - 1) / BM) * (n / BN);
+    const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
+    gemm_fp8_bs_kernel<BN><<<grid, NUM_THREADS, C::SMEM, stream>>>(
+        map_a, map_b, a_scale, a_scale_ld, w_scale, (bf16*)out, (int)m, (int)n, (int)k, status);
+    return launch_status("qb_gemm_fp8_bs");
+}
+
+}  // namespace
+
+extern "C" int qb_gemm_fp8_bs(const void* a, const float* a_scale, int64_t a_scale_ld,
+                              const void* w, const float* w_scale, void* out, int64_t m, int64_t n,
+                              int64_t k, void* stream) {
+    if (m < 0 || n <= 0 || k <= 0) return invalid("qb_gemm_fp8_bs: bad sizes");
+    if (k % BK != 0) return invalid("qb_gemm_fp8_bs: k must be a multiple of 128");
+    if (n % 128 != 0) return invalid("qb_gemm_fp8_bs: n must be a multiple of 128");
+    if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL)
+        return invalid("qb_gemm_fp8_bs: sizes exceed int32");
+    if (a_scale_ld < m) return invalid("qb_gemm_fp8_bs: a_scale_ld < m");
+    if (!aligned(a, 16) || !aligned(w, 16) || !aligned(out, 16))
+        return invalid("qb_gemm_fp8_bs: a, w and out must be 16-byte aligned");
+    if (!a_scale || !w_scale) return invalid("qb_gemm_fp8_bs: NULL scales");
+    if (m == 0) return QB_OK;
+    if (n % 256 == 0)
+        return launch<256>(a, a_scale, a_scale_ld, w, w_scale, out, m, n, k, (cudaStream_t)stream);
+    return launch<128>(a, a_scale, a_scale_ld, w, w_scale, out, m, n, k, (cudaStream_t)stream);
+}

@@ -1,0 +1,180 @@
+// RMSNorm + fp8 quantisation kernels (HBM-bound): the layer-0 embedding
+// norm, the fused residual-add norm of every later norm, and the SiLU-gated
+// product of the MLP. One 16-byte vector (8 bf16) per thread; a 128-column
+// quantisation group is 16 consecutive lanes (a half warp).
+#include "common.cuh"
+
+namespace {
+
+using namespace qb;
+
+// Max |v| over the 16 lanes of a half warp (one quantisation group).
+__device__ __forceinline__ float group_amax(float v) {
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Quantise 8 values of one group slice; the half warp's lane 0 writes the scale.
+__device__ __forceinline__ void quant_store8(const float* y, uint8_t* q_row, float* scale_out,
+                                             int64_t scale_ld, int64_t row, int col8) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(y[i]));
+    amax = group_amax(amax);
+    const float scale = group_scale(amax);
+    uint2 packed;
+    uint16_t* p = reinterpret_cast<uint16_t*>(&packed);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        p[i] = fp8x2(quant_clamp(y[2 * i], scale), quant_clamp(y[2 * i + 1], scale));
+    *reinterpret_cast<uint2*>(q_row + col8 * 8) = packed;
+    if ((threadIdx.x & 15) == 0) scale_out[(int64_t)(col8 / 16) * scale_ld + row] = scale;
+}
+
+// blockDim.x == hidden / 8; one row per block.
+__global__ void embed_rmsnorm_quant_kernel(const int64_t* __restrict__ ids,
+                                           const bf16* __restrict__ embed, int64_t vocab,
+                                           int hidden, const bf16* __restrict__ w, float eps,
+                                           bf16* __restrict__ residual_out,
+                                           uint8_t* __restrict__ q_out,
+                                           float* __restrict__ scale_out, int64_t scale_ld,
+                                           uint32_t* status) {
+    __shared__ float scratch[32];
+    const int64_t row = blockIdx.x;
+    const int t = threadIdx.x;
+    int64_t id = ids[row];
+    uint4 raw = make_uint4(0, 0, 0, 0);
+    if (id >= 0 && id < vocab) {
+        raw = *reinterpret_cast<const uint4*>(embed + id * hidden + t * 8);
+    } else if (t == 0) {
+        atomicOr(status, STATUS_BAD_TOKEN);
+    }
+    *reinterpret_cast<uint4*>(residual_out + row * hidden + t * 8) = raw;
+    float x[8];
+    bf16x8_to_float(raw, x);
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
+    const float total = block_sum(ss, scratch);
+    const float rstd = 1.0f / sqrtf(total / (float)hidden + eps);
+    float wf[8];
+    bf16x8_to_float(*reinterpret_cast<const uint4*>(w + t * 8), wf);
+    float y[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = bf16_round(bf16_round(x[i] * rstd) * wf[i]);
+    quant_store8(y, q_out + row * hidden, scale_out, scale_ld, row, t);
+}
+
+// blockDim.x == hidden / 8; one row per block.
+__global__ void add_rmsnorm_quant_kernel(const bf16* __restrict__ hidden_in,
+                                         bf16* __restrict__ residual,
+                                         const bf16* __restrict__ w, float eps, int hidden,
+                                         uint8_t* __restrict__ q_out,
+                                         float* __restrict__ scale_out, int64_t scale_ld) {
+    __shared__ float scratch[32];
+    const int64_t row = blockIdx.x;
+    const int t = threadIdx.x;
+    const int64_t off = row * hidden + t * 8;
+    float h[8], r[8], x[8];
+    bf16x8_to_float(*reinterpret_cast<const uint4*>(hidden_in + off), h);
+    bf16x8_to_float(*reinterpret_cast<const uint4*>(residual + off), r);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = h[i] + r[i];
+    *reinterpret_cast<uint4*>(residual + off) = float_to_bf16x8(x);
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
+    const float total = block_sum(ss, scratch);
+    const float rstd = 1.0f / sqrtf(total / (float)hidden + eps);
+    float wf[8];
+    bf16x8_to_float(*reinterpret_cast<const uint4*>(w + t * 8), wf);
+    float y[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = x[i] * rstd * wf[i];
+    quant_store8(y, q_out + row * hidden, scale_out, scale_ld, row, t);
+}
+
+// One warp per 256 outputs of one row (two quantisation groups).
+__global__ void silu_mul_quant_kernel(const bf16* __restrict__ gate_up, int64_t rows, int inter,
+                                      uint8_t* __restrict__ q_out, float* __restrict__ scale_out,
+                                      int64_t scale_ld) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int per_row = inter / 256;
+    if (warp >= rows * per_row) return;  // whole warps exit together
+    const int64_t row = warp / per_row;
+    const int col8 = (int)(warp % per_row) * 32 + lane;  // 8-column vector index
+    const bf16* base = gate_up + row * (int64_t)(2 * inter);
+    float g[8], u[8], y[8];
+    bf16x8_to_float(*reinterpret_cast<const uint4*>(base + col8 * 8), g);
+    bf16x8_to_float(*reinterpret_cast<const uint4*>(base + inter + col8 * 8), u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = g[i] * sigmoidf_ref(g[i]) * u[i];
+    quant_store8(y, q_out + row * inter, scale_out, scale_ld, row, col8);
+}
+
+int check_rows(int64_t rows, int64_t hidden, const char* who) {
+    if (rows < 0) return invalid(who);
+    if (hidden <= 0 || hidden % 256 != 0 || hidden / 8 > 1024) {
+        set_error("%s: hidden %lld must be a positive multiple of 256 and <= 8192", who,
+                  (long long)hidden);
+        return QB_ERR_INVALID;
+    }
+    if (rows > 0x7fffffffLL) return invalid("rows exceed the grid limit");
+    return QB_OK;
+}
+
+}  // namespace
+
+extern "C" int qb_embed_rmsnorm_quant(const int64_t* ids, int64_t rows, const void* embed,
+                                      int64_t vocab, int64_t hidden, const void* norm_w,
+                                      float eps, void* residual_out, void* q_out,
+                                      float* scale_out, int64_t scale_ld, void* stream) {
+    int st = check_rows(rows, hidden, "qb_embed_rmsnorm_quant");
+    if (st) return st;
+    if (scale_ld < rows) return invalid("qb_embed_rmsnorm_quant: scale_ld < rows");
+    if (!aligned(embed, 16) || !aligned(residual_out, 16) || !aligned(norm_w, 16) ||
+        !aligned(q_out, 8))
+        return invalid("qb_embed_rmsnorm_quant: pointers must be 16-byte aligned (q_out 8)");
+    if (rows == 0) return QB_OK;
+    uint32_t* status = device_status_ptr();
+    if (!status) return launch_status("qb_embed_rmsnorm_quant: status word");
+    embed_rmsnorm_quant_kernel<<<(unsigned)rows, (unsigned)(hidden / 8), 0,
+                                 (cudaStream_t)stream>>>(
+        ids, (const bf16*)embed, vocab, (int)hidden, (const bf16*)norm_w, eps,
+        (bf16*)residual_out, (uint8_t*)q_out, scale_out, scale_ld, status);
+    return launch_status("qb_embed_rmsnorm_quant");
+}
+
+extern "C" int qb_add_rmsnorm_quant(const void* hidden, void* residual, const void* w, float eps,
+                                    int64_t rows, int64_t hidden_dim, void* q_out,
+                                    float* scale_out, int64_t scale_ld, void* stream) {
+    int st = check_rows(rows, hidden_dim, "qb_add_rmsnorm_quant");
+    if (st) return st;
+    if (scale_ld < rows) return invalid("qb_add_rmsnorm_quant: scale_ld < rows");
+    if (!aligned(hidden, 16) || !aligned(residual, 16) || !aligned(w, 16) || !aligned(q_out, 8))
+        return invalid("qb_add_rmsnorm_quant: pointers must be 16-byte aligned (q_out 8)");
+    if (rows == 0) return QB_OK;
+    add_rmsnorm_quant_kernel<<<(unsigned)rows, (unsigned)(hidden_dim / 8), 0,
+                               (cudaStream_t)stream>>>(
+        (const bf16*)hidden, (bf16*)residual, (const bf16*)w, eps, (int)hidden_dim,
+        (uint8_t*)q_out, scale_out, scale_ld);
+    return launch_status("qb_add_rmsnorm_quant");
+}
+
+extern "C" int qb_silu_mul_quant(const void* gate_up, int64_t rows, int64_t inter, void* q_out,
+                                 float* scale_out, int64_t scale_ld, void* stream) {
+    if (rows < 0 || inter <= 0 || inter % 256 != 0)
+        return invalid("qb_silu_mul_quant: inter must be a positive multiple of 256");
+    if (scale_ld < rows) return invalid("qb_silu_mul_quant: scale_ld < rows");
+    if (!aligned(gate_up, 16) || !aligned(q_out, 8))
+        return invalid("qb_silu_mul_quant: gate_up must be 16-byte aligned, q_out 8");
+    if (rows == 0) return QB_OK;
+    const int64_t warps = rows * (inter / 256);
+    const int64_t blocks = (warps + 7) / 8;
+    if (blocks > 0x7fffffffLL) return invalid("qb_silu_mul_quant: too many rows");
+    silu_mul_quant_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
+        (const bf16*)gate_up, rows, (int)inter, (uint8_t*)q_out, scale_out, scale_ld);
+    return launch_status("qb_silu_mul_quant");
+}

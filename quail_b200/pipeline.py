@@ -1,0 +1,92 @@
+"""The Qwen3 forward pass over the B200 kernels, behind Quail's pipeline seam.
+
+``ModelPipeline`` is Quail's contract between the chunk loop and a model
+(quail/backends/quail/executor/models/base.py:11-47); ``Qwen3Pipeline``
+runs the layer order of quail/backends/quail/executor/models/qwen3.py:46-77
+with every op on libquailb200:
+
+    embed + RMSNorm + quant        (layer 0)  | add + RMSNorm + quant (later)
+    QKV GEMM -> q/k norm + rotary + paged KV append
+    attention (tree or unified) -> fp8 o_proj input
+    O GEMM -> add + RMSNorm + quant -> gate_up GEMM -> SiLU*up + quant
+    -> down GEMM
+    final add + RMSNorm on the answer rows only
+
+forward_chunk returns the final-normed bf16 rows of chunk.final_indices.
+"""
+
+from quail_b200.engine import Engine
+
+
+class ModelPipeline:
+    """The chunk loop's view of one model family (Quail's attribute set)."""
+
+    engine = None
+    max_chunk_tokens = None
+    warm_tokens = (64, 128, 256, 512, 1024, 2048)
+    canvas_ids = ()
+    canvas_answer_row = 0
+    needs_pages = False
+    tree_attention = True
+    gemm_warmup = False
+
+    def forward_chunk(self, chunk):
+        raise NotImplementedError
+
+    def linears(self):
+        raise NotImplementedError
+
+
+class Qwen3Pipeline(ModelPipeline):
+    """Qwen3 FP8 forward passes on sm_100a kernels."""
+
+    def __init__(self, torch, weights, arena):
+        self.torch = torch
+        self.weights = weights
+        self.cfg = weights.config
+        self.arena = arena
+        self.engine = Engine(torch, arena, self.cfg)
+        self.tree_attention = True
+        self.max_chunk_tokens = self.cfg.max_chunk_tokens
+        self.layers = weights.layers
+
+    def linears(self):
+        layer = self.layers[0]
+        return ((layer.qkv_w, layer.qkv_s), (layer.o_w, layer.o_s),
+                (layer.gate_up_w, layer.gate_up_s), (layer.down_w, layer.down_s))
+
+    def forward_chunk(self, chunk):
+        eng = self.engine
+        w = self.weights
+        meta = chunk.meta
+        meta["layer"] = 0
+        rows = chunk.tokens
+        tree = chunk.attention_mode == "tree"
+        row_dst = None
+        if tree and meta["kv_src"] is not None and meta["kv_src"].numel():
+            row_dst = eng.kv_row_map(meta["kv_src"], meta["kv_dst"], rows)
+        hidden = None
+        residual = None
+        for index, layer in enumerate(self.layers):
+            if index == 0:
+                residual, x = eng.embed_norm_quant(chunk.input_ids, w.embed, layer.input_ln)
+            else:
+                x = eng.norm_quant(hidden, layer.input_ln, residual)
+            qkv = eng.gemm(x, layer.qkv_w, layer.qkv_s)
+            q, k, v = eng.qk_norm_rope(qkv, chunk.positions, w.cos_sin, layer.q_norm,
+                                       layer.k_norm, meta["layer"], row_dst)
+            if tree:
+                o_in = eng.attention_tree(q, k, v, meta)
+            else:
+                o_in = eng.attention_unified(q, k, v, meta)
+            hidden = eng.gemm(o_in, layer.o_w, layer.o_s)
+            x = eng.norm_quant(hidden, layer.post_ln, residual)
+            gate_up = eng.gemm(x, layer.gate_up_w, layer.gate_up_s)
+            x = eng.activation_quant(gate_up)
+            hidden = eng.gemm(x, layer.down_w, layer.down_s)
+        return eng.final_norm(hidden, residual, chunk.final_indices, w.final_norm)
+
+
+def build_pipeline(torch, weights, arena):
+    """The pipeline for weights.config (Quail's build_pipeline seam)."""
+    return Qwen3Pipeline(torch, weights, arena)

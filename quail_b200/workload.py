@@ -1,0 +1,102 @@
+"""Seeded synthetic AI.IF rows with the BASELINE configurations' shapes.
+
+The reference's benchmark data (QUAIL-B) is not available here; these
+seeded rows stand in for it with the configurations' lengths and token-id
+ranges. Each row is one document ``prefix | suffix`` (the shared
+instruction prefix is the first tokens of every document, as Quail's
+DocumentPrefixes lays it out, quail/execution/tokens.py:412-429) and the
+stage question is a one-token tail drawn with seed 3.
+
+Rows are generated on access (row i's suffix from its own seeded
+generator), so a rank materialises only the rows of its slice.
+"""
+
+from collections.abc import Sequence
+from dataclasses import dataclass
+
+import numpy as np
+
+
+class DocRows(Sequence):
+    """Lazy documents: row i = prefix | suffix_i, suffix_i from rng(seed, i)."""
+
+    def __init__(self, prefix, lengths, lo, hi, seed, start=0, stop=None):
+        self.prefix = np.asarray(prefix, dtype=np.int32)
+        self.lengths = np.asarray(lengths, dtype=np.int64)
+        self.lo, self.hi, self.seed = lo, hi, seed
+        self.start = start
+        self.stop = len(self.lengths) if stop is None else stop
+        self._cache = {}
+
+    def __len__(self):
+        return self.stop - self.start
+
+    def __getitem__(self, i):
+        if isinstance(i, slice):
+            a, b, step = i.indices(len(self))
+            if step != 1:
+                return [self[j] for j in range(a, b, step)]
+            return DocRows(self.prefix, self.lengths, self.lo, self.hi, self.seed,
+                           self.start + a, self.start + b)
+        if i < 0:
+            i += len(self)
+        if not 0 <= i < len(self):
+            raise IndexError(i)
+        row = self.start + i
+        got = self._cache.get(row)
+        if got is None:
+            rng = np.random.default_rng([self.seed, row])
+            body = rng.integers(self.lo, self.hi, int(self.lengths[row]), dtype=np.int32)
+            got = np.concatenate([self.prefix, body])
+            self._cache[row] = got
+        return got
+
+
+@dataclass
+class Workload:
+    name: str
+    model: str
+    docs: Sequence
+    questions: list
+    prefix_tokens: int
+
+    @property
+    def rows(self) -> int:
+        return len(self.docs)
+
+    def logical_tokens(self, lo=0, hi=None) -> int:
+        """prefix + suffix + question tail per row, over rows [lo, hi)."""
+        hi = len(self.docs) if hi is None else hi
+        lengths = self.docs.lengths[self.docs.start + lo:self.docs.start + hi]
+        n = hi - lo
+        return int(lengths.sum() + n * (self.prefix_tokens + len(self.questions[0])))
+
+
+def _question():
+    return [int(np.random.default_rng(3).integers(1000, 150000))]
+
+
+def config1(rows=100_000, seed=0) -> Workload:
+    """Qwen3-4B FP8 AI.IF filter: a 64-token shared prefix, suffixes
+    lognormal(5.3, 0.6) clipped to [32, 2048], ids uniform in [1000, 150000)."""
+    rng = np.random.default_rng(seed)
+    prefix = rng.integers(1000, 150000, 64)
+    lens = np.clip(rng.lognormal(5.3, 0.6, rows).astype(np.int64), 32, 2048)
+    return Workload("config1", "qwen3-4b-fp8", DocRows(prefix, lens, 1000, 150000, seed),
+                    [_question()], 64)
+
+
+def config3(rows=50_000, seed=0) -> Workload:
+    """Qwen3-32B FP8 filter: 96-token prefix, lognormal(5.5, 0.5) in [64, 2048]."""
+    rng = np.random.default_rng(seed)
+    prefix = rng.integers(1000, 150000, 96)
+    lens = np.clip(rng.lognormal(5.5, 0.5, rows).astype(np.int64), 64, 2048)
+    return Workload("config3", "qwen3-32b-fp8", DocRows(prefix, lens, 1000, 150000, seed),
+                    [_question()], 96)
+
+
+def shard(n_rows: int, rank: int, world: int) -> tuple:
+    """Contiguous row slice [lo, hi) of one rank."""
+    per = -(-n_rows // world)
+    lo = min(n_rows, rank * per)
+    return lo, min(n_rows, lo + per)

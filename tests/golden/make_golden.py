@@ -1,0 +1,320 @@
+"""Generate the golden fixtures under tests/golden/ from the reference itself.
+
+Run in a container that has the reference checkout (not on the GPU box):
+
+    python tests/golden/make_golden.py /path/to/quail
+
+Two kinds of fixtures:
+
+- host_<scenario>.npz + .json: the reference's own run_filter
+  (quail/backends/quail/executor/loop.py:1535) driven over seeded
+  documents with a CPU KVArena and a recording pipeline; every packed
+  chunk's arrays (ids, positions, finals, KV scatter, reads, source map,
+  unified tables) and the final answers. quail_b200's packer must match
+  them bit for bit.
+- kernels.npz: seeded inputs and outputs of the reference's fused Triton
+  kernels (add_rms_norm_quant, qk_norm_rope, silu_mul_quant,
+  merge_attn_quant, kv_row_scatter; attention.py:293-642) run on CPU
+  tensors under TRITON_INTERPRET=1. The oracle must reproduce them.
+
+The reference imports sqlglot at package import; only the SQL frontend
+uses it, so an empty stand-in module is installed for the import.
+"""
+
+import json
+import os
+import sys
+import types
+from pathlib import Path
+
+os.environ.setdefault("TRITON_INTERPRET", "1")
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+HERE = Path(__file__).resolve().parent
+
+
+def _install_reference(path):
+    class _Anything(types.ModuleType):
+        def __getattr__(self, name):
+            if name.startswith("__"):
+                raise AttributeError(name)
+            return type(name, (), {})
+
+    stub = _Anything("sqlglot")
+    stub.exp = _Anything("sqlglot.exp")
+    stub.errors = types.SimpleNamespace(SqlglotError=Exception)
+    sys.modules.setdefault("sqlglot", stub)
+    sys.modules.setdefault("sqlglot.exp", stub.exp)
+    sys.path.insert(0, str(path))
+
+
+class _Torch:
+    """The real torch with CPU-only stand-ins for the CUDA events."""
+
+    def __getattr__(self, name):
+        return getattr(torch, name)
+
+    cuda = types.SimpleNamespace(
+        Event=lambda **kw: types.SimpleNamespace(record=lambda: None,
+                                                 synchronize=lambda: None,
+                                                 elapsed_time=lambda other: 0.0),
+        synchronize=lambda: None)
+
+
+def answer_bits(input_ids, positions, finals):
+    """The recording pipeline's answers: (token + position) % 2 at each final row."""
+    ids = np.asarray(input_ids)
+    pos = np.asarray(positions)
+    fin = np.asarray(finals)
+    return [int(b) for b in (ids[fin] + pos[fin]) % 2]
+
+
+# ---- host scenarios (shared with tests/test_host_parity.py) ------------------
+
+def scenario_docs(name):
+    """(documents, question_ids, budget, n_pages, attention, tree, arena_writes)."""
+    rng = np.random.default_rng({"cfg1_tree": 0, "cfg1_unified": 0, "stages_tree": 1,
+                                 "stages_unified": 1, "tight_tree": 2, "headers_tree": 3,
+                                 "headers_unified": 3, "plain_tree": 4}[name])
+    if name.startswith("cfg1") or name.startswith("tight"):
+        prefix = rng.integers(1000, 150000, 64).tolist()
+        lens = np.clip(rng.lognormal(5.3, 0.6, 40).astype(int), 32, 2048)
+        docs = [prefix + rng.integers(1000, 150000, int(n)).tolist() for n in lens]
+        questions = [[int(rng.integers(1000, 150000))]]
+        budget, pages = 2048 + 64 + 8, 600
+        if name.startswith("tight"):
+            pages = 130
+    elif name.startswith("stages"):
+        prefix = rng.integers(1000, 150000, 48).tolist()
+        lens = rng.integers(20, 200, 30)
+        docs = [prefix + rng.integers(1000, 150000, int(n)).tolist() for n in lens]
+        pre = rng.integers(1000, 150000, 3).tolist()
+        questions = [pre + [5, 6], pre + [7], pre + [8, 9, 10]]
+        budget, pages = 700, 300
+    elif name.startswith("headers"):
+        headers = [rng.integers(1000, 150000, int(n)).tolist() for n in (16, 40, 70)]
+        docs = []
+        for _ in range(36):
+            h = headers[int(rng.integers(0, 3))]
+            body = rng.integers(1000, 150000, int(rng.integers(1, 90))).tolist()
+            docs.append(h + body)
+        docs.append(list(docs[3]))      # a duplicate document
+        questions = [[int(rng.integers(1000, 150000)), 4]]
+        budget, pages = 400, 200
+    else:  # plain: no prefix tree, no arena writes
+        docs = [rng.integers(1000, 150000, int(rng.integers(5, 120))).tolist()
+                for _ in range(25)]
+        questions = [[17]]
+        budget, pages = 300, 64
+    attention = "unified" if name.endswith("unified") else "tree"
+    tree = name != "plain_tree"
+    writes = name != "plain_tree"
+    return docs, questions, budget, pages, attention, tree, writes
+
+
+SCENARIOS = ("cfg1_tree", "cfg1_unified", "stages_tree", "stages_unified", "tight_tree",
+             "headers_tree", "headers_unified", "plain_tree")
+
+CHUNK_FIELDS = ("input_ids", "positions", "final_indices", "kv_src", "kv_dst", "cu_a")
+READ_FIELDS = ("rows", "cu_q", "used", "table", "source")
+UNIFIED_FIELDS = ("src", "dst", "tail_src", "tail_dst", "used", "table", "cu_q")
+
+
+def _np(x):
+    if x is None:
+        return None
+    if torch.is_tensor(x):
+        return x.detach().cpu().numpy()
+    return np.asarray(x)
+
+
+def chunk_record(chunk, arrays, index):
+    """Flatten a chunk (reference or quail_b200) into arrays + a JSON entry."""
+    meta = chunk.meta
+    entry = dict(tokens=int(chunk.tokens), mode=chunk.attention_mode,
+                 max_a=int(meta["max_a"]),
+                 layout=[[k if isinstance(k, int) else str(k), int(n)]
+                         for k, n in chunk.layout])
+    for f in CHUNK_FIELDS:
+        src = getattr(chunk, f, None) if f in ("input_ids", "positions", "final_indices") \
+            else meta[f]
+        val = _np(src)
+        if val is not None:
+            arrays[f"c{index}_{f}"] = val
+    reads = meta["reads"]
+    entry["reads"] = None
+    if reads is not None:
+        entry["reads"] = dict(max_q=int(reads["max_q"]), max_used=int(reads["max_used"]))
+        for f in READ_FIELDS:
+            arrays[f"c{index}_reads_{f}"] = _np(reads[f])
+    uni = meta["unified"]
+    entry["unified"] = None
+    if uni is not None:
+        entry["unified"] = dict(max_q=int(uni["max_q"]), max_used=int(uni["max_used"]))
+        for f in UNIFIED_FIELDS:
+            val = _np(uni[f])
+            if val is not None:
+                arrays[f"c{index}_unified_{f}"] = val
+    return entry
+
+
+def run_reference_scenario(name):
+    from quail.backends.quail.executor import loop
+    from quail.backends.quail.executor.arena import KVArena
+    from quail.backends.quail.executor.models.base import ModelPipeline
+    from quail.execution.tokens import prefix_tree
+
+    def staged(torch_, data, dtype, pinned=True):
+        if isinstance(data, np.ndarray) or torch.is_tensor(data):
+            return torch.as_tensor(data, dtype=dtype)
+        return torch.tensor(data, dtype=dtype)
+
+    def token_parts(torch_, sequences, total, pinned=True, staging=None):
+        ids = [int(t) for seq in sequences for part in loop._token_parts(seq) for t in part]
+        assert len(ids) == total
+        return torch.tensor(ids, dtype=torch.int64)
+
+    loop._staged = staged
+    loop._staged_token_parts = token_parts
+    docs, questions, budget, pages, attention, use_tree, writes = scenario_docs(name)
+    arena = KVArena(1, pages, 16, 1, 8, dtype=torch.bfloat16, device="cpu")
+    chunks, arrays, entries = [], {}, []
+
+    class Recorder(ModelPipeline):
+        tree_attention = True
+
+        def forward_chunk(self, chunk):
+            entries.append(chunk_record(chunk, arrays, len(entries)))
+            return chunk
+
+    class Answers:
+        dtype = None
+
+        def submit(self, chunk):
+            return answer_bits(chunk.input_ids, chunk.positions, chunk.final_indices)
+
+        def result(self, handle):
+            return handle
+
+    tree = prefix_tree(docs, 16) if use_tree else None
+    stats = {}
+    answers, _, tokens = loop.run_filter(
+        _Torch(), arena, Recorder(), Answers(), docs, questions, budget, pinned=False,
+        arena_writes=writes, attention_mode=attention, prefix_tree=tree, stats=stats)
+    del chunks
+    summary = dict(name=name, chunks=entries, tokens=int(tokens),
+                   borrowed_tokens=int(stats.get("borrowed_tokens", 0)),
+                   answers={str(k): v for k, v in sorted(answers.items())},
+                   free_pages_after=int(arena.free_pages),
+                   tree=None if tree is None else dict(order=list(map(int, tree.order)),
+                                                       parent=tree.parent,
+                                                       shared=list(map(int, tree.shared))))
+    np.savez_compressed(HERE / f"host_{name}.npz", **arrays)
+    (HERE / f"host_{name}.json").write_text(json.dumps(summary, separators=(",", ":")))
+    return summary
+
+
+# ---- kernel vectors ---------------------------------------------------------------
+
+def make_kernel_vectors():
+    from quail.backends.quail.executor.attention import Engine
+
+    eng = Engine.__new__(Engine)
+    eng.torch = torch
+    eng.use_ue8m0 = False
+    eng.fp8 = torch.float8_e4m3fn
+    eng.is_fp8 = True
+    k = eng._triton_kernels()
+    g = torch.Generator().manual_seed(7)
+    out = {}
+
+    # add_rms_norm_quant: rows x 512, residual updated in place
+    n, h = 6, 512
+    x = (torch.randn(n, h, generator=g) * 2).to(torch.bfloat16)
+    r = torch.randn(n, h, generator=g).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(h, generator=g)).to(torch.bfloat16)
+    out.update(norm_x=x, norm_r_in=r.clone(), norm_w=w)
+    q = torch.empty(n, h, dtype=torch.float8_e4m3fn)
+    s = torch.empty(h // 128, n, dtype=torch.float32).t()
+    k["norm"][(n,)](x, r, w, q, s, x.stride(0), r.stride(0), q.stride(0), s.stride(1),
+                    s.stride(0), 1e-6, H=h, BLOCK=512, GROUP_C=128, NG=h // 128, UE8M0=False)
+    out.update(norm_r_out=r, norm_q=q.view(torch.uint8), norm_s=s.t().contiguous())
+
+    # qk_norm_rope: 4 q heads, 2 kv heads, head 128
+    n, qh, kh, d = 5, 4, 2, 128
+    qkv = torch.randn(n, (qh + 2 * kh) * d, generator=g).to(torch.bfloat16)
+    pos = torch.tensor([0, 3, 17, 100, 127], dtype=torch.int64)
+    t = torch.arange(128, dtype=torch.float32)
+    inv = 1.0 / (1e6 ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+    f = torch.einsum("i,j->ij", t, inv)
+    cs = torch.cat((f.cos(), f.sin()), dim=-1).to(torch.bfloat16)
+    qw = (1 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+    qo = torch.empty(n, qh * d, dtype=torch.bfloat16)
+    ko = torch.empty(n, kh * d, dtype=torch.bfloat16)
+    k["qk"][(n,)](qkv, qo, ko, cs, pos, qw, kw, qkv.stride(0), qo.stride(0), ko.stride(0),
+                  1e-6, QH=qh, KH=kh, HD=d, HALF=d // 2)
+    out.update(rope_qkv=qkv, rope_pos=pos, rope_cs=cs, rope_qw=qw, rope_kw=kw, rope_q=qo,
+               rope_k=ko)
+
+    # silu_mul_quant: rows x (2 x 1024)
+    n, half = 4, 1024
+    gu = (torch.randn(n, 2 * half, generator=g) * 3).to(torch.bfloat16)
+    q = torch.empty(n, half, dtype=torch.float8_e4m3fn)
+    s = torch.empty(half // 128, n, dtype=torch.float32).t()
+    k["silu"][(n, half // 512)](gu, q, s, gu.stride(0), q.stride(0), s.stride(1), s.stride(0),
+                                HALF=half, GROUP_C=128, GPB=4, UE8M0=False)
+    out.update(silu_gu=gu, silu_q=q.view(torch.uint8), silu_s=s.t().contiguous())
+
+    # merge_attn_quant: 6 rows, 4 heads x 128; rows 1 and 4 read nothing
+    n, heads, d = 6, 4, 128
+    a = torch.randn(n, heads, d, generator=g).to(torch.bfloat16)
+    b = torch.randn(4, heads, d, generator=g).to(torch.bfloat16)
+    la = torch.randn(heads, n, generator=g).t()
+    lb = torch.randn(heads, 4, generator=g).t()
+    src = torch.tensor([0, -1, 1, 2, -1, 3], dtype=torch.int32)
+    q = torch.empty(n, heads * d, dtype=torch.float8_e4m3fn)
+    s = torch.empty(heads, n, dtype=torch.float32).t()
+    k["merge_quant"][(n, heads // 4)](
+        a, b, la, lb, src, q, s, a.stride(0), a.stride(1), b.stride(0), b.stride(1),
+        la.stride(0), la.stride(1), lb.stride(0), lb.stride(1), q.stride(0), s.stride(1),
+        s.stride(0), D=d, GPB=4, UE8M0=False)
+    out.update(merge_a=a, merge_b=b, merge_la=la.contiguous(), merge_lb=lb.contiguous(),
+               merge_src=src, merge_q=q.view(torch.uint8), merge_s=s.t().contiguous())
+
+    # kv_row_scatter: 3 rows into a 10-row pool of 2 x 128
+    kk = torch.randn(4, 2, 128, generator=g).to(torch.bfloat16)
+    vv = torch.randn(4, 2, 128, generator=g).to(torch.bfloat16)
+    kpool = torch.zeros(10, 2, 128, dtype=torch.bfloat16)
+    vpool = torch.zeros(10, 2, 128, dtype=torch.bfloat16)
+    ssrc = torch.tensor([0, 2, 3], dtype=torch.int64)
+    sdst = torch.tensor([9, 0, 5], dtype=torch.int64)
+    k["kv_scatter"][(3,)](kk, vv, kpool, vpool, ssrc, sdst, ROW=256, ROW_POW2=256)
+    out.update(scat_k=kk, scat_v=vv, scat_src=ssrc, scat_dst=sdst, scat_kpool=kpool,
+               scat_vpool=vpool)
+
+    arrays = {}
+    for name, val in out.items():
+        if val.dtype == torch.bfloat16:
+            arrays[name + "__bf16"] = val.contiguous().view(torch.int16).numpy()
+        else:
+            arrays[name] = val.contiguous().numpy()
+    np.savez_compressed(HERE / "kernels.npz", **arrays)
+
+
+def main():
+    ref = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("QUAIL_REFERENCE", ""))
+    if not (ref / "quail").is_dir():
+        sys.exit("usage: make_golden.py <reference checkout>")
+    _install_reference(ref)
+    for name in SCENARIOS:
+        summary = run_reference_scenario(name)
+        print(name, "chunks", len(summary["chunks"]), "tokens", summary["tokens"])
+    make_kernel_vectors()
+    print("kernels.npz written")
+
+
+if __name__ == "__main__":
+    main()

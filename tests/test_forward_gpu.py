@@ -1,0 +1,96 @@
+"""End-to-end parity: the filter loop on the GPU against the CPU oracle.
+
+quail_b200.loop.run_filter drives the sm_100a pipeline over seeded rows
+that share an instruction prefix (the BASELINE config-1 row layout:
+prefix | suffix, one-token question tail); every packed chunk is replayed
+through the oracle's forward pass on the CPU in the same order, over a CPU
+copy of the arena. The north-star bar: yes-minus-no margins within 0.05
+absolute, and equal decisions wherever the oracle's |margin| > 0.1.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import forward as of
+from oracle import numerics as nx
+from quail_b200 import _native as nat
+from quail_b200 import loop
+from quail_b200.arena import KVArena
+from quail_b200.model import QWEN3_4B, TINY, random_weights
+from quail_b200.pipeline import Qwen3Pipeline
+from quail_b200.readout import AnswerRows, AsyncAnswers
+from quail_b200.tokens import prefix_tree
+
+pytestmark = pytest.mark.gpu
+
+MARGIN_TOL = 0.05
+DECISION_MARGIN = 0.1
+
+
+def rows_with_prefix(seed, n, prefix_len, lo, hi, vocab_lo, vocab_hi):
+    rng = np.random.default_rng(seed)
+    prefix = rng.integers(vocab_lo, vocab_hi, prefix_len).tolist()
+    lens = rng.integers(lo, hi + 1, n)
+    docs = [prefix + rng.integers(vocab_lo, vocab_hi, int(s)).tolist() for s in lens]
+    question = [int(np.random.default_rng(3).integers(vocab_lo, vocab_hi))]
+    return docs, [question]
+
+
+def run_and_compare(cfg, weights, docs, questions, budget, n_pages, mode):
+    dev = torch.device("cuda")
+    arena = KVArena(cfg.n_layers, n_pages, 16, cfg.n_kv, cfg.head_dim, device=dev)
+    arena.pools.zero_()
+    pipe = Qwen3Pipeline(torch, weights, arena)
+    ans = AsyncAnswers(torch, AnswerRows(torch, weights), keep_margins=True)
+    hosts = []
+    answers, _, _ = loop.run_filter(
+        torch, arena, pipe, ans, docs, questions, budget, arena_writes=True,
+        attention_mode=mode, prefix_tree=prefix_tree(docs, 16), device=dev,
+        on_chunk=lambda host, groups: hosts.append((host, list(groups))))
+    torch.cuda.synchronize()
+    assert nat.kernel_status(torch.cuda.current_device()) == 0
+    assert len(ans.margins) == len(hosts)
+    cpu_w = weights.to("cpu")
+    cpu_arena = of.CpuArena(cfg.n_layers, arena.pool_rows, cfg.n_kv, cfg.head_dim)
+    allowed, ans_w, tc, fc = cpu_w.answer_rows()
+    worst = 0.0
+    compared = 0
+    for (host, groups), got in zip(hosts, ans.margins):
+        normed = of.forward_chunk(cpu_w, host, cpu_arena)
+        want, _ = nx.answer_margin(normed, ans_w, tc, fc)
+        want = want.numpy()
+        diff = np.abs(got - want)
+        worst = max(worst, float(diff.max()))
+        assert diff.max() <= MARGIN_TOL, (diff.max(), got, want)
+        sure = np.abs(want) > DECISION_MARGIN
+        assert np.array_equal(got[sure] > 0, want[sure] > 0)
+        compared += len(want)
+    assert compared == sum(len(h.final_indices) for h, _ in hosts)
+    return answers, worst
+
+
+@pytest.mark.parametrize("mode", ["tree", "unified"])
+def test_tiny_filter_matches_oracle(mode):
+    cfg = TINY
+    weights = random_weights(cfg, seed=0, device="cuda")
+    docs, questions = rows_with_prefix(1, 48, 64, 16, 200, 16, cfg.vocab)
+    answers, worst = run_and_compare(cfg, weights, docs, questions, budget=1500,
+                                     n_pages=400, mode=mode)
+    assert len(answers) == len(docs)
+
+
+def test_tiny_multistage_filter_matches_oracle():
+    cfg = TINY
+    weights = random_weights(cfg, seed=4, device="cuda")
+    docs, _ = rows_with_prefix(2, 20, 48, 8, 100, 16, cfg.vocab)
+    questions = [[30, 31, 32], [30, 31, 40, 41], [30, 50]]
+    run_and_compare(cfg, weights, docs, questions, budget=800, n_pages=300, mode="tree")
+
+
+def test_qwen3_4b_shaped_rows_match_oracle():
+    """Full-width 36-layer model on a handful of config-1-shaped rows."""
+    cfg = QWEN3_4B
+    weights = random_weights(cfg, seed=0, device="cuda")
+    docs, questions = rows_with_prefix(0, 5, 64, 32, 120, 1000, 150000)
+    run_and_compare(cfg, weights, docs, questions, budget=4096, n_pages=200, mode="tree")

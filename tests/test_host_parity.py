@@ -1,0 +1,129 @@
+"""quail_b200's host loop against the reference's own, chunk by chunk.
+
+The fixtures (tests/golden/host_*.npz/.json) were produced by running the
+reference's run_filter with a recording pipeline (tests/golden/
+make_golden.py). The same documents go through quail_b200.loop.run_filter
+here; every packed array must match bit for bit: token ids, positions,
+answer rows, KV scatter rows, segment bounds, reader rows, block tables,
+the merge source map, unified tables, chunk layouts and final answers.
+"""
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from quail_b200 import loop
+from quail_b200.arena import KVArena
+from quail_b200.pipeline import ModelPipeline
+from quail_b200.tokens import prefix_tree
+from tests.golden import make_golden as mg
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def run_ours(name):
+    docs, questions, budget, pages, attention, use_tree, writes = mg.scenario_docs(name)
+    arena = KVArena(1, pages, 16, 1, 8, device=None)
+    arrays, entries = {}, []
+
+    class Recorder(ModelPipeline):
+        tree_attention = True
+
+        def forward_chunk(self, chunk):
+            entries.append(mg.chunk_record(chunk.host, arrays, len(entries)))
+            return chunk.host
+
+    class Answers:
+        def submit(self, host):
+            return mg.answer_bits(host.input_ids, host.positions, host.final_indices)
+
+        def result(self, handle):
+            return handle
+
+    tree = prefix_tree(docs, 16) if use_tree else None
+    stats = {}
+    answers, _, tokens = loop.run_filter(
+        torch, arena, Recorder(), Answers(), docs, questions, budget, arena_writes=writes,
+        attention_mode=attention, prefix_tree=tree, stats=stats, device="cpu")
+    return dict(entries=entries, arrays=arrays, tokens=tokens, answers=answers, stats=stats,
+                arena=arena, tree=tree)
+
+
+@pytest.mark.parametrize("name", mg.SCENARIOS)
+def test_packed_chunks_match_reference(name):
+    want = json.loads((GOLDEN / f"host_{name}.json").read_text())
+    want_arrays = np.load(GOLDEN / f"host_{name}.npz")
+    got = run_ours(name)
+    assert len(got["entries"]) == len(want["chunks"])
+    for i, (g, w) in enumerate(zip(got["entries"], want["chunks"])):
+        assert g == w, f"chunk {i} metadata differs"
+    assert sorted(got["arrays"]) == sorted(want_arrays.files)
+    for key in want_arrays.files:
+        a, b = got["arrays"][key], want_arrays[key]
+        assert a.shape == b.shape, key
+        assert np.array_equal(a.astype(np.int64), b.astype(np.int64)), key
+    assert got["tokens"] == want["tokens"]
+    assert got["stats"]["borrowed_tokens"] == want["borrowed_tokens"]
+    assert {str(k): v for k, v in sorted(got["answers"].items())} == want["answers"]
+    assert got["arena"].free_pages == want["free_pages_after"]
+    if want["tree"] is not None:
+        assert list(got["tree"].order) == want["tree"]["order"]
+        assert got["tree"].parent == want["tree"]["parent"]
+        assert list(got["tree"].shared) == want["tree"]["shared"]
+
+
+def test_prefix_tree_shapes():
+    """The reference's own prefix-tree cases (tests/test_tokens.py:74-108)."""
+    docs = [list(range(40)), list(range(50)), list(range(32)) + [99] * 20, [7] * 20, [7] * 10]
+    tree = prefix_tree(docs, 16)
+    assert tree.order == [0, 1, 2, 4, 3]
+    assert tree.parent == [None, 0, 0, None, None]
+    assert tree.shared == [0, 32, 32, 0, 0]
+    assert tree.shared_tokens == 64
+    assert prefix_tree([], 16).shared_tokens == 0
+    tree = prefix_tree([[], [], [5] * 16 + [6]], 16)
+    assert tree.parent == [None, None, None]
+    header = list(range(64))
+    docs = [header + [1] * 8, header + [2] * 8, header + [3] * 8,
+            header + [3] * 8 + [4] * 40, header + [5] * 8]
+    tree = prefix_tree(docs, 16)
+    assert tree.parent == [None, 0, 0, 0, 0]
+    assert tree.shared == [0, 64, 64, 64, 64]
+    docs = [header + [1] * 32, header + [1] * 32 + [2] * 8, header + [1] * 32 + [3] * 8]
+    tree = prefix_tree(docs, 16)
+    assert tree.parent == [None, 0, 0]
+    assert tree.shared == [0, 96, 96]
+
+
+def test_attention_tiles_cover_every_row_once():
+    cu = [0, 5, 5, 200, 264, 265]
+    tiles = loop.attention_tiles(cu)
+    covered = []
+    for seg, row0 in tiles:
+        end = min(row0 + loop.ATTN_TILE, cu[seg + 1])
+        assert cu[seg] <= row0 < cu[seg + 1]
+        covered.extend(range(row0, end))
+    assert sorted(covered) == list(range(265))
+    # most work first: offsets within a segment never increase
+    offsets = [row0 - cu[seg] for seg, row0 in tiles]
+    assert offsets == sorted(offsets, reverse=True)
+
+
+def test_arena_free_stack_and_borrow_holds():
+    arena = KVArena(1, 8, 16, 1, 8, device=None)
+    assert arena.alloc("a", 40) == [0, 1, 2]
+    assert arena.alloc("b", 48, borrow=("a", 32)) == [3]
+    assert arena.owned_pages("b") == [0, 1, 3]
+    assert list(arena.capacity_rows("b")[:3]) == [0, 1, 2]
+    arena.hold("a", 1)
+    assert arena.free_key("a") == 0          # deferred: a borrower is queued
+    arena.release("a")                       # the last borrower admitted
+    assert not arena.is_resident("a")
+    assert arena.free_pages == 8 - 3         # pages 0, 1 still held by b
+    arena.free_key("b")
+    assert arena.free_pages == 8
+    # LIFO: freed pages come back in release order
+    assert arena.alloc("c", 16) == [3]

@@ -1,0 +1,286 @@
+"""Per-kernel parity on the GPU: each libquailb200 entry point, called
+through the C ABI, against the CPU oracle on the same seeded inputs.
+
+Tolerances (written per test): norm/quant kernels use the oracle's fp32
+operation order, so bf16 outputs are exact and fp8 codes differ by at most
+one step on a few elements whose value sits on a rounding tie (fp32
+reductions in another order); GEMM outputs are within one bf16 ulp of
+the oracle (fp32 accumulation order); attention outputs are within one
+fp8 step (FlashAttention-style bf16 P and exp2 against exact softmax).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import forward as of
+from oracle import numerics as nx
+from quail_b200 import _native as nat
+from quail_b200 import loop
+from quail_b200.arena import KVArena
+from quail_b200.engine import Engine, QuantRows
+from quail_b200.model import TINY, random_weights
+from quail_b200.tokens import prefix_tree
+
+pytestmark = pytest.mark.gpu
+
+
+def codes_close(got, want, max_step=1, max_frac=0.002):
+    g = got.cpu().view(torch.uint8).to(torch.int32)
+    w = want.cpu().view(torch.uint8).to(torch.int32)
+    # e4m3 codes are monotone in value within a sign; compare signed values
+    gs = torch.where(g >= 128, -(g - 128), g)
+    ws = torch.where(w >= 128, -(w - 128), w)
+    d = (gs - ws).abs()
+    assert int(d.max()) <= max_step, int(d.max())
+    frac = float((d > 0).float().mean())
+    assert frac <= max_frac, frac
+
+
+def bf16_close(got, want, ulps=1, max_frac=1.0):
+    g = got.detach().cpu().to(torch.float32)
+    w = want.detach().cpu().to(torch.float32)
+    tol = w.abs() * (2.0 ** -8) * ulps + 1e-6 + 2e-3 * float(w.abs().mean())
+    bad = (g - w).abs() > tol
+    assert not bool(bad.any()), f"{int(bad.sum())} of {bad.numel()} beyond {ulps} ulp"
+    frac = float(((g - w).abs() > 0).float().mean())
+    assert frac <= max_frac, frac
+
+
+@pytest.fixture(scope="module")
+def dev():
+    torch.manual_seed(0)
+    return torch.device("cuda")
+
+
+def assert_status_clean():
+    assert nat.kernel_status(torch.cuda.current_device()) == 0
+
+
+class _Arena:
+    pool_rows = 64
+
+
+def engine_for(cfg, arena=None):
+    return Engine(torch, arena or _Arena(), cfg)
+
+
+@pytest.mark.parametrize("rows,hidden", [(1, 512), (37, 512), (300, 2560)])
+def test_embed_rmsnorm_quant(dev, rows, hidden):
+    g = torch.Generator().manual_seed(rows)
+    embed = (0.02 * torch.randn(1000, hidden, generator=g)).to(torch.bfloat16)
+    w = (1 + 0.05 * torch.randn(hidden, generator=g)).to(torch.bfloat16)
+    ids = torch.randint(0, 1000, (rows,), generator=g)
+    cfg = TINY
+    eng = engine_for(cfg)
+    res, out = eng.embed_norm_quant(ids.to(dev), embed.to(dev), w.to(dev))
+    r_ref, q_ref, s_ref = nx.embed_rmsnorm_quant(ids, embed, w, cfg.eps)
+    assert torch.equal(res.cpu().view(torch.int16), r_ref.view(torch.int16))
+    codes_close(out.q, q_ref)
+    torch.testing.assert_close(out.scale[:, :rows].cpu(), s_ref, rtol=1e-6, atol=0)
+    assert_status_clean()
+
+
+@pytest.mark.parametrize("rows,hidden", [(1, 512), (77, 2560), (5, 5120)])
+def test_add_rmsnorm_quant(dev, rows, hidden):
+    g = torch.Generator().manual_seed(hidden + rows)
+    x = (2 * torch.randn(rows, hidden, generator=g)).to(torch.bfloat16)
+    r = torch.randn(rows, hidden, generator=g).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(hidden, generator=g)).to(torch.bfloat16)
+    eng = engine_for(TINY)
+    r_dev = r.to(dev)
+    out = eng.norm_quant(x.to(dev), w.to(dev), r_dev)
+    r_ref, q_ref, s_ref = nx.add_rmsnorm_quant(x, r, w, TINY.eps)
+    assert torch.equal(r_dev.cpu().view(torch.int16), r_ref.view(torch.int16))
+    codes_close(out.q, q_ref)
+    torch.testing.assert_close(out.scale[:, :rows].cpu(), s_ref, rtol=1e-6, atol=0)
+
+
+@pytest.mark.parametrize("rows,inter", [(3, 1024), (129, 9728)])
+def test_silu_mul_quant(dev, rows, inter):
+    g = torch.Generator().manual_seed(inter)
+    gu = (3 * torch.randn(rows, 2 * inter, generator=g)).to(torch.bfloat16)
+    eng = engine_for(TINY)
+    out = eng.activation_quant(gu.to(dev))
+    q_ref, s_ref = nx.silu_mul_quant(gu)
+    # expf (CUDA, <= 2 ulp) against the CPU's exp: ties only
+    codes_close(out.q, q_ref, max_frac=0.003)
+    torch.testing.assert_close(out.scale[:, :rows].cpu(), s_ref, rtol=1e-6, atol=0)
+
+
+def _fp8_operands(g, m, n, k):
+    a = torch.randn(m, k, generator=g) * (1 + torch.rand(m, 1, generator=g))
+    aq, as_ = nx.quant_groups(a)
+    wq = torch.randn(n, k, generator=g).to(torch.float8_e4m3fn)
+    ws = torch.exp(np.log(0.02) + 0.3 * torch.randn(n // 128, k // 128, generator=g))
+    return aq, as_, wq, ws
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 256, 256), (7, 384, 512), (128, 256, 128),
+                                   (300, 1024, 2560), (257, 2560, 4096), (1000, 512, 9728)])
+def test_gemm_fp8_block_scaled(dev, m, n, k):
+    g = torch.Generator().manual_seed(m * 7 + n + k)
+    aq, as_, wq, ws = _fp8_operands(g, m, n, k)
+    eng = engine_for(TINY)
+    x = QuantRows(aq.to(dev), as_.to(dev).contiguous(), m)
+    out = eng.gemm(x, wq.to(dev), ws.to(dev))
+    torch.cuda.synchronize()
+    ref = nx.gemm_fp8_bs(aq, as_, wq, ws)
+    bf16_close(out, ref, ulps=1)
+    assert_status_clean()
+
+
+def test_gemm_large_against_dequantised_matmul(dev):
+    """A full 4B QKV-shaped GEMM against fp32 torch on the dequantised operands."""
+    g = torch.Generator(device="cuda").manual_seed(5)
+    m, n, k = 4096 + 77, 6144, 2560
+    a = torch.randn(m, k, device=dev, generator=g)
+    g2 = torch.Generator().manual_seed(6)
+    aq, as_ = nx.quant_groups(a.cpu())
+    wq = torch.randn(n, k, generator=g2).to(torch.float8_e4m3fn)
+    ws = torch.exp(np.log(0.02) + 0.3 * torch.randn(n // 128, k // 128, generator=g2))
+    eng = engine_for(TINY)
+    out = eng.gemm(QuantRows(aq.to(dev), as_.to(dev), m), wq.to(dev), ws.to(dev))
+    a_deq = nx.dequant(aq, as_).to(dev)
+    w_deq = (wq.float() * ws.repeat_interleave(128, 0).repeat_interleave(128, 1)).to(dev)
+    ref = (a_deq @ w_deq.t())
+    err = (out.float() - ref).abs()
+    assert float((err / (ref.abs() + 1e-2 * ref.abs().mean())).max()) < 0.02
+    assert float(err.mean() / ref.abs().mean()) < 2e-3
+    assert_status_clean()
+
+
+def test_qk_norm_rope_and_kv_append(dev):
+    cfg = TINY
+    rows = 50
+    g = torch.Generator().manual_seed(3)
+    qkv = torch.randn(rows, cfg.qkv_width, generator=g).to(torch.bfloat16)
+    pos = torch.randint(0, 4000, (rows,), generator=g)
+    w = random_weights(cfg, seed=1, device="cpu")
+    qw, kw = w.layers[0].q_norm, w.layers[0].k_norm
+    arena = KVArena(cfg.n_layers, 16, 16, cfg.n_kv, cfg.head_dim, device=dev)
+    arena.pools.zero_()
+    eng = Engine(torch, arena, cfg)
+    src = torch.tensor([0, 5, 7, 49], dtype=torch.int64)
+    dst = torch.tensor([3, 200, 0, 255], dtype=torch.int64)
+    row_dst = eng.kv_row_map(src.to(dev), dst.to(dev), rows)
+    q, k, v = eng.qk_norm_rope(qkv.to(dev), pos.to(dev), w.cos_sin.to(dev), qw.to(dev),
+                               kw.to(dev), 1, row_dst)
+    q_ref, k_ref, v_ref = nx.qk_norm_rope(qkv, pos, w.cos_sin, qw, kw, cfg.eps, cfg.n_q,
+                                          cfg.n_kv)
+    for got, want in ((q, q_ref), (k, k_ref)):
+        d = (got.cpu().view(torch.int16).int() - want.view(torch.int16).int()).abs()
+        assert int(d.max()) <= 1 and float((d > 0).float().mean()) < 0.01
+    assert torch.equal(v.cpu(), v_ref)
+    kp, vp = arena.layer_kv(1)
+    kp = kp.reshape(-1, cfg.n_kv * cfg.head_dim).cpu()
+    vp = vp.reshape(-1, cfg.n_kv * cfg.head_dim).cpu()
+    assert torch.equal(kp[dst], k.cpu()[src])
+    assert torch.equal(vp[dst], v.cpu()[src])
+    untouched = torch.ones(kp.shape[0], dtype=torch.bool)
+    untouched[dst] = False
+    assert int(kp[untouched].abs().sum()) == 0
+    assert_status_clean()
+
+
+def _attention_case(mode, dev, seed=0):
+    """A packed chunk (our packer) with random q/k/v and random resident KV."""
+    cfg = TINY
+    rng = np.random.default_rng(seed)
+    prefix = rng.integers(1000, 2000, 64).tolist()
+    lens = rng.integers(1, 150, 12)
+    docs = [prefix + rng.integers(1000, 2000, int(n)).tolist() for n in lens]
+    docs.append(prefix + rng.integers(1000, 2000, 300).tolist())
+    arena = KVArena(cfg.n_layers, 200, 16, cfg.n_kv, cfg.head_dim, device=dev)
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    arena.pools.copy_(torch.randn(arena.pools.shape, device=dev, generator=g))
+    chunks = []
+
+    class Capture:
+        tree_attention = True
+
+        def forward_chunk(self, chunk):
+            chunks.append(chunk)
+            return chunk
+
+    class Answers:
+        def submit(self, chunk):
+            return [1] * len(chunk.layout)
+
+        def result(self, h):
+            return h
+
+    # two stages so the second chunk has kept groups reading their own pages
+    loop.run_filter(torch, arena, Capture(), Answers(), docs, [[7, 8], [7, 9, 9]], 3000,
+                    arena_writes=True, attention_mode=mode, prefix_tree=prefix_tree(docs, 16),
+                    device=dev)
+    return cfg, arena, chunks
+
+
+@pytest.mark.parametrize("mode", ["tree", "unified"])
+def test_attention_against_oracle(dev, mode):
+    cfg, arena, chunks = _attention_case(mode, dev)
+    eng = Engine(torch, arena, cfg)
+    scale = cfg.head_dim ** -0.5
+    checked = 0
+    for chunk in chunks:
+        rows = chunk.tokens
+        g = torch.Generator(device="cuda").manual_seed(rows)
+        q = torch.randn(rows, cfg.n_q * cfg.head_dim, device=dev, generator=g).to(torch.bfloat16)
+        k = torch.randn(rows, cfg.n_kv * cfg.head_dim, device=dev, generator=g).to(torch.bfloat16)
+        v = torch.randn(rows, cfg.n_kv * cfg.head_dim, device=dev, generator=g).to(torch.bfloat16)
+        meta = chunk.meta
+        meta["layer"] = 0
+        kp, vp = arena.layer_kv(0)
+        kp2 = kp.reshape(-1, cfg.n_kv * cfg.head_dim)
+        vp2 = vp.reshape(-1, cfg.n_kv * cfg.head_dim)
+        host = chunk.host
+        if mode == "tree":
+            if meta["kv_src"] is not None:
+                kp2[meta["kv_dst"]] = k[meta["kv_src"]]
+                vp2[meta["kv_dst"]] = v[meta["kv_src"]]
+            kp_ref, vp_ref = kp2.cpu().clone(), vp2.cpu().clone()
+            out = eng.attention_tree(q, k, v, meta)
+            q_ref, s_ref = of.tree_attention(q.cpu(), k.cpu(), v.cpu(), host.meta, kp_ref,
+                                             vp_ref, cfg, arena.page_tokens)
+        else:
+            kp_ref, vp_ref = kp2.cpu().clone(), vp2.cpu().clone()
+            out = eng.attention_unified(q, k, v, meta)
+            q_ref, s_ref = of.unified_attention(q.cpu(), k.cpu(), v.cpu(), host.meta, kp_ref,
+                                                vp_ref, cfg, arena.page_tokens)
+            assert torch.equal(kp2.cpu(), kp_ref) and torch.equal(vp2.cpu(), vp_ref)
+        torch.cuda.synchronize()
+        codes_close(out.q, q_ref, max_step=1, max_frac=0.08)
+        torch.testing.assert_close(out.scale[:, :rows].cpu(), s_ref, rtol=2e-2, atol=0)
+        deq = nx.dequant(out.q.cpu(), out.scale[:, :rows].cpu())
+        ref = nx.dequant(q_ref, s_ref)
+        assert float((deq - ref).abs().mean() / ref.abs().mean()) < 0.01
+        checked += 1
+        assert scale > 0
+    assert checked >= 2
+    assert_status_clean()
+
+
+def test_final_norm_and_answer_margin(dev):
+    cfg = TINY
+    g = torch.Generator().manual_seed(11)
+    rows = 40
+    hidden = torch.randn(rows, cfg.hidden, generator=g).to(torch.bfloat16)
+    residual = torch.randn(rows, cfg.hidden, generator=g).to(torch.bfloat16)
+    finals = torch.tensor([3, 0, 39, 17], dtype=torch.int64)
+    w = random_weights(cfg, seed=2, device="cpu")
+    eng = engine_for(cfg)
+    normed = eng.final_norm(hidden.to(dev), residual.to(dev), finals.to(dev),
+                            w.final_norm.to(dev))
+    ref = nx.final_norm(hidden, residual, finals, w.final_norm, cfg.eps)
+    d = (normed.cpu().view(torch.int16).int() - ref.view(torch.int16).int()).abs()
+    assert int(d.max()) <= 1
+    from quail_b200.readout import AnswerRows
+    wd = w.to(dev)
+    rows_obj = AnswerRows(torch, wd)
+    margin, bits = rows_obj.margins(normed)
+    allowed, ans_w, tc, fc = w.answer_rows()
+    m_ref, b_ref = nx.answer_margin(normed.cpu(), ans_w, tc, fc)
+    torch.testing.assert_close(margin.cpu(), m_ref, rtol=0, atol=2 ** -6)
+    assert torch.equal(bits.cpu()[m_ref.abs() > 2 ** -5], b_ref[m_ref.abs() > 2 ** -5])
+    assert_status_clean()
