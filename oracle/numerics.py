@@ -40,6 +40,18 @@ def bf16(x):
     return to_bf16(x).to(torch.float32)
 
 
+# GEMM["partial_f64"]: exact per-block partial sums (a sensitivity probe; the
+# default is fp32 accumulation, as the tensor cores do).
+GEMM = {"partial_f64": False}
+
+
+def fma(a, b, c):
+    """fp32 a * b + c with one rounding (CUDA's fmaf / FFMA): the product of
+    two fp32 values is exact in fp64, and so is its sum with c unless the
+    exponents are far apart, where the result rounds the same way."""
+    return (a.double() * b.double() + c.double()).float()
+
+
 def quant_groups(y):
     """1x128 fp8 quantisation of fp32 rows.
 
@@ -108,7 +120,8 @@ def gemm_fp8_bs(a_codes, a_scales, w_codes, w_scales):
     """DeepGEMM fp8_gemm_nt as Quail calls it (attention.py:129-141):
     per 128-deep K block an fp32 partial product of the fp8 codes, scaled
     by a_scale[kb, m] * w_scale[n/128, kb] and accumulated in fp32 in K
-    order; bf16 output. a_scales is group-major (K/128, M)."""
+    order with one rounding per block (FFMA, as DeepGEMM's promotion
+    compiles); bf16 output. a_scales is group-major (K/128, M)."""
     m, k = a_codes.shape
     n = w_codes.shape[0]
     kb = k // GROUP
@@ -118,7 +131,10 @@ def gemm_fp8_bs(a_codes, a_scales, w_codes, w_scales):
     ws = w_scales.to(torch.float32).repeat_interleave(GROUP, dim=0)  # [n, kb]
     for b in range(kb):
         partial = a[b] @ w[b]
-        acc = acc + partial * (a_scales[b][:, None] * ws[:, b][None, :])
+        if GEMM["partial_f64"]:
+            partial = (a[b].double() @ w[b].double()).float()
+        sc = a_scales[b][:, None] * ws[:, b][None, :]
+        acc = fma(partial, sc, acc)
     return to_bf16(acc)
 
 
@@ -150,20 +166,53 @@ def qk_norm_rope(qkv, positions, cos_sin, q_w, k_w, eps, n_q, n_kv, head_dim=128
     return q, k, v
 
 
+# FlashAttention's algorithm (Dao et al., FlashAttention-2, 2023): keys in
+# blocks, a running row max m, P = exp2((s - m) * scale * log2 e) rounded to
+# the input dtype (bf16) before the PV product, row sums from the unrounded
+# fp32 P (exp2 of an FFMA), the accumulator rescaled when m grows, out =
+# acc / l rounded to
+# bf16, lse = m * scale + log(l). KEY_BLOCK is the key block of the sm_100a
+# kernel. ATTENTION["exact"] switches to exact fp32 softmax instead.
+KEY_BLOCK = 64
+ATTENTION = {"exact": False}
+_LOG2E = 1.4426950408889634
+
+
 def attend(q, k, v, scale, mask=None):
-    """Exact softmax attention in fp32 for one query head group.
+    """Softmax attention for one query head group (FlashAttention numerics).
 
     q [nq, d], k/v [nk, d] (bf16 values); mask [nq, nk] True = visible.
     Returns (out bf16 [nq, d], lse f32 [nq]) with lse the natural
     log-sum-exp of the scaled scores, FlashAttention's softmax_lse
     (attention.py:802-818, return_softmax_lse=True)."""
-    s = (q.to(torch.float32) @ k.to(torch.float32).t()) * scale
+    qf = q.to(torch.float32)
+    kf = k.to(torch.float32)
+    vf = v.to(torch.float32)
+    s = qf @ kf.t()
     if mask is not None:
         s = s.masked_fill(~mask, float("-inf"))
-    lse = torch.logsumexp(s, dim=-1)
-    p = torch.exp(s - lse[:, None])
-    out = p @ v.to(torch.float32)
-    return to_bf16(out), lse
+    if ATTENTION["exact"]:
+        s = s * scale
+        lse = torch.logsumexp(s, dim=-1)
+        out = torch.exp(s - lse[:, None]) @ vf
+        return to_bf16(out), lse
+    nq, nk = s.shape
+    sl2 = torch.tensor(scale * _LOG2E, dtype=torch.float32)
+    m = torch.full((nq,), float("-inf"))
+    l = torch.zeros(nq)
+    acc = torch.zeros(nq, v.shape[1])
+    for j0 in range(0, nk, KEY_BLOCK):
+        sb = s[:, j0:j0 + KEY_BLOCK]
+        m_new = torch.maximum(m, sb.amax(dim=1))
+        seen = m_new > float("-inf")
+        alpha = torch.where(seen, torch.exp2((m - m_new) * sl2), torch.ones(nq))
+        msl = torch.where(seen, m_new * sl2, torch.zeros(nq))
+        p = torch.exp2(fma(sb, sl2, -msl[:, None]))
+        l = l * alpha + p.sum(dim=1)
+        acc = acc * alpha[:, None] + bf16(p) @ vf[j0:j0 + KEY_BLOCK]
+        m = m_new
+    out = acc * (1.0 / l)[:, None]
+    return to_bf16(out), m * scale + torch.log(l)
 
 
 def attention_heads(q, k, v, n_q, n_kv, scale, mask=None, head_dim=128):

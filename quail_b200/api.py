@@ -1,0 +1,101 @@
+"""The public entry point of the B200 AI.IF path: one loaded GPU, one filter.
+
+``B200Executor`` is what Quail's per-GPU state holds after boot
+(quail/backends/quail/worker.py:46-148: model, KVArena, pipeline) and
+``filter`` is the AiFilter branch of QuailModelExecution._execute_quail_node
+(quail/backends/quail/backend.py:107-162): build the prefix tree when the
+plan shares prefixes, run the filter loop to the end, return per-document
+answers. Margins (yes - no logits) come back too, for parity checks.
+"""
+
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from quail_b200 import loop
+from quail_b200.arena import KVArena
+from quail_b200.model import random_weights
+from quail_b200.pipeline import build_pipeline
+from quail_b200.readout import AnswerRows, AsyncAnswers
+from quail_b200.tokens import prefix_tree
+
+
+@dataclass
+class FilterResult:
+    answers: dict                      # doc -> [0/1 per answered stage]
+    bits: np.ndarray                   # last answered stage's bit per doc
+    margins: np.ndarray                # last answered stage's margin per doc
+    fresh_tokens: int
+    borrowed_tokens: int
+    chunks: int
+    h2d_bytes: int
+    d2h_bytes: int
+    gpu_s: float
+    wall_s: float
+    timing: dict = field(default_factory=dict)
+
+
+class B200Executor:
+    """A model replica, its KV arena and pipeline on one GPU.
+
+    Args:
+        torch: the torch module.
+        cfg: ModelConfig (FP8 Qwen3 shapes).
+        n_pages: KV arena pages (16 tokens each).
+        weights: loaded Weights, or None for seeded random-init weights.
+        device: the CUDA device.
+    """
+
+    def __init__(self, torch, cfg, n_pages, weights=None, device="cuda", seed=0):
+        self.torch = torch
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.weights = weights or random_weights(cfg, seed=seed, device=self.device)
+        self.arena = KVArena(cfg.n_layers, n_pages, 16, cfg.n_kv, cfg.head_dim,
+                             device=self.device)
+        self.pipeline = build_pipeline(torch, self.weights, self.arena)
+        self.answer_rows = AnswerRows(torch, self.weights)
+        self.budget = cfg.max_chunk_tokens
+
+    def reset_arena(self):
+        """Free every page (the pools stay allocated)."""
+        self.arena.reset()
+
+    def filter(self, documents, question_ids, *, budget=None, attention="tree",
+               share_prefixes=True, arena_writes=True, limit=None) -> FilterResult:
+        """Run one AI.IF filter over documents; returns answers and margins."""
+        torch = self.torch
+        t0 = time.perf_counter()
+        tree = prefix_tree(documents, self.arena.page_tokens) if share_prefixes else None
+        ans = AsyncAnswers(torch, self.answer_rows, keep_margins=True)
+        last_margin = {}
+
+        def done(finished):
+            pass
+
+        stats, timing = {}, {}
+        order = []
+
+        def on_chunk(host, groups):
+            order.append([(doc, stage) for doc, stage, _ in groups])
+
+        answers, spans, tokens = loop.run_filter(
+            torch, self.arena, self.pipeline, ans, documents,
+            [list(q) for q in question_ids], budget or self.budget, timing=timing,
+            limit=limit, arena_writes=arena_writes, attention_mode=attention,
+            document_done=done, prefix_tree=tree, stats=stats, device=self.device,
+            on_chunk=on_chunk)
+        for groups, margins in zip(order, ans.margins):
+            for (doc, _stage), m in zip(groups, margins):
+                last_margin[doc] = float(m)
+        torch.cuda.synchronize(self.device)
+        wall = time.perf_counter() - t0
+        n = len(documents)
+        bits = np.array([answers.get(d, [0])[-1] for d in range(n)], dtype=np.uint8)
+        margins = np.array([last_margin.get(d, np.nan) for d in range(n)], dtype=np.float32)
+        gpu_s = sum(a.elapsed_time(b) for _, a, b in spans if a is not None) / 1000.0
+        return FilterResult(answers=answers, bits=bits, margins=margins, fresh_tokens=tokens,
+                            borrowed_tokens=stats.get("borrowed_tokens", 0),
+                            chunks=stats.get("chunks", 0), h2d_bytes=stats.get("h2d_bytes", 0),
+                            d2h_bytes=ans.d2h_bytes, gpu_s=gpu_s, wall_s=wall, timing=timing)

@@ -146,6 +146,14 @@ class KVArena:
         self._deferred = set()
         self.retention_cap_pages = None
 
+    def reset(self) -> None:
+        """Forget every key and hold (the pools stay allocated)."""
+        self.accounting = PageArena(self.accounting.n_pages, self.accounting.page_tokens)
+        self._capacity_rows = {}
+        self._holds = {}
+        self._deferred = set()
+        self.retention_cap_pages = None
+
     # ---- geometry ---------------------------------------------------------
 
     @property

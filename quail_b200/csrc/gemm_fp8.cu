@@ -171,11 +171,12 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <int BN>
+// OutT = bf16 (the library) or float (numerics probes: the fp32 accumulator).
+template <int BN, typename OutT = bf16>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                    const __grid_constant__ CUtensorMap map_b, const float* __restrict__ a_scale,
-                   int64_t a_scale_ld, const float* __restrict__ w_scale, bf16* __restrict__ out,
+                   int64_t a_scale_ld, const float* __restrict__ w_scale, OutT* __restrict__ out,
                    int M, int N, int K, uint32_t* status) {
     using C = Cfg<BN>;
     extern __shared__ uint8_t smem_raw[];
@@ -336,10 +337,17 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
             }
             if (!ok) break;
             if (valid) {
-                bf16* dst = out + (int64_t)m * N + n0 + col0;
+                OutT* dst = out + (int64_t)m * N + n0 + col0;
+                if constexpr (sizeof(OutT) == 2) {
 #pragma unroll
-                for (int j = 0; j < C::SLICE; j += 8)
-                    *reinterpret_cast<uint4*>(dst + j) = float_to_bf16x8(acc + j);
+                    for (int j = 0; j < C::SLICE; j += 8)
+                        *reinterpret_cast<uint4*>(dst + j) = float_to_bf16x8(acc + j);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < C::SLICE; j += 4)
+                        *reinterpret_cast<float4*>(dst + j) =
+                            make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+                }
             }
         }
     }

@@ -1,0 +1,65 @@
+"""Data parallelism over rows: one process per GPU, contiguous row slices.
+
+The reference runs one spawned child per GPU and merges pickled results on
+the host (quail/backends/quail/worker.py:646-711, coordinator.py:45-83).
+Here every rank is a torch.distributed process (NCCL over NVLink on GPUs,
+gloo on CPU for the host-logic tests): rank r filters rows
+[r * ceil(n / world), ...) of the input on its own model replica with its
+own prefix tree, and the per-row results (bit, margin) are all-gathered so
+every rank ends with the answers of all rows in input order. There is no
+other cross-GPU traffic: rows are independent.
+
+Failure handling (the reference re-raises a child's exception as
+"GPU child failed", worker.py:382-384, 665-667): every rank reports
+success or failure in one all-reduce before the result gather, so an
+exception on any rank raises RankFailed on all of them instead of leaving
+the others waiting; a rank that dies outright ends the others' next
+collective with the process group's timeout error.
+"""
+
+import numpy as np
+
+from quail_b200.workload import shard
+
+
+class RankFailed(RuntimeError):
+    """Another rank (or this one) failed during the sharded filter."""
+
+
+def gather_rows(torch, dist, values, device):
+    """All-gather a variable-length 1-D array from every rank, in rank order."""
+    world = dist.get_world_size()
+    n = torch.tensor([len(values)], dtype=torch.int64, device=device)
+    sizes = [torch.zeros_like(n) for _ in range(world)]
+    dist.all_gather(sizes, n)
+    width = int(max(int(s) for s in sizes))
+    buf = torch.zeros(max(width, 1), dtype=torch.float32, device=device)
+    buf[:len(values)] = torch.as_tensor(np.asarray(values, dtype=np.float32), device=device)
+    parts = [torch.zeros_like(buf) for _ in range(world)]
+    dist.all_gather(parts, buf)
+    return np.concatenate([p[:int(s)].cpu().numpy() for p, s in zip(parts, sizes)])
+
+
+def run_sharded(torch, dist, n_rows, run_slice, device="cpu"):
+    """Run run_slice(lo, hi) -> (bits, margins) on this rank's rows; gather all.
+
+    Returns (bits uint8 [n_rows], margins float32 [n_rows]) in row order on
+    every rank. Raises RankFailed on every rank when any rank raised.
+    """
+    rank, world = dist.get_rank(), dist.get_world_size()
+    lo, hi = shard(n_rows, rank, world)
+    error = None
+    bits = margins = np.zeros(0, dtype=np.float32)
+    try:
+        bits, margins = run_slice(lo, hi)
+    except Exception as exc:  # reported to every rank below
+        error = exc
+    ok = torch.tensor([0 if error is not None else 1], dtype=torch.int32, device=device)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if int(ok) == 0:
+        raise RankFailed(f"rank {rank}: a rank failed during the sharded filter") from error
+    all_bits = gather_rows(torch, dist, np.asarray(bits, dtype=np.float32), device)
+    all_margins = gather_rows(torch, dist, np.asarray(margins, dtype=np.float32), device)
+    if len(all_bits) != n_rows:
+        raise RankFailed(f"gathered {len(all_bits)} rows, expected {n_rows}")
+    return all_bits.astype(np.uint8), all_margins

@@ -168,7 +168,8 @@ def _norm(gen, n, device):
     return w.to(torch.bfloat16)
 
 
-def random_weights(cfg: ModelConfig, seed: int = 0, device="cpu") -> Weights:
+def random_weights(cfg: ModelConfig, seed: int = 0, device="cpu", embed_std=0.02,
+                   branch_scale=1.0, final_norm_scale=1.0) -> Weights:
     """Seeded random-init weights of a Qwen3 FP8 model.
 
     The same (cfg, seed, device type) always gives the same weights; CPU
@@ -180,14 +181,17 @@ def random_weights(cfg: ModelConfig, seed: int = 0, device="cpu") -> Weights:
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
     h, d = cfg.hidden, cfg.head_dim
-    embed = (0.02 * torch.randn(cfg.vocab, h, generator=gen, device=device)
+    embed = (embed_std * torch.randn(cfg.vocab, h, generator=gen, device=device)
              ).to(torch.bfloat16)
-    w = Weights(cfg, embed, _norm(gen, h, device), rotary_cache(cfg, device))
+    final_norm = (_norm(gen, h, device).float() * final_norm_scale).to(torch.bfloat16)
+    w = Weights(cfg, embed, final_norm, rotary_cache(cfg, device))
     for _ in range(cfg.n_layers):
         qkv_w, qkv_s = _fp8_linear(gen, cfg.qkv_width, h, device)
         o_w, o_s = _fp8_linear(gen, h, cfg.n_q * d, device)
         gu_w, gu_s = _fp8_linear(gen, 2 * cfg.inter, h, device)
         dn_w, dn_s = _fp8_linear(gen, h, cfg.inter, device)
+        o_s *= branch_scale
+        dn_s *= branch_scale
         w.layers.append(Layer(
             input_ln=_norm(gen, h, device), post_ln=_norm(gen, h, device),
             q_norm=_norm(gen, d, device), k_norm=_norm(gen, d, device),

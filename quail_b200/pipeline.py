@@ -49,6 +49,9 @@ class Qwen3Pipeline(ModelPipeline):
         self.tree_attention = True
         self.max_chunk_tokens = self.cfg.max_chunk_tokens
         self.layers = weights.layers
+        # a list records every op's output of the next forward passes as
+        # (layer, name, tensor); parity diagnostics only
+        self.trace = None
 
     def linears(self):
         layer = self.layers[0]
@@ -67,10 +70,13 @@ class Qwen3Pipeline(ModelPipeline):
             row_dst = eng.kv_row_map(meta["kv_src"], meta["kv_dst"], rows)
         hidden = None
         residual = None
+        trace = self.trace
         for index, layer in enumerate(self.layers):
             if index == 0:
                 residual, x = eng.embed_norm_quant(chunk.input_ids, w.embed, layer.input_ln)
             else:
+                if trace is not None:
+                    trace.append((index, "residual_in", residual.clone()))
                 x = eng.norm_quant(hidden, layer.input_ln, residual)
             qkv = eng.gemm(x, layer.qkv_w, layer.qkv_s)
             q, k, v = eng.qk_norm_rope(qkv, chunk.positions, w.cos_sin, layer.q_norm,
@@ -80,10 +86,18 @@ class Qwen3Pipeline(ModelPipeline):
             else:
                 o_in = eng.attention_unified(q, k, v, meta)
             hidden = eng.gemm(o_in, layer.o_w, layer.o_s)
+            if trace is not None:
+                trace.extend([(index, "x", x), (index, "qkv", qkv), (index, "q", q),
+                              (index, "k", k), (index, "v", v), (index, "o_in", o_in),
+                              (index, "o", hidden), (index, "residual_mid_in",
+                                                     residual.clone())])
             x = eng.norm_quant(hidden, layer.post_ln, residual)
             gate_up = eng.gemm(x, layer.gate_up_w, layer.gate_up_s)
-            x = eng.activation_quant(gate_up)
-            hidden = eng.gemm(x, layer.down_w, layer.down_s)
+            x2 = eng.activation_quant(gate_up)
+            hidden = eng.gemm(x2, layer.down_w, layer.down_s)
+            if trace is not None:
+                trace.extend([(index, "g_in", x), (index, "gate_up", gate_up),
+                              (index, "d_in", x2), (index, "down", hidden)])
         return eng.final_norm(hidden, residual, chunk.final_indices, w.final_norm)
 
 

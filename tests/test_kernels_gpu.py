@@ -37,10 +37,29 @@ def codes_close(got, want, max_step=1, max_frac=0.002):
     assert frac <= max_frac, frac
 
 
+def fp8_rows_close(q_got, s_got, q_ref, s_ref, max_frac=0.01):
+    """fp8 rows with per-group scales against the oracle's: scales within
+    1e-5 relative, dequantised values within one e4m3 step of the larger of
+    the two (2^-3 relative, or the group's subnormal step near zero), and
+    at most max_frac of the codes different (rounding ties: the kernel and
+    the oracle run the same FlashAttention algorithm, in another fp32 order)."""
+    s_got = s_got.cpu()
+    torch.testing.assert_close(s_got, s_ref, rtol=1e-5, atol=0)
+    deq = nx.dequant(q_got.cpu(), s_got)
+    ref = nx.dequant(q_ref, s_ref)
+    scale = s_ref.t().repeat_interleave(128, dim=1)
+    tol = torch.maximum(deq.abs(), ref.abs()) * 2.0 ** -3 + scale * 2.0 ** -6
+    assert bool(((deq - ref).abs() <= tol).all())
+    frac = float((q_got.cpu().view(torch.uint8) != q_ref.view(torch.uint8)).float().mean())
+    assert frac <= max_frac, frac
+
+
 def bf16_close(got, want, ulps=1, max_frac=1.0):
+    """Within `ulps` bf16 ulps of the oracle, where an ulp near zero is that
+    of the typical magnitude (cancellation in the fp32 sums)."""
     g = got.detach().cpu().to(torch.float32)
     w = want.detach().cpu().to(torch.float32)
-    tol = w.abs() * (2.0 ** -8) * ulps + 1e-6 + 2e-3 * float(w.abs().mean())
+    tol = (w.abs() * (2.0 ** -8) + (2.0 ** -8) * float(w.abs().mean())) * ulps
     bad = (g - w).abs() > tol
     assert not bool(bad.any()), f"{int(bad.sum())} of {bad.numel()} beyond {ulps} ulp"
     frac = float(((g - w).abs() > 0).float().mean())
@@ -250,11 +269,7 @@ def test_attention_against_oracle(dev, mode):
                                                 vp_ref, cfg, arena.page_tokens)
             assert torch.equal(kp2.cpu(), kp_ref) and torch.equal(vp2.cpu(), vp_ref)
         torch.cuda.synchronize()
-        codes_close(out.q, q_ref, max_step=1, max_frac=0.08)
-        torch.testing.assert_close(out.scale[:, :rows].cpu(), s_ref, rtol=2e-2, atol=0)
-        deq = nx.dequant(out.q.cpu(), out.scale[:, :rows].cpu())
-        ref = nx.dequant(q_ref, s_ref)
-        assert float((deq - ref).abs().mean() / ref.abs().mean()) < 0.01
+        fp8_rows_close(out.q, out.scale[:, :rows], q_ref, s_ref)
         checked += 1
         assert scale > 0
     assert checked >= 2
