@@ -5,12 +5,23 @@ boundaries in the dtypes the reference stores (bf16 activations, fp8 e4m3
 codes with fp32 scales), so roundings happen where the reference's do.
 Scales are returned group-major, (width / 128, rows), as the kernels
 write them.
+
+Two modes (MODE["exact"]):
+- exact (default, the parity oracle): every reduction in the order the
+  sm_100a kernels use, tensor-core products under the measured accumulation
+  model, exp2 / ln by the FMA-only methods both sides share (oracle/tc.py,
+  oracle/tcmodel.c). Agrees with the kernels bit for bit.
+- fast (the CPU baseline): the same algorithm with torch's own reductions,
+  fp32 BLAS GEMMs and exp; agrees to the last bits, runs at BLAS speed.
 """
 
 import torch
 
+from oracle import tc
+
 GROUP = 128
 FP8_MAX = 448.0
+MODE = {"exact": True}
 
 
 def _to_bf16(x):
@@ -40,16 +51,21 @@ def bf16(x):
     return to_bf16(x).to(torch.float32)
 
 
-# GEMM["partial_f64"]: exact per-block partial sums (a sensitivity probe; the
-# default is fp32 accumulation, as the tensor cores do).
-GEMM = {"partial_f64": False}
+def _sumsq_rows(x):
+    if MODE["exact"]:
+        return tc.sumsq_rows(x)[:, None]
+    return (x * x).sum(dim=-1, keepdim=True)
+
+
+def _sigmoid(x):
+    if MODE["exact"]:
+        return tc.sigmoid(x)
+    return 1.0 / (1.0 + torch.exp(-x))
 
 
 def fma(a, b, c):
-    """fp32 a * b + c with one rounding (CUDA's fmaf / FFMA): the product of
-    two fp32 values is exact in fp64, and so is its sum with c unless the
-    exponents are far apart, where the result rounds the same way."""
-    return (a.double() * b.double() + c.double()).float()
+    """fp32 a * b + c with one rounding (CUDA's fmaf / FFMA)."""
+    return tc.fma(a, b, c)
 
 
 def quant_groups(y):
@@ -76,13 +92,16 @@ def dequant(codes, scales):
     return (codes.to(torch.float32).reshape(rows, width // GROUP, GROUP) * s).reshape(rows, width)
 
 
+def _rstd(total, width, eps):
+    return 1.0 / torch.sqrt(total / width + eps)
+
+
 def rms_norm_bf16(x, w, eps):
     """vLLM rms_norm on bf16 rows (vllm/ir/ops/layernorm.py rms_norm):
     fp32 variance, x * rsqrt(var + eps) rounded to bf16, times the bf16
     weight, rounded to bf16."""
     x = x.to(torch.float32)
-    var = x.pow(2).mean(dim=-1, keepdim=True)
-    y = bf16(x * (1.0 / torch.sqrt(var + eps)))
+    y = bf16(x * _rstd(_sumsq_rows(x), x.shape[-1], eps))
     return bf16(y * w.to(torch.float32))
 
 
@@ -99,9 +118,7 @@ def add_rmsnorm_quant(hidden, residual, w, eps):
     residual in fp32; residual stored as bf16(x); y = x * rstd * w in fp32
     from the unrounded x; per-group quant. Returns (new residual, q, s)."""
     x = hidden.to(torch.float32) + residual.to(torch.float32)
-    ms = (x * x).sum(dim=-1, keepdim=True) / x.shape[-1]
-    rstd = 1.0 / torch.sqrt(ms + eps)
-    y = x * rstd * w.to(torch.float32)
+    y = x * _rstd(_sumsq_rows(x), x.shape[-1], eps) * w.to(torch.float32)
     q, s = quant_groups(y)
     return to_bf16(x), q, s
 
@@ -112,16 +129,19 @@ def silu_mul_quant(gate_up):
     half = gate_up.shape[1] // 2
     g = gate_up[:, :half].to(torch.float32)
     u = gate_up[:, half:].to(torch.float32)
-    y = g * (1.0 / (1.0 + torch.exp(-g))) * u
+    y = g * _sigmoid(g) * u
     return quant_groups(y)
 
 
 def gemm_fp8_bs(a_codes, a_scales, w_codes, w_scales):
-    """DeepGEMM fp8_gemm_nt as Quail calls it (attention.py:129-141):
-    per 128-deep K block an fp32 partial product of the fp8 codes, scaled
-    by a_scale[kb, m] * w_scale[n/128, kb] and accumulated in fp32 in K
-    order with one rounding per block (FFMA, as DeepGEMM's promotion
-    compiles); bf16 output. a_scales is group-major (K/128, M)."""
+    """DeepGEMM fp8_gemm_nt as Quail calls it (attention.py:129-141): per
+    128-deep K block an fp32 partial product of the fp8 codes, promoted
+    with acc = fma(partial, a_scale[kb, m] * w_scale[n/128, kb], acc) in K
+    order (DeepGEMM's promotion), bf16 output. a_scales is group-major
+    (K/128, M). Exact mode: the partials follow the tensor cores'
+    accumulation (tcmodel.c); fast mode: fp32 BLAS partials."""
+    if MODE["exact"]:
+        return tc.gemm_fp8(a_codes, a_scales, w_codes, w_scales)
     m, k = a_codes.shape
     n = w_codes.shape[0]
     kb = k // GROUP
@@ -130,11 +150,7 @@ def gemm_fp8_bs(a_codes, a_scales, w_codes, w_scales):
     acc = torch.zeros(m, n, dtype=torch.float32)
     ws = w_scales.to(torch.float32).repeat_interleave(GROUP, dim=0)  # [n, kb]
     for b in range(kb):
-        partial = a[b] @ w[b]
-        if GEMM["partial_f64"]:
-            partial = (a[b].double() @ w[b].double()).float()
-        sc = a_scales[b][:, None] * ws[:, b][None, :]
-        acc = fma(partial, sc, acc)
+        acc = acc + (a[b] @ w[b]) * (a_scales[b][:, None] * ws[:, b][None, :])
     return to_bf16(acc)
 
 
@@ -149,12 +165,14 @@ def qk_norm_rope(qkv, positions, cos_sin, q_w, k_w, eps, n_q, n_kv, head_dim=128
 
     def norm_rope(x, w, heads):
         x = x.reshape(rows, heads, head_dim).to(torch.float32)
-        a, b = x[..., :half], x[..., half:]
-        ms = ((a * a).sum(-1, keepdim=True) + (b * b).sum(-1, keepdim=True)) / head_dim
-        rstd = 1.0 / torch.sqrt(ms + eps)
+        if MODE["exact"]:
+            ss = tc.sumsq_heads(x).reshape(rows, heads, 1)
+        else:
+            ss = (x * x).sum(-1, keepdim=True)
+        rstd = 1.0 / torch.sqrt(ss / head_dim + eps)
         wf = w.to(torch.float32)
-        a = a * rstd * wf[:half]
-        b = b * rstd * wf[half:]
+        a = x[..., :half] * rstd * wf[:half]
+        b = x[..., half:] * rstd * wf[half:]
         out = torch.cat((a * cos - b * sin, b * cos + a * sin), dim=-1)
         return to_bf16(out).reshape(rows, heads * head_dim)
 
@@ -166,53 +184,73 @@ def qk_norm_rope(qkv, positions, cos_sin, q_w, k_w, eps, n_q, n_kv, head_dim=128
     return q, k, v
 
 
-# FlashAttention's algorithm (Dao et al., FlashAttention-2, 2023): keys in
-# blocks, a running row max m, P = exp2((s - m) * scale * log2 e) rounded to
-# the input dtype (bf16) before the PV product, row sums from the unrounded
-# fp32 P (exp2 of an FFMA), the accumulator rescaled when m grows, out =
-# acc / l rounded to
-# bf16, lse = m * scale + log(l). KEY_BLOCK is the key block of the sm_100a
-# kernel. ATTENTION["exact"] switches to exact fp32 softmax instead.
+# FlashAttention's algorithm (Dao, FlashAttention-2, 2023): keys in blocks,
+# a running row max m, P = exp2(s * scale * log2 e - m * scale * log2 e)
+# (an FFMA) rounded to bf16 before the PV product, row sums from the fp32 P,
+# the accumulator rescaled when m grows, out = acc * (1 / l) rounded to bf16,
+# lse = m * scale + ln(l). KEY_BLOCK is the key block of the sm_100a kernel.
+# Exact mode follows the kernel's thread layout for the row sums: thread tq
+# of a quad owns keys 8 nt + 2 tq + {0, 1} of each block, and the quad's four
+# sums combine as (l0 + l1) + (l2 + l3).
 KEY_BLOCK = 64
-ATTENTION = {"exact": False}
-_LOG2E = 1.4426950408889634
+LOG2E_F = 1.44269504088896341
 
 
 def attend(q, k, v, scale, mask=None):
-    """Softmax attention for one query head group (FlashAttention numerics).
+    """Softmax attention for one query head (FlashAttention numerics).
 
     q [nq, d], k/v [nk, d] (bf16 values); mask [nq, nk] True = visible.
     Returns (out bf16 [nq, d], lse f32 [nq]) with lse the natural
     log-sum-exp of the scaled scores, FlashAttention's softmax_lse
     (attention.py:802-818, return_softmax_lse=True)."""
-    qf = q.to(torch.float32)
-    kf = k.to(torch.float32)
-    vf = v.to(torch.float32)
-    s = qf @ kf.t()
+    nq, nk = q.shape[0], k.shape[0]
+    exact = MODE["exact"]
+    sl2 = torch.tensor(scale, dtype=torch.float32) * torch.tensor(LOG2E_F, dtype=torch.float32)
+    if exact:
+        s = tc.mma_bf16(q, k)
+    else:
+        s = q.to(torch.float32) @ k.to(torch.float32).t()
     if mask is not None:
         s = s.masked_fill(~mask, float("-inf"))
-    if ATTENTION["exact"]:
-        s = s * scale
-        lse = torch.logsumexp(s, dim=-1)
-        out = torch.exp(s - lse[:, None]) @ vf
-        return to_bf16(out), lse
-    nq, nk = s.shape
-    sl2 = torch.tensor(scale * _LOG2E, dtype=torch.float32)
     m = torch.full((nq,), float("-inf"))
-    l = torch.zeros(nq)
+    lq = torch.zeros(nq, 4)
     acc = torch.zeros(nq, v.shape[1])
+    exp2 = tc.exp2 if exact else torch.exp2
     for j0 in range(0, nk, KEY_BLOCK):
         sb = s[:, j0:j0 + KEY_BLOCK]
+        nb = sb.shape[1]
+        if nb < KEY_BLOCK:
+            sb = torch.cat([sb, torch.full((nq, KEY_BLOCK - nb), float("-inf"))], dim=1)
         m_new = torch.maximum(m, sb.amax(dim=1))
         seen = m_new > float("-inf")
-        alpha = torch.where(seen, torch.exp2((m - m_new) * sl2), torch.ones(nq))
+        alpha = torch.where(seen, exp2((m - m_new) * sl2), torch.ones(nq))
         msl = torch.where(seen, m_new * sl2, torch.zeros(nq))
-        p = torch.exp2(fma(sb, sl2, -msl[:, None]))
-        l = l * alpha + p.sum(dim=1)
-        acc = acc * alpha[:, None] + bf16(p) @ vf[j0:j0 + KEY_BLOCK]
+        if exact:
+            p = exp2(tc.fma(sb, sl2.expand_as(sb), (-msl)[:, None].expand_as(sb)))
+        else:
+            p = exp2(sb * sl2 - msl[:, None])
+        # per-thread row sums: thread tq adds keys 8 nt + 2 tq + e in (nt, e) order
+        lq = lq * alpha[:, None]
+        pv = p.reshape(nq, 8, 4, 2)
+        for nt in range(8):
+            for e in range(2):
+                lq = lq + pv[:, nt, :, e]
+        acc = acc * alpha[:, None]
+        pb = bf16(p)
+        vb = torch.zeros(KEY_BLOCK, v.shape[1], dtype=torch.bfloat16)
+        vb[:nb] = v[j0:j0 + nb]
+        if exact:
+            acc = tc.mma_bf16(pb, vb.t(), acc)
+        else:
+            acc = acc + pb @ vb.to(torch.float32)
         m = m_new
+    l = (lq[:, 0] + lq[:, 1]) + (lq[:, 2] + lq[:, 3])
     out = acc * (1.0 / l)[:, None]
-    return to_bf16(out), m * scale + torch.log(l)
+    if exact:
+        lse = tc.fma(m, torch.full_like(m, scale), tc.ln(l))
+    else:
+        lse = m * scale + torch.log(l)
+    return to_bf16(out), lse
 
 
 def attention_heads(q, k, v, n_q, n_kv, scale, mask=None, head_dim=128):
@@ -244,7 +282,7 @@ def merge_attn_quant(out_a, lse_a, out_b, lse_b, source, n_q, head_dim=128):
     safe = torch.clamp(source, min=0).long()
     b = out_b.to(torch.float32).reshape(-1, n_q, head_dim)[safe]
     lb = lse_b[safe]
-    w = bf16(1.0 / (1.0 + torch.exp(-(lb - lse_a))))
+    w = bf16(_sigmoid(lb - lse_a))
     merged = bf16(a + (b - a) * w[:, :, None])
     y = torch.where(has_b[:, None, None], merged, a)
     return quant_groups(y.reshape(rows, n_q * head_dim))
@@ -256,8 +294,7 @@ def final_norm(hidden, residual, finals, w, eps):
     x = hidden + residual in fp32, rstd from the unrounded x,
     bf16(bf16(x * rstd) * w)."""
     x = hidden[finals].to(torch.float32) + residual[finals].to(torch.float32)
-    var = x.pow(2).mean(dim=-1, keepdim=True)
-    y = bf16(x * (1.0 / torch.sqrt(var + eps)))
+    y = bf16(x * _rstd(_sumsq_rows(x), x.shape[-1], eps))
     return to_bf16(y * w.to(torch.float32))
 
 
@@ -265,7 +302,11 @@ def answer_margin(normed, ans_w, true_cols, false_cols):
     """AnswerRows.logits + AsyncAnswers.submit (readout.py:45-49, 70-80):
     bf16 scores of the retained head rows (fp32 accumulate), max per class,
     margin = t - f, bit = t > f."""
-    scores = bf16(normed.to(torch.float32) @ ans_w.to(torch.float32).t())
+    if MODE["exact"]:
+        raw = tc.dot_rows(normed.to(torch.float32), ans_w.to(torch.float32))
+    else:
+        raw = normed.to(torch.float32) @ ans_w.to(torch.float32).t()
+    scores = bf16(raw)
     t = scores[:, list(true_cols)].amax(dim=1)
     f = scores[:, list(false_cols)].amax(dim=1)
     return t - f, (t > f).to(torch.uint8)

@@ -30,13 +30,9 @@ __global__ void final_norm_kernel(const bf16* __restrict__ hidden,
     float h[8], r[8], x[8];
     bf16x8_to_float(*reinterpret_cast<const uint4*>(hidden + row * hdim + t * 8), h);
     bf16x8_to_float(*reinterpret_cast<const uint4*>(residual + row * hdim + t * 8), r);
-    float ss = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        x[j] = h[j] + r[j];
-        ss += x[j] * x[j];
-    }
-    const float total = block_sum(ss, scratch);
+    for (int j = 0; j < 8; ++j) x[j] = h[j] + r[j];
+    const float total = block_sum(sumsq8(x), scratch);
     const float rstd = 1.0f / sqrtf(total / (float)hdim + eps);
     float wf[8], y[8];
     bf16x8_to_float(*reinterpret_cast<const uint4*>(final_w + t * 8), wf);
@@ -61,16 +57,16 @@ __global__ void answer_margin_kernel(const bf16* __restrict__ normed, int hdim,
     for (int id = 0; id < n_ids; ++id) {
         float aw[8];
         bf16x8_to_float(*reinterpret_cast<const uint4*>(ans_w + (int64_t)id * hdim + t * 8), aw);
-        float d = 0.0f;
+        float d = __fmul_rn(y[0], aw[0]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) d = fmaf(y[j], aw[j], d);
+        for (int j = 1; j < 8; ++j) d = __fmaf_rn(y[j], aw[j], d);
         d = warp_sum(d);
         if (lane == 0) partial[warp][id] = d;
     }
     __syncthreads();
     if (t < n_ids) {
         float s = 0.0f;
-        for (int w = 0; w < n_warps; ++w) s += partial[w][t];
+        for (int w = 0; w < n_warps; ++w) s = __fadd_rn(s, partial[w][t]);
         scores[t] = bf16_round(s);
     }
     __syncthreads();

@@ -6,7 +6,11 @@
 // 4 warps x 16 rows. K/V tiles of 64 keys are staged in shared memory
 // (16-byte XOR swizzle) with cp.async double buffering; QK^T and PV use
 // bf16 mma.sync with fp32 accumulation. P is rounded to bf16 before PV and
-// the row sum uses the fp32 P, as FlashAttention does.
+// the row sum uses the fp32 P, as FlashAttention does. Every rounding step
+// is explicit (__f*_rn, the FMA-only exp2 / ln of common.cuh) and the row
+// sums follow one fixed order: thread tq of a quad adds keys 8 nt + 2 tq +
+// {0, 1} of each tile in (nt, e) order, and the quad combines its four sums
+// with an xor butterfly - so a CPU restatement can reproduce every bit.
 #include "common.cuh"
 
 namespace {
@@ -192,18 +196,18 @@ __device__ __forceinline__ void attend(const KeySource& src, int n_keys, bool ca
                 alpha[r] = 1.0f;
                 msl[r] = 0.0f;
             } else {
-                alpha[r] = exp2f((st.m[r] - m_new) * sl2);
-                msl[r] = m_new * sl2;
+                alpha[r] = qexp2f(__fmul_rn(__fsub_rn(st.m[r], m_new), sl2));
+                msl[r] = __fmul_rn(m_new, sl2);
             }
             st.m[r] = m_new;
-            st.l[r] *= alpha[r];
+            st.l[r] = __fmul_rn(st.l[r], alpha[r]);
         }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-            st.acc[i][0] *= alpha[0];
-            st.acc[i][1] *= alpha[0];
-            st.acc[i][2] *= alpha[1];
-            st.acc[i][3] *= alpha[1];
+            st.acc[i][0] = __fmul_rn(st.acc[i][0], alpha[0]);
+            st.acc[i][1] = __fmul_rn(st.acc[i][1], alpha[0]);
+            st.acc[i][2] = __fmul_rn(st.acc[i][2], alpha[1]);
+            st.acc[i][3] = __fmul_rn(st.acc[i][3], alpha[1]);
         }
         // P = exp2(s * sl2 - m * sl2); fp32 row sums; bf16 P for PV
         uint32_t pa[4][4];
@@ -212,8 +216,8 @@ __device__ __forceinline__ void attend(const KeySource& src, int n_keys, bool ca
             float p[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                p[e] = exp2f(fmaf(s[nt][e], sl2, -msl[e >> 1]));
-                st.l[e >> 1] += p[e];
+                p[e] = qexp2f(__fmaf_rn(s[nt][e], sl2, -msl[e >> 1]));
+                st.l[e >> 1] = __fadd_rn(st.l[e >> 1], p[e]);
             }
             const int kk = nt >> 1, half = nt & 1;
             pa[kk][half * 2 + 0] = pack_bf16(p[0], p[1]);
@@ -239,8 +243,8 @@ __device__ __forceinline__ void attend(const KeySource& src, int n_keys, bool ca
     cp_async_wait<0>();
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
-        st.l[r] += __shfl_xor_sync(0xffffffffu, st.l[r], 1);
-        st.l[r] += __shfl_xor_sync(0xffffffffu, st.l[r], 2);
+        st.l[r] = __fadd_rn(st.l[r], __shfl_xor_sync(0xffffffffu, st.l[r], 1));
+        st.l[r] = __fadd_rn(st.l[r], __shfl_xor_sync(0xffffffffu, st.l[r], 2));
     }
 }
 
@@ -285,7 +289,7 @@ tree_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
     }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gr = lane >> 2, tq = lane & 3;
-    const float sl2 = scale * 1.4426950408889634f;
+    const float sl2 = __fmul_rn(scale, 1.44269504088896341f);
 
     // query fragments (A operand), zero past the segment end
     uint32_t qa[8][4];
@@ -346,11 +350,12 @@ tree_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
         for (int r = 0; r < 2; ++r) {
             if (s_grp[my_row[r]] != g) continue;
             has_b[r] = true;
-            const float inv = 1.0f / st.l[r];
+            const float inv = __fdiv_rn(1.0f, st.l[r]);
 #pragma unroll
             for (int nd = 0; nd < 16; ++nd)
-                ob[r][nd] = pack_bf16(st.acc[nd][2 * r] * inv, st.acc[nd][2 * r + 1] * inv);
-            lse_b[r] = st.m[r] * scale + logf(st.l[r]);
+                ob[r][nd] = pack_bf16(__fmul_rn(st.acc[nd][2 * r], inv),
+                                      __fmul_rn(st.acc[nd][2 * r + 1], inv));
+            lse_b[r] = __fmaf_rn(st.m[r], scale, qlnf(st.l[r]));
         }
     }
 
@@ -377,17 +382,17 @@ tree_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
         const int row = row0 + my_row[r];
-        const float inv = 1.0f / st.l[r];
-        const float lse_a = st.m[r] * scale + logf(st.l[r]);
+        const float inv = __fdiv_rn(1.0f, st.l[r]);
+        const float lse_a = __fmaf_rn(st.m[r], scale, qlnf(st.l[r]));
         float y[32];
         float amax = 0.0f;
         float w = 0.0f;
-        if (has_b[r]) w = bf16_round(sigmoidf_ref(lse_b[r] - lse_a));
+        if (has_b[r]) w = bf16_round(sigmoidf_ref(__fsub_rn(lse_b[r], lse_a)));
 #pragma unroll
         for (int nd = 0; nd < 16; ++nd) {
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-                const float a = bf16_round(st.acc[nd][2 * r + e] * inv);
+                const float a = bf16_round(__fmul_rn(st.acc[nd][2 * r + e], inv));
                 float val = a;
                 if (has_b[r]) {
                     const bf162 bb = *reinterpret_cast<const bf162*>(&ob[r][nd]);

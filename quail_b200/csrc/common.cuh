@@ -77,8 +77,71 @@ __device__ __forceinline__ uint16_t fp8x2(float a, float b) {
     return static_cast<uint16_t>(s);
 }
 
+// ---- exp2 / exp / sigmoid / ln by fixed FMA-only methods -----------------
+// Every transcendental on the path goes through these, so a CPU restatement
+// with the same operations rounds identically (CUDA's expf / logf differ
+// from a CPU libm in the last bits, and one such bit moves a quantisation
+// group's scale).
+//   exp2: n = rint(x), f = x - n in [-1/2, 1/2], 2^f by the degree-7 Taylor
+//         series sum (ln 2)^k f^k / k! in Horner form, times 2^n;
+//   ln:   x = 2^e m with m in [sqrt(1/2), sqrt 2), ln m = 2 atanh(t),
+//         t = (m - 1) / (m + 1), atanh(t) = t (1 + t^2/3 + ... + t^12/13).
+
+__device__ __forceinline__ float qexp2f(float x) {
+    if (!(x >= -149.0f)) return (x != x) ? x : 0.0f;
+    if (x >= 128.0f) return __int_as_float(0x7f800000);
+    const float n = rintf(x);
+    const float f = __fsub_rn(x, n);
+    float p = 0.0000152527338040598403f;
+    p = __fmaf_rn(p, f, 0.000154035303933816099f);
+    p = __fmaf_rn(p, f, 0.00133335581464284434f);
+    p = __fmaf_rn(p, f, 0.00961812910762847716f);
+    p = __fmaf_rn(p, f, 0.0555041086648215800f);
+    p = __fmaf_rn(p, f, 0.240226506959100712f);
+    p = __fmaf_rn(p, f, 0.693147180559945309f);
+    p = __fmaf_rn(p, f, 1.0f);
+    const int ni = (int)n;
+    if (ni >= -126) return __fmul_rn(p, __int_as_float((ni + 127) << 23));
+    return __fmul_rn(__fmul_rn(p, __int_as_float((ni + 126 + 127) << 23)),
+                     __int_as_float(1 << 23));
+}
+
+__device__ __forceinline__ float qexpf(float x) {
+    return qexp2f(__fmul_rn(x, 1.44269504088896341f));
+}
+
 __device__ __forceinline__ float sigmoidf_ref(float x) {
-    return 1.0f / (1.0f + expf(-x));
+    return __fdiv_rn(1.0f, __fadd_rn(1.0f, qexpf(-x)));
+}
+
+// ln x for normal positive x
+__device__ __forceinline__ float qlnf(float x) {
+    const unsigned b = __float_as_uint(x);
+    int e = (int)((b >> 23) & 0xFF) - 127;
+    float m = __uint_as_float((b & 0x7FFFFFu) | 0x3F800000u);
+    if (m > 1.41421356237309505f) {
+        m = __fmul_rn(m, 0.5f);
+        e += 1;
+    }
+    const float t = __fdiv_rn(__fsub_rn(m, 1.0f), __fadd_rn(m, 1.0f));
+    const float t2 = __fmul_rn(t, t);
+    float p = 1.0f / 13.0f;
+    p = __fmaf_rn(p, t2, 1.0f / 11.0f);
+    p = __fmaf_rn(p, t2, 1.0f / 9.0f);
+    p = __fmaf_rn(p, t2, 1.0f / 7.0f);
+    p = __fmaf_rn(p, t2, 1.0f / 5.0f);
+    p = __fmaf_rn(p, t2, 1.0f / 3.0f);
+    p = __fmaf_rn(p, t2, 1.0f);
+    const float lnm = __fmul_rn(__fmul_rn(t, p), 2.0f);
+    return __fmaf_rn((float)e, 0.693147180559945309f, lnm);
+}
+
+// Sum of squares of 8 values in a fixed order: x0*x0, then FMAs.
+__device__ __forceinline__ float sumsq8(const float* x) {
+    float ss = __fmul_rn(x[0], x[0]);
+#pragma unroll
+    for (int i = 1; i < 8; ++i) ss = __fmaf_rn(x[i], x[i], ss);
+    return ss;
 }
 
 // unpack 8 bf16 held in a uint4 into floats
@@ -112,7 +175,9 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
-// Sum over the block; every thread gets the result. scratch holds 32 floats.
+// Sum over the block in a fixed order: an xor butterfly inside each warp
+// (every lane ends with the same bits), then the warp totals added in warp
+// order. Every thread gets the result. scratch holds 32 floats.
 __device__ __forceinline__ float block_sum(float v, float* scratch) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int n_warps = (blockDim.x + 31) >> 5;
@@ -120,8 +185,9 @@ __device__ __forceinline__ float block_sum(float v, float* scratch) {
     __syncthreads();
     if (lane == 0) scratch[warp] = v;
     __syncthreads();
-    float t = (lane < n_warps) ? scratch[lane] : 0.0f;
-    return warp_sum(t);
+    float t = scratch[0];
+    for (int w = 1; w < n_warps; ++w) t = __fadd_rn(t, scratch[w]);
+    return t;
 }
 
 }  // namespace qb

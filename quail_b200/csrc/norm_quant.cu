@@ -53,10 +53,7 @@ __global__ void embed_rmsnorm_quant_kernel(const int64_t* __restrict__ ids,
     *reinterpret_cast<uint4*>(residual_out + row * hidden + t * 8) = raw;
     float x[8];
     bf16x8_to_float(raw, x);
-    float ss = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
-    const float total = block_sum(ss, scratch);
+    const float total = block_sum(sumsq8(x), scratch);
     const float rstd = 1.0f / sqrtf(total / (float)hidden + eps);
     float wf[8];
     bf16x8_to_float(*reinterpret_cast<const uint4*>(w + t * 8), wf);
@@ -82,16 +79,13 @@ __global__ void add_rmsnorm_quant_kernel(const bf16* __restrict__ hidden_in,
 #pragma unroll
     for (int i = 0; i < 8; ++i) x[i] = h[i] + r[i];
     *reinterpret_cast<uint4*>(residual + off) = float_to_bf16x8(x);
-    float ss = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
-    const float total = block_sum(ss, scratch);
+    const float total = block_sum(sumsq8(x), scratch);
     const float rstd = 1.0f / sqrtf(total / (float)hidden + eps);
     float wf[8];
     bf16x8_to_float(*reinterpret_cast<const uint4*>(w + t * 8), wf);
     float y[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) y[i] = x[i] * rstd * wf[i];
+    for (int i = 0; i < 8; ++i) y[i] = __fmul_rn(__fmul_rn(x[i], rstd), wf[i]);
     quant_store8(y, q_out + row * hidden, scale_out, scale_ld, row, t);
 }
 
@@ -110,7 +104,7 @@ __global__ void silu_mul_quant_kernel(const bf16* __restrict__ gate_up, int64_t 
     bf16x8_to_float(*reinterpret_cast<const uint4*>(base + col8 * 8), g);
     bf16x8_to_float(*reinterpret_cast<const uint4*>(base + inter + col8 * 8), u);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) y[i] = g[i] * sigmoidf_ref(g[i]) * u[i];
+    for (int i = 0; i < 8; ++i) y[i] = __fmul_rn(__fmul_rn(g[i], sigmoidf_ref(g[i])), u[i]);
     quant_store8(y, q_out + row * inter, scale_out, scale_ld, row, col8);
 }
 

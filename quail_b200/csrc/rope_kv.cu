@@ -20,7 +20,11 @@ __device__ __forceinline__ void norm_rope_head(const bf16* src, bf16* dst, bf16*
                                                int lane) {
     float2 a = __bfloat1622float2(*reinterpret_cast<const bf162*>(src + 2 * lane));
     float2 b = __bfloat1622float2(*reinterpret_cast<const bf162*>(src + HALF + 2 * lane));
-    float ss = warp_sum(a.x * a.x + a.y * a.y + b.x * b.x + b.y * b.y);
+    float ss = __fmul_rn(a.x, a.x);
+    ss = __fmaf_rn(a.y, a.y, ss);
+    ss = __fmaf_rn(b.x, b.x, ss);
+    ss = __fmaf_rn(b.y, b.y, ss);
+    ss = warp_sum(ss);
     const float rstd = 1.0f / sqrtf(ss / (float)HEAD + eps);
     a.x = __fmul_rn(__fmul_rn(a.x, rstd), w_a.x);
     a.y = __fmul_rn(__fmul_rn(a.y, rstd), w_a.y);

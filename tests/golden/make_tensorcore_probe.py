@@ -1,0 +1,107 @@
+"""Measure the B200 tensor cores' fp32 accumulation and save it as a fixture.
+
+Needs a B200: builds tests/golden/tensorcore_probe.cu (the library's GEMM
+instantiated with an fp32 output, plus one mma.sync m16n8k16 bf16 per
+launch) and records, for seeded operands with a wide exponent spread:
+
+- gemm_s{3,6}_*: e4m3 codes a [64, 128], w [64, 128] and the fp32
+  accumulator of one 128-deep block (four tcgen05 K=32 MMAs, unit scales);
+- mma_*: bf16 A [16, 16], B [16, 8], fp32 C and the fp32 D = C + A B of one
+  mma.sync.
+
+tests/test_oracle_model.py checks that oracle/tcmodel.c reproduces every
+output bit for bit. Run: python tests/golden/make_tensorcore_probe.py
+"""
+
+import ctypes
+import subprocess
+import tempfile
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parent.parent
+
+
+def build(tmp):
+    so = Path(tmp) / "probe.so"
+    subprocess.run(["nvcc", "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17",
+                    "-Xcompiler", "-fPIC", "-shared", "-cudart", "static", "-I",
+                    str(ROOT / "include"), "-o", str(so), str(HERE / "tensorcore_probe.cu"),
+                    str(ROOT / "quail_b200" / "csrc" / "capi.cu")], check=True)
+    return ctypes.CDLL(str(so))
+
+
+def operands(rng, shape, spread):
+    x = rng.standard_normal(shape) * np.exp2(rng.integers(-spread, spread + 1, shape))
+    return np.clip(x, -400, 400).astype(np.float32)
+
+
+def main():
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(0)
+    out = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        lib = build(tmp)
+        P = ctypes.c_void_p
+        stream = P(torch.cuda.current_stream().cuda_stream)
+        for spread in (3, 6):
+            a = torch.from_numpy(operands(rng, (128, 128), spread)).to(torch.float8_e4m3fn)
+            w = torch.from_numpy(operands(rng, (256, 128), spread)).to(torch.float8_e4m3fn)
+            A, W = a.to(dev), w.to(dev)
+            AS, WS = torch.ones(1, 128, device=dev), torch.ones(2, 1, device=dev)
+            res = torch.zeros(128, 256, device=dev)
+            assert lib.probe_gemm_f32(P(A.data_ptr()), P(AS.data_ptr()), ctypes.c_int64(128),
+                                      P(W.data_ptr()), P(WS.data_ptr()), P(res.data_ptr()),
+                                      ctypes.c_int64(128), ctypes.c_int64(256),
+                                      ctypes.c_int64(128), stream) == 0
+            torch.cuda.synchronize()
+            out[f"gemm_s{spread}_a"] = a.view(torch.uint8).numpy()[:64]
+            out[f"gemm_s{spread}_w"] = w.view(torch.uint8).numpy()[:64]
+            out[f"gemm_s{spread}_out"] = res.cpu().numpy()[:64, :64]
+        reps = 96
+        A = np.zeros((reps, 16, 16), np.float32)
+        B = np.zeros((reps, 16, 8), np.float32)
+        C = np.zeros((reps, 16, 8), np.float32)
+        af = np.zeros((reps, 32, 4), np.uint32)
+        bfr = np.zeros((reps, 32, 2), np.uint32)
+        cf = np.zeros((reps, 32, 4), np.float32)
+        for r in range(reps):
+            s = (0, 4, 8)[r % 3]
+            ta = torch.from_numpy(operands(rng, (16, 16), s)).to(torch.bfloat16)
+            tb = torch.from_numpy(operands(rng, (16, 8), s)).to(torch.bfloat16)
+            A[r], B[r] = ta.float().numpy(), tb.float().numpy()
+            C[r] = 0 if r % 4 == 0 else operands(rng, (16, 8), s)
+            ba = ta.view(torch.int16).numpy().astype(np.uint16).astype(np.uint32)
+            bb = tb.view(torch.int16).numpy().astype(np.uint16).astype(np.uint32)
+            for t in range(32):
+                g, q = t // 4, t % 4
+                af[r, t] = [ba[g, 2 * q] | ba[g, 2 * q + 1] << 16,
+                            ba[g + 8, 2 * q] | ba[g + 8, 2 * q + 1] << 16,
+                            ba[g, 2 * q + 8] | ba[g, 2 * q + 9] << 16,
+                            ba[g + 8, 2 * q + 8] | ba[g + 8, 2 * q + 9] << 16]
+                bfr[r, t] = [bb[2 * q, g] | bb[2 * q + 1, g] << 16,
+                             bb[2 * q + 8, g] | bb[2 * q + 9, g] << 16]
+                cf[r, t] = [C[r, g, 2 * q], C[r, g, 2 * q + 1], C[r, g + 8, 2 * q],
+                            C[r, g + 8, 2 * q + 1]]
+        ad = torch.from_numpy(af.view(np.int32)).to(dev)
+        bd = torch.from_numpy(bfr.view(np.int32)).to(dev)
+        cd = torch.from_numpy(cf).to(dev)
+        dd = torch.zeros_like(cd)
+        assert lib.probe_mma(P(ad.data_ptr()), P(bd.data_ptr()), P(cd.data_ptr()),
+                             P(dd.data_ptr()), reps, stream) == 0
+        torch.cuda.synchronize()
+        dn = dd.cpu().numpy()
+        D = np.zeros((reps, 16, 8), np.float32)
+        for t in range(32):
+            g, q = t // 4, t % 4
+            D[:, g, 2 * q], D[:, g, 2 * q + 1] = dn[:, t, 0], dn[:, t, 1]
+            D[:, g + 8, 2 * q], D[:, g + 8, 2 * q + 1] = dn[:, t, 2], dn[:, t, 3]
+        out.update(mma_A=A, mma_B=B, mma_C=C, mma_D=D)
+    np.savez_compressed(HERE / "tensorcore_probe.npz", **out)
+
+
+if __name__ == "__main__":
+    main()

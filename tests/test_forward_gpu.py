@@ -4,8 +4,14 @@ quail_b200.loop.run_filter drives the sm_100a pipeline over seeded rows
 that share an instruction prefix (the BASELINE config-1 row layout:
 prefix | suffix, one-token question tail); every packed chunk is replayed
 through the oracle's forward pass on the CPU in the same order, over a CPU
-copy of the arena. The north-star bar: yes-minus-no margins within 0.05
-absolute, and equal decisions wherever the oracle's |margin| > 0.1.
+copy of the arena.
+
+The north-star bar is |margin difference| <= 0.05 and equal decisions
+where the oracle's |margin| > 0.1. These tests hold the stronger bar the
+exact oracle allows: margins equal bit for bit. (With random-init weights
+the bar needs it: one rounding tie that moves a single FP8 group scale
+changes a 36-layer model's margins by up to about 0.3, the oracle against
+itself with fp32 instead of exact GEMM partial sums included.)
 """
 
 import numpy as np
@@ -65,6 +71,8 @@ def run_and_compare(cfg, weights, docs, questions, budget, n_pages, mode):
         assert diff.max() <= MARGIN_TOL, (diff.max(), got, want)
         sure = np.abs(want) > DECISION_MARGIN
         assert np.array_equal(got[sure] > 0, want[sure] > 0)
+        assert np.array_equal(got.view(np.int32), want.astype(np.float32).view(np.int32)), \
+            (got, want)
         compared += len(want)
     assert compared == sum(len(h.final_indices) for h, _ in hosts)
     return answers, worst
@@ -92,5 +100,5 @@ def test_qwen3_4b_shaped_rows_match_oracle():
     """Full-width 36-layer model on a handful of config-1-shaped rows."""
     cfg = QWEN3_4B
     weights = random_weights(cfg, seed=0, device="cuda")
-    docs, questions = rows_with_prefix(0, 5, 64, 32, 120, 1000, 150000)
+    docs, questions = rows_with_prefix(0, 3, 64, 16, 48, 1000, 150000)
     run_and_compare(cfg, weights, docs, questions, budget=4096, n_pages=200, mode="tree")
