@@ -15,6 +15,7 @@ Two modes (MODE["exact"]):
   fp32 BLAS GEMMs and exp; agrees to the last bits, runs at BLAS speed.
 """
 
+import numpy as np
 import torch
 
 from oracle import tc
@@ -92,8 +93,15 @@ def dequant(codes, scales):
     return (codes.to(torch.float32).reshape(rows, width // GROUP, GROUP) * s).reshape(rows, width)
 
 
+def sqrt(x):
+    """IEEE (correctly rounded) fp32 square root, as CUDA's sqrtf computes it.
+    torch's CPU sqrt is not correctly rounded for float32; numpy's is."""
+    x = x.to(torch.float32).contiguous()
+    return torch.from_numpy(np.sqrt(x.numpy()))
+
+
 def _rstd(total, width, eps):
-    return 1.0 / torch.sqrt(total / width + eps)
+    return 1.0 / sqrt(total / width + eps)
 
 
 def rms_norm_bf16(x, w, eps):
@@ -169,7 +177,7 @@ def qk_norm_rope(qkv, positions, cos_sin, q_w, k_w, eps, n_q, n_kv, head_dim=128
             ss = tc.sumsq_heads(x).reshape(rows, heads, 1)
         else:
             ss = (x * x).sum(-1, keepdim=True)
-        rstd = 1.0 / torch.sqrt(ss / head_dim + eps)
+        rstd = 1.0 / sqrt(ss / head_dim + eps)
         wf = w.to(torch.float32)
         a = x[..., :half] * rstd * wf[:half]
         b = x[..., half:] * rstd * wf[half:]
