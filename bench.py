@@ -182,6 +182,9 @@ def cpu_baseline(torch, weights, wl, rows, page_tokens=16):
 
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
+    # the baseline times the reference's algorithm at BLAS speed (the
+    # oracle's fast mode), not the bit-exact tensor-core model
+    nx.MODE["exact"] = False
     cpu_w = weights.to("cpu")
     docs = [wl.docs[i] for i in range(rows)]
     arena = KVArena(1, 4096, page_tokens, 1, 8, device=None)

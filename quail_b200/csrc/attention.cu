@@ -2,15 +2,19 @@
 // own cu_a segment, (B) attention over the resident KV pages of its read
 // group (the shared prefix it borrows), then the LSE merge with the
 // reference's bf16 roundings and the per-head fp8 quantisation of the
-// o_proj input. One block = 64 query rows of one segment x one query head;
-// 4 warps x 16 rows. K/V tiles of 64 keys are staged in shared memory
-// (16-byte XOR swizzle) with cp.async double buffering; QK^T and PV use
-// bf16 mma.sync with fp32 accumulation. P is rounded to bf16 before PV and
-// the row sum uses the fp32 P, as FlashAttention does. Every rounding step
-// is explicit (__f*_rn, the FMA-only exp2 / ln of common.cuh) and the row
-// sums follow one fixed order: thread tq of a quad adds keys 8 nt + 2 tq +
-// {0, 1} of each tile in (nt, e) order, and the quad combines its four sums
-// with an xor butterfly - so a CPU restatement can reproduce every bit.
+// o_proj input.
+//
+// One block = 64 query rows of one segment x HP query heads of one KV head
+// (the GQA group, HP <= 4): K/V tiles of 64 keys are staged once in shared
+// memory (16-byte XOR swizzle, cp.async double buffering) and read by all
+// HP heads. Warp w computes rows 16 (w % 4) .. +16 of head w / 4 with bf16
+// mma.sync (fp32 accumulation); Q tiles and call B's results live in shared
+// memory. P is rounded to bf16 before PV and the row sum uses the fp32 P, as
+// FlashAttention does. Every rounding step is explicit (__f*_rn, the
+// FMA-only exp2 / ln of common.cuh) and the row sums follow one fixed
+// order: thread tq of a quad adds keys 8 nt + 2 tq + {0, 1} of each tile in
+// (nt, e) order, and the quad combines its four sums with an xor butterfly
+// - so a CPU restatement can reproduce every bit.
 #include "common.cuh"
 
 namespace {
@@ -20,9 +24,10 @@ using namespace qb;
 constexpr int D = 128;       // head dim
 constexpr int BM = 64;       // query rows per block
 constexpr int BN = 64;       // keys per tile
-constexpr int NWARPS = 4;
-constexpr int NTHREADS = NWARPS * 32;
+constexpr int ROW_GROUPS = BM / 16;
+constexpr int MAX_HP = 4;    // query heads per block
 constexpr int TILE_ELEMS = BN * D;
+constexpr int OB_LD = D + 8;  // padded row of call B's staged output
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -64,15 +69,15 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// element offset of (key row, 16-byte chunk) in a swizzled [BN][D] tile
-__device__ __forceinline__ int swz(int key, int chunk) { return key * D + ((chunk ^ (key & 7)) << 3); }
+// element offset of (row, 16-byte chunk) in a swizzled [64][D] tile
+__device__ __forceinline__ int swz(int row, int chunk) { return row * D + ((chunk ^ (row & 7)) << 3); }
 
 struct KeySource {
     const bf16* k;       // row-major [rows][n_kv][D]
     const bf16* v;
     int64_t n_rows;      // rows the source holds (bounds check)
-    // paged source (call B): key j lives at row table[j / page_tokens] *
-    // page_tokens + j % page_tokens; contiguous source (call A): row base + j
+    // paged source: key j lives at row table[j / page_tokens] * page_tokens +
+    // j % page_tokens; contiguous source: row base + j
     const int32_t* table;
     int page_tokens;
     int64_t base;
@@ -89,13 +94,12 @@ __device__ __forceinline__ int64_t key_row(const KeySource& s, int j, uint32_t* 
     return r;
 }
 
-// Stage keys [j0, j0 + BN) of head hk into buffers (zeros past n_keys).
+// Stage keys [j0, j0 + BN) of KV head hk into one K and one V tile (zeros
+// past n_keys); all threads of the block take part.
 __device__ __forceinline__ void load_tile(const KeySource& s, int j0, int n_keys, int n_kv, int hk,
                                           bf16* sk, bf16* sv, uint32_t* status) {
     const uint32_t k_base = smem_u32(sk), v_base = smem_u32(sv);
-#pragma unroll
-    for (int i = 0; i < (BN * D / 8) / NTHREADS; ++i) {
-        const int idx = threadIdx.x + i * NTHREADS;
+    for (int idx = threadIdx.x; idx < BN * D / 8; idx += blockDim.x) {
         const int kr = idx >> 4, chunk = idx & 15;
         int64_t row = -1;
         if (j0 + kr < n_keys) row = key_row(s, j0 + kr, status);
@@ -112,16 +116,15 @@ struct Softmax {
     float acc[16][4];  // 16 dim tiles of 8 x (rows gr, gr+8)
 };
 
-// Attend the warp's 16 query rows (q fragments qa) to keys [0, n_keys) of a
-// source; causal masks key j > query position (qpos - kpos0). Results are
-// left unnormalised in st.
-__device__ __forceinline__ void attend(const KeySource& src, int n_keys, bool causal, int q_first, int n_kv,
-                       int hk, const uint32_t (&qa)[8][4], float sl2, Softmax& st, bf16* smem,
-                       uint32_t* status) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+// Attend the warp's 16 query rows (Q tile in shared memory at q_tile, rows
+// r16 .. r16+15) to keys [0, n_keys) of a source; causal masks key j >
+// query position q_first + row. Leaves m, unnormalised l and acc in st.
+__device__ __forceinline__ void attend(const KeySource& src, int n_keys, bool causal, int q_first,
+                                       int n_kv, int hk, uint32_t q_tile, int r16, float sl2,
+                                       Softmax& st, bf16* kv, uint32_t* status) {
+    const int lane = threadIdx.x & 31;
     const int gr = lane >> 2, tq = lane & 3;
-    // query rows of this thread, relative to the source's key 0
-    const int qr0 = q_first + warp * 16 + gr, qr1 = qr0 + 8;
+    const int qr0 = q_first + r16 + gr, qr1 = qr0 + 8;
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
         st.m[r] = -INFINITY;
@@ -132,14 +135,13 @@ __device__ __forceinline__ void attend(const KeySource& src, int n_keys, bool ca
 #pragma unroll
         for (int j = 0; j < 4; ++j) st.acc[i][j] = 0.0f;
 
-    // causal: the block's last query row bounds the keys it needs
     int key_end = n_keys;
-    if (causal) key_end = min(n_keys, q_first + BM);
+    if (causal) key_end = min(n_keys, q_first + BM);  // the block's last row bounds its keys
     const int n_tiles = (key_end + BN - 1) / BN;
-    bf16* bufk[2] = {smem, smem + 2 * TILE_ELEMS};
-    bf16* bufv[2] = {smem + TILE_ELEMS, smem + 3 * TILE_ELEMS};
+    bf16* bufk[2] = {kv, kv + 2 * TILE_ELEMS};
+    bf16* bufv[2] = {kv + TILE_ELEMS, kv + 3 * TILE_ELEMS};
 
-    __syncthreads();  // buffers may still be read by a previous call
+    __syncthreads();  // the buffers may still be read by a previous call
     if (n_tiles > 0) load_tile(src, 0, key_end, n_kv, hk, bufk[0], bufv[0], status);
     cp_async_commit();
     for (int t = 0; t < n_tiles; ++t) {
@@ -149,12 +151,10 @@ __device__ __forceinline__ void attend(const KeySource& src, int n_keys, bool ca
         cp_async_commit();
         cp_async_wait<1>();
         __syncthreads();
-        const bf16* sk = bufk[t & 1];
-        const bf16* sv = bufv[t & 1];
-        const uint32_t kb = smem_u32(sk), vb = smem_u32(sv);
+        const uint32_t kb = smem_u32(bufk[t & 1]), vb = smem_u32(bufv[t & 1]);
         const int j0 = t * BN;
 
-        // S = Q K^T for 64 keys: 8 key tiles of 8
+        // S = Q K^T for 64 keys: 8 key tiles of 8, dims in 8 steps of 16
         float s[8][4];
 #pragma unroll
         for (int i = 0; i < 8; ++i)
@@ -162,6 +162,13 @@ __device__ __forceinline__ void attend(const KeySource& src, int n_keys, bool ca
             for (int j = 0; j < 4; ++j) s[i][j] = 0.0f;
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
+            uint32_t qa[4];
+            {
+                const int mi = lane >> 3, i = lane & 7;
+                const int row = r16 + (mi & 1) * 8 + i;
+                ldsm_x4(q_tile + (uint32_t)swz(row, 2 * ks + (mi >> 1)) * 2u, qa[0], qa[1], qa[2],
+                        qa[3]);
+            }
 #pragma unroll
             for (int nt = 0; nt < 8; nt += 2) {
                 const int mi = lane >> 3, i = lane & 7;
@@ -169,8 +176,8 @@ __device__ __forceinline__ void attend(const KeySource& src, int n_keys, bool ca
                 const int chunk = 2 * ks + (mi & 1);
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4(kb + (uint32_t)swz(key, chunk) * 2u, b0, b1, b2, b3);
-                mma_bf16(s[nt], qa[ks], b0, b1);
-                mma_bf16(s[nt + 1], qa[ks], b2, b3);
+                mma_bf16(s[nt], qa, b0, b1);
+                mma_bf16(s[nt + 1], qa, b2, b3);
             }
         }
         // mask and row max
@@ -226,7 +233,6 @@ __device__ __forceinline__ void attend(const KeySource& src, int n_keys, bool ca
         // O += P V: 4 key steps of 16 x 16 dim tiles of 8
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t a[4] = {pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3]};
 #pragma unroll
             for (int nd = 0; nd < 16; nd += 2) {
                 const int mi = lane >> 3, i = lane & 7;
@@ -234,8 +240,8 @@ __device__ __forceinline__ void attend(const KeySource& src, int n_keys, bool ca
                 const int chunk = nd + (mi >> 1);
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4_t(vb + (uint32_t)swz(key, chunk) * 2u, b0, b1, b2, b3);
-                mma_bf16(st.acc[nd], a, b0, b1);
-                mma_bf16(st.acc[nd + 1], a, b2, b3);
+                mma_bf16(st.acc[nd], pa[kk], b0, b1);
+                mma_bf16(st.acc[nd + 1], pa[kk], b2, b3);
             }
         }
         __syncthreads();  // the buffer is refilled two tiles later
@@ -250,7 +256,7 @@ __device__ __forceinline__ void attend(const KeySource& src, int n_keys, bool ca
 
 __device__ __forceinline__ int read_group(const int32_t* cu_q, int64_t n_reads, int idx) {
     // the group g with cu_q[g] <= idx < cu_q[g + 1]
-    int lo = 0, hi = (int)n_reads;  // invariant: cu_q[lo] <= idx < cu_q[hi]
+    int lo = 0, hi = (int)n_reads;
     while (hi - lo > 1) {
         const int mid = (lo + hi) >> 1;
         if (cu_q[mid] <= idx) lo = mid; else hi = mid;
@@ -258,14 +264,21 @@ __device__ __forceinline__ int read_group(const int32_t* cu_q, int64_t n_reads, 
     return lo;
 }
 
+// Shared memory: Q [hp][64][128] | K/V tiles x2 | (tree) call B output
+// [hp][64][OB_LD] bf16 | call B lse [hp][64] f32.
+__host__ __device__ constexpr size_t smem_bytes(int hp, bool tree) {
+    return (size_t)hp * BM * D * 2 + 4 * (size_t)TILE_ELEMS * 2 +
+           (tree ? (size_t)hp * BM * OB_LD * 2 + (size_t)hp * BM * 4 : 0);
+}
+
 // UNIFIED = false: the tree path (cu_a segments, call B over read groups,
 // merge). UNIFIED = true: the unified path, one causal paged call; cu_a is
 // then the unified cu_q, sequence s reads read_used[s] keys through table
 // row s, and its queries are the last cu_a[s+1] - cu_a[s] of those keys.
 template <bool UNIFIED>
-__global__ void __launch_bounds__(NTHREADS)
+__global__ void __launch_bounds__(ROW_GROUPS * 32 * MAX_HP, 1)
 tree_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
-                      const bf16* __restrict__ v, int64_t rows, int n_q, int n_kv,
+                      const bf16* __restrict__ v, int64_t rows, int n_q, int n_kv, int hp,
                       const int32_t* __restrict__ cu_a, const int32_t* __restrict__ tiles,
                       const int32_t* __restrict__ read_cu_q, const int32_t* __restrict__ read_used,
                       const int32_t* __restrict__ read_table, int64_t n_reads,
@@ -275,13 +288,17 @@ tree_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
                       uint8_t* __restrict__ q_out, float* __restrict__ scale_out,
                       int64_t scale_ld, uint32_t* status) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    bf16* smem = reinterpret_cast<bf16*>(smem_raw);
+    bf16* qs = reinterpret_cast<bf16*>(smem_raw);
+    bf16* kv = qs + hp * BM * D;
+    bf16* ob = kv + 4 * TILE_ELEMS;
+    float* lse_b_s = reinterpret_cast<float*>(ob + hp * BM * OB_LD);
     __shared__ int s_grp[BM];
 
     const int seg = tiles[2 * blockIdx.x];
     const int row0 = tiles[2 * blockIdx.x + 1];
-    const int h = blockIdx.y;
-    const int hk = h / (n_q / n_kv);
+    const int group = n_q / n_kv;
+    const int hk = blockIdx.y / (group / hp);
+    const int h_first = hk * group + (blockIdx.y % (group / hp)) * hp;
     const int seg_start = cu_a[seg], seg_end = cu_a[seg + 1];
     if (seg_start < 0 || seg_end > rows || row0 < seg_start || row0 >= seg_end) {
         if (threadIdx.x == 0) atomicOr(status, STATUS_BAD_INDEX);
@@ -289,77 +306,79 @@ tree_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
     }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gr = lane >> 2, tq = lane & 3;
+    const int r16 = (warp % ROW_GROUPS) * 16;
+    const int g = warp / ROW_GROUPS;     // head within the block
+    const int h = h_first + g;
     const float sl2 = __fmul_rn(scale, 1.44269504088896341f);
+    const uint32_t q_tile = smem_u32(qs + g * BM * D);
 
-    // query fragments (A operand), zero past the segment end
-    uint32_t qa[8][4];
-    {
-        const int r0 = row0 + warp * 16 + gr, r1 = r0 + 8;
-        const bf16* q0 = q + ((int64_t)r0 * n_q + h) * D;
-        const bf16* q1 = q + ((int64_t)r1 * n_q + h) * D;
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-            const int c = ks * 16 + 2 * tq;
-            qa[ks][0] = r0 < seg_end ? *reinterpret_cast<const uint32_t*>(q0 + c) : 0u;
-            qa[ks][1] = r1 < seg_end ? *reinterpret_cast<const uint32_t*>(q1 + c) : 0u;
-            qa[ks][2] = r0 < seg_end ? *reinterpret_cast<const uint32_t*>(q0 + c + 8) : 0u;
-            qa[ks][3] = r1 < seg_end ? *reinterpret_cast<const uint32_t*>(q1 + c + 8) : 0u;
-        }
+    // Q tiles of the block's heads, zero past the segment end
+    for (int idx = threadIdx.x; idx < hp * BM * (D / 8); idx += blockDim.x) {
+        const int hh = idx / (BM * (D / 8)), rem = idx % (BM * (D / 8));
+        const int r = rem >> 4, chunk = rem & 15;
+        const int row = row0 + r;
+        const bool ok = row < seg_end;
+        const bf16* src = q + ((int64_t)(ok ? row : row0) * n_q + h_first + hh) * D + chunk * 8;
+        cp_async16(smem_u32(qs + hh * BM * D + swz(r, chunk)), src, ok ? 16 : 0);
     }
+    cp_async_commit();
 
     // read group per tile row (-1: reads nothing resident)
     if (threadIdx.x < BM) {
         const int r = row0 + threadIdx.x;
-        int g = -1;
+        int grp = -1;
         if (!UNIFIED && r < seg_end && n_reads > 0) {
             const int src = source[r];
             if (src >= 0) {
                 if (src >= read_cu_q[n_reads]) atomicOr(status, STATUS_BAD_INDEX);
-                else g = read_group(read_cu_q, n_reads, src);
+                else grp = read_group(read_cu_q, n_reads, src);
             }
         }
-        s_grp[threadIdx.x] = g;
+        s_grp[threadIdx.x] = grp;
     }
+    cp_async_wait<0>();
     __syncthreads();
 
     Softmax st;
-    // call B results per thread row: bf16 out (16 dim tiles x 2 values) and lse
-    uint32_t ob[2][16];
-    float lse_b[2] = {0.0f, 0.0f};
-    bool has_b[2] = {false, false};
-    const int my_row[2] = {warp * 16 + gr, warp * 16 + gr + 8};
+    const int my_row[2] = {r16 + gr, r16 + gr + 8};
+    bf16* ob_head = ob + g * BM * OB_LD;
+    float* lse_head = lse_b_s + g * BM;
 
-    int g = -1;
-    while (true) {
-        int next = INT_MAX;
-        for (int i = 0; i < BM; ++i) {
-            const int x = s_grp[i];
-            if (x > g && x < next) next = x;
-        }
-        if (next == INT_MAX) break;
-        g = next;
-        KeySource src{k_pool, v_pool, pool_rows, read_table + (int64_t)g * table_width,
-                      page_tokens, 0};
-        int used = read_used[g];
-        if (used < 0 || (int64_t)((used + page_tokens - 1) / page_tokens) > table_width) {
-            if (threadIdx.x == 0) atomicOr(status, STATUS_BAD_INDEX);
-            used = 0;
-        }
-        attend(src, used, false, 0, n_kv, hk, qa, sl2, st, smem, status);
+    if (!UNIFIED) {
+        int cur = -1;
+        while (true) {
+            int next = INT_MAX;
+            for (int i = 0; i < BM; ++i) {
+                const int x = s_grp[i];
+                if (x > cur && x < next) next = x;
+            }
+            if (next == INT_MAX) break;
+            cur = next;
+            KeySource src{k_pool, v_pool, pool_rows, read_table + (int64_t)cur * table_width,
+                          page_tokens, 0};
+            int used = read_used[cur];
+            if (used < 0 || (int64_t)((used + page_tokens - 1) / page_tokens) > table_width) {
+                if (threadIdx.x == 0) atomicOr(status, STATUS_BAD_INDEX);
+                used = 0;
+            }
+            attend(src, used, false, 0, n_kv, hk, q_tile, r16, sl2, st, kv, status);
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            if (s_grp[my_row[r]] != g) continue;
-            has_b[r] = true;
-            const float inv = __fdiv_rn(1.0f, st.l[r]);
+            for (int r = 0; r < 2; ++r) {
+                if (s_grp[my_row[r]] != cur) continue;
+                const float inv = __fdiv_rn(1.0f, st.l[r]);
 #pragma unroll
-            for (int nd = 0; nd < 16; ++nd)
-                ob[r][nd] = pack_bf16(__fmul_rn(st.acc[nd][2 * r], inv),
-                                      __fmul_rn(st.acc[nd][2 * r + 1], inv));
-            lse_b[r] = __fmaf_rn(st.m[r], scale, qlnf(st.l[r]));
+                for (int nd = 0; nd < 16; ++nd)
+                    *reinterpret_cast<uint32_t*>(ob_head + my_row[r] * OB_LD + nd * 8 + 2 * tq) =
+                        pack_bf16(__fmul_rn(st.acc[nd][2 * r], inv),
+                                  __fmul_rn(st.acc[nd][2 * r + 1], inv));
+                if (tq == 0) lse_head[my_row[r]] = __fmaf_rn(st.m[r], scale, qlnf(st.l[r]));
+            }
         }
-    }
-
-    if (UNIFIED) {
+        // call A: causal over the segment's own rows
+        KeySource own{k, v, rows, nullptr, 1, seg_start};
+        attend(own, seg_end - seg_start, true, row0 - seg_start, n_kv, hk, q_tile, r16, sl2, st,
+               kv, status);
+    } else {
         // one causal call over the sequence's pages: retained KV + current rows
         int used = read_used[seg];
         const int q_len = seg_end - seg_start;
@@ -369,33 +388,32 @@ tree_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
         }
         KeySource paged{k_pool, v_pool, pool_rows, read_table + (int64_t)seg * table_width,
                         page_tokens, 0};
-        attend(paged, used, true, used - q_len + (row0 - seg_start), n_kv, hk, qa, sl2, st, smem,
-               status);
-    } else {
-        // call A: causal over the segment's own rows
-        KeySource own{k, v, rows, nullptr, 1, seg_start};
-        attend(own, seg_end - seg_start, true, row0 - seg_start, n_kv, hk, qa, sl2, st, smem,
-               status);
+        attend(paged, used, true, used - q_len + (row0 - seg_start), n_kv, hk, q_tile, r16, sl2,
+               st, kv, status);
     }
+    __syncwarp();
 
     // merge + per-head fp8 quantisation; one head = one 128-column group
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
         const int row = row0 + my_row[r];
+        const bool has_b = !UNIFIED && s_grp[my_row[r]] >= 0;
         const float inv = __fdiv_rn(1.0f, st.l[r]);
         const float lse_a = __fmaf_rn(st.m[r], scale, qlnf(st.l[r]));
         float y[32];
         float amax = 0.0f;
         float w = 0.0f;
-        if (has_b[r]) w = bf16_round(sigmoidf_ref(__fsub_rn(lse_b[r], lse_a)));
+        if (has_b) w = bf16_round(sigmoidf_ref(__fsub_rn(lse_head[my_row[r]], lse_a)));
 #pragma unroll
         for (int nd = 0; nd < 16; ++nd) {
+            bf162 bb;
+            if (has_b)
+                bb = *reinterpret_cast<const bf162*>(ob_head + my_row[r] * OB_LD + nd * 8 + 2 * tq);
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 const float a = bf16_round(__fmul_rn(st.acc[nd][2 * r + e], inv));
                 float val = a;
-                if (has_b[r]) {
-                    const bf162 bb = *reinterpret_cast<const bf162*>(&ob[r][nd]);
+                if (has_b) {
                     const float b = e == 0 ? __low2float(bb) : __high2float(bb);
                     val = bf16_round(__fadd_rn(a, __fmul_rn(__fsub_rn(b, a), w)));
                 }
@@ -429,9 +447,15 @@ int launch_attention(const char* who, const void* q, const void* k, const void* 
         set_error("%s: too many tiles", who);
         return QB_ERR_INVALID;
     }
+    const int group = n_q / n_kv;
+    const int hp = group < MAX_HP ? group : MAX_HP;
+    if (group % hp != 0) {
+        set_error("%s: query heads per KV head must be 1, 2, 4 or a multiple of 4", who);
+        return QB_ERR_INVALID;
+    }
     uint32_t* status = device_status_ptr();
     if (!status) return launch_status(who);
-    const size_t smem = 4 * TILE_ELEMS * sizeof(bf16);  // K and V, double buffered
+    const size_t smem = smem_bytes(MAX_HP, !UNIFIED);
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -442,10 +466,11 @@ int launch_attention(const char* who, const void* q, const void* k, const void* 
             return launch_status(who);
         attr_set[dev] = true;
     }
-    dim3 grid((unsigned)n_tiles, (unsigned)n_q);
-    tree_attention_kernel<UNIFIED><<<grid, NTHREADS, smem, (cudaStream_t)stream>>>(
-        (const bf16*)q, (const bf16*)k, (const bf16*)v, rows, n_q, n_kv, cu, tiles, read_cu_q,
-        read_used, table, n_reads, table_width, source, (const bf16*)k_pool,
+    dim3 grid((unsigned)n_tiles, (unsigned)(n_kv * (group / hp)));
+    tree_attention_kernel<UNIFIED><<<grid, ROW_GROUPS * 32 * hp, smem_bytes(hp, !UNIFIED),
+                                     (cudaStream_t)stream>>>(
+        (const bf16*)q, (const bf16*)k, (const bf16*)v, rows, n_q, n_kv, hp, cu, tiles,
+        read_cu_q, read_used, table, n_reads, table_width, source, (const bf16*)k_pool,
         (const bf16*)v_pool, n_pages * (int64_t)page_tokens, page_tokens, softmax_scale,
         (uint8_t*)q_out, scale_out, scale_ld, status);
     return launch_status(who);

@@ -156,9 +156,8 @@ __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// 16 consecutive 32-bit columns of this warp's 32 TMEM lanes.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-    uint32_t r[16];
+// 16 consecutive 32-bit columns of this warp's 32 TMEM lanes (no wait).
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t* r) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -166,9 +165,21 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
           "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
           "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// acc[0..1] = fma(v[0..1], s, acc[0..1]): two IEEE fp32 FMAs in one
+// instruction (fma.rn.f32x2), each rounded exactly as fmaf would.
+__device__ __forceinline__ void fma2(float* acc, const uint32_t* v, float s) {
+    uint64_t a, x, y;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(acc[0]), "f"(acc[1]));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "r"(v[0]), "r"(v[1]));
+    asm("mov.b64 %0, {%1, %1};" : "=l"(y) : "f"(s));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(a) : "l"(x), "l"(y));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(acc[0]), "=f"(acc[1]) : "l"(a));
 }
 
 // OutT = bf16 (the library) or float (numerics probes: the fp32 accumulator).
@@ -325,11 +336,14 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                 tc_fence_after();
                 const uint32_t taddr = tmem_base + lane_addr + (uint32_t)(buf * BN + col0);
 #pragma unroll
-                for (int c = 0; c < C::SLICE; c += 16) {
-                    float v[16];
-                    tmem_ld16(taddr + (uint32_t)c, v);
+                for (int c = 0; c < C::SLICE; c += 32) {
+                    // two loads in flight per wait
+                    uint32_t v[32];
+                    tmem_ld16_nowait(taddr + (uint32_t)c, v);
+                    tmem_ld16_nowait(taddr + (uint32_t)c + 16u, v + 16);
+                    tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) acc[c + j] = fmaf(v[j], sc, acc[c + j]);
+                    for (int j = 0; j < 32; j += 2) fma2(acc + c + j, v + j, sc);
                 }
                 tc_fence_before();
                 __syncwarp();
