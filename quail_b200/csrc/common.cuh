@@ -12,6 +12,7 @@
 #include <cuda_fp8.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <string.h>
 
 #include "../../include/quail_b200.h"
 

@@ -7,16 +7,22 @@
 // weights), so they cannot ride on the MX block-scale hardware path (UE8M0
 // only); each 128-deep K block is accumulated by the tensor cores into its
 // own TMEM buffer and promoted into fp32 registers by the epilogue warps with
-// that block's scales, while the tensor cores fill the other buffer.
+// that block's scales, while the tensor cores fill the next buffer.
 //
-// Persistent kernel, one block per SM, 18 warps:
+// Persistent kernel, one block per SM, 19 warps:
 //   warp 0      TMA producer: A [128 x 128] and W [BN x 128] tiles into a
 //               4-stage shared-memory ring (128-byte swizzle), one mbarrier
 //               transaction per stage;
-//   warp 1      allocates TMEM (2 x BN columns) and issues tcgen05.mma
+//   warp 1      allocates TMEM (512 columns: 512 / BN accumulator buffers)
+//               and issues tcgen05.mma
 //               (M=128, N=BN, K=32, kind::f8f6f4) from one thread;
-//   warps 2-17  epilogue: warp w reads TMEM lanes 32*(w%4).. (its rows) and
-//               columns (w-2)/4 * BN/4 .. (its slice), scales and accumulates.
+//   warp 2      scale loader: the K block's 128 activation scales and BN/128
+//               weight scales into an 8-slot shared-memory ring by cp.async,
+//               up to 8 K blocks ahead of the epilogue (the activation scales
+//               stream from HBM, and a load issued one K block ahead stalls
+//               the promotion on DRAM latency);
+//   warps 3-18  epilogue: warp w reads TMEM lanes 32*(w%4).. (its rows) and
+//               columns (w-3)/4 * BN/4 .. (its slice), scales and accumulates.
 // No cluster launch and no TMA multicast: every block loads its own tiles.
 // Every mbarrier wait is bounded (about one second); a wait that gives up
 // sets a status bit, makes the other roles stop, drains the copies and MMAs
@@ -31,30 +37,53 @@ using namespace qb;
 
 constexpr int BM = 128;
 constexpr int BK = 128;
-constexpr int STAGES = 4;
+constexpr int MAX_STAGES = 4;
 constexpr int EPI_WARPS = 16;
-constexpr int NUM_THREADS = (2 + EPI_WARPS) * 32;
+constexpr int FIRST_EPI_WARP = 3;
+constexpr int NUM_THREADS = (FIRST_EPI_WARP + EPI_WARPS) * 32;
+constexpr int SCALE_SLOTS = 8;
 constexpr uint64_t TIMEOUT_NS = 1000000000ull;
 
-template <int BN>
+// BN: tile width; NST: shared-memory pipeline stages; TSTORE: the tile is
+// written through a 128-byte-swizzled shared-memory staging area by TMA
+// stores (one 32 x 64 box per epilogue warp) instead of per-thread row
+// stores, so the epilogue returns to the next tile at once.
+template <int BN, int NST = MAX_STAGES, bool TSTORE = false>
 struct Cfg {
+    static constexpr int STAGES = NST;
+    static_assert(NST >= 2 && NST <= MAX_STAGES, "stages");
     static constexpr int A_BYTES = BM * BK;
     static constexpr int B_BYTES = BN * BK;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int TMEM_COLS = 2 * BN;  // two accumulator buffers
+    static constexpr int NBUF = 512 / BN;       // accumulator buffers in TMEM
+    static constexpr int TMEM_COLS = NBUF * BN;  // all 512 columns
     static constexpr int SLICE = BN / 4;      // columns per epilogue warp
-    static constexpr int BAR_BYTES = 256;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+    static_assert(!TSTORE || SLICE == 64, "TMA-store staging rows are 128 bytes");
+    static constexpr int OUT_BYTES = TSTORE ? EPI_WARPS * 32 * SLICE * 2 : 0;
+    static constexpr int SCALE_OFF = STAGES * STAGE_BYTES + OUT_BYTES;
+    static constexpr int BAR_OFF = SCALE_OFF + SCALE_SLOTS * 528;
+    static constexpr int BAR_BYTES = 512;
+    static constexpr int SMEM = BAR_OFF + BAR_BYTES + 1024;
     // instruction descriptor: D f32, A/B e4m3, both K-major, N, M=128
     static constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) |
                                       ((uint32_t)(BM >> 4) << 24);
 };
 
+// one K block's scales: a[r] for tile row r (0 past the last row), w[j] for
+// the tile's j-th 128-column weight block
+struct ScaleSlot {
+    float a[BM];
+    float w[4];
+};
+static_assert(sizeof(ScaleSlot) == 528, "scale slot layout");
+
 struct Barriers {
-    uint64_t full[STAGES];
-    uint64_t empty[STAGES];
-    uint64_t tmem_full[2];
-    uint64_t tmem_empty[2];
+    uint64_t full[MAX_STAGES];
+    uint64_t empty[MAX_STAGES];
+    uint64_t tmem_full[4];
+    uint64_t tmem_empty[4];
+    uint64_t scale_full[SCALE_SLOTS];
+    uint64_t scale_empty[SCALE_SLOTS];
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
@@ -116,6 +145,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
+// shared -> global tile store, tracked by this thread's bulk groups
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(src)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
                                             uint64_t* bar) {
     asm volatile(
@@ -147,6 +184,19 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
             smem_u32(bar))
         : "memory");
+}
+
+// 4-byte asynchronous copy global -> shared; src_bytes 0 writes a zero
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src),
+                 "r"(src_bytes)
+                 : "memory");
+}
+
+// arrives on the mbarrier once this thread's earlier cp.async copies landed
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -183,18 +233,23 @@ __device__ __forceinline__ void fma2(float* acc, const uint32_t* v, float s) {
 }
 
 // OutT = bf16 (the library) or float (numerics probes: the fp32 accumulator).
-template <int BN, typename OutT = bf16>
+// map_c (bf16 out, box 64 x 32, 128-byte swizzle) is read only when TSTORE.
+template <int BN, typename OutT = bf16, int NST = MAX_STAGES, bool TSTORE = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
-                   const __grid_constant__ CUtensorMap map_b, const float* __restrict__ a_scale,
+                   const __grid_constant__ CUtensorMap map_b,
+                   const __grid_constant__ CUtensorMap map_c, const float* __restrict__ a_scale,
                    int64_t a_scale_ld, const float* __restrict__ w_scale, OutT* __restrict__ out,
                    int M, int N, int K, uint32_t* status) {
-    using C = Cfg<BN>;
+    using C = Cfg<BN, NST, TSTORE>;
+    constexpr int STAGES = C::STAGES;
+    static_assert(!TSTORE || sizeof(OutT) == 2, "TMA stores write bf16");
     extern __shared__ uint8_t smem_raw[];
     // SWIZZLE_128B tiles need 1024-byte aligned shared memory
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
-    Barriers* bars = reinterpret_cast<Barriers*>(smem + STAGES * C::STAGE_BYTES);
+    ScaleSlot* scales = reinterpret_cast<ScaleSlot*>(smem + C::SCALE_OFF);
+    Barriers* bars = reinterpret_cast<Barriers*>(smem + C::BAR_OFF);
     volatile int* abort_flag = &bars->abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -208,9 +263,13 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
             mbar_init(&bars->full[s], 1);
             mbar_init(&bars->empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < C::NBUF; ++b) {
             mbar_init(&bars->tmem_full[b], 1);
             mbar_init(&bars->tmem_empty[b], EPI_WARPS);
+        }
+        for (int s = 0; s < SCALE_SLOTS; ++s) {
+            mbar_init(&bars->scale_full[s], 32);
+            mbar_init(&bars->scale_empty[s], EPI_WARPS);
         }
         mbar_init(&bars->drain, 1);
         bars->abort = 0;
@@ -277,8 +336,8 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                         ok = false;
                         break;
                     }
-                    const int buf = acc_it & 1;
-                    const uint32_t use = (uint32_t)(acc_it >> 1);
+                    const int buf = acc_it % C::NBUF;
+                    const uint32_t use = (uint32_t)(acc_it / C::NBUF);
                     if (!mbar_wait(&bars->tmem_empty[buf], (use & 1u) ^ 1u, abort_flag, status,
                                    STATUS_GEMM_MMA)) {
                         ok = false;
@@ -302,9 +361,42 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
             int flag = 0;
             mbar_wait(&bars->drain, 0, &flag, status, STATUS_GEMM_DRAIN);
         }
+    } else if (warp == 2) {
+        // ---------------- scale loader ----------------
+        int it = 0;
+        constexpr int NB = BN / 128;
+        for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+            const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
+            bool ok = true;
+            for (int kb = 0; kb < n_kb; ++kb, ++it) {
+                const int slot = it % SCALE_SLOTS;
+                const uint32_t round = (uint32_t)(it / SCALE_SLOTS);
+                if (!mbar_wait(&bars->scale_empty[slot], (round & 1u) ^ 1u, abort_flag, status,
+                               STATUS_GEMM_EPILOGUE)) {
+                    ok = false;
+                    break;
+                }
+                ScaleSlot* sl = scales + slot;
+                const float* col = a_scale + (int64_t)kb * a_scale_ld;
+#pragma unroll
+                for (int j = 0; j < BM / 32; ++j) {
+                    const int r = j * 32 + lane;
+                    const bool valid = m0 + r < M;
+                    cp_async4(smem_u32(&sl->a[r]), valid ? col + m0 + r : a_scale,
+                              valid ? 4u : 0u);
+                }
+                if (lane < NB)
+                    cp_async4(smem_u32(&sl->w[lane]),
+                              w_scale + (int64_t)(n0 / 128 + lane) * n_kb + kb, 4u);
+                cp_async_arrive(&bars->scale_full[slot]);
+            }
+            if (!ok) break;
+        }
+        // copies still in flight complete on their own; none may land after exit
+        asm volatile("cp.async.wait_all;" ::: "memory");
     } else {
         // ---------------- epilogue: promote, accumulate, store ----------------
-        const int ew = warp - 2;
+        const int ew = warp - FIRST_EPI_WARP;
         const int quarter = warp & 3;          // TMEM lanes this warp may access
         const int col0 = (ew >> 2) * C::SLICE; // its column slice
         const int row_in_tile = quarter * 32 + lane;
@@ -315,20 +407,20 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
             const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
             const int m = m0 + row_in_tile;
             const bool valid = m < M;
-            const float* ws_row = w_scale + (int64_t)((n0 + col0) / 128) * n_kb;
+            const int wblk = col0 / 128;
             float acc[C::SLICE];
 #pragma unroll
             for (int j = 0; j < C::SLICE; ++j) acc[j] = 0.0f;
-            float as_next = valid ? a_scale[m] : 0.0f;
-            float ws_next = ws_row[0];
             for (int kb = 0; kb < n_kb; ++kb, ++acc_it) {
-                const float sc = as_next * ws_next;
-                if (kb + 1 < n_kb) {
-                    as_next = valid ? a_scale[(int64_t)(kb + 1) * a_scale_ld + m] : 0.0f;
-                    ws_next = ws_row[kb + 1];
+                const int slot = acc_it % SCALE_SLOTS;
+                if (!mbar_wait(&bars->scale_full[slot], (uint32_t)(acc_it / SCALE_SLOTS) & 1u,
+                               abort_flag, status, STATUS_GEMM_EPILOGUE)) {
+                    ok = false;
+                    break;
                 }
-                const int buf = acc_it & 1;
-                if (!mbar_wait(&bars->tmem_full[buf], (uint32_t)(acc_it >> 1) & 1u, abort_flag,
+                const float sc = scales[slot].a[row_in_tile] * scales[slot].w[wblk];
+                const int buf = acc_it % C::NBUF;
+                if (!mbar_wait(&bars->tmem_full[buf], (uint32_t)(acc_it / C::NBUF) & 1u, abort_flag,
                                status, STATUS_GEMM_EPILOGUE)) {
                     ok = false;
                     break;
@@ -347,10 +439,31 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&bars->tmem_empty[buf]);
+                if (lane == 0) {
+                    mbar_arrive(&bars->tmem_empty[buf]);
+                    mbar_arrive(&bars->scale_empty[slot]);
+                }
             }
             if (!ok) break;
-            if (valid) {
+            if constexpr (TSTORE) {
+                // this warp's 32 rows x 64 columns, row r's 16-byte chunk j at
+                // r * 128 + (j ^ r % 8) * 16: the 128-byte swizzle of map_c,
+                // and conflict-free for one row per lane
+                uint8_t* stage = smem + STAGES * C::STAGE_BYTES + ew * 4096;
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                __syncwarp();
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    *reinterpret_cast<uint4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                        float_to_bf16x8(acc + 8 * j);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                // rows past M are clipped by the tensor map's bounds
+                if (lane == 0 && m0 + quarter * 32 < M) {
+                    tma_store_2d(&map_c, smem_u32(stage), n0 + col0, m0 + quarter * 32);
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                }
+            } else if (valid) {
                 OutT* dst = out + (int64_t)m * N + n0 + col0;
                 if constexpr (sizeof(OutT) == 2) {
 #pragma unroll
@@ -364,6 +477,8 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                 }
             }
         }
+        // the global writes of the last stores complete before the block exits
+        if (TSTORE && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
 
     tc_fence_before();
@@ -411,6 +526,27 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, int bo
     return QB_OK;
 }
 
+// bf16 output map: rows x n, box 32 rows x 64 columns, 128-byte swizzle
+int make_out_map(CUtensorMap* map, void* base, int64_t rows, int64_t n) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = get_encoder();
+    if (!enc) {
+        set_error("qb_gemm_fp8_bs: cuTensorMapEncodeTiled unavailable");
+        return QB_ERR_CUDA;
+    }
+    cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)n * 2};
+    cuuint32_t box[2] = {64, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("qb_gemm_fp8_bs: cuTensorMapEncodeTiled (out) failed (%d)", (int)r);
+        return QB_ERR_CUDA;
+    }
+    return QB_OK;
+}
+
 int sm_count() {
     static int count[64] = {0};
     int dev = 0;
@@ -424,21 +560,27 @@ int sm_count() {
     return count[dev];
 }
 
-template <int BN>
+template <int BN, int NST = MAX_STAGES, bool TSTORE = false>
 int launch(const void* a, const float* a_scale, int64_t a_scale_ld, const void* w,
            const float* w_scale, void* out, int64_t m, int64_t n, int64_t k, cudaStream_t stream) {
-    using C = Cfg<BN>;
-    CUtensorMap map_a, map_b;
+    using C = Cfg<BN, NST, TSTORE>;
+    CUtensorMap map_a, map_b, map_c;
+    memset(&map_c, 0, sizeof(map_c));
     int st = make_map(&map_a, a, m, k, BM);
     if (st) return st;
     st = make_map(&map_b, w, n, k, BN);
     if (st) return st;
+    if (TSTORE) {
+        st = make_out_map(&map_c, out, m, n);
+        if (st) return st;
+    }
+    auto kernel = gemm_fp8_bs_kernel<BN, bf16, NST, TSTORE>;
     static bool attr[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_fp8_bs_kernel<BN>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             C::SMEM);
         if (e != cudaSuccess) return launch_status("qb_gemm_fp8_bs: smem attribute");
         attr[dev] = true;
     }
@@ -446,8 +588,9 @@ int launch(const void* a, const float* a_scale, int64_t a_scale_ld, const void* 
     if (!status) return launch_status("qb_gemm_fp8_bs: status word");
     const int64_t tiles = ((m + BM - 1) / BM) * (n / BN);
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
-    gemm_fp8_bs_kernel<BN><<<grid, NUM_THREADS, C::SMEM, stream>>>(
-        map_a, map_b, a_scale, a_scale_ld, w_scale, (bf16*)out, (int)m, (int)n, (int)k, status);
+    kernel<<<grid, NUM_THREADS, C::SMEM, stream>>>(map_a, map_b, map_c, a_scale, a_scale_ld,
+                                                   w_scale, (bf16*)out, (int)m, (int)n, (int)k,
+                                                   status);
     return launch_status("qb_gemm_fp8_bs");
 }
 
@@ -466,7 +609,14 @@ extern "C" int qb_gemm_fp8_bs(const void* a, const float* a_scale, int64_t a_sca
         return invalid("qb_gemm_fp8_bs: a, w and out must be 16-byte aligned");
     if (!a_scale || !w_scale) return invalid("qb_gemm_fp8_bs: NULL scales");
     if (m == 0) return QB_OK;
+    cudaStream_t s = (cudaStream_t)stream;
+    // Short K (few K blocks per tile): the tile-end stores dominate, so the
+    // TMA-store epilogue wins even with 3 stages (measured on B200, 4B
+    // shapes: qkv, o and gate_up +12-24%). Long K (down, 76 K blocks): the
+    // fourth stage matters more.
+    if (n % 256 == 0 && k < 8192)
+        return launch<256, 3, true>(a, a_scale, a_scale_ld, w, w_scale, out, m, n, k, s);
     if (n % 256 == 0)
-        return launch<256>(a, a_scale, a_scale_ld, w, w_scale, out, m, n, k, (cudaStream_t)stream);
-    return launch<128>(a, a_scale, a_scale_ld, w, w_scale, out, m, n, k, (cudaStream_t)stream);
+        return launch<256, 4, false>(a, a_scale, a_scale_ld, w, w_scale, out, m, n, k, s);
+    return launch<128, 4, false>(a, a_scale, a_scale_ld, w, w_scale, out, m, n, k, s);
 }

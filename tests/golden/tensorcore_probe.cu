@@ -7,14 +7,15 @@
 extern "C" int probe_gemm_f32(const void* a, const float* as, int64_t ld, const void* w,
                               const float* ws, float* out, int64_t m, int64_t n, int64_t k,
                               void* stream) {
-    CUtensorMap ma, mb;
+    CUtensorMap ma, mb, mc;
+    memset(&mc, 0, sizeof(mc));  // no TMA store on the fp32 path
     if (make_map(&ma, a, m, k, BM) || make_map(&mb, w, n, k, 256)) return 1;
     cudaFuncSetAttribute(gemm_fp8_bs_kernel<256, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          Cfg<256>::SMEM);
     uint32_t* status = device_status_ptr();
     int64_t tiles = ((m + BM - 1) / BM) * (n / 256);
     gemm_fp8_bs_kernel<256, float><<<(int)(tiles < 148 ? tiles : 148), NUM_THREADS, Cfg<256>::SMEM,
-                                     (cudaStream_t)stream>>>(ma, mb, as, ld, ws, out, (int)m, (int)n,
+                                     (cudaStream_t)stream>>>(ma, mb, mc, as, ld, ws, out, (int)m, (int)n,
                                                              (int)k, status);
     return cudaGetLastError() != cudaSuccess;
 }
