@@ -206,14 +206,19 @@ static const float EXP2_C[8] = {
     0.00961812910762847716f, 0.00133335581464284434f, 0.000154035303933816099f,
     0.0000152527338040598403f};
 
+/* x is clamped to [-150, 128] (NaN stays NaN): 2^-150 rounds to 0 and
+   2^128 overflows to inf, so no other special case is needed. n = rint(x)
+   by adding and removing 1.5 * 2^23 (unit spacing: round to nearest even),
+   whose low mantissa bits hold n. */
 float qbm_exp2f(float x) {
-    if (!(x >= -149.0f)) return x != x ? x : 0.0f;
-    if (x >= 128.0f) return INFINITY;
-    const float n = rintf(x);
-    const float f = x - n;
+    if (x != x) return f32_from_bits(0x7fffffffu);
+    const float xc = x < -150.0f ? -150.0f : (x > 128.0f ? 128.0f : x);
+    const float t = xc + 12582912.0f;
+    const float n = t - 12582912.0f;
+    const float f = xc - n;
     float p = EXP2_C[7];
     for (int k = 6; k >= 0; --k) p = fmaf(p, f, EXP2_C[k]);
-    int ni = (int)n;
+    const int ni = (int)(f32_bits(t) - 0x4B400000u);
     if (ni >= -126) return p * f32_from_bits((uint32_t)(ni + 127) << 23);
     return (p * f32_from_bits((uint32_t)(ni + 126 + 127) << 23)) * f32_from_bits(1u << 23);
 }

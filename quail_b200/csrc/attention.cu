@@ -137,6 +137,8 @@ __device__ __forceinline__ void attend(const KeySource& src, int n_keys, bool ca
 
     int key_end = n_keys;
     if (causal) key_end = min(n_keys, q_first + BM);  // the block's last row bounds its keys
+    // keys past this bound are masked for all 16 rows of the warp
+    const int warp_end = causal ? min(key_end, q_first + r16 + 16) : key_end;
     const int n_tiles = (key_end + BN - 1) / BN;
     bf16* bufk[2] = {kv, kv + 2 * TILE_ELEMS};
     bf16* bufv[2] = {kv + TILE_ELEMS, kv + 3 * TILE_ELEMS};
@@ -153,6 +155,12 @@ __device__ __forceinline__ void attend(const KeySource& src, int n_keys, bool ca
         __syncthreads();
         const uint32_t kb = smem_u32(bufk[t & 1]), vb = smem_u32(bufv[t & 1]);
         const int j0 = t * BN;
+
+        // 8-key groups of the tile visible to some row of the warp; the rest
+        // have p = 0 exactly, so their QK^T, exp2 and PV steps are skipped
+        // (an all-zero PV step leaves the accumulator unchanged)
+        const int vis = warp_end - j0;
+        const int n8 = vis >= BN ? 8 : (vis <= 0 ? 0 : (vis + 7) >> 3);
 
         // S = Q K^T for 64 keys: 8 key tiles of 8, dims in 8 steps of 16
         float s[8][4];
@@ -171,6 +179,7 @@ __device__ __forceinline__ void attend(const KeySource& src, int n_keys, bool ca
             }
 #pragma unroll
             for (int nt = 0; nt < 8; nt += 2) {
+                if (nt >= n8) break;
                 const int mi = lane >> 3, i = lane & 7;
                 const int key = (nt + (mi >> 1)) * 8 + i;
                 const int chunk = 2 * ks + (mi & 1);
@@ -180,18 +189,28 @@ __device__ __forceinline__ void attend(const KeySource& src, int n_keys, bool ca
                 mma_bf16(s[nt + 1], qa, b2, b3);
             }
         }
-        // mask and row max
+        // mask (only tiles that reach past the keys or the warp's first row's
+        // diagonal) and row max
         float mx[2] = {-INFINITY, -INFINITY};
+        const bool edge = j0 + BN > key_end || (causal && j0 + BN - 1 > q_first + r16);
+        if (edge) {
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt) {
+                if (nt >= n8) break;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int key = j0 + nt * 8 + 2 * tq + (e & 1);
+                    const int qr = (e < 2) ? qr0 : qr1;
+                    const bool ok = key < key_end && (!causal || key <= qr);
+                    if (!ok) s[nt][e] = -INFINITY;
+                }
+            }
+        }
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
+            if (nt >= n8) break;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int key = j0 + nt * 8 + 2 * tq + (e & 1);
-                const int qr = (e < 2) ? qr0 : qr1;
-                const bool ok = key < key_end && (!causal || key <= qr);
-                if (!ok) s[nt][e] = -INFINITY;
-                mx[e >> 1] = fmaxf(mx[e >> 1], s[nt][e]);
-            }
+            for (int e = 0; e < 4; ++e) mx[e >> 1] = fmaxf(mx[e >> 1], s[nt][e]);
         }
         float alpha[2], msl[2];
 #pragma unroll
@@ -209,22 +228,34 @@ __device__ __forceinline__ void attend(const KeySource& src, int n_keys, bool ca
             st.m[r] = m_new;
             st.l[r] = __fmul_rn(st.l[r], alpha[r]);
         }
+        // a row whose max did not move has alpha == 1: its rescale is exact
+        // and skipped (warp-uniform in the common case)
+        if (alpha[0] != 1.0f || alpha[1] != 1.0f) {
+            const uint64_t a0 = f2pack(alpha[0], alpha[0]), a1 = f2pack(alpha[1], alpha[1]);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            st.acc[i][0] = __fmul_rn(st.acc[i][0], alpha[0]);
-            st.acc[i][1] = __fmul_rn(st.acc[i][1], alpha[0]);
-            st.acc[i][2] = __fmul_rn(st.acc[i][2], alpha[1]);
-            st.acc[i][3] = __fmul_rn(st.acc[i][3], alpha[1]);
+            for (int i = 0; i < 16; ++i) {
+                f2unpack(f2mul(f2pack(st.acc[i][0], st.acc[i][1]), a0), st.acc[i][0],
+                         st.acc[i][1]);
+                f2unpack(f2mul(f2pack(st.acc[i][2], st.acc[i][3]), a1), st.acc[i][2],
+                         st.acc[i][3]);
+            }
         }
         // P = exp2(s * sl2 - m * sl2); fp32 row sums; bf16 P for PV
         uint32_t pa[4][4];
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
-            float p[4];
+            float p[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (nt < n8) {
+                // x = s * sl2 - m * sl2 and exp2, two lanes per instruction
+                const uint64_t sl = f2pack(sl2, sl2);
+                f2unpack(f2fma(f2pack(s[nt][0], s[nt][1]), sl, f2pack(-msl[0], -msl[0])), p[0],
+                         p[1]);
+                f2unpack(f2fma(f2pack(s[nt][2], s[nt][3]), sl, f2pack(-msl[1], -msl[1])), p[2],
+                         p[3]);
+                qexp2f_x2(p[0], p[1]);
+                qexp2f_x2(p[2], p[3]);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                p[e] = qexp2f(__fmaf_rn(s[nt][e], sl2, -msl[e >> 1]));
-                st.l[e >> 1] = __fadd_rn(st.l[e >> 1], p[e]);
+                for (int e = 0; e < 4; ++e) st.l[e >> 1] = __fadd_rn(st.l[e >> 1], p[e]);
             }
             const int kk = nt >> 1, half = nt & 1;
             pa[kk][half * 2 + 0] = pack_bf16(p[0], p[1]);
@@ -233,6 +264,7 @@ __device__ __forceinline__ void attend(const KeySource& src, int n_keys, bool ca
         // O += P V: 4 key steps of 16 x 16 dim tiles of 8
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
+            if (2 * kk >= n8) break;
 #pragma unroll
             for (int nd = 0; nd < 16; nd += 2) {
                 const int mi = lane >> 3, i = lane & 7;
@@ -293,6 +325,8 @@ tree_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
     bf16* ob = kv + 4 * TILE_ELEMS;
     float* lse_b_s = reinterpret_cast<float*>(ob + hp * BM * OB_LD);
     __shared__ int s_grp[BM];
+    __shared__ int s_list[BM];  // the distinct read groups of the tile, ascending
+    __shared__ int s_nlist;
 
     const int seg = tiles[2 * blockIdx.x];
     const int row0 = tiles[2 * blockIdx.x + 1];
@@ -338,6 +372,23 @@ tree_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
     }
     cp_async_wait<0>();
     __syncthreads();
+    if (!UNIFIED) {
+        if (threadIdx.x == 0) {
+            int n = 0, cur = -1;
+            while (true) {
+                int next = INT_MAX;
+                for (int i = 0; i < BM; ++i) {
+                    const int x = s_grp[i];
+                    if (x > cur && x < next) next = x;
+                }
+                if (next == INT_MAX) break;
+                s_list[n++] = next;
+                cur = next;
+            }
+            s_nlist = n;
+        }
+        __syncthreads();
+    }
 
     Softmax st;
     const int my_row[2] = {r16 + gr, r16 + gr + 8};
@@ -345,15 +396,9 @@ tree_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
     float* lse_head = lse_b_s + g * BM;
 
     if (!UNIFIED) {
-        int cur = -1;
-        while (true) {
-            int next = INT_MAX;
-            for (int i = 0; i < BM; ++i) {
-                const int x = s_grp[i];
-                if (x > cur && x < next) next = x;
-            }
-            if (next == INT_MAX) break;
-            cur = next;
+        const int n_list = s_nlist;
+        for (int li = 0; li < n_list; ++li) {
+            const int cur = s_list[li];
             KeySource src{k_pool, v_pool, pool_rows, read_table + (int64_t)cur * table_width,
                           page_tokens, 0};
             int used = read_used[cur];
@@ -365,7 +410,7 @@ tree_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
                 if (s_grp[my_row[r]] != cur) continue;
-                const float inv = __fdiv_rn(1.0f, st.l[r]);
+                const float inv = __frcp_rn(st.l[r]);
 #pragma unroll
                 for (int nd = 0; nd < 16; ++nd)
                     *reinterpret_cast<uint32_t*>(ob_head + my_row[r] * OB_LD + nd * 8 + 2 * tq) =
@@ -398,7 +443,7 @@ tree_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
     for (int r = 0; r < 2; ++r) {
         const int row = row0 + my_row[r];
         const bool has_b = !UNIFIED && s_grp[my_row[r]] >= 0;
-        const float inv = __fdiv_rn(1.0f, st.l[r]);
+        const float inv = __frcp_rn(st.l[r]);
         const float lse_a = __fmaf_rn(st.m[r], scale, qlnf(st.l[r]));
         float y[32];
         float amax = 0.0f;
@@ -425,11 +470,12 @@ tree_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
         if (row >= seg_end) continue;
         const float sc = group_scale(amax);
+        const GroupDivider dv(sc);
         uint8_t* out = q_out + ((int64_t)row * n_q + h) * D;
 #pragma unroll
         for (int nd = 0; nd < 16; ++nd)
             *reinterpret_cast<uint16_t*>(out + nd * 8 + 2 * tq) =
-                fp8x2(quant_clamp(y[2 * nd], sc), quant_clamp(y[2 * nd + 1], sc));
+                fp8x2(dv.quant(y[2 * nd]), dv.quant(y[2 * nd + 1]));
         if (tq == 0) scale_out[(int64_t)h * scale_ld + row] = sc;
     }
 }

@@ -23,11 +23,15 @@ __device__ __forceinline__ void quant_store8(const float* y, uint8_t* q_row, flo
     for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(y[i]));
     amax = group_amax(amax);
     const float scale = group_scale(amax);
+    const GroupDivider dv(scale);
     uint2 packed;
     uint16_t* p = reinterpret_cast<uint16_t*>(&packed);
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-        p[i] = fp8x2(quant_clamp(y[2 * i], scale), quant_clamp(y[2 * i + 1], scale));
+    for (int i = 0; i < 4; ++i) {
+        float a = y[2 * i], b = y[2 * i + 1];
+        dv.quant2(a, b);
+        p[i] = fp8x2(a, b);
+    }
     *reinterpret_cast<uint2*>(q_row + col8 * 8) = packed;
     if ((threadIdx.x & 15) == 0) scale_out[(int64_t)(col8 / 16) * scale_ld + row] = scale;
 }
@@ -104,7 +108,13 @@ __global__ void silu_mul_quant_kernel(const bf16* __restrict__ gate_up, int64_t 
     bf16x8_to_float(*reinterpret_cast<const uint4*>(base + col8 * 8), g);
     bf16x8_to_float(*reinterpret_cast<const uint4*>(base + inter + col8 * 8), u);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) y[i] = __fmul_rn(__fmul_rn(g[i], sigmoidf_ref(g[i])), u[i]);
+    for (int i = 0; i < 8; i += 2) {
+        // y = (g * sigmoid(g)) * u, two lanes per instruction
+        float sa = g[i], sb = g[i + 1];
+        sigmoidf_ref_x2(sa, sb);
+        const uint64_t gs = f2mul(f2pack(g[i], g[i + 1]), f2pack(sa, sb));
+        f2unpack(f2mul(gs, f2pack(u[i], u[i + 1])), y[i], y[i + 1]);
+    }
     quant_store8(y, q_out + row * inter, scale_out, scale_ld, row, col8);
 }
 
