@@ -17,6 +17,18 @@
 // - so a CPU restatement can reproduce every bit.
 #include "common.cuh"
 
+namespace qb {
+// attention_tc.cu: the tcgen05 kernel for even GQA groups; -1 = not its shapes
+int launch_attention_tc(bool unified, const char* who, const void* q, const void* k,
+                        const void* v, int64_t rows, int n_q, int n_kv, const int32_t* cu,
+                        const int32_t* tiles, int64_t n_tiles, const int32_t* read_cu_q,
+                        const int32_t* read_used, const int32_t* table, int64_t n_reads,
+                        int64_t table_width, const int32_t* source, const void* k_pool,
+                        const void* v_pool, int64_t n_pages, int page_tokens,
+                        float softmax_scale, void* q_out, float* scale_out, int64_t scale_ld,
+                        void* stream);
+}  // namespace qb
+
 namespace {
 
 using namespace qb;
@@ -582,6 +594,12 @@ extern "C" int qb_tree_attention(const void* q, const void* k, const void* v, in
     if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) ||
         (n_reads > 0 && (!aligned(k_pool, 16) || !aligned(v_pool, 16))))
         return invalid("qb_tree_attention: q, k, v and pools must be 16-byte aligned");
+    if (n_tiles == 0 || rows == 0) return QB_OK;
+    st = qb::launch_attention_tc(false, who, q, k, v, rows, n_q, n_kv, cu_a, tiles, n_tiles,
+                                 read_cu_q, read_used, read_table, n_reads, table_width, source,
+                                 k_pool, v_pool, n_pages, page_tokens, softmax_scale, q_out,
+                                 scale_out, scale_ld, stream);
+    if (st != -1) return st;
     return launch_attention<false>(who, q, k, v, rows, n_q, n_kv, cu_a, tiles, n_tiles,
                                    read_cu_q, read_used, read_table, n_reads, table_width, source,
                                    k_pool, v_pool, n_pages, page_tokens, softmax_scale, q_out,
@@ -605,6 +623,12 @@ extern "C" int qb_unified_attention(const void* q, int64_t rows, int n_q, int n_
         return invalid("qb_unified_attention: page_tokens must divide 64");
     if (!aligned(q, 16) || !aligned(k_pool, 16) || !aligned(v_pool, 16))
         return invalid("qb_unified_attention: q and pools must be 16-byte aligned");
+    if (n_tiles == 0 || rows == 0) return QB_OK;
+    st = qb::launch_attention_tc(true, who, q, nullptr, nullptr, rows, n_q, n_kv, cu_q, tiles,
+                                 n_tiles, nullptr, used, table, 0, table_width, nullptr, k_pool,
+                                 v_pool, n_pages, page_tokens, softmax_scale, q_out, scale_out,
+                                 scale_ld, stream);
+    if (st != -1) return st;
     return launch_attention<true>(who, q, k_pool, v_pool, rows, n_q, n_kv, cu_q, tiles, n_tiles,
                                   nullptr, used, table, 0, table_width, nullptr, k_pool, v_pool,
                                   n_pages, page_tokens, softmax_scale, q_out, scale_out, scale_ld,

@@ -1,0 +1,733 @@
+// Tree and unified attention on tcgen05 tensor cores (sm_100a).
+//
+// Same results, bit for bit, as the mma.sync kernel of attention.cu (and the
+// CPU oracle): the B200's tcgen05 kind::f16 MMA accumulates exactly like
+// mma.sync m16n8k16 - per 16-deep step, every product and the accumulator
+// aligned to the largest exponent, truncated 25 bits below it, summed and
+// rounded toward zero (measured: tests/golden/tensorcore_probe.npz) - and
+// this kernel keeps that kernel's order of operations:
+//   S = Q K^T in eight 16-deep steps from zero; per 64-key tile the masked
+//   row max, alpha = exp2((m_old - m_new) sl2), O *= alpha before P V,
+//   P = bf16(exp2(s sl2 - m sl2)); the row sum in four partials (key
+//   8n + 2q + e goes to partial q, in key order) combined as
+//   (l0 + l1) + (l2 + l3); then the LSE merge with bf16 roundings and the
+//   per-head fp8 quantisation.
+//
+// Block: 64 query rows of one cu_a segment x 4 query heads of one KV head
+// (2 when the GQA group is 2) as two M=128 tiles (rows 0-63 one head, rows
+// 64-127 the next) that share every K/V tile. 14 warps:
+//   warp 0       TMA loader: Q once, then K and V tiles of 64 keys into a
+//                2-stage ring - the segment's own keys as contiguous rows, the
+//                resident keys one box per page through the block table;
+//   warp 1       TMEM allocator and MMA issuer: S = Q K^T into TMEM, then
+//                O += P V with P from shared memory and V read MN-major; it
+//                also zeroes the V rows of a paged tile past the last key
+//                (pool rows there may hold anything, and 0 * NaN is NaN);
+//   warps 2-9    softmax, one thread per row of an M tile: S from TMEM (read
+//                twice: the row max, then exp2), P to shared memory (128-byte
+//                swizzle, two buffers by tile parity), alpha likewise;
+//                after each call the same thread's epilogue: the normalised
+//                call-B output (bf16, kept in TMEM), or the merge, the
+//                quantisation and the fp8 store;
+//   warps 10-13  correction, one thread per row of each M tile: O *= alpha in
+//                TMEM between P V steps.
+// TMEM (512 columns): O [2][128] | S [2][64] | call-B output bf16x2 [2][64].
+// Every wait is bounded (about a second): a wait that gives up sets a status
+// bit and the abort flag, the other roles stop at their next wait, the MMA
+// issuer drains its MMAs and the loader its copies before TMEM is freed.
+#include "tc_common.cuh"
+
+namespace qb {
+namespace attn_tc {
+
+using namespace qb::tc;
+
+constexpr int D = 128;
+constexpr int QR = 64;  // query rows per block
+constexpr int KT = 64;  // keys per tile
+constexpr int NST = 2;  // K/V stages
+constexpr int MAX_CALLS = QR + 1;
+constexpr int FIRST_SOFT = 2, FIRST_CORR = 10;
+constexpr int NUM_THREADS = 14 * 32;
+
+constexpr int Q_BYTES = 2 * 2 * 128 * 128;  // [mt][half][128 rows][128 B]
+constexpr int KV_HALF = 64 * 128;           // [64 keys][64 dims]
+constexpr int KV_TILE = 2 * KV_HALF;        // K or V: two 64-dim halves
+constexpr int STAGE_BYTES = 2 * KV_TILE;    // K then V
+constexpr int P_TILE = 128 * 128;           // [128 rows][64 keys]
+constexpr int OFF_KV = Q_BYTES;
+constexpr int OFF_P = OFF_KV + NST * STAGE_BYTES;
+constexpr int OFF_AUX = OFF_P + 4 * P_TILE;  // P: [buffer 2][mt 2]
+
+constexpr uint32_t TM_O = 0, TM_S = 256, TM_OB = 384;
+
+// S: M=128, N=64; P V: M=128, N=128 with B (V) MN-major; bf16 in, f32 out
+constexpr uint32_t IDESC_S = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(KT >> 3) << 17) |
+                             ((uint32_t)(128 >> 4) << 24);
+constexpr uint32_t IDESC_PV = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) |
+                              ((uint32_t)(D >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+
+enum : int { CALL_READS = 0, CALL_OWN = 1, CALL_UNIFIED = 2 };
+
+struct Call {
+    int kind, group, n_keys, key_end, q_first, n_tiles;
+};
+
+struct Aux {
+    uint64_t q_full;
+    uint64_t kv_full[NST], kv_empty[NST];
+    uint64_t s_full[2], s_empty[2], o_ready[2];
+    // per P buffer (tile parity) and M tile; phase = tile / 2, so a producer
+    // can only complete a buffer's next phase after every waiter observed
+    // the previous one (a parity wait needs that)
+    uint64_t p_full[2][2], pv_done[2][2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort;
+    int n_calls;
+    int total_tiles;
+    float alpha[2][2][128];  // [buffer][mt][row]
+    int s_grp[QR];
+    Call calls[MAX_CALLS];
+};
+
+constexpr size_t SMEM_BYTES = OFF_AUX + sizeof(Aux) + 1024;
+static_assert(SMEM_BYTES <= 232448, "shared memory");
+
+__device__ __forceinline__ int read_group(const int32_t* cu_q, int64_t n_reads, int idx) {
+    int lo = 0, hi = (int)n_reads;
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (cu_q[mid] <= idx) lo = mid; else hi = mid;
+    }
+    return lo;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_bits(float a, float b) {
+    bf162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// One merged output value: a = bf16(o * inv); with call B,
+// bf16(a + (b - a) w), b the call-B output (high or low half of ob).
+__device__ __forceinline__ float merge_value(uint32_t o_bits, uint32_t ob, int high, float inv,
+                                             float w, bool has_b) {
+    const float a = bf16_round(__fmul_rn(__uint_as_float(o_bits), inv));
+    if (!has_b) return a;
+    const float b = __uint_as_float(high ? (ob & 0xFFFF0000u) : (ob << 16));
+    return bf16_round(__fadd_rn(a, __fmul_rn(__fsub_rn(b, a), w)));
+}
+
+// Operand descriptors. Q: [mt][half][128 rows][128 B]; K, V: [half][64][128 B].
+__device__ __forceinline__ uint64_t q_desc(uint32_t q_base, int mt, int ks) {
+    return sw128_desc(q_base + (uint32_t)(mt * 32768 + (ks >> 2) * 16384)) + (uint64_t)(2 * (ks & 3));
+}
+__device__ __forceinline__ uint64_t k_desc(uint32_t k_base, int ks) {
+    return sw128_desc(k_base + (uint32_t)((ks >> 2) * KV_HALF)) + (uint64_t)(2 * (ks & 3));
+}
+__device__ __forceinline__ uint64_t v_desc(uint32_t v_base, int kk) {
+    return sw128_mn_desc(v_base + (uint32_t)(kk * 16 * 128), KV_HALF, 1024);
+}
+__device__ __forceinline__ uint64_t p_desc(uint32_t p_base, int kk) {
+    return sw128_desc(p_base) + (uint64_t)(2 * kk);
+}
+
+template <bool UNIFIED>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
+                    const __grid_constant__ CUtensorMap map_k,
+                    const __grid_constant__ CUtensorMap map_v,
+                    const __grid_constant__ CUtensorMap map_kp,
+                    const __grid_constant__ CUtensorMap map_vp, int64_t rows, int n_q, int n_kv,
+                    int hp, const int32_t* __restrict__ cu_a, const int32_t* __restrict__ tiles,
+                    const int32_t* __restrict__ read_cu_q, const int32_t* __restrict__ read_used,
+                    const int32_t* __restrict__ read_table, int64_t n_reads, int64_t table_width,
+                    const int32_t* __restrict__ source, int64_t n_pages, int page_tokens,
+                    float scale, uint8_t* __restrict__ q_out, float* __restrict__ scale_out,
+                    int64_t scale_ld, uint32_t* status) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
+    Aux* aux = reinterpret_cast<Aux*>(smem + OFF_AUX);
+    volatile int* abort_flag = &aux->abort;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    const int seg = tiles[2 * blockIdx.x], row0 = tiles[2 * blockIdx.x + 1];
+    const int group_sz = n_q / n_kv;
+    const int per_kv = group_sz / hp;
+    const int hk = blockIdx.y / per_kv;
+    const int h0 = hk * group_sz + (blockIdx.y % per_kv) * hp;
+    const int nmt = hp >> 1;
+    const int seg_start = cu_a[seg], seg_end = cu_a[seg + 1];
+    if (seg_start < 0 || seg_end > rows || row0 < seg_start || row0 >= seg_end) {
+        if (threadIdx.x == 0) atomicOr(status, STATUS_BAD_INDEX);
+        return;
+    }
+
+    if (threadIdx.x == 0) {
+        mbar_init(&aux->q_full, 1);
+        for (int s = 0; s < NST; ++s) {
+            mbar_init(&aux->kv_full[s], 1);
+            mbar_init(&aux->kv_empty[s], 1);
+        }
+        for (int m = 0; m < 2; ++m) {
+            mbar_init(&aux->s_full[m], 1);
+            mbar_init(&aux->s_empty[m], 4);
+            mbar_init(&aux->p_full[0][m], 4);
+            mbar_init(&aux->p_full[1][m], 4);
+            mbar_init(&aux->pv_done[0][m], 1);
+            mbar_init(&aux->pv_done[1][m], 1);
+            mbar_init(&aux->o_ready[m], 4);
+        }
+        mbar_init(&aux->drain, 1);
+        aux->abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
+                         smem_u32(&aux->tmem_base))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    // read group per tile row (-1: reads nothing resident)
+    if (threadIdx.x < QR) {
+        const int r = row0 + threadIdx.x;
+        int grp = -1;
+        if (!UNIFIED && r < seg_end && n_reads > 0) {
+            const int src = source[r];
+            if (src >= 0) {
+                if (src >= read_cu_q[n_reads]) atomicOr(status, STATUS_BAD_INDEX);
+                else grp = read_group(read_cu_q, n_reads, src);
+            }
+        }
+        aux->s_grp[threadIdx.x] = grp;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // the block's attention calls: each distinct read group (resident keys,
+    // not causal) in ascending order, then the segment's own keys (causal);
+    // or the one causal paged call of the unified path
+    if (threadIdx.x == 0) {
+        int nc = 0, total = 0;
+        auto add = [&](int kind, int grp, int n_keys, int q_first, bool causal) {
+            int key_end = causal ? min(n_keys, q_first + QR) : n_keys;
+            if (key_end < 0) key_end = 0;
+            const int nt = (key_end + KT - 1) / KT;
+            aux->calls[nc++] = Call{kind, grp, n_keys, key_end, q_first, nt};
+            total += nt;
+        };
+        if (UNIFIED) {
+            int used = read_used[seg];
+            const int q_len = seg_end - seg_start;
+            if (used < q_len || (int64_t)((used + page_tokens - 1) / page_tokens) > table_width) {
+                atomicOr(status, STATUS_BAD_INDEX);
+                used = q_len;
+            }
+            add(CALL_UNIFIED, seg, used, used - q_len + (row0 - seg_start), true);
+        } else {
+            int cur = -1;
+            while (true) {
+                int next = INT_MAX;
+                for (int i = 0; i < QR; ++i) {
+                    const int x = aux->s_grp[i];
+                    if (x > cur && x < next) next = x;
+                }
+                if (next == INT_MAX) break;
+                cur = next;
+                int used = read_used[cur];
+                if (used < 0 || (int64_t)((used + page_tokens - 1) / page_tokens) > table_width) {
+                    atomicOr(status, STATUS_BAD_INDEX);
+                    used = 0;
+                }
+                if (used > 0) {
+                    add(CALL_READS, cur, used, 0, false);
+                } else {
+                    // a read group without keys: its rows attend to their own keys only
+                    for (int i = 0; i < QR; ++i)
+                        if (aux->s_grp[i] == cur) aux->s_grp[i] = -1;
+                }
+            }
+            add(CALL_OWN, -1, seg_end - seg_start, row0 - seg_start, true);
+        }
+        aux->n_calls = nc;
+        aux->total_tiles = total;
+    }
+    __syncthreads();
+    const int n_calls = aux->n_calls;
+    const uint32_t tmem = aux->tmem_base;
+
+    if (warp == 0) {
+        // ---------------- TMA loader ----------------
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_q))
+                         : "memory");
+            mbar_arrive_expect_tx(&aux->q_full, (uint32_t)(nmt * 32768));
+            for (int mt = 0; mt < nmt; ++mt)
+                for (int hh = 0; hh < 2; ++hh)
+                    for (int half = 0; half < 2; ++half)
+                        tma_load_2d(smem_u32(smem + mt * 32768 + half * 16384 + hh * 8192), &map_q,
+                                    (h0 + 2 * mt + hh) * D + half * 64, row0, &aux->q_full);
+            int g = 0;
+            bool ok = true;
+            for (int c = 0; c < n_calls && ok; ++c) {
+                const Call cl = aux->calls[c];
+                for (int t = 0; t < cl.n_tiles; ++t, ++g) {
+                    const int st = g % NST;
+                    if (!mbar_wait(&aux->kv_empty[st], ((uint32_t)(g / NST) & 1u) ^ 1u, abort_flag,
+                                   status, STATUS_ATTN_LOAD)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* kd = smem + OFF_KV + st * STAGE_BYTES;
+                    uint8_t* vd = kd + KV_TILE;
+                    mbar_arrive_expect_tx(&aux->kv_full[st], STAGE_BYTES);
+                    const int j0 = t * KT;
+                    if (cl.kind == CALL_OWN) {
+                        const int y = seg_start + j0;
+                        for (int half = 0; half < 2; ++half) {
+                            tma_load_2d(smem_u32(kd + half * KV_HALF), &map_k, hk * D + half * 64,
+                                        y, &aux->kv_full[st]);
+                            tma_load_2d(smem_u32(vd + half * KV_HALF), &map_v, hk * D + half * 64,
+                                        y, &aux->kv_full[st]);
+                        }
+                    } else {
+                        const int32_t* trow =
+                            read_table + (int64_t)(cl.kind == CALL_UNIFIED ? seg : cl.group) *
+                                             table_width;
+                        for (int pg = 0; pg < KT / page_tokens; ++pg) {
+                            const int key = j0 + pg * page_tokens;
+                            int64_t page = 0;  // keys past the last one: any valid page
+                            if (key < cl.n_keys) {
+                                page = trow[key / page_tokens];
+                                if (page < 0 || page >= n_pages) {
+                                    atomicOr(status, STATUS_BAD_INDEX);
+                                    page = 0;
+                                }
+                            }
+                            const int y = (int)(page * page_tokens);
+                            const int off = pg * page_tokens * 128;
+                            for (int half = 0; half < 2; ++half) {
+                                tma_load_2d(smem_u32(kd + half * KV_HALF + off), &map_kp,
+                                            hk * D + half * 64, y, &aux->kv_full[st]);
+                                tma_load_2d(smem_u32(vd + half * KV_HALF + off), &map_vp,
+                                            hk * D + half * 64, y, &aux->kv_full[st]);
+                            }
+                        }
+                    }
+                }
+            }
+            // no copy may still be landing when the block exits
+            int flag = 0;
+            if (!mbar_try_wait(smem_u32(&aux->q_full), 0))
+                mbar_wait(&aux->q_full, 0, &flag, status, STATUS_ATTN_LOAD);
+            for (int j = (g > NST ? g - NST : 0); j < g; ++j) {
+                const int st = j % NST;
+                if (!mbar_try_wait(smem_u32(&aux->kv_full[st]), (uint32_t)(j / NST) & 1u))
+                    mbar_wait(&aux->kv_full[st], (uint32_t)(j / NST) & 1u, &flag, status,
+                              STATUS_ATTN_LOAD);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (lane 0 issues; the warp zeroes V tails) ----
+        const uint32_t q_base = smem_u32(smem);
+        const uint32_t p_base = smem_u32(smem + OFF_P);
+        const int total = aux->total_tiles;
+        bool ok = mbar_wait(&aux->q_full, 0, abort_flag, status, STATUS_ATTN_MMA);
+        // S for tile gs (call cs, tile ts of the call)
+        int gs = 0, cs = 0, ts = 0;
+        auto issue_s = [&]() -> bool {
+            while (cs < n_calls && ts >= aux->calls[cs].n_tiles) {
+                ++cs;
+                ts = 0;
+            }
+            const int st = gs % NST;
+            if (!mbar_wait(&aux->kv_full[st], (uint32_t)(gs / NST) & 1u, abort_flag, status,
+                           STATUS_ATTN_MMA))
+                return false;
+            const uint32_t k_base = smem_u32(smem + OFF_KV + st * STAGE_BYTES);
+            for (int mt = 0; mt < nmt; ++mt) {
+                if (gs > 0 && !mbar_wait(&aux->s_empty[mt], (uint32_t)(gs - 1) & 1u, abort_flag,
+                                         status, STATUS_ATTN_MMA))
+                    return false;
+                tc_fence_after();
+                if (lane == 0) {
+#pragma unroll
+                    for (int ks = 0; ks < D / 16; ++ks)
+                        mma_bf16_ss(tmem + TM_S + (uint32_t)(mt * 64), q_desc(q_base, mt, ks),
+                                    k_desc(k_base, ks), IDESC_S, ks > 0 ? 1u : 0u);
+                    mma_commit(&aux->s_full[mt]);
+                }
+                __syncwarp();
+            }
+            ++gs;
+            ++ts;
+            return true;
+        };
+        if (ok && total > 0) ok = issue_s();
+        int g = 0;
+        for (int c = 0; c < n_calls && ok; ++c) {
+            const Call cl = aux->calls[c];
+            for (int t = 0; t < cl.n_tiles; ++t, ++g) {
+                if (g + 1 < total && !issue_s()) {
+                    ok = false;
+                    break;
+                }
+                const int st = g % NST;
+                uint8_t* vd = smem + OFF_KV + st * STAGE_BYTES + KV_TILE;
+                const int valid = cl.n_keys - t * KT;
+                if (cl.kind != CALL_OWN && valid < KT) {
+                    // the V rows past the last key: zeros (the tile landed: S
+                    // of this tile waited for it)
+                    const int first = valid < 0 ? 0 : valid;
+                    for (int idx = first * 8 + lane; idx < KT * 8; idx += 32) {
+                        const int r = idx >> 3, ch = idx & 7;
+                        *reinterpret_cast<uint4*>(vd + r * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+                        *reinterpret_cast<uint4*>(vd + KV_HALF + r * 128 + ch * 16) =
+                            make_uint4(0, 0, 0, 0);
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                }
+                const uint32_t v_base = smem_u32(vd);
+                for (int mt = 0; mt < nmt && ok; ++mt) {
+                    if (!mbar_wait(&aux->p_full[g & 1][mt], (uint32_t)(g >> 1) & 1u, abort_flag,
+                                   status, STATUS_ATTN_MMA) ||
+                        !mbar_wait(&aux->o_ready[mt], (uint32_t)g & 1u, abort_flag, status,
+                                   STATUS_ATTN_MMA)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (lane == 0) {
+#pragma unroll
+                        for (int kk = 0; kk < KT / 16; ++kk)
+                            mma_bf16_ss(tmem + TM_O + (uint32_t)(mt * 128),
+                                        p_desc(p_base + (uint32_t)(((g & 1) * 2 + mt) * P_TILE), kk),
+                                        v_desc(v_base, kk), IDESC_PV, (t > 0 || kk > 0) ? 1u : 0u);
+                        mma_commit(&aux->pv_done[g & 1][mt]);
+                    }
+                    __syncwarp();
+                }
+                if (!ok) break;
+                if (lane == 0) mma_commit(&aux->kv_empty[st]);
+                __syncwarp();
+            }
+        }
+        // every MMA issued must finish before TMEM is freed
+        if (lane == 0) mma_commit(&aux->drain);
+        __syncwarp();
+        int flag = 0;
+        mbar_wait(&aux->drain, 0, &flag, status, STATUS_ATTN_MMA);
+    } else if (warp < FIRST_CORR) {
+        // ------- softmax, then each call's epilogue: one thread per row of an M tile -------
+        const int mt = (warp - FIRST_SOFT) >> 2;
+        if (mt < nmt) {
+            const int q4 = warp & 3;
+            const int i = q4 * 32 + lane;
+            const int qi = i & (QR - 1);
+            const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+            const uint32_t s_addr = tmem + lane_off + TM_S + (uint32_t)(mt * 64);
+            const uint32_t o_addr = tmem + lane_off + TM_O + (uint32_t)(mt * 128);
+            const uint32_t ob_addr = tmem + lane_off + TM_OB + (uint32_t)(mt * 64);
+            const float sl2 = __fmul_rn(scale, 1.44269504088896341f);
+            const uint64_t sl = f2pack(sl2, sl2);
+            float lse_b = 0.0f;  // this row's call-B log-sum-exp
+            int g = 0;
+            bool ok = true;
+            for (int c = 0; c < n_calls && ok; ++c) {
+                const Call cl = aux->calls[c];
+                const bool causal = cl.kind != CALL_READS;
+                const int qpos = cl.q_first + qi;
+                // keys [0, visible) exist for this row
+                const int visible = causal ? min(cl.key_end, qpos + 1) : cl.key_end;
+                float m = -INFINITY;
+                float lp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                for (int t = 0; t < cl.n_tiles; ++t, ++g) {
+                    if (!mbar_wait(&aux->s_full[mt], (uint32_t)g & 1u, abort_flag, status,
+                                   STATUS_ATTN_SOFTMAX)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const int lim = visible - t * KT;  // keys [0, lim) of the tile exist
+                    // pass 1: the masked row max
+                    float mx = -INFINITY;
+#pragma unroll 1
+                    for (int c0 = 0; c0 < KT; c0 += 16) {
+                        uint32_t sr[16];
+                        tmem_ld16_nowait(s_addr + (uint32_t)c0, sr);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int k = 0; k < 16; ++k)
+                            mx = fmaxf(mx, c0 + k < lim ? __uint_as_float(sr[k]) : -INFINITY);
+                    }
+                    const float m_new = fmaxf(m, mx);
+                    float alpha, msl;
+                    if (m_new == -INFINITY) {
+                        alpha = 1.0f;
+                        msl = 0.0f;
+                    } else {
+                        alpha = qexp2f(__fmul_rn(__fsub_rn(m, m_new), sl2));
+                        msl = __fmul_rn(m_new, sl2);
+                    }
+                    m = m_new;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) lp[k] = __fmul_rn(lp[k], alpha);
+                    // P buffer (g & 1) was last read by the P V two tiles back
+                    if (g >= 2 && !mbar_wait(&aux->pv_done[g & 1][mt], (uint32_t)((g - 2) >> 1) & 1u,
+                                             abort_flag, status, STATUS_ATTN_SOFTMAX)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* prow = smem + OFF_P + ((g & 1) * 2 + mt) * P_TILE + i * 128;
+                    const uint64_t nm = f2pack(-msl, -msl);
+                    // pass 2: p = exp2(s sl2 - m sl2), the row-sum partials, bf16 P
+#pragma unroll 1
+                    for (int c0 = 0; c0 < KT; c0 += 16) {
+                        uint32_t sr[16];
+                        tmem_ld16_nowait(s_addr + (uint32_t)c0, sr);
+                        tmem_wait_ld();
+                        uint32_t pk[8];
+#pragma unroll
+                        for (int k = 0; k < 16; k += 2) {
+                            const float s0 = c0 + k < lim ? __uint_as_float(sr[k]) : -INFINITY;
+                            const float s1 = c0 + k + 1 < lim ? __uint_as_float(sr[k + 1]) : -INFINITY;
+                            float a, b;
+                            f2unpack(f2fma(f2pack(s0, s1), sl, nm), a, b);
+                            qexp2f_x2(a, b);
+                            // keys c0 + k, c0 + k + 1 belong to partial (k / 2) % 4 (c0 % 8 == 0)
+                            lp[(k >> 1) & 3] = __fadd_rn(__fadd_rn(lp[(k >> 1) & 3], a), b);
+                            pk[k >> 1] = bf16x2_bits(a, b);
+                        }
+                        const int ch = c0 >> 3;  // 16-byte chunks ch, ch + 1 of the row
+                        *reinterpret_cast<uint4*>(prow + ((ch ^ (i & 7)) << 4)) =
+                            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                        *reinterpret_cast<uint4*>(prow + (((ch + 1) ^ (i & 7)) << 4)) =
+                            make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                    }
+                    tc_fence_before();
+                    aux->alpha[g & 1][mt][i] = alpha;
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&aux->s_empty[mt]);
+                        mbar_arrive(&aux->p_full[g & 1][mt]);
+                    }
+                }
+                if (!ok) break;
+                // ---- epilogue of call c for this row: the last P V must be done ----
+                if (!mbar_wait(&aux->pv_done[(g - 1) & 1][mt], (uint32_t)((g - 1) >> 1) & 1u,
+                               abort_flag, status, STATUS_ATTN_SOFTMAX)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const float l = __fadd_rn(__fadd_rn(lp[0], lp[1]), __fadd_rn(lp[2], lp[3]));
+                const float inv = __frcp_rn(l);
+                if (cl.kind == CALL_READS) {
+                    // normalised call-B output, bf16, for the rows of this read group
+                    const bool member = aux->s_grp[qi] == cl.group;
+                    if (member) lse_b = __fmaf_rn(m, scale, qlnf(l));
+#pragma unroll 1
+                    for (int c0 = 0; c0 < D; c0 += 32) {
+                        uint32_t r[32], ob[16];
+                        tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
+                        tmem_ld16_nowait(ob_addr + (uint32_t)(c0 >> 1), ob);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const uint32_t v = bf16x2_bits(__fmul_rn(__uint_as_float(r[2 * j]), inv),
+                                                           __fmul_rn(__uint_as_float(r[2 * j + 1]), inv));
+                            if (member) ob[j] = v;
+                        }
+                        tmem_st16(ob_addr + (uint32_t)(c0 >> 1), ob);
+                    }
+                    tmem_wait_st();
+                } else {
+                    // merge with call B, per-head fp8 quantisation, store
+                    const float lse_a = __fmaf_rn(m, scale, qlnf(l));
+                    const bool has_b = !UNIFIED && aux->s_grp[qi] >= 0;
+                    float w = 0.0f;
+                    if (has_b) w = bf16_round(sigmoidf_ref(__fsub_rn(lse_b, lse_a)));
+                    // pass 1: the row's amax; pass 2: the same values again,
+                    // quantised and stored (32 columns per step, small code)
+                    float amax = 0.0f;
+#pragma unroll 1
+                    for (int c0 = 0; c0 < D; c0 += 32) {
+                        uint32_t r[32], ob[16];
+                        tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
+                        tmem_ld16_nowait(ob_addr + (uint32_t)(c0 >> 1), ob);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            amax = fmaxf(amax, fabsf(merge_value(r[j], ob[j >> 1], j & 1, inv, w,
+                                                                 has_b)));
+                    }
+                    const int row = row0 + qi;
+                    const int h = h0 + 2 * mt + (i >> 6);
+                    const float sc = group_scale(amax);
+                    const GroupDivider dv(sc);
+                    uint8_t* out = q_out + ((int64_t)(row < seg_end ? row : row0) * n_q + h) * D;
+#pragma unroll 1
+                    for (int c0 = 0; c0 < D; c0 += 32) {
+                        uint32_t r[32], ob[16];
+                        tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
+                        tmem_ld16_nowait(ob_addr + (uint32_t)(c0 >> 1), ob);
+                        tmem_wait_ld();
+                        uint32_t packed[8];
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            float a0 = merge_value(r[j], ob[j >> 1], 0, inv, w, has_b);
+                            float a1 = merge_value(r[j + 1], ob[j >> 1], 1, inv, w, has_b);
+                            float b0 = merge_value(r[j + 2], ob[(j >> 1) + 1], 0, inv, w, has_b);
+                            float b1 = merge_value(r[j + 3], ob[(j >> 1) + 1], 1, inv, w, has_b);
+                            dv.quant2(a0, a1);
+                            dv.quant2(b0, b1);
+                            packed[j >> 2] = (uint32_t)fp8x2(a0, a1) | ((uint32_t)fp8x2(b0, b1) << 16);
+                        }
+                        if (row < seg_end) {
+                            uint4* o4 = reinterpret_cast<uint4*>(out + c0);
+                            o4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                            o4[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                        }
+                    }
+                    if (row < seg_end) scale_out[(int64_t)h * scale_ld + row] = sc;
+                }
+                // O (and the call-B output) read before the next call's first P V
+                tc_fence_before();
+            }
+        }
+    } else {
+        // ---------------- correction: O *= alpha between P V steps ----------------
+        const int q4 = warp & 3;
+        const int i = q4 * 32 + lane;
+        const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+        int g = 0;
+        bool ok = true;
+        for (int c = 0; c < n_calls && ok; ++c) {
+            const Call cl = aux->calls[c];
+            for (int t = 0; t < cl.n_tiles && ok; ++t, ++g) {
+                for (int mt = 0; mt < nmt; ++mt) {
+                    // every p_full phase is waited for (a parity wait is only
+                    // sound when the waiter is at most one phase behind)
+                    if (!mbar_wait(&aux->p_full[g & 1][mt], (uint32_t)(g >> 1) & 1u, abort_flag,
+                                   status, STATUS_ATTN_CORRECTION)) {
+                        ok = false;
+                        break;
+                    }
+                    if (t > 0) {
+                        if (!mbar_wait(&aux->pv_done[(g - 1) & 1][mt], (uint32_t)((g - 1) >> 1) & 1u,
+                                       abort_flag, status, STATUS_ATTN_CORRECTION)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const float a = aux->alpha[g & 1][mt][i];
+                        if (__any_sync(0xffffffffu, a != 1.0f)) {
+                            const uint64_t a2 = f2pack(a, a);
+                            const uint32_t o_addr = tmem + lane_off + TM_O + (uint32_t)(mt * 128);
+#pragma unroll 1
+                            for (int c0 = 0; c0 < D; c0 += 32) {
+                                uint32_t r[32];
+                                tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
+                                tmem_wait_ld();
+#pragma unroll
+                                for (int j = 0; j < 32; j += 2) {
+                                    float x, y;
+                                    f2unpack(f2mul(f2pack(__uint_as_float(r[j]),
+                                                          __uint_as_float(r[j + 1])),
+                                                   a2),
+                                             x, y);
+                                    r[j] = __float_as_uint(x);
+                                    r[j + 1] = __float_as_uint(y);
+                                }
+                                tmem_st32(o_addr + (uint32_t)c0, r);
+                            }
+                            tmem_wait_st();
+                        }
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&aux->o_ready[mt]);
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem)
+                     : "memory");
+    }
+}
+
+}  // namespace attn_tc
+
+// Launch of the tcgen05 kernel; returns -1 when the shapes are not its
+// (odd GQA group, page size not dividing 64), the caller then uses the
+// mma.sync kernel.
+int launch_attention_tc(bool unified, const char* who, const void* q, const void* k,
+                        const void* v, int64_t rows, int n_q, int n_kv, const int32_t* cu,
+                        const int32_t* tiles, int64_t n_tiles, const int32_t* read_cu_q,
+                        const int32_t* read_used, const int32_t* table, int64_t n_reads,
+                        int64_t table_width, const int32_t* source, const void* k_pool,
+                        const void* v_pool, int64_t n_pages, int page_tokens,
+                        float softmax_scale, void* q_out, float* scale_out, int64_t scale_ld,
+                        void* stream) {
+    using namespace attn_tc;
+    const int group = n_q / n_kv;
+    if (group % 2 != 0) return -1;
+    const int hp = group % 4 == 0 ? 4 : 2;
+    const bool paged = unified || n_reads > 0;
+    if (paged && (page_tokens <= 0 || KT % page_tokens != 0 || page_tokens < 8)) return -1;
+    if (!unified && rows < 1) return QB_OK;
+    uint32_t* status = device_status_ptr();
+    if (!status) return launch_status(who);
+    CUtensorMap mq, mk, mv, mkp, mvp;
+    const CUtensorMapDataType bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
+    int st = encode_2d(&mq, bf, q, (int64_t)n_q * D, rows, (int64_t)n_q * D * 2, 64, QR, sw, who);
+    if (st) return st;
+    if (!unified) {
+        st = encode_2d(&mk, bf, k, (int64_t)n_kv * D, rows, (int64_t)n_kv * D * 2, 64, KT, sw, who);
+        if (st) return st;
+        st = encode_2d(&mv, bf, v, (int64_t)n_kv * D, rows, (int64_t)n_kv * D * 2, 64, KT, sw, who);
+        if (st) return st;
+    } else {
+        mk = mq;
+        mv = mq;
+    }
+    if (paged) {
+        const int64_t pool_rows = n_pages * (int64_t)page_tokens;
+        st = encode_2d(&mkp, bf, k_pool, (int64_t)n_kv * D, pool_rows, (int64_t)n_kv * D * 2, 64,
+                       page_tokens, sw, who);
+        if (st) return st;
+        st = encode_2d(&mvp, bf, v_pool, (int64_t)n_kv * D, pool_rows, (int64_t)n_kv * D * 2, 64,
+                       page_tokens, sw, who);
+        if (st) return st;
+    } else {
+        mkp = mk;
+        mvp = mv;
+    }
+    auto kernel = unified ? attention_tc_kernel<true> : attention_tc_kernel<false>;
+    static bool attr[2][64] = {{false}};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr[unified][dev]) {
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)SMEM_BYTES) != cudaSuccess)
+            return launch_status(who);
+        attr[unified][dev] = true;
+    }
+    dim3 grid((unsigned)n_tiles, (unsigned)(n_kv * (group / hp)));
+    kernel<<<grid, NUM_THREADS, SMEM_BYTES, (cudaStream_t)stream>>>(
+        mq, mk, mv, mkp, mvp, rows, n_q, n_kv, hp, cu, tiles, read_cu_q, read_used, table,
+        n_reads, table_width, source, n_pages, page_tokens, softmax_scale, (uint8_t*)q_out,
+        scale_out, scale_ld, status);
+    return launch_status(who);
+}
+
+}  // namespace qb

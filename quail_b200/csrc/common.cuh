@@ -40,6 +40,10 @@ enum : uint32_t {
     STATUS_GEMM_MMA = 1u << 1,
     STATUS_GEMM_EPILOGUE = 1u << 2,
     STATUS_GEMM_DRAIN = 1u << 3,
+    STATUS_ATTN_LOAD = 1u << 4,     // tcgen05 attention: loader, MMA, softmax, correction
+    STATUS_ATTN_MMA = 1u << 5,
+    STATUS_ATTN_SOFTMAX = 1u << 6,
+    STATUS_ATTN_CORRECTION = 1u << 7,
     STATUS_BAD_TOKEN = 1u << 8,     // a token id outside [0, vocab)
     STATUS_BAD_INDEX = 1u << 9,     // a page, row or segment index out of range
 };
@@ -73,6 +77,9 @@ __device__ __forceinline__ float group_scale(float amax) {
 // underflow); smaller, huge and non-finite y (and the sign of zero) take
 // the IEEE division. Equal to y / scale bit for bit (checked against it on
 // 4e8 random pairs over the range quantisation sees).
+// out of line: rare paths stay out of the unrolled hot loops' code
+static __device__ __noinline__ float div_slow(float y, float s) { return __fdiv_rn(y, s); }
+
 struct GroupDivider {
     float s, r;
     __device__ __forceinline__ explicit GroupDivider(float scale) {
@@ -81,7 +88,7 @@ struct GroupDivider {
     }
     __device__ __forceinline__ float div(float y) const {
         const float a = fabsf(y);
-        if (!(a >= 0x1p-96f && a < 0x1p+100f)) return __fdiv_rn(y, s);
+        if (!(a >= 0x1p-96f && a < 0x1p+100f)) return div_slow(y, s);
         const float q0 = __fmul_rn(y, r);
         const float e = __fmaf_rn(-s, q0, y);
         return __fmaf_rn(e, r, q0);
@@ -187,6 +194,13 @@ __device__ __forceinline__ void GroupDivider::quant2(float& a, float& b) const {
     STEP(0.240226506959100712f)                     \
     STEP(0.693147180559945309f)                     \
     STEP(1.0f)
+// a subnormal result on either lane (rare): out of line
+static __device__ __noinline__ void exp2_finish_slow(float& a, float& b, float pa, float pb, float ta,
+                                              float tb) {
+    a = exp2_finish(pa, ta);
+    b = exp2_finish(pb, tb);
+}
+
 constexpr float QB_EXP2_C7 = 0.0000152527338040598403f;
 
 __device__ __forceinline__ float qexp2f(float x) {
@@ -220,8 +234,7 @@ __device__ __forceinline__ void qexp2f_x2(float& a, float& b) {
     if (__float_as_int(ta) - 0x4B400000 >= -126 && __float_as_int(tb) - 0x4B400000 >= -126) {
         f2unpack(f2mul(p, f2pack(exp2_scale(ta), exp2_scale(tb))), a, b);
     } else {
-        a = exp2_finish(pa, ta);
-        b = exp2_finish(pb, tb);
+        exp2_finish_slow(a, b, pa, pb, ta, tb);
     }
 }
 

@@ -29,11 +29,12 @@
 // in flight and frees TMEM before the block exits.
 #include <cudaTypedefs.h>
 
-#include "common.cuh"
+#include "tc_common.cuh"
 
 namespace {
 
 using namespace qb;
+using namespace qb::tc;
 
 constexpr int BM = 128;
 constexpr int BK = 128;
@@ -42,7 +43,6 @@ constexpr int EPI_WARPS = 16;
 constexpr int FIRST_EPI_WARP = 3;
 constexpr int NUM_THREADS = (FIRST_EPI_WARP + EPI_WARPS) * 32;
 constexpr int SCALE_SLOTS = 8;
-constexpr uint64_t TIMEOUT_NS = 1000000000ull;
 
 // BN: tile width; NST: shared-memory pipeline stages; TSTORE: the tile is
 // written through a 128-byte-swizzled shared-memory staging area by TMA
@@ -89,86 +89,6 @@ struct Barriers {
     int abort;
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ uint64_t globaltimer() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(addr), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Waits for the phase with the given parity; false when it gave up (timeout
-// or another role aborted), after which the caller stops its loop.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          uint32_t* status, uint32_t bit) {
-    const uint32_t addr = smem_u32(bar);
-    if (mbar_try_wait(addr, parity)) return true;
-    const uint64_t start = globaltimer();
-    for (uint32_t it = 1;; ++it) {
-        if (mbar_try_wait(addr, parity)) return true;
-        if ((it & 255u) == 0) {
-            if (*abort_flag) return false;
-            if (globaltimer() - start > TIMEOUT_NS) {
-                atomicOr(status, bit);
-                *abort_flag = 1;
-                return false;
-            }
-        }
-    }
-}
-
-// shared -> global tile store, tracked by this thread's bulk groups
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
-    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
-                     reinterpret_cast<uint64_t>(map)),
-                 "r"(x), "r"(y), "r"(src)
-                 : "memory");
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
-                                            uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
-// 1024 bytes apart (SBO), version 1 (sm_100), base offset 0.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
 __device__ __forceinline__ void mma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                        uint32_t idesc, uint32_t accumulate) {
     asm volatile(
@@ -177,48 +97,6 @@ __device__ __forceinline__ void mma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t
         "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-    asm volatile(
-        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-            smem_u32(bar))
-        : "memory");
-}
-
-// 4-byte asynchronous copy global -> shared; src_bytes 0 writes a zero
-__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t src_bytes) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src),
-                 "r"(src_bytes)
-                 : "memory");
-}
-
-// arrives on the mbarrier once this thread's earlier cp.async copies landed
-__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() {
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-// 16 consecutive 32-bit columns of this warp's 32 TMEM lanes (no wait).
-__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t* r) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-          "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_wait_ld() {
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 // acc[0..1] = fma(v[0..1], s, acc[0..1]): two IEEE fp32 FMAs in one
@@ -491,20 +369,6 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 get_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    if (fn == nullptr) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
-                cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return nullptr;
-        fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    }
-    return fn;
-}
-
 // 2-D K-major fp8 tensor map: rows x k bytes, box box_rows x 128, 128B swizzle.
 int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, int box_rows) {
     PFN_cuTensorMapEncodeTiled_v12000 enc = get_encoder();
@@ -545,19 +409,6 @@ int make_out_map(CUtensorMap* map, void* base, int64_t rows, int64_t n) {
         return QB_ERR_CUDA;
     }
     return QB_OK;
-}
-
-int sm_count() {
-    static int count[64] = {0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return 148;
-    if (count[dev] == 0) {
-        int c = 0;
-        cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
-        count[dev] = c > 0 ? c : 148;
-    }
-    return count[dev];
 }
 
 template <int BN, int NST = MAX_STAGES, bool TSTORE = false>

@@ -7,7 +7,11 @@ launch) and records, for seeded operands with a wide exponent spread:
 - gemm_s{3,6}_*: e4m3 codes a [64, 128], w [64, 128] and the fp32
   accumulator of one 128-deep block (four tcgen05 K=32 MMAs, unit scales);
 - mma_*: bf16 A [16, 16], B [16, 8], fp32 C and the fp32 D = C + A B of one
-  mma.sync.
+  mma.sync;
+- tcf16_m{0,1}_r*: tcgen05 kind::f16 (bf16) chains of four K=16 MMAs in the
+  tcgen05 attention's layouts: bf16 A [128, 64], B [64, 64] read K-major
+  (mode 0, N = 64) or V [64, 128] read MN-major (mode 1, N = 128), the fp32
+  C preloaded into TMEM (NaN placeholder: not loaded) and D.
 
 tests/test_oracle_model.py checks that oracle/tcmodel.c reproduces every
 output bit for bit. Run: python tests/golden/make_tensorcore_probe.py
@@ -100,6 +104,29 @@ def main():
             D[:, g, 2 * q], D[:, g, 2 * q + 1] = dn[:, t, 0], dn[:, t, 1]
             D[:, g + 8, 2 * q], D[:, g + 8, 2 * q + 1] = dn[:, t, 2], dn[:, t, 3]
         out.update(mma_A=A, mma_B=B, mma_C=C, mma_D=D)
+        # tcgen05 kind::f16: mode 0 = S (B K-major, N 64), mode 1 = PV (B = V
+        # MN-major, N 128); C preloaded in TMEM (zero for r % 4 == 1) or not
+        for mode in (0, 1):
+            n = 64 if mode == 0 else 128
+            for r in range(6):
+                s = (0, 4, 8)[r % 3]
+                use_c = 0 if r % 4 == 0 else 1
+                ta = torch.from_numpy(operands(rng, (128, 64), s)).to(torch.bfloat16)
+                tb = torch.from_numpy(operands(rng, (64, n), s)).to(torch.bfloat16)
+                c = np.zeros((128, n), np.float32)
+                if use_c and r % 4 != 1:
+                    c = operands(rng, (128, n), s)
+                ad, bd = ta.to(dev), tb.to(dev)
+                cd = torch.from_numpy(c).to(dev)
+                dd = torch.zeros(128, n, device=dev)
+                assert lib.probe_tc_f16(mode, P(ad.data_ptr()), P(bd.data_ptr()),
+                                        P(cd.data_ptr()), P(dd.data_ptr()), use_c, stream) == 0
+                torch.cuda.synchronize()
+                key = f"tcf16_m{mode}_r{r}"
+                out[key + "_a"] = ta.view(torch.int16).numpy()
+                out[key + "_b"] = tb.view(torch.int16).numpy()
+                out[key + "_c"] = c if use_c else np.full((1,), np.nan, np.float32)
+                out[key + "_d"] = dd.cpu().numpy()
     np.savez_compressed(HERE / "tensorcore_probe.npz", **out)
 
 

@@ -9,6 +9,8 @@ model measured on the B200 (tests/test_oracle_model.py). So fp8 codes,
 scales, bf16 outputs, KV pool rows and margins must match bit for bit.
 """
 
+import dataclasses
+
 import numpy as np
 import pytest
 import torch
@@ -184,9 +186,14 @@ def test_qk_norm_rope_and_kv_append(dev):
     assert_status_clean()
 
 
-def _attention_case(mode, dev, seed=0):
+# GQA groups of 2 and 4 run the tcgen05 kernel (one and two 128-row M tiles),
+# an odd group the mma.sync kernel
+ATTN_CONFIGS = {"g2": TINY, "g4": dataclasses.replace(TINY, name="tiny-g4", n_q=8),
+                "g3": dataclasses.replace(TINY, name="tiny-g3", n_q=3, n_kv=1)}
+
+
+def _attention_case(mode, dev, seed=0, cfg=TINY):
     """A packed chunk (our packer) with random q/k/v and random resident KV."""
-    cfg = TINY
     rng = np.random.default_rng(seed)
     prefix = rng.integers(1000, 2000, 64).tolist()
     lens = rng.integers(1, 150, 12)
@@ -218,9 +225,10 @@ def _attention_case(mode, dev, seed=0):
     return cfg, arena, chunks
 
 
+@pytest.mark.parametrize("group", sorted(ATTN_CONFIGS))
 @pytest.mark.parametrize("mode", ["tree", "unified"])
-def test_attention_against_oracle(dev, mode):
-    cfg, arena, chunks = _attention_case(mode, dev)
+def test_attention_against_oracle(dev, mode, group):
+    cfg, arena, chunks = _attention_case(mode, dev, cfg=ATTN_CONFIGS[group])
     eng = Engine(torch, arena, cfg)
     scale = cfg.head_dim ** -0.5
     checked = 0
