@@ -182,6 +182,15 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
         mbar_init(&aux->drain, 1);
         aux->abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        // Q of the block's heads: needs only the tile, so it starts first
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_q))
+                     : "memory");
+        mbar_arrive_expect_tx(&aux->q_full, (uint32_t)(nmt * 32768));
+        for (int mt = 0; mt < nmt; ++mt)
+            for (int hh = 0; hh < 2; ++hh)
+                for (int half = 0; half < 2; ++half)
+                    tma_load_2d(smem_u32(smem + mt * 32768 + half * 16384 + hh * 8192), &map_q,
+                                (h0 + 2 * mt + hh) * D + half * 64, row0, &aux->q_full);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
@@ -260,14 +269,6 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
     if (warp == 0) {
         // ---------------- TMA loader ----------------
         if (lane == 0) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_q))
-                         : "memory");
-            mbar_arrive_expect_tx(&aux->q_full, (uint32_t)(nmt * 32768));
-            for (int mt = 0; mt < nmt; ++mt)
-                for (int hh = 0; hh < 2; ++hh)
-                    for (int half = 0; half < 2; ++half)
-                        tma_load_2d(smem_u32(smem + mt * 32768 + half * 16384 + hh * 8192), &map_q,
-                                    (h0 + 2 * mt + hh) * D + half * 64, row0, &aux->q_full);
             int g = 0;
             bool ok = true;
             for (int c = 0; c < n_calls && ok; ++c) {
@@ -336,78 +337,116 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
         bool ok = mbar_wait(&aux->q_full, 0, abort_flag, status, STATUS_ATTN_MMA);
         // S for tile gs (call cs, tile ts of the call)
         int gs = 0, cs = 0, ts = 0;
-        auto issue_s = [&]() -> bool {
+        auto do_s = [&]() {
             while (cs < n_calls && ts >= aux->calls[cs].n_tiles) {
                 ++cs;
                 ts = 0;
             }
             const int st = gs % NST;
-            if (!mbar_wait(&aux->kv_full[st], (uint32_t)(gs / NST) & 1u, abort_flag, status,
-                           STATUS_ATTN_MMA))
-                return false;
             const uint32_t k_base = smem_u32(smem + OFF_KV + st * STAGE_BYTES);
-            for (int mt = 0; mt < nmt; ++mt) {
-                if (gs > 0 && !mbar_wait(&aux->s_empty[mt], (uint32_t)(gs - 1) & 1u, abort_flag,
-                                         status, STATUS_ATTN_MMA))
-                    return false;
-                tc_fence_after();
-                if (lane == 0) {
+            tc_fence_after();
+            if (lane == 0) {
+                for (int mt = 0; mt < nmt; ++mt) {
 #pragma unroll
                     for (int ks = 0; ks < D / 16; ++ks)
                         mma_bf16_ss(tmem + TM_S + (uint32_t)(mt * 64), q_desc(q_base, mt, ks),
                                     k_desc(k_base, ks), IDESC_S, ks > 0 ? 1u : 0u);
                     mma_commit(&aux->s_full[mt]);
                 }
-                __syncwarp();
             }
+            __syncwarp();
             ++gs;
             ++ts;
-            return true;
         };
-        if (ok && total > 0) ok = issue_s();
+        // readiness probes: lane 0 looks, the warp follows its answer
+        auto s_ready = [&]() -> bool {
+            int r = 1;
+            if (lane == 0) {
+                r = mbar_try_wait(smem_u32(&aux->kv_full[gs % NST]), (uint32_t)(gs / NST) & 1u);
+                for (int mt = 0; mt < nmt && r && gs > 0; ++mt)
+                    r = mbar_try_wait(smem_u32(&aux->s_empty[mt]), (uint32_t)(gs - 1) & 1u);
+            }
+            return __shfl_sync(0xffffffffu, r, 0) != 0;
+        };
+        auto pv_ready = [&](int g, int mt) -> bool {
+            int r = 0;
+            if (lane == 0)
+                r = mbar_try_wait(smem_u32(&aux->p_full[g & 1][mt]), (uint32_t)(g >> 1) & 1u) &&
+                    mbar_try_wait(smem_u32(&aux->o_ready[mt]), (uint32_t)g & 1u);
+            return __shfl_sync(0xffffffffu, r, 0) != 0;
+        };
+        if (ok && total > 0) {
+            ok = mbar_wait(&aux->kv_full[0], 0, abort_flag, status, STATUS_ATTN_MMA);
+            if (ok) do_s();
+        }
         int g = 0;
         for (int c = 0; c < n_calls && ok; ++c) {
             const Call cl = aux->calls[c];
             for (int t = 0; t < cl.n_tiles; ++t, ++g) {
-                if (g + 1 < total && !issue_s()) {
-                    ok = false;
-                    break;
-                }
                 const int st = g % NST;
                 uint8_t* vd = smem + OFF_KV + st * STAGE_BYTES + KV_TILE;
-                const int valid = cl.n_keys - t * KT;
-                if (cl.kind != CALL_OWN && valid < KT) {
-                    // the V rows past the last key: zeros (the tile landed: S
-                    // of this tile waited for it)
-                    const int first = valid < 0 ? 0 : valid;
-                    for (int idx = first * 8 + lane; idx < KT * 8; idx += 32) {
-                        const int r = idx >> 3, ch = idx & 7;
-                        *reinterpret_cast<uint4*>(vd + r * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
-                        *reinterpret_cast<uint4*>(vd + KV_HALF + r * 128 + ch * 16) =
-                            make_uint4(0, 0, 0, 0);
-                    }
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    __syncwarp();
-                }
                 const uint32_t v_base = smem_u32(vd);
-                for (int mt = 0; mt < nmt && ok; ++mt) {
-                    if (!mbar_wait(&aux->p_full[g & 1][mt], (uint32_t)(g >> 1) & 1u, abort_flag,
-                                   status, STATUS_ATTN_MMA) ||
-                        !mbar_wait(&aux->o_ready[mt], (uint32_t)g & 1u, abort_flag, status,
-                                   STATUS_ATTN_MMA)) {
-                        ok = false;
-                        break;
+                bool s_issued = g + 1 >= total;
+                bool pv_issued[2] = {nmt < 1, nmt < 2};
+                bool zeroed = false;
+                uint64_t t0 = 0;
+                for (uint32_t spins = 0; !(s_issued && pv_issued[0] && pv_issued[1]); ++spins) {
+                    bool progress = false;
+                    if (!s_issued && s_ready()) {
+                        do_s();
+                        s_issued = true;
+                        progress = true;
                     }
-                    tc_fence_after();
-                    if (lane == 0) {
+                    for (int mt = 0; mt < nmt; ++mt) {
+                        if (pv_issued[mt] || !pv_ready(g, mt)) continue;
+                        const int valid = cl.n_keys - t * KT;
+                        if (!zeroed && cl.kind != CALL_OWN && valid < KT) {
+                            // the V rows past the last key: zeros (the tile
+                            // landed: this tile's S waited for it)
+                            const int first = valid < 0 ? 0 : valid;
+                            for (int idx = first * 8 + lane; idx < KT * 8; idx += 32) {
+                                const int r = idx >> 3, ch = idx & 7;
+                                *reinterpret_cast<uint4*>(vd + r * 128 + ch * 16) =
+                                    make_uint4(0, 0, 0, 0);
+                                *reinterpret_cast<uint4*>(vd + KV_HALF + r * 128 + ch * 16) =
+                                    make_uint4(0, 0, 0, 0);
+                            }
+                            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                            __syncwarp();
+                        }
+                        zeroed = true;
+                        tc_fence_after();
+                        if (lane == 0) {
 #pragma unroll
-                        for (int kk = 0; kk < KT / 16; ++kk)
-                            mma_bf16_ss(tmem + TM_O + (uint32_t)(mt * 128),
-                                        p_desc(p_base + (uint32_t)(((g & 1) * 2 + mt) * P_TILE), kk),
-                                        v_desc(v_base, kk), IDESC_PV, (t > 0 || kk > 0) ? 1u : 0u);
-                        mma_commit(&aux->pv_done[g & 1][mt]);
+                            for (int kk = 0; kk < KT / 16; ++kk)
+                                mma_bf16_ss(tmem + TM_O + (uint32_t)(mt * 128),
+                                            p_desc(p_base + (uint32_t)(((g & 1) * 2 + mt) * P_TILE), kk),
+                                            v_desc(v_base, kk), IDESC_PV, (t > 0 || kk > 0) ? 1u : 0u);
+                            mma_commit(&aux->pv_done[g & 1][mt]);
+                        }
+                        __syncwarp();
+                        pv_issued[mt] = true;
+                        progress = true;
                     }
-                    __syncwarp();
+                    if (!progress && (spins & 255u) == 255u) {
+                        // bounded: give up after the timeout or when another role did
+                        int stop = 0;
+                        if (lane == 0) {
+                            const uint64_t now = globaltimer();
+                            if (t0 == 0) t0 = now;
+                            if (*abort_flag) {
+                                stop = 1;
+                            } else if (now - t0 > TIMEOUT_NS) {
+                                atomicOr(status, STATUS_ATTN_MMA);
+                                *abort_flag = 1;
+                                stop = 1;
+                            }
+                        }
+                        if (__shfl_sync(0xffffffffu, stop, 0)) {
+                            ok = false;
+                            break;
+                        }
+                    }
                 }
                 if (!ok) break;
                 if (lane == 0) mma_commit(&aux->kv_empty[st]);
@@ -488,17 +527,34 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         uint32_t sr[16];
                         tmem_ld16_nowait(s_addr + (uint32_t)c0, sr);
                         tmem_wait_ld();
-                        uint32_t pk[8];
+                        float pv[16];
+                        bool rare = false;
 #pragma unroll
                         for (int k = 0; k < 16; k += 2) {
                             const float s0 = c0 + k < lim ? __uint_as_float(sr[k]) : -INFINITY;
                             const float s1 = c0 + k + 1 < lim ? __uint_as_float(sr[k + 1]) : -INFINITY;
-                            float a, b;
-                            f2unpack(f2fma(f2pack(s0, s1), sl, nm), a, b);
-                            qexp2f_x2(a, b);
+                            f2unpack(f2fma(f2pack(s0, s1), sl, nm), pv[k], pv[k + 1]);
+                            qexp2f_x2_fast(pv[k], pv[k + 1], rare);
+                        }
+                        if (rare) {  // a subnormal p: the exact two-step scaling
+#pragma unroll
+                            for (int k = 0; k < 16; k += 2) {
+                                const float s0 = c0 + k < lim ? __uint_as_float(sr[k]) : -INFINITY;
+                                const float s1 =
+                                    c0 + k + 1 < lim ? __uint_as_float(sr[k + 1]) : -INFINITY;
+                                float a, b;
+                                f2unpack(f2fma(f2pack(s0, s1), sl, nm), a, b);
+                                qexp2f_x2(a, b);
+                                pv[k] = a;
+                                pv[k + 1] = b;
+                            }
+                        }
+                        uint32_t pk[8];
+#pragma unroll
+                        for (int k = 0; k < 16; k += 2) {
                             // keys c0 + k, c0 + k + 1 belong to partial (k / 2) % 4 (c0 % 8 == 0)
-                            lp[(k >> 1) & 3] = __fadd_rn(__fadd_rn(lp[(k >> 1) & 3], a), b);
-                            pk[k >> 1] = bf16x2_bits(a, b);
+                            lp[(k >> 1) & 3] = __fadd_rn(__fadd_rn(lp[(k >> 1) & 3], pv[k]), pv[k + 1]);
+                            pk[k >> 1] = bf16x2_bits(pv[k], pv[k + 1]);
                         }
                         const int ch = c0 >> 3;  // 16-byte chunks ch, ch + 1 of the row
                         *reinterpret_cast<uint4*>(prow + ((ch ^ (i & 7)) << 4)) =
@@ -550,8 +606,12 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                     const bool has_b = !UNIFIED && aux->s_grp[qi] >= 0;
                     float w = 0.0f;
                     if (has_b) w = bf16_round(sigmoidf_ref(__fsub_rn(lse_b, lse_a)));
-                    // pass 1: the row's amax; pass 2: the same values again,
-                    // quantised and stored (32 columns per step, small code)
+                    // pass 1: the merged row (bf16) into this M tile's two P
+                    // buffers (free: its last P V finished) and its amax; pass 2:
+                    // from there, quantised and stored. A row's 16-byte chunk j
+                    // sits at (j ^ i % 16) * 16 of its 256 bytes: conflict-free.
+                    // rows 0-63 in P[0][mt], rows 64-127 in P[1][mt]
+                    uint8_t* yrow = smem + OFF_P + ((i >> 6) * 2 + mt) * P_TILE + (i & 63) * 256;
                     float amax = 0.0f;
 #pragma unroll 1
                     for (int c0 = 0; c0 < D; c0 += 32) {
@@ -559,10 +619,20 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
                         tmem_ld16_nowait(ob_addr + (uint32_t)(c0 >> 1), ob);
                         tmem_wait_ld();
+                        uint32_t yv[16];
 #pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            amax = fmaxf(amax, fabsf(merge_value(r[j], ob[j >> 1], j & 1, inv, w,
-                                                                 has_b)));
+                        for (int j = 0; j < 16; ++j) {
+                            const float a = merge_value(r[2 * j], ob[j], 0, inv, w, has_b);
+                            const float b = merge_value(r[2 * j + 1], ob[j], 1, inv, w, has_b);
+                            amax = fmaxf(amax, fmaxf(fabsf(a), fabsf(b)));
+                            yv[j] = bf16x2_bits(a, b);
+                        }
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int j = (c0 >> 3) + u;
+                            *reinterpret_cast<uint4*>(yrow + ((j ^ (i & 15)) << 4)) =
+                                make_uint4(yv[4 * u], yv[4 * u + 1], yv[4 * u + 2], yv[4 * u + 3]);
+                        }
                     }
                     const int row = row0 + qi;
                     const int h = h0 + 2 * mt + (i >> 6);
@@ -571,21 +641,39 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                     uint8_t* out = q_out + ((int64_t)(row < seg_end ? row : row0) * n_q + h) * D;
 #pragma unroll 1
                     for (int c0 = 0; c0 < D; c0 += 32) {
-                        uint32_t r[32], ob[16];
-                        tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
-                        tmem_ld16_nowait(ob_addr + (uint32_t)(c0 >> 1), ob);
-                        tmem_wait_ld();
+                        uint32_t yv[16];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int j = (c0 >> 3) + u;
+                            const uint4 v4 = *reinterpret_cast<const uint4*>(yrow + ((j ^ (i & 15)) << 4));
+                            yv[4 * u] = v4.x;
+                            yv[4 * u + 1] = v4.y;
+                            yv[4 * u + 2] = v4.z;
+                            yv[4 * u + 3] = v4.w;
+                        }
+                        float qv[32];
+                        bool rare = false;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            qv[2 * j] = __uint_as_float(yv[j] << 16);
+                            qv[2 * j + 1] = __uint_as_float(yv[j] & 0xFFFF0000u);
+                            dv.quant2_fast(qv[2 * j], qv[2 * j + 1], rare);
+                        }
+                        if (rare) {  // a value outside the one-reciprocal range: IEEE division
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                float a = __uint_as_float(yv[j] << 16);
+                                float b = __uint_as_float(yv[j] & 0xFFFF0000u);
+                                dv.quant2(a, b);
+                                qv[2 * j] = a;
+                                qv[2 * j + 1] = b;
+                            }
+                        }
                         uint32_t packed[8];
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            float a0 = merge_value(r[j], ob[j >> 1], 0, inv, w, has_b);
-                            float a1 = merge_value(r[j + 1], ob[j >> 1], 1, inv, w, has_b);
-                            float b0 = merge_value(r[j + 2], ob[(j >> 1) + 1], 0, inv, w, has_b);
-                            float b1 = merge_value(r[j + 3], ob[(j >> 1) + 1], 1, inv, w, has_b);
-                            dv.quant2(a0, a1);
-                            dv.quant2(b0, b1);
-                            packed[j >> 2] = (uint32_t)fp8x2(a0, a1) | ((uint32_t)fp8x2(b0, b1) << 16);
-                        }
+                        for (int j = 0; j < 32; j += 4)
+                            packed[j >> 2] = (uint32_t)fp8x2(qv[j], qv[j + 1]) |
+                                             ((uint32_t)fp8x2(qv[j + 2], qv[j + 3]) << 16);
                         if (row < seg_end) {
                             uint4* o4 = reinterpret_cast<uint4*>(out + c0);
                             o4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);

@@ -98,6 +98,10 @@ struct GroupDivider {
     }
     // quant of two values with f32x2 arithmetic (same bits as quant on each)
     __device__ __forceinline__ void quant2(float& a, float& b) const;
+    // quant2 without its rare branch: exact unless a value is outside
+    // [2^-96, 2^100) in magnitude (or not finite), which sets *rare; the
+    // caller then redoes the values with quant2
+    __device__ __forceinline__ void quant2_fast(float& a, float& b, bool& rare) const;
 };
 
 // two floats -> two e4m3 bytes (low byte = first value)
@@ -185,6 +189,17 @@ __device__ __forceinline__ void GroupDivider::quant2(float& a, float& b) const {
     b = fminf(fmaxf(b, -QB_FP8_MAX), QB_FP8_MAX);
 }
 
+__device__ __forceinline__ void GroupDivider::quant2_fast(float& a, float& b, bool& rare) const {
+    const float fa = fabsf(a), fb = fabsf(b);
+    rare |= !(fa >= 0x1p-96f && fa < 0x1p+100f && fb >= 0x1p-96f && fb < 0x1p+100f);
+    const uint64_t y = f2pack(a, b), rr = f2pack(r, r);
+    const uint64_t q0 = f2mul(y, rr);
+    const uint64_t e = f2fma(f2pack(-s, -s), q0, y);
+    f2unpack(f2fma(e, rr, q0), a, b);
+    a = fminf(fmaxf(a, -QB_FP8_MAX), QB_FP8_MAX);
+    b = fminf(fmaxf(b, -QB_FP8_MAX), QB_FP8_MAX);
+}
+
 // 2^f on [-1/2, 1/2]: Taylor coefficients (ln 2)^k / k!, k = 7 .. 0, Horner
 #define QB_EXP2_POLY(STEP)                          \
     STEP(0.000154035303933816099f)                  \
@@ -245,6 +260,32 @@ __device__ __forceinline__ float qexpf(float x) {
 __device__ __forceinline__ float sigmoidf_ref(float x) {
     // __frcp_rn is the correctly rounded 1 / d, the same value as 1.0f / d
     return __frcp_rn(__fadd_rn(1.0f, qexpf(-x)));
+}
+
+// qexp2f_x2 without its rare branch: exact unless a lane's result is
+// subnormal (n < -126, x above the clamp), which sets *rare; the caller then
+// redoes the values with qexp2f_x2. Branch-free, so independent pairs
+// interleave.
+__device__ __forceinline__ void qexp2f_x2_fast(float& a, float& b, bool& rare) {
+    const uint64_t M = f2pack(12582912.0f, 12582912.0f);
+    const float ac = exp2_clamp(a), bc = exp2_clamp(b);
+    const uint64_t x = f2pack(ac, bc);
+    const uint64_t t = f2add(x, M);
+    const uint64_t f = f2sub(x, f2sub(t, M));
+    uint64_t p = f2pack(QB_EXP2_C7, QB_EXP2_C7);
+#define QB_STEP3(c) p = f2fma(p, f, f2pack(c, c));
+    QB_EXP2_POLY(QB_STEP3)
+#undef QB_STEP3
+    float ta, tb;
+    f2unpack(t, ta, tb);
+    // n < -126: a subnormal result, except at the clamp x = -150 (masked keys,
+    // -inf), where 2^-150 rounds to exactly 0
+    const bool sa = __float_as_int(ta) - 0x4B400000 < -126;
+    const bool sb = __float_as_int(tb) - 0x4B400000 < -126;
+    rare |= (sa & (ac > -150.0f)) | (sb & (bc > -150.0f));
+    f2unpack(f2mul(p, f2pack(exp2_scale(ta), exp2_scale(tb))), a, b);
+    a = sa ? 0.0f : a;
+    b = sb ? 0.0f : b;
 }
 
 // two sigmoidf_ref at once (same bits on each)
