@@ -45,6 +45,14 @@ METRIC = "AI.IF rows/sec (Qwen3-4B FP8 filter, config 1)"
 UNIT = "rows/s"
 
 
+# DRAM bytes (read + write) per qb_gemm_fp8_bs launch, averaged over the 144
+# launches of one config-1 chunk (qkv, o, gate_up, down x 36 layers), from the
+# ncu launch list in profiles/launch_list_config1.md (dram__bytes_read.sum +
+# dram__bytes_write.sum, one pass, same workload as this bench)
+GEMM_DRAM_BYTES_PER_LAUNCH = 2.760e9
+GEMM_TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/launch_list_config1.md"
+
+
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -53,6 +61,8 @@ def parse_args():
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--pages", type=int, default=16384)
     p.add_argument("--cpu-rows", type=int, default=2)
+    p.add_argument("--ref-rows", type=int, default=1,
+                   help="config-1 rows per step of the reference arm's CPU sample")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--budget", type=int, default=0)
@@ -230,7 +240,7 @@ def reference_arm(args):
 
     wl = config1()
     weights = random_weights(QWEN3_4B, seed=0, device="cpu")
-    run_once, cores, rows, tokens = cpu_baseline(torch, weights, wl, args.cpu_rows)
+    run_once, cores, rows, tokens = cpu_baseline(torch, weights, wl, args.ref_rows)
     for _ in range(args.warmup):
         run_once()
     t0 = time.perf_counter()
@@ -314,8 +324,9 @@ def main():
     ms = e0.elapsed_time(e1)
     gemm = ex.pipeline.engine.gemm_events
     ex.pipeline.engine.gemm_events = None
-    gemm_ms = sum(a.elapsed_time(b) for a, b, _ in gemm)
-    gemm_flops = sum(f for _, _, f in gemm)
+    gemm_ms = sum(a.elapsed_time(b) for a, b, _, _ in gemm)
+    gemm_flops = sum(f for _, _, f, _ in gemm)
+    gemm_bytes = sum(nb for _, _, _, nb in gemm)
     rows_timed = sum(len(c.layout) for c in timed)
     tokens_timed = sum(c.tokens for c in timed)
     status = nat.kernel_status(local)
@@ -343,13 +354,11 @@ def main():
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         res = ex.filter(e2e_docs, wl.questions, budget=budget, attention="tree")
-        bits = torch.from_numpy(res.bits).to(dev)
-        margins = torch.from_numpy(res.margins).to(dev)
         if world > 1:
-            gb = [torch.empty_like(bits) for _ in range(world)]
-            gm = [torch.empty_like(margins) for _ in range(world)]
-            dist.all_gather(gb, bits)
-            dist.all_gather(gm, margins)
+            # ranks hold different row counts: size-aware gather of (bit, margin)
+            from quail_b200.distributed import gather_rows
+            gather_rows(torch, dist, res.bits, dev)
+            gather_rows(torch, dist, res.margins, dev)
         torch.cuda.synchronize()
         e2e_s = time.perf_counter() - t0
         t = torch.tensor([e2e_s, len(e2e_docs), res.h2d_bytes, res.d2h_bytes, res.chunks],
@@ -398,7 +407,10 @@ def main():
                        "status_word": status},
             "roofline": {"bound": "tensor", "kernel": "qb_gemm_fp8_bs",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak if peak else None, "traffic": None,
+                         "frac": achieved / peak if peak else None,
+                         "traffic": GEMM_DRAM_BYTES_PER_LAUNCH,
+                         "traffic_source": GEMM_TRAFFIC_SOURCE,
+                         "algorithmic_bytes": gemm_bytes / max(len(gemm), 1),
                          "peak_source": f"2 x bf16_tflops_sustained of {src} (of measured)",
                          "launches": len(gemm), "gemm_ms": gemm_ms,
                          "gemm_share_of_step": gemm_ms / ms if ms else None},

@@ -43,7 +43,8 @@ class Engine:
         self.head_dim = cfg.head_dim
         self.softmax_scale = cfg.head_dim ** -0.5
         # a list turns on per-launch CUDA events around every GEMM:
-        # (start, end, flops) tuples, read by bench.py's roofline
+        # (start, end, flops, algorithmic bytes) tuples, read by bench.py's
+        # roofline
         self.gemm_events = None
         nat.load()
 
@@ -101,7 +102,9 @@ class Engine:
                  nat.ptr(weight_scale), nat.ptr(out), m, n, k, self._stream())
         if timed:
             end.record()
-            self.gemm_events.append((start, end, 2.0 * m * n * k))
+            # algorithmic bytes: A and W once, C once, both scale arrays
+            nbytes = m * k + n * k + 2 * m * n + 4 * (m * (k // 128) + (n // 128) * (k // 128))
+            self.gemm_events.append((start, end, 2.0 * m * n * k, nbytes))
         return out
 
     # ---- rotary + KV append -------------------------------------------------
