@@ -73,8 +73,18 @@ struct Call {
     int kind, group, n_keys, key_end, q_first, n_tiles;
 };
 
+// One work item (a 64-row query tile x one head group): filled by the loader
+// warp, read by the other roles, released by all of them.
+struct Info {
+    int seg, row0, h0, hk, seg_start, seg_end;
+    int n_calls, total_tiles;
+    int s_grp[QR];  // read group per tile row (-1: reads nothing resident)
+    Call calls[MAX_CALLS];
+};
+
 struct Aux {
-    uint64_t q_full;
+    uint64_t q_full, q_empty;
+    uint64_t info_full[2], info_empty[2];
     uint64_t kv_full[NST], kv_empty[NST];
     uint64_t s_full[2], s_empty[2], o_ready[2];
     // per P buffer (tile parity) and M tile; phase = tile / 2, so a producer
@@ -84,11 +94,8 @@ struct Aux {
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
-    int n_calls;
-    int total_tiles;
     float alpha[2][2][128];  // [buffer][mt][row]
-    int s_grp[QR];
-    Call calls[MAX_CALLS];
+    Info info[2];
 };
 
 constexpr size_t SMEM_BYTES = OFF_AUX + sizeof(Aux) + 1024;
@@ -140,35 +147,35 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                     const __grid_constant__ CUtensorMap map_kp,
                     const __grid_constant__ CUtensorMap map_vp, int64_t rows, int n_q, int n_kv,
                     int hp, const int32_t* __restrict__ cu_a, const int32_t* __restrict__ tiles,
-                    const int32_t* __restrict__ read_cu_q, const int32_t* __restrict__ read_used,
-                    const int32_t* __restrict__ read_table, int64_t n_reads, int64_t table_width,
-                    const int32_t* __restrict__ source, int64_t n_pages, int page_tokens,
-                    float scale, uint8_t* __restrict__ q_out, float* __restrict__ scale_out,
-                    int64_t scale_ld, uint32_t* status) {
+                    int n_tiles, const int32_t* __restrict__ read_cu_q,
+                    const int32_t* __restrict__ read_used, const int32_t* __restrict__ read_table,
+                    int64_t n_reads, int64_t table_width, const int32_t* __restrict__ source,
+                    int64_t n_pages, int page_tokens, float scale, uint8_t* __restrict__ q_out,
+                    float* __restrict__ scale_out, int64_t scale_ld, uint32_t* status) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
     Aux* aux = reinterpret_cast<Aux*>(smem + OFF_AUX);
     volatile int* abort_flag = &aux->abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-    const int seg = tiles[2 * blockIdx.x], row0 = tiles[2 * blockIdx.x + 1];
     const int group_sz = n_q / n_kv;
     const int per_kv = group_sz / hp;
-    const int hk = blockIdx.y / per_kv;
-    const int h0 = hk * group_sz + (blockIdx.y % per_kv) * hp;
+    const int n_hg = n_kv * per_kv;  // head groups
+    const int n_items = n_tiles * n_hg;
     const int nmt = hp >> 1;
-    const int seg_start = cu_a[seg], seg_end = cu_a[seg + 1];
-    if (seg_start < 0 || seg_end > rows || row0 < seg_start || row0 >= seg_end) {
-        if (threadIdx.x == 0) atomicOr(status, STATUS_BAD_INDEX);
-        return;
-    }
 
     if (threadIdx.x == 0) {
         mbar_init(&aux->q_full, 1);
-        for (int s = 0; s < NST; ++s) {
-            mbar_init(&aux->kv_full[s], 1);
-            mbar_init(&aux->kv_empty[s], 1);
+        mbar_init(&aux->q_empty, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&aux->info_full[b], 1);
+            // released by the MMA warp, the active softmax warps and the
+            // correction warps
+            mbar_init(&aux->info_empty[b], 1 + 4 * nmt + 4);
+        }
+        for (int st = 0; st < NST; ++st) {
+            mbar_init(&aux->kv_full[st], 1);
+            mbar_init(&aux->kv_empty[st], 1);
         }
         for (int m = 0; m < 2; ++m) {
             mbar_init(&aux->s_full[m], 1);
@@ -182,15 +189,6 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
         mbar_init(&aux->drain, 1);
         aux->abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        // Q of the block's heads: needs only the tile, so it starts first
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_q))
-                     : "memory");
-        mbar_arrive_expect_tx(&aux->q_full, (uint32_t)(nmt * 32768));
-        for (int mt = 0; mt < nmt; ++mt)
-            for (int hh = 0; hh < 2; ++hh)
-                for (int half = 0; half < 2; ++half)
-                    tma_load_2d(smem_u32(smem + mt * 32768 + half * 16384 + hh * 8192), &map_q,
-                                (h0 + 2 * mt + hh) * D + half * 64, row0, &aux->q_full);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
@@ -198,130 +196,172 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    // read group per tile row (-1: reads nothing resident)
-    if (threadIdx.x < QR) {
-        const int r = row0 + threadIdx.x;
-        int grp = -1;
-        if (!UNIFIED && r < seg_end && n_reads > 0) {
-            const int src = source[r];
-            if (src >= 0) {
-                if (src >= read_cu_q[n_reads]) atomicOr(status, STATUS_BAD_INDEX);
-                else grp = read_group(read_cu_q, n_reads, src);
-            }
-        }
-        aux->s_grp[threadIdx.x] = grp;
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    // the block's attention calls: each distinct read group (resident keys,
-    // not causal) in ascending order, then the segment's own keys (causal);
-    // or the one causal paged call of the unified path
-    if (threadIdx.x == 0) {
-        int nc = 0, total = 0;
-        auto add = [&](int kind, int grp, int n_keys, int q_first, bool causal) {
-            int key_end = causal ? min(n_keys, q_first + QR) : n_keys;
-            if (key_end < 0) key_end = 0;
-            const int nt = (key_end + KT - 1) / KT;
-            aux->calls[nc++] = Call{kind, grp, n_keys, key_end, q_first, nt};
-            total += nt;
-        };
-        if (UNIFIED) {
-            int used = read_used[seg];
-            const int q_len = seg_end - seg_start;
-            if (used < q_len || (int64_t)((used + page_tokens - 1) / page_tokens) > table_width) {
-                atomicOr(status, STATUS_BAD_INDEX);
-                used = q_len;
-            }
-            add(CALL_UNIFIED, seg, used, used - q_len + (row0 - seg_start), true);
-        } else {
-            int cur = -1;
-            while (true) {
-                int next = INT_MAX;
-                for (int i = 0; i < QR; ++i) {
-                    const int x = aux->s_grp[i];
-                    if (x > cur && x < next) next = x;
-                }
-                if (next == INT_MAX) break;
-                cur = next;
-                int used = read_used[cur];
-                if (used < 0 || (int64_t)((used + page_tokens - 1) / page_tokens) > table_width) {
-                    atomicOr(status, STATUS_BAD_INDEX);
-                    used = 0;
-                }
-                if (used > 0) {
-                    add(CALL_READS, cur, used, 0, false);
-                } else {
-                    // a read group without keys: its rows attend to their own keys only
-                    for (int i = 0; i < QR; ++i)
-                        if (aux->s_grp[i] == cur) aux->s_grp[i] = -1;
-                }
-            }
-            add(CALL_OWN, -1, seg_end - seg_start, row0 - seg_start, true);
-        }
-        aux->n_calls = nc;
-        aux->total_tiles = total;
-    }
-    __syncthreads();
-    const int n_calls = aux->n_calls;
     const uint32_t tmem = aux->tmem_base;
 
     if (warp == 0) {
-        // ---------------- TMA loader ----------------
-        if (lane == 0) {
-            int g = 0;
-            bool ok = true;
-            for (int c = 0; c < n_calls && ok; ++c) {
-                const Call cl = aux->calls[c];
-                for (int t = 0; t < cl.n_tiles; ++t, ++g) {
-                    const int st = g % NST;
-                    if (!mbar_wait(&aux->kv_empty[st], ((uint32_t)(g / NST) & 1u) ^ 1u, abort_flag,
-                                   status, STATUS_ATTN_LOAD)) {
-                        ok = false;
-                        break;
+        // ---------------- loader: item info, Q, K and V tiles ----------------
+        int g = 0, jq = 0;  // tiles loaded, Q loads issued
+        bool ok = true;
+        for (int item = blockIdx.x, k = 0; item < n_items && ok; item += gridDim.x, ++k) {
+            const int slot = k & 1;
+            if (k >= 2 && !mbar_wait(&aux->info_empty[slot], (uint32_t)((k - 2) >> 1) & 1u,
+                                     abort_flag, status, STATUS_ATTN_LOAD))
+                break;
+            Info* inf = &aux->info[slot];
+            const int tile = item / n_hg, hg = item % n_hg;
+            const int seg = tiles[2 * tile], row0 = tiles[2 * tile + 1];
+            const int hk = hg / per_kv;
+            const int h0 = hk * group_sz + (hg % per_kv) * hp;
+            const int seg_start = cu_a[seg], seg_end = cu_a[seg + 1];
+            const bool good = seg_start >= 0 && seg_end <= rows && row0 >= seg_start && row0 < seg_end;
+            // read group per tile row, two rows per lane
+            for (int r = lane; r < QR; r += 32) {
+                int grp = -1;
+                if (!UNIFIED && good && row0 + r < seg_end && n_reads > 0) {
+                    const int src = source[row0 + r];
+                    if (src >= 0) {
+                        if (src >= read_cu_q[n_reads]) atomicOr(status, STATUS_BAD_INDEX);
+                        else grp = read_group(read_cu_q, n_reads, src);
                     }
-                    uint8_t* kd = smem + OFF_KV + st * STAGE_BYTES;
-                    uint8_t* vd = kd + KV_TILE;
-                    mbar_arrive_expect_tx(&aux->kv_full[st], STAGE_BYTES);
-                    const int j0 = t * KT;
-                    if (cl.kind == CALL_OWN) {
-                        const int y = seg_start + j0;
-                        for (int half = 0; half < 2; ++half) {
-                            tma_load_2d(smem_u32(kd + half * KV_HALF), &map_k, hk * D + half * 64,
-                                        y, &aux->kv_full[st]);
-                            tma_load_2d(smem_u32(vd + half * KV_HALF), &map_v, hk * D + half * 64,
-                                        y, &aux->kv_full[st]);
+                }
+                inf->s_grp[r] = grp;
+            }
+            __threadfence_block();
+            __syncwarp();
+            if (lane == 0) {
+                // the item's attention calls: each distinct read group (resident
+                // keys, not causal) ascending, then the segment's own keys
+                // (causal); or the one causal paged call of the unified path
+                int nc = 0, total = 0;
+                auto add = [&](int kind, int grp, int n_keys, int q_first, bool causal) {
+                    int key_end = causal ? min(n_keys, q_first + QR) : n_keys;
+                    if (key_end < 0) key_end = 0;
+                    const int nt = (key_end + KT - 1) / KT;
+                    inf->calls[nc++] = Call{kind, grp, n_keys, key_end, q_first, nt};
+                    total += nt;
+                };
+                if (!good) {
+                    atomicOr(status, STATUS_BAD_INDEX);
+                } else if (UNIFIED) {
+                    int used = read_used[seg];
+                    const int q_len = seg_end - seg_start;
+                    if (used < q_len ||
+                        (int64_t)((used + page_tokens - 1) / page_tokens) > table_width) {
+                        atomicOr(status, STATUS_BAD_INDEX);
+                        used = q_len;
+                    }
+                    add(CALL_UNIFIED, seg, used, used - q_len + (row0 - seg_start), true);
+                } else {
+                    int cur = -1;
+                    while (true) {
+                        int next = INT_MAX;
+                        for (int i = 0; i < QR; ++i) {
+                            const int x = inf->s_grp[i];
+                            if (x > cur && x < next) next = x;
                         }
+                        if (next == INT_MAX) break;
+                        cur = next;
+                        int used = read_used[cur];
+                        if (used < 0 ||
+                            (int64_t)((used + page_tokens - 1) / page_tokens) > table_width) {
+                            atomicOr(status, STATUS_BAD_INDEX);
+                            used = 0;
+                        }
+                        if (used > 0) {
+                            add(CALL_READS, cur, used, 0, false);
+                        } else {
+                            // a read group without keys: its rows attend to their own keys only
+                            for (int i = 0; i < QR; ++i)
+                                if (inf->s_grp[i] == cur) inf->s_grp[i] = -1;
+                        }
+                    }
+                    add(CALL_OWN, -1, seg_end - seg_start, row0 - seg_start, true);
+                }
+                inf->seg = seg;
+                inf->row0 = row0;
+                inf->h0 = h0;
+                inf->hk = hk;
+                inf->seg_start = seg_start;
+                inf->seg_end = seg_end;
+                inf->n_calls = nc;
+                inf->total_tiles = total;
+                mbar_arrive(&aux->info_full[slot]);
+                if (total > 0) {
+                    // Q of the item's heads, once the previous item's S MMAs are done
+                    if (jq > 0 && !mbar_wait(&aux->q_empty, (uint32_t)(jq - 1) & 1u, abort_flag,
+                                             status, STATUS_ATTN_LOAD)) {
+                        ok = false;
                     } else {
-                        const int32_t* trow =
-                            read_table + (int64_t)(cl.kind == CALL_UNIFIED ? seg : cl.group) *
-                                             table_width;
-                        for (int pg = 0; pg < KT / page_tokens; ++pg) {
-                            const int key = j0 + pg * page_tokens;
-                            int64_t page = 0;  // keys past the last one: any valid page
-                            if (key < cl.n_keys) {
-                                page = trow[key / page_tokens];
-                                if (page < 0 || page >= n_pages) {
-                                    atomicOr(status, STATUS_BAD_INDEX);
-                                    page = 0;
-                                }
-                            }
-                            const int y = (int)(page * page_tokens);
-                            const int off = pg * page_tokens * 128;
+                        mbar_arrive_expect_tx(&aux->q_full, (uint32_t)(nmt * 32768));
+                        for (int mt = 0; mt < nmt; ++mt)
+                            for (int hh = 0; hh < 2; ++hh)
+                                for (int half = 0; half < 2; ++half)
+                                    tma_load_2d(smem_u32(smem + mt * 32768 + half * 16384 + hh * 8192),
+                                                &map_q, (h0 + 2 * mt + hh) * D + half * 64, row0,
+                                                &aux->q_full);
+                        ++jq;
+                    }
+                }
+                for (int c = 0; c < nc && ok; ++c) {
+                    const Call cl = inf->calls[c];
+                    for (int t = 0; t < cl.n_tiles; ++t, ++g) {
+                        const int st = g % NST;
+                        if (!mbar_wait(&aux->kv_empty[st], ((uint32_t)(g / NST) & 1u) ^ 1u,
+                                       abort_flag, status, STATUS_ATTN_LOAD)) {
+                            ok = false;
+                            break;
+                        }
+                        uint8_t* kd = smem + OFF_KV + st * STAGE_BYTES;
+                        uint8_t* vd = kd + KV_TILE;
+                        mbar_arrive_expect_tx(&aux->kv_full[st], STAGE_BYTES);
+                        const int j0 = t * KT;
+                        if (cl.kind == CALL_OWN) {
+                            const int y = seg_start + j0;
                             for (int half = 0; half < 2; ++half) {
-                                tma_load_2d(smem_u32(kd + half * KV_HALF + off), &map_kp,
+                                tma_load_2d(smem_u32(kd + half * KV_HALF), &map_k,
                                             hk * D + half * 64, y, &aux->kv_full[st]);
-                                tma_load_2d(smem_u32(vd + half * KV_HALF + off), &map_vp,
+                                tma_load_2d(smem_u32(vd + half * KV_HALF), &map_v,
                                             hk * D + half * 64, y, &aux->kv_full[st]);
+                            }
+                        } else {
+                            const int32_t* trow =
+                                read_table +
+                                (int64_t)(cl.kind == CALL_UNIFIED ? seg : cl.group) * table_width;
+                            for (int pg = 0; pg < KT / page_tokens; ++pg) {
+                                const int key = j0 + pg * page_tokens;
+                                int64_t page = 0;  // keys past the last one: any valid page
+                                if (key < cl.n_keys) {
+                                    page = trow[key / page_tokens];
+                                    if (page < 0 || page >= n_pages) {
+                                        atomicOr(status, STATUS_BAD_INDEX);
+                                        page = 0;
+                                    }
+                                }
+                                const int y = (int)(page * page_tokens);
+                                const int off = pg * page_tokens * 128;
+                                for (int half = 0; half < 2; ++half) {
+                                    tma_load_2d(smem_u32(kd + half * KV_HALF + off), &map_kp,
+                                                hk * D + half * 64, y, &aux->kv_full[st]);
+                                    tma_load_2d(smem_u32(vd + half * KV_HALF + off), &map_vp,
+                                                hk * D + half * 64, y, &aux->kv_full[st]);
+                                }
                             }
                         }
                     }
                 }
             }
-            // no copy may still be landing when the block exits
+            ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
+            g = __shfl_sync(0xffffffffu, g, 0);
+            jq = __shfl_sync(0xffffffffu, jq, 0);
+        }
+        // no copy may still be landing when the block exits
+        if (lane == 0) {
             int flag = 0;
-            if (!mbar_try_wait(smem_u32(&aux->q_full), 0))
-                mbar_wait(&aux->q_full, 0, &flag, status, STATUS_ATTN_LOAD);
+            if (jq > 0 && !mbar_try_wait(smem_u32(&aux->q_full), (uint32_t)(jq - 1) & 1u))
+                mbar_wait(&aux->q_full, (uint32_t)(jq - 1) & 1u, &flag, status, STATUS_ATTN_LOAD);
             for (int j = (g > NST ? g - NST : 0); j < g; ++j) {
                 const int st = j % NST;
                 if (!mbar_try_wait(smem_u32(&aux->kv_full[st]), (uint32_t)(j / NST) & 1u))
@@ -330,39 +370,86 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             }
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer (lane 0 issues; the warp zeroes V tails) ----
+        // ------ MMA issuer (lane 0 issues; the warp zeroes V tails): S of the
+        // next tile (possibly the next item's first) and P V of this tile, each
+        // as soon as its inputs are ready ------
         const uint32_t q_base = smem_u32(smem);
         const uint32_t p_base = smem_u32(smem + OFF_P);
-        const int total = aux->total_tiles;
-        bool ok = mbar_wait(&aux->q_full, 0, abort_flag, status, STATUS_ATTN_MMA);
-        // S for tile gs (call cs, tile ts of the call)
-        int gs = 0, cs = 0, ts = 0;
-        auto do_s = [&]() {
-            while (cs < n_calls && ts >= aux->calls[cs].n_tiles) {
-                ++cs;
-                ts = 0;
+        bool ok = true;
+        // S cursor: item ks (local index), call cs, tile ts; gs = tiles issued;
+        // jq = items with tiles whose Q the S cursor consumed
+        int s_item = blockIdx.x, ks = 0, cs = 0, ts = 0, gs = 0, jq = 0;
+        bool s_have_info = false;  // the S cursor's item info is acquired
+        // moves the S cursor to its next tile; false when the items are done
+        // or a wait gave up. Blocking only when told so.
+        auto s_seek = [&](bool block, bool& ready) -> bool {
+            ready = false;
+            while (s_item < n_items) {
+                const int slot = ks & 1;
+                if (!s_have_info) {
+                    int r = 1;
+                    if (lane == 0) {
+                        if (block)
+                            r = mbar_wait(&aux->info_full[slot], (uint32_t)(ks >> 1) & 1u,
+                                          abort_flag, status, STATUS_ATTN_MMA) ? 1 : -1;
+                        else
+                            r = mbar_try_wait(smem_u32(&aux->info_full[slot]),
+                                              (uint32_t)(ks >> 1) & 1u) ? 1 : 0;
+                    }
+                    r = __shfl_sync(0xffffffffu, r, 0);
+                    if (r < 0) return false;
+                    if (r == 0) return true;  // not yet: try again later
+                    s_have_info = true;
+                    cs = 0;
+                    ts = 0;
+                }
+                const Info* inf = &aux->info[slot];
+                while (cs < inf->n_calls && ts >= inf->calls[cs].n_tiles) {
+                    ++cs;
+                    ts = 0;
+                }
+                if (cs < inf->n_calls) {
+                    ready = true;
+                    return true;
+                }
+                s_item += gridDim.x;
+                ++ks;
+                s_have_info = false;
             }
+            return true;
+        };
+        auto s_issue = [&]() {
+            const Info* inf = &aux->info[ks & 1];
             const int st = gs % NST;
             const uint32_t k_base = smem_u32(smem + OFF_KV + st * STAGE_BYTES);
             tc_fence_after();
             if (lane == 0) {
                 for (int mt = 0; mt < nmt; ++mt) {
 #pragma unroll
-                    for (int ks = 0; ks < D / 16; ++ks)
-                        mma_bf16_ss(tmem + TM_S + (uint32_t)(mt * 64), q_desc(q_base, mt, ks),
-                                    k_desc(k_base, ks), IDESC_S, ks > 0 ? 1u : 0u);
+                    for (int kk = 0; kk < D / 16; ++kk)
+                        mma_bf16_ss(tmem + TM_S + (uint32_t)(mt * 64), q_desc(q_base, mt, kk),
+                                    k_desc(k_base, kk), IDESC_S, kk > 0 ? 1u : 0u);
                     mma_commit(&aux->s_full[mt]);
                 }
             }
-            __syncwarp();
             ++gs;
             ++ts;
+            // the item's last S: Q may be reloaded once these MMAs are done
+            int c = cs, t = ts;
+            while (c < inf->n_calls && t >= inf->calls[c].n_tiles) {
+                ++c;
+                t = 0;
+            }
+            if (c >= inf->n_calls && lane == 0) mma_commit(&aux->q_empty);
+            __syncwarp();
         };
-        // readiness probes: lane 0 looks, the warp follows its answer
+        // S of the cursor's tile can go: its item's Q, its K tile, the S buffers
         auto s_ready = [&]() -> bool {
             int r = 1;
             if (lane == 0) {
-                r = mbar_try_wait(smem_u32(&aux->kv_full[gs % NST]), (uint32_t)(gs / NST) & 1u);
+                if (ts == 0 && cs == 0)  // the item's first S: its Q
+                    r = mbar_try_wait(smem_u32(&aux->q_full), (uint32_t)jq & 1u);
+                if (r) r = mbar_try_wait(smem_u32(&aux->kv_full[gs % NST]), (uint32_t)(gs / NST) & 1u);
                 for (int mt = 0; mt < nmt && r && gs > 0; ++mt)
                     r = mbar_try_wait(smem_u32(&aux->s_empty[mt]), (uint32_t)(gs - 1) & 1u);
             }
@@ -375,83 +462,107 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                     mbar_try_wait(smem_u32(&aux->o_ready[mt]), (uint32_t)g & 1u);
             return __shfl_sync(0xffffffffu, r, 0) != 0;
         };
-        if (ok && total > 0) {
-            ok = mbar_wait(&aux->kv_full[0], 0, abort_flag, status, STATUS_ATTN_MMA);
-            if (ok) do_s();
-        }
+        // issues the S cursor's tile when ready; returns false on give-up
+        auto try_s = [&](bool block, bool& issued) -> bool {
+            issued = false;
+            bool ready;
+            if (!s_seek(block, ready)) return false;
+            if (!ready || !s_ready()) return true;
+            if (ts == 0 && cs == 0) ++jq;
+            s_issue();
+            issued = true;
+            return true;
+        };
         int g = 0;
-        for (int c = 0; c < n_calls && ok; ++c) {
-            const Call cl = aux->calls[c];
-            for (int t = 0; t < cl.n_tiles; ++t, ++g) {
-                const int st = g % NST;
-                uint8_t* vd = smem + OFF_KV + st * STAGE_BYTES + KV_TILE;
-                const uint32_t v_base = smem_u32(vd);
-                bool s_issued = g + 1 >= total;
-                bool pv_issued[2] = {nmt < 1, nmt < 2};
-                bool zeroed = false;
-                uint64_t t0 = 0;
-                for (uint32_t spins = 0; !(s_issued && pv_issued[0] && pv_issued[1]); ++spins) {
-                    bool progress = false;
-                    if (!s_issued && s_ready()) {
-                        do_s();
-                        s_issued = true;
-                        progress = true;
-                    }
-                    for (int mt = 0; mt < nmt; ++mt) {
-                        if (pv_issued[mt] || !pv_ready(g, mt)) continue;
-                        const int valid = cl.n_keys - t * KT;
-                        if (!zeroed && cl.kind != CALL_OWN && valid < KT) {
-                            // the V rows past the last key: zeros (the tile
-                            // landed: this tile's S waited for it)
-                            const int first = valid < 0 ? 0 : valid;
-                            for (int idx = first * 8 + lane; idx < KT * 8; idx += 32) {
-                                const int r = idx >> 3, ch = idx & 7;
-                                *reinterpret_cast<uint4*>(vd + r * 128 + ch * 16) =
-                                    make_uint4(0, 0, 0, 0);
-                                *reinterpret_cast<uint4*>(vd + KV_HALF + r * 128 + ch * 16) =
-                                    make_uint4(0, 0, 0, 0);
-                            }
-                            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                            __syncwarp();
-                        }
-                        zeroed = true;
-                        tc_fence_after();
-                        if (lane == 0) {
-#pragma unroll
-                            for (int kk = 0; kk < KT / 16; ++kk)
-                                mma_bf16_ss(tmem + TM_O + (uint32_t)(mt * 128),
-                                            p_desc(p_base + (uint32_t)(((g & 1) * 2 + mt) * P_TILE), kk),
-                                            v_desc(v_base, kk), IDESC_PV, (t > 0 || kk > 0) ? 1u : 0u);
-                            mma_commit(&aux->pv_done[g & 1][mt]);
-                        }
-                        __syncwarp();
-                        pv_issued[mt] = true;
-                        progress = true;
-                    }
-                    if (!progress && (spins & 255u) == 255u) {
-                        // bounded: give up after the timeout or when another role did
-                        int stop = 0;
-                        if (lane == 0) {
-                            const uint64_t now = globaltimer();
-                            if (t0 == 0) t0 = now;
-                            if (*abort_flag) {
-                                stop = 1;
-                            } else if (now - t0 > TIMEOUT_NS) {
-                                atomicOr(status, STATUS_ATTN_MMA);
-                                *abort_flag = 1;
-                                stop = 1;
-                            }
-                        }
-                        if (__shfl_sync(0xffffffffu, stop, 0)) {
-                            ok = false;
-                            break;
-                        }
-                    }
-                }
-                if (!ok) break;
-                if (lane == 0) mma_commit(&aux->kv_empty[st]);
-                __syncwarp();
+        for (int item = blockIdx.x, k = 0; item < n_items && ok; item += gridDim.x, ++k) {
+            const int slot = k & 1;
+            if (!mbar_wait(&aux->info_full[slot], (uint32_t)(k >> 1) & 1u, abort_flag, status,
+                           STATUS_ATTN_MMA)) {
+                ok = false;
+                break;
             }
+            const Info* inf = &aux->info[slot];
+            const int n_calls = inf->n_calls;
+            for (int c = 0; c < n_calls && ok; ++c) {
+                const Call cl = inf->calls[c];
+                for (int t = 0; t < cl.n_tiles; ++t, ++g) {
+                    const int st = g % NST;
+                    uint8_t* vd = smem + OFF_KV + st * STAGE_BYTES + KV_TILE;
+                    const uint32_t v_base = smem_u32(vd);
+                    bool pv_issued[2] = {nmt < 1, nmt < 2};
+                    bool zeroed = false;
+                    uint64_t t0 = 0;
+                    for (uint32_t spins = 0; !(pv_issued[0] && pv_issued[1]); ++spins) {
+                        bool progress = false;
+                        // S runs at most one tile ahead of P V: S(g) first, then S(g + 1)
+                        if (gs <= g + 1) {
+                            bool issued;
+                            if (!try_s(gs <= g, issued)) {
+                                ok = false;
+                                break;
+                            }
+                            progress |= issued;
+                        }
+                        for (int mt = 0; mt < nmt && gs > g; ++mt) {
+                            if (pv_issued[mt] || !pv_ready(g, mt)) continue;
+                            const int valid = cl.n_keys - t * KT;
+                            if (!zeroed && cl.kind != CALL_OWN && valid < KT) {
+                                // the V rows past the last key: zeros (the tile
+                                // landed: this tile's S waited for it)
+                                const int first = valid < 0 ? 0 : valid;
+                                for (int idx = first * 8 + lane; idx < KT * 8; idx += 32) {
+                                    const int r = idx >> 3, ch = idx & 7;
+                                    *reinterpret_cast<uint4*>(vd + r * 128 + ch * 16) =
+                                        make_uint4(0, 0, 0, 0);
+                                    *reinterpret_cast<uint4*>(vd + KV_HALF + r * 128 + ch * 16) =
+                                        make_uint4(0, 0, 0, 0);
+                                }
+                                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                                __syncwarp();
+                            }
+                            zeroed = true;
+                            tc_fence_after();
+                            if (lane == 0) {
+#pragma unroll
+                                for (int kk = 0; kk < KT / 16; ++kk)
+                                    mma_bf16_ss(tmem + TM_O + (uint32_t)(mt * 128),
+                                                p_desc(p_base + (uint32_t)(((g & 1) * 2 + mt) * P_TILE), kk),
+                                                v_desc(v_base, kk), IDESC_PV,
+                                                (t > 0 || kk > 0) ? 1u : 0u);
+                                mma_commit(&aux->pv_done[g & 1][mt]);
+                            }
+                            __syncwarp();
+                            pv_issued[mt] = true;
+                            progress = true;
+                        }
+                        if (!progress && (spins & 255u) == 255u) {
+                            // bounded: give up after the timeout or when another role did
+                            int stop = 0;
+                            if (lane == 0) {
+                                const uint64_t now = globaltimer();
+                                if (t0 == 0) t0 = now;
+                                if (*abort_flag) {
+                                    stop = 1;
+                                } else if (now - t0 > TIMEOUT_NS) {
+                                    atomicOr(status, STATUS_ATTN_MMA);
+                                    *abort_flag = 1;
+                                    stop = 1;
+                                }
+                            }
+                            if (__shfl_sync(0xffffffffu, stop, 0)) {
+                                ok = false;
+                                break;
+                            }
+                        }
+                    }
+                    if (!ok) break;
+                    if (lane == 0) mma_commit(&aux->kv_empty[st]);
+                    __syncwarp();
+                }
+            }
+            // done with the item's info (its S and P V are all issued)
+            if (lane == 0) mbar_arrive(&aux->info_empty[slot]);
+            __syncwarp();
         }
         // every MMA issued must finish before TMEM is freed
         if (lane == 0) mma_commit(&aux->drain);
@@ -471,219 +582,231 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             const uint32_t ob_addr = tmem + lane_off + TM_OB + (uint32_t)(mt * 64);
             const float sl2 = __fmul_rn(scale, 1.44269504088896341f);
             const uint64_t sl = f2pack(sl2, sl2);
-            float lse_b = 0.0f;  // this row's call-B log-sum-exp
             int g = 0;
             bool ok = true;
-            for (int c = 0; c < n_calls && ok; ++c) {
-                const Call cl = aux->calls[c];
-                const bool causal = cl.kind != CALL_READS;
-                const int qpos = cl.q_first + qi;
-                // keys [0, visible) exist for this row
-                const int visible = causal ? min(cl.key_end, qpos + 1) : cl.key_end;
-                float m = -INFINITY;
-                float lp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                for (int t = 0; t < cl.n_tiles; ++t, ++g) {
-                    if (!mbar_wait(&aux->s_full[mt], (uint32_t)g & 1u, abort_flag, status,
-                                   STATUS_ATTN_SOFTMAX)) {
+            for (int item = blockIdx.x, k = 0; item < n_items && ok; item += gridDim.x, ++k) {
+                const int slot = k & 1;
+                if (!mbar_wait(&aux->info_full[slot], (uint32_t)(k >> 1) & 1u, abort_flag, status,
+                               STATUS_ATTN_SOFTMAX))
+                    break;
+                const Info* inf = &aux->info[slot];
+                const int n_calls = inf->n_calls;
+                const int row0 = inf->row0, seg_end = inf->seg_end, h0 = inf->h0;
+                float lse_b = 0.0f;  // this row's call-B log-sum-exp
+                for (int c = 0; c < n_calls && ok; ++c) {
+                    const Call cl = inf->calls[c];
+                    const bool causal = cl.kind != CALL_READS;
+                    const int qpos = cl.q_first + qi;
+                    // keys [0, visible) exist for this row
+                    const int visible = causal ? min(cl.key_end, qpos + 1) : cl.key_end;
+                    float m = -INFINITY;
+                    float lp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    for (int t = 0; t < cl.n_tiles; ++t, ++g) {
+                        if (!mbar_wait(&aux->s_full[mt], (uint32_t)g & 1u, abort_flag, status,
+                                       STATUS_ATTN_SOFTMAX)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const int lim = visible - t * KT;  // keys [0, lim) of the tile exist
+                        // pass 1: the masked row max
+                        float mx = -INFINITY;
+#pragma unroll 1
+                        for (int c0 = 0; c0 < KT; c0 += 16) {
+                            uint32_t sr[16];
+                            tmem_ld16_nowait(s_addr + (uint32_t)c0, sr);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int k = 0; k < 16; ++k)
+                                mx = fmaxf(mx, c0 + k < lim ? __uint_as_float(sr[k]) : -INFINITY);
+                        }
+                        const float m_new = fmaxf(m, mx);
+                        float alpha, msl;
+                        if (m_new == -INFINITY) {
+                            alpha = 1.0f;
+                            msl = 0.0f;
+                        } else {
+                            alpha = qexp2f(__fmul_rn(__fsub_rn(m, m_new), sl2));
+                            msl = __fmul_rn(m_new, sl2);
+                        }
+                        m = m_new;
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) lp[k] = __fmul_rn(lp[k], alpha);
+                        // P buffer (g & 1) was last read by the P V two tiles back
+                        if (g >= 2 && !mbar_wait(&aux->pv_done[g & 1][mt], (uint32_t)((g - 2) >> 1) & 1u,
+                                                 abort_flag, status, STATUS_ATTN_SOFTMAX)) {
+                            ok = false;
+                            break;
+                        }
+                        uint8_t* prow = smem + OFF_P + ((g & 1) * 2 + mt) * P_TILE + i * 128;
+                        const uint64_t nm = f2pack(-msl, -msl);
+                        // pass 2: p = exp2(s sl2 - m sl2), the row-sum partials, bf16 P
+#pragma unroll 1
+                        for (int c0 = 0; c0 < KT; c0 += 16) {
+                            uint32_t sr[16];
+                            tmem_ld16_nowait(s_addr + (uint32_t)c0, sr);
+                            tmem_wait_ld();
+                            float pv[16];
+                            bool rare = false;
+#pragma unroll
+                            for (int k = 0; k < 16; k += 2) {
+                                const float s0 = c0 + k < lim ? __uint_as_float(sr[k]) : -INFINITY;
+                                const float s1 = c0 + k + 1 < lim ? __uint_as_float(sr[k + 1]) : -INFINITY;
+                                f2unpack(f2fma(f2pack(s0, s1), sl, nm), pv[k], pv[k + 1]);
+                                qexp2f_x2_fast(pv[k], pv[k + 1], rare);
+                            }
+                            if (rare) {  // a subnormal p: the exact two-step scaling
+#pragma unroll
+                                for (int k = 0; k < 16; k += 2) {
+                                    const float s0 = c0 + k < lim ? __uint_as_float(sr[k]) : -INFINITY;
+                                    const float s1 =
+                                        c0 + k + 1 < lim ? __uint_as_float(sr[k + 1]) : -INFINITY;
+                                    float a, b;
+                                    f2unpack(f2fma(f2pack(s0, s1), sl, nm), a, b);
+                                    qexp2f_x2(a, b);
+                                    pv[k] = a;
+                                    pv[k + 1] = b;
+                                }
+                            }
+                            uint32_t pk[8];
+#pragma unroll
+                            for (int k = 0; k < 16; k += 2) {
+                                // keys c0 + k, c0 + k + 1 belong to partial (k / 2) % 4 (c0 % 8 == 0)
+                                lp[(k >> 1) & 3] = __fadd_rn(__fadd_rn(lp[(k >> 1) & 3], pv[k]), pv[k + 1]);
+                                pk[k >> 1] = bf16x2_bits(pv[k], pv[k + 1]);
+                            }
+                            const int ch = c0 >> 3;  // 16-byte chunks ch, ch + 1 of the row
+                            *reinterpret_cast<uint4*>(prow + ((ch ^ (i & 7)) << 4)) =
+                                make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                            *reinterpret_cast<uint4*>(prow + (((ch + 1) ^ (i & 7)) << 4)) =
+                                make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                        }
+                        tc_fence_before();
+                        aux->alpha[g & 1][mt][i] = alpha;
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        __syncwarp();
+                        if (lane == 0) {
+                            mbar_arrive(&aux->s_empty[mt]);
+                            mbar_arrive(&aux->p_full[g & 1][mt]);
+                        }
+                    }
+                    if (!ok) break;
+                    // ---- epilogue of call c for this row: the last P V must be done ----
+                    if (!mbar_wait(&aux->pv_done[(g - 1) & 1][mt], (uint32_t)((g - 1) >> 1) & 1u,
+                                   abort_flag, status, STATUS_ATTN_SOFTMAX)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const int lim = visible - t * KT;  // keys [0, lim) of the tile exist
-                    // pass 1: the masked row max
-                    float mx = -INFINITY;
+                    const float l = __fadd_rn(__fadd_rn(lp[0], lp[1]), __fadd_rn(lp[2], lp[3]));
+                    const float inv = __frcp_rn(l);
+                    if (cl.kind == CALL_READS) {
+                        // normalised call-B output, bf16, for the rows of this read group
+                        const bool member = inf->s_grp[qi] == cl.group;
+                        if (member) lse_b = __fmaf_rn(m, scale, qlnf(l));
 #pragma unroll 1
-                    for (int c0 = 0; c0 < KT; c0 += 16) {
-                        uint32_t sr[16];
-                        tmem_ld16_nowait(s_addr + (uint32_t)c0, sr);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int k = 0; k < 16; ++k)
-                            mx = fmaxf(mx, c0 + k < lim ? __uint_as_float(sr[k]) : -INFINITY);
-                    }
-                    const float m_new = fmaxf(m, mx);
-                    float alpha, msl;
-                    if (m_new == -INFINITY) {
-                        alpha = 1.0f;
-                        msl = 0.0f;
-                    } else {
-                        alpha = qexp2f(__fmul_rn(__fsub_rn(m, m_new), sl2));
-                        msl = __fmul_rn(m_new, sl2);
-                    }
-                    m = m_new;
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) lp[k] = __fmul_rn(lp[k], alpha);
-                    // P buffer (g & 1) was last read by the P V two tiles back
-                    if (g >= 2 && !mbar_wait(&aux->pv_done[g & 1][mt], (uint32_t)((g - 2) >> 1) & 1u,
-                                             abort_flag, status, STATUS_ATTN_SOFTMAX)) {
-                        ok = false;
-                        break;
-                    }
-                    uint8_t* prow = smem + OFF_P + ((g & 1) * 2 + mt) * P_TILE + i * 128;
-                    const uint64_t nm = f2pack(-msl, -msl);
-                    // pass 2: p = exp2(s sl2 - m sl2), the row-sum partials, bf16 P
-#pragma unroll 1
-                    for (int c0 = 0; c0 < KT; c0 += 16) {
-                        uint32_t sr[16];
-                        tmem_ld16_nowait(s_addr + (uint32_t)c0, sr);
-                        tmem_wait_ld();
-                        float pv[16];
-                        bool rare = false;
-#pragma unroll
-                        for (int k = 0; k < 16; k += 2) {
-                            const float s0 = c0 + k < lim ? __uint_as_float(sr[k]) : -INFINITY;
-                            const float s1 = c0 + k + 1 < lim ? __uint_as_float(sr[k + 1]) : -INFINITY;
-                            f2unpack(f2fma(f2pack(s0, s1), sl, nm), pv[k], pv[k + 1]);
-                            qexp2f_x2_fast(pv[k], pv[k + 1], rare);
-                        }
-                        if (rare) {  // a subnormal p: the exact two-step scaling
-#pragma unroll
-                            for (int k = 0; k < 16; k += 2) {
-                                const float s0 = c0 + k < lim ? __uint_as_float(sr[k]) : -INFINITY;
-                                const float s1 =
-                                    c0 + k + 1 < lim ? __uint_as_float(sr[k + 1]) : -INFINITY;
-                                float a, b;
-                                f2unpack(f2fma(f2pack(s0, s1), sl, nm), a, b);
-                                qexp2f_x2(a, b);
-                                pv[k] = a;
-                                pv[k + 1] = b;
-                            }
-                        }
-                        uint32_t pk[8];
-#pragma unroll
-                        for (int k = 0; k < 16; k += 2) {
-                            // keys c0 + k, c0 + k + 1 belong to partial (k / 2) % 4 (c0 % 8 == 0)
-                            lp[(k >> 1) & 3] = __fadd_rn(__fadd_rn(lp[(k >> 1) & 3], pv[k]), pv[k + 1]);
-                            pk[k >> 1] = bf16x2_bits(pv[k], pv[k + 1]);
-                        }
-                        const int ch = c0 >> 3;  // 16-byte chunks ch, ch + 1 of the row
-                        *reinterpret_cast<uint4*>(prow + ((ch ^ (i & 7)) << 4)) =
-                            make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                        *reinterpret_cast<uint4*>(prow + (((ch + 1) ^ (i & 7)) << 4)) =
-                            make_uint4(pk[4], pk[5], pk[6], pk[7]);
-                    }
-                    tc_fence_before();
-                    aux->alpha[g & 1][mt][i] = alpha;
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    __syncwarp();
-                    if (lane == 0) {
-                        mbar_arrive(&aux->s_empty[mt]);
-                        mbar_arrive(&aux->p_full[g & 1][mt]);
-                    }
-                }
-                if (!ok) break;
-                // ---- epilogue of call c for this row: the last P V must be done ----
-                if (!mbar_wait(&aux->pv_done[(g - 1) & 1][mt], (uint32_t)((g - 1) >> 1) & 1u,
-                               abort_flag, status, STATUS_ATTN_SOFTMAX)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const float l = __fadd_rn(__fadd_rn(lp[0], lp[1]), __fadd_rn(lp[2], lp[3]));
-                const float inv = __frcp_rn(l);
-                if (cl.kind == CALL_READS) {
-                    // normalised call-B output, bf16, for the rows of this read group
-                    const bool member = aux->s_grp[qi] == cl.group;
-                    if (member) lse_b = __fmaf_rn(m, scale, qlnf(l));
-#pragma unroll 1
-                    for (int c0 = 0; c0 < D; c0 += 32) {
-                        uint32_t r[32], ob[16];
-                        tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
-                        tmem_ld16_nowait(ob_addr + (uint32_t)(c0 >> 1), ob);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            const uint32_t v = bf16x2_bits(__fmul_rn(__uint_as_float(r[2 * j]), inv),
-                                                           __fmul_rn(__uint_as_float(r[2 * j + 1]), inv));
-                            if (member) ob[j] = v;
-                        }
-                        tmem_st16(ob_addr + (uint32_t)(c0 >> 1), ob);
-                    }
-                    tmem_wait_st();
-                } else {
-                    // merge with call B, per-head fp8 quantisation, store
-                    const float lse_a = __fmaf_rn(m, scale, qlnf(l));
-                    const bool has_b = !UNIFIED && aux->s_grp[qi] >= 0;
-                    float w = 0.0f;
-                    if (has_b) w = bf16_round(sigmoidf_ref(__fsub_rn(lse_b, lse_a)));
-                    // pass 1: the merged row (bf16) into this M tile's two P
-                    // buffers (free: its last P V finished) and its amax; pass 2:
-                    // from there, quantised and stored. A row's 16-byte chunk j
-                    // sits at (j ^ i % 16) * 16 of its 256 bytes: conflict-free.
-                    // rows 0-63 in P[0][mt], rows 64-127 in P[1][mt]
-                    uint8_t* yrow = smem + OFF_P + ((i >> 6) * 2 + mt) * P_TILE + (i & 63) * 256;
-                    float amax = 0.0f;
-#pragma unroll 1
-                    for (int c0 = 0; c0 < D; c0 += 32) {
-                        uint32_t r[32], ob[16];
-                        tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
-                        tmem_ld16_nowait(ob_addr + (uint32_t)(c0 >> 1), ob);
-                        tmem_wait_ld();
-                        uint32_t yv[16];
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            const float a = merge_value(r[2 * j], ob[j], 0, inv, w, has_b);
-                            const float b = merge_value(r[2 * j + 1], ob[j], 1, inv, w, has_b);
-                            amax = fmaxf(amax, fmaxf(fabsf(a), fabsf(b)));
-                            yv[j] = bf16x2_bits(a, b);
-                        }
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const int j = (c0 >> 3) + u;
-                            *reinterpret_cast<uint4*>(yrow + ((j ^ (i & 15)) << 4)) =
-                                make_uint4(yv[4 * u], yv[4 * u + 1], yv[4 * u + 2], yv[4 * u + 3]);
-                        }
-                    }
-                    const int row = row0 + qi;
-                    const int h = h0 + 2 * mt + (i >> 6);
-                    const float sc = group_scale(amax);
-                    const GroupDivider dv(sc);
-                    uint8_t* out = q_out + ((int64_t)(row < seg_end ? row : row0) * n_q + h) * D;
-#pragma unroll 1
-                    for (int c0 = 0; c0 < D; c0 += 32) {
-                        uint32_t yv[16];
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const int j = (c0 >> 3) + u;
-                            const uint4 v4 = *reinterpret_cast<const uint4*>(yrow + ((j ^ (i & 15)) << 4));
-                            yv[4 * u] = v4.x;
-                            yv[4 * u + 1] = v4.y;
-                            yv[4 * u + 2] = v4.z;
-                            yv[4 * u + 3] = v4.w;
-                        }
-                        float qv[32];
-                        bool rare = false;
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            qv[2 * j] = __uint_as_float(yv[j] << 16);
-                            qv[2 * j + 1] = __uint_as_float(yv[j] & 0xFFFF0000u);
-                            dv.quant2_fast(qv[2 * j], qv[2 * j + 1], rare);
-                        }
-                        if (rare) {  // a value outside the one-reciprocal range: IEEE division
+                        for (int c0 = 0; c0 < D; c0 += 32) {
+                            uint32_t r[32], ob[16];
+                            tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
+                            tmem_ld16_nowait(ob_addr + (uint32_t)(c0 >> 1), ob);
+                            tmem_wait_ld();
 #pragma unroll
                             for (int j = 0; j < 16; ++j) {
-                                float a = __uint_as_float(yv[j] << 16);
-                                float b = __uint_as_float(yv[j] & 0xFFFF0000u);
-                                dv.quant2(a, b);
-                                qv[2 * j] = a;
-                                qv[2 * j + 1] = b;
+                                const uint32_t v = bf16x2_bits(__fmul_rn(__uint_as_float(r[2 * j]), inv),
+                                                               __fmul_rn(__uint_as_float(r[2 * j + 1]), inv));
+                                if (member) ob[j] = v;
+                            }
+                            tmem_st16(ob_addr + (uint32_t)(c0 >> 1), ob);
+                        }
+                        tmem_wait_st();
+                    } else {
+                        // merge with call B, per-head fp8 quantisation, store
+                        const float lse_a = __fmaf_rn(m, scale, qlnf(l));
+                        const bool has_b = !UNIFIED && inf->s_grp[qi] >= 0;
+                        float w = 0.0f;
+                        if (has_b) w = bf16_round(sigmoidf_ref(__fsub_rn(lse_b, lse_a)));
+                        // pass 1: the merged row (bf16) into this M tile's two P
+                        // buffers (free: its last P V finished) and its amax; pass 2:
+                        // from there, quantised and stored. A row's 16-byte chunk j
+                        // sits at (j ^ i % 16) * 16 of its 256 bytes: conflict-free.
+                        // rows 0-63 in P[0][mt], rows 64-127 in P[1][mt]
+                        uint8_t* yrow = smem + OFF_P + ((i >> 6) * 2 + mt) * P_TILE + (i & 63) * 256;
+                        float amax = 0.0f;
+#pragma unroll 1
+                        for (int c0 = 0; c0 < D; c0 += 32) {
+                            uint32_t r[32], ob[16];
+                            tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
+                            tmem_ld16_nowait(ob_addr + (uint32_t)(c0 >> 1), ob);
+                            tmem_wait_ld();
+                            uint32_t yv[16];
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                const float a = merge_value(r[2 * j], ob[j], 0, inv, w, has_b);
+                                const float b = merge_value(r[2 * j + 1], ob[j], 1, inv, w, has_b);
+                                amax = fmaxf(amax, fmaxf(fabsf(a), fabsf(b)));
+                                yv[j] = bf16x2_bits(a, b);
+                            }
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                const int j = (c0 >> 3) + u;
+                                *reinterpret_cast<uint4*>(yrow + ((j ^ (i & 15)) << 4)) =
+                                    make_uint4(yv[4 * u], yv[4 * u + 1], yv[4 * u + 2], yv[4 * u + 3]);
                             }
                         }
-                        uint32_t packed[8];
+                        const int row = row0 + qi;
+                        const int h = h0 + 2 * mt + (i >> 6);
+                        const float sc = group_scale(amax);
+                        const GroupDivider dv(sc);
+                        uint8_t* out = q_out + ((int64_t)(row < seg_end ? row : row0) * n_q + h) * D;
+#pragma unroll 1
+                        for (int c0 = 0; c0 < D; c0 += 32) {
+                            uint32_t yv[16];
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            packed[j >> 2] = (uint32_t)fp8x2(qv[j], qv[j + 1]) |
-                                             ((uint32_t)fp8x2(qv[j + 2], qv[j + 3]) << 16);
-                        if (row < seg_end) {
-                            uint4* o4 = reinterpret_cast<uint4*>(out + c0);
-                            o4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                            o4[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                            for (int u = 0; u < 4; ++u) {
+                                const int j = (c0 >> 3) + u;
+                                const uint4 v4 = *reinterpret_cast<const uint4*>(yrow + ((j ^ (i & 15)) << 4));
+                                yv[4 * u] = v4.x;
+                                yv[4 * u + 1] = v4.y;
+                                yv[4 * u + 2] = v4.z;
+                                yv[4 * u + 3] = v4.w;
+                            }
+                            float qv[32];
+                            bool rare = false;
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                qv[2 * j] = __uint_as_float(yv[j] << 16);
+                                qv[2 * j + 1] = __uint_as_float(yv[j] & 0xFFFF0000u);
+                                dv.quant2_fast(qv[2 * j], qv[2 * j + 1], rare);
+                            }
+                            if (rare) {  // a value outside the one-reciprocal range: IEEE division
+#pragma unroll
+                                for (int j = 0; j < 16; ++j) {
+                                    float a = __uint_as_float(yv[j] << 16);
+                                    float b = __uint_as_float(yv[j] & 0xFFFF0000u);
+                                    dv.quant2(a, b);
+                                    qv[2 * j] = a;
+                                    qv[2 * j + 1] = b;
+                                }
+                            }
+                            uint32_t packed[8];
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4)
+                                packed[j >> 2] = (uint32_t)fp8x2(qv[j], qv[j + 1]) |
+                                                 ((uint32_t)fp8x2(qv[j + 2], qv[j + 3]) << 16);
+                            if (row < seg_end) {
+                                uint4* o4 = reinterpret_cast<uint4*>(out + c0);
+                                o4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                                o4[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                            }
                         }
+                        if (row < seg_end) scale_out[(int64_t)h * scale_ld + row] = sc;
                     }
-                    if (row < seg_end) scale_out[(int64_t)h * scale_ld + row] = sc;
+                    // O (and the call-B output) read before the next call's first P V
+                    tc_fence_before();
                 }
-                // O (and the call-B output) read before the next call's first P V
-                tc_fence_before();
+                // done with the item's info (its calls and epilogues are through)
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&aux->info_empty[slot]);
             }
         }
     } else {
@@ -693,53 +816,64 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
         const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
         int g = 0;
         bool ok = true;
-        for (int c = 0; c < n_calls && ok; ++c) {
-            const Call cl = aux->calls[c];
-            for (int t = 0; t < cl.n_tiles && ok; ++t, ++g) {
-                for (int mt = 0; mt < nmt; ++mt) {
-                    // every p_full phase is waited for (a parity wait is only
-                    // sound when the waiter is at most one phase behind)
-                    if (!mbar_wait(&aux->p_full[g & 1][mt], (uint32_t)(g >> 1) & 1u, abort_flag,
-                                   status, STATUS_ATTN_CORRECTION)) {
-                        ok = false;
-                        break;
-                    }
-                    if (t > 0) {
-                        if (!mbar_wait(&aux->pv_done[(g - 1) & 1][mt], (uint32_t)((g - 1) >> 1) & 1u,
-                                       abort_flag, status, STATUS_ATTN_CORRECTION)) {
+        for (int item = blockIdx.x, k = 0; item < n_items && ok; item += gridDim.x, ++k) {
+            const int slot = k & 1;
+            if (!mbar_wait(&aux->info_full[slot], (uint32_t)(k >> 1) & 1u, abort_flag, status,
+                           STATUS_ATTN_CORRECTION))
+                break;
+            const Info* inf = &aux->info[slot];
+            const int n_calls = inf->n_calls;
+            for (int c = 0; c < n_calls && ok; ++c) {
+                const int n_t = inf->calls[c].n_tiles;
+                for (int t = 0; t < n_t && ok; ++t, ++g) {
+                    for (int mt = 0; mt < nmt; ++mt) {
+                        // every p_full phase is waited for (a parity wait is only
+                        // sound when the waiter is at most one phase behind)
+                        if (!mbar_wait(&aux->p_full[g & 1][mt], (uint32_t)(g >> 1) & 1u, abort_flag,
+                                       status, STATUS_ATTN_CORRECTION)) {
                             ok = false;
                             break;
                         }
-                        tc_fence_after();
-                        const float a = aux->alpha[g & 1][mt][i];
-                        if (__any_sync(0xffffffffu, a != 1.0f)) {
-                            const uint64_t a2 = f2pack(a, a);
-                            const uint32_t o_addr = tmem + lane_off + TM_O + (uint32_t)(mt * 128);
-#pragma unroll 1
-                            for (int c0 = 0; c0 < D; c0 += 32) {
-                                uint32_t r[32];
-                                tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
-                                tmem_wait_ld();
-#pragma unroll
-                                for (int j = 0; j < 32; j += 2) {
-                                    float x, y;
-                                    f2unpack(f2mul(f2pack(__uint_as_float(r[j]),
-                                                          __uint_as_float(r[j + 1])),
-                                                   a2),
-                                             x, y);
-                                    r[j] = __float_as_uint(x);
-                                    r[j + 1] = __float_as_uint(y);
-                                }
-                                tmem_st32(o_addr + (uint32_t)c0, r);
+                        if (t > 0) {
+                            if (!mbar_wait(&aux->pv_done[(g - 1) & 1][mt],
+                                           (uint32_t)((g - 1) >> 1) & 1u, abort_flag, status,
+                                           STATUS_ATTN_CORRECTION)) {
+                                ok = false;
+                                break;
                             }
-                            tmem_wait_st();
+                            tc_fence_after();
+                            const float a = aux->alpha[g & 1][mt][i];
+                            if (__any_sync(0xffffffffu, a != 1.0f)) {
+                                const uint64_t a2 = f2pack(a, a);
+                                const uint32_t o_addr = tmem + lane_off + TM_O + (uint32_t)(mt * 128);
+#pragma unroll 1
+                                for (int c0 = 0; c0 < D; c0 += 32) {
+                                    uint32_t r[32];
+                                    tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
+                                    tmem_wait_ld();
+#pragma unroll
+                                    for (int j = 0; j < 32; j += 2) {
+                                        float x, y;
+                                        f2unpack(f2mul(f2pack(__uint_as_float(r[j]),
+                                                              __uint_as_float(r[j + 1])),
+                                                       a2),
+                                                 x, y);
+                                        r[j] = __float_as_uint(x);
+                                        r[j + 1] = __float_as_uint(y);
+                                    }
+                                    tmem_st32(o_addr + (uint32_t)c0, r);
+                                }
+                                tmem_wait_st();
+                            }
                         }
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&aux->o_ready[mt]);
                     }
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&aux->o_ready[mt]);
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&aux->info_empty[slot]);
         }
     }
 
@@ -810,11 +944,16 @@ int launch_attention_tc(bool unified, const char* who, const void* q, const void
             return launch_status(who);
         attr[unified][dev] = true;
     }
-    dim3 grid((unsigned)n_tiles, (unsigned)(n_kv * (group / hp)));
+    // persistent: one block per SM walks the items (query tile x head group,
+    // head groups of a tile adjacent so they share K/V in L2)
+    const int64_t items = n_tiles * (int64_t)(n_kv * (group / hp));
+    if (items > 0x7fffffffLL) return invalid("attention: too many work items");
+    const int64_t sms = sm_count();
+    const unsigned grid = (unsigned)(items < sms ? items : sms);
     kernel<<<grid, NUM_THREADS, SMEM_BYTES, (cudaStream_t)stream>>>(
-        mq, mk, mv, mkp, mvp, rows, n_q, n_kv, hp, cu, tiles, read_cu_q, read_used, table,
-        n_reads, table_width, source, n_pages, page_tokens, softmax_scale, (uint8_t*)q_out,
-        scale_out, scale_ld, status);
+        mq, mk, mv, mkp, mvp, rows, n_q, n_kv, hp, cu, tiles, (int)n_tiles, read_cu_q, read_used,
+        table, n_reads, table_width, source, n_pages, page_tokens, softmax_scale,
+        (uint8_t*)q_out, scale_out, scale_ld, status);
     return launch_status(who);
 }
 
