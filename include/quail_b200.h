@@ -235,6 +235,20 @@ int qb_answer_margin(const void* normed, int64_t n_rows, int64_t hidden_dim,
                      int n_true, const int32_t* false_cols, int n_false,
                      float* margin_out, uint8_t* bits_out, void* stream);
 
+/*
+ * AI.SCORE readout over the retained output rows: fp32 scores
+ * normed . ans_w[j] (the same fixed summation order as qb_answer_margin,
+ * no bf16 rounding), t = max over true_cols, f = max over false_cols,
+ * score_out = sigmoid(t - f) in fp32. Replaces AsyncScores.submit
+ * (quail/backends/quail/executor/readout.py:88-111: fp32 F.linear, amax per
+ * class, torch.sigmoid(yes - no)).
+ * normed: bf16 [n_rows, hidden_dim]; ans_w: bf16 [n_ids, hidden_dim];
+ * score_out: f32 [n_rows]. n_ids <= 16.
+ */
+int qb_answer_score(const void* normed, int64_t n_rows, int64_t hidden_dim, const void* ans_w,
+                    int n_ids, const int32_t* true_cols, int n_true, const int32_t* false_cols,
+                    int n_false, float* score_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

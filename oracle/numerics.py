@@ -306,6 +306,18 @@ def final_norm(hidden, residual, finals, w, eps):
     return to_bf16(y * w.to(torch.float32))
 
 
+def answer_score(normed, ans_w, true_cols, false_cols):
+    """AsyncScores.submit (readout.py:88-111): fp32 scores of the retained head
+    rows (no bf16 rounding), max per class, sigmoid(yes - no) in fp32."""
+    if MODE["exact"]:
+        raw = tc.dot_rows(normed.to(torch.float32), ans_w.to(torch.float32))
+    else:
+        raw = normed.to(torch.float32) @ ans_w.to(torch.float32).t()
+    t = raw[:, list(true_cols)].amax(dim=1)
+    f = raw[:, list(false_cols)].amax(dim=1)
+    return tc.sigmoid(t - f) if MODE["exact"] else torch.sigmoid(t - f)
+
+
 def answer_margin(normed, ans_w, true_cols, false_cols):
     """AnswerRows.logits + AsyncAnswers.submit (readout.py:45-49, 70-80):
     bf16 scores of the retained head rows (fp32 accumulate), max per class,

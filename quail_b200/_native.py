@@ -47,6 +47,7 @@ SIGNATURES = {
     "qb_silu_mul_quant": [_P, _I64, _I64, _P, _P, _I64, _P],
     "qb_final_norm": [_P, _P, _I64, _I64, _P, _I64, _P, _F32, _P, _P],
     "qb_answer_margin": [_P, _I64, _I64, _P, _I32, _P, _I32, _P, _I32, _P, _P, _P],
+    "qb_answer_score": [_P, _I64, _I64, _P, _I32, _P, _I32, _P, _I32, _P, _P],
 }
 
 _lib = None

@@ -41,6 +41,9 @@ __global__ void final_norm_kernel(const bf16* __restrict__ hidden,
     *reinterpret_cast<uint4*>(normed_out + i * hdim + t * 8) = float_to_bf16x8(y);
 }
 
+// SCORE = false: bf16 scores, margin and bit (AI_FILTER / AI_JOIN);
+// SCORE = true: fp32 scores, out = sigmoid(t - f) (AI.SCORE), bits unused.
+template <bool SCORE>
 __global__ void answer_margin_kernel(const bf16* __restrict__ normed, int hdim,
                                      const bf16* __restrict__ ans_w, int n_ids,
                                      const int32_t* __restrict__ true_cols, int n_true,
@@ -67,7 +70,7 @@ __global__ void answer_margin_kernel(const bf16* __restrict__ normed, int hdim,
     if (t < n_ids) {
         float s = 0.0f;
         for (int w = 0; w < n_warps; ++w) s = __fadd_rn(s, partial[w][t]);
-        scores[t] = bf16_round(s);
+        scores[t] = SCORE ? s : bf16_round(s);
     }
     __syncthreads();
     if (t == 0) {
@@ -82,8 +85,12 @@ __global__ void answer_margin_kernel(const bf16* __restrict__ normed, int hdim,
             if (c >= 0 && c < n_ids) best_f = fmaxf(best_f, scores[c]);
             else atomicOr(status, STATUS_BAD_INDEX);
         }
-        margin_out[i] = best_t - best_f;
-        bits_out[i] = best_t > best_f ? 1 : 0;
+        if (SCORE) {
+            margin_out[i] = sigmoidf_ref(__fsub_rn(best_t, best_f));
+        } else {
+            margin_out[i] = best_t - best_f;
+            bits_out[i] = best_t > best_f ? 1 : 0;
+        }
     }
 }
 
@@ -131,8 +138,31 @@ extern "C" int qb_answer_margin(const void* normed, int64_t n_rows, int64_t hidd
     if (n_rows > 0x7fffffffLL) return invalid("qb_answer_margin: too many rows");
     uint32_t* status = device_status_ptr();
     if (!status) return launch_status("qb_answer_margin: status word");
-    answer_margin_kernel<<<(unsigned)n_rows, (unsigned)(hidden_dim / 8), 0, (cudaStream_t)stream>>>(
+    answer_margin_kernel<false><<<(unsigned)n_rows, (unsigned)(hidden_dim / 8), 0,
+                                  (cudaStream_t)stream>>>(
         (const bf16*)normed, (int)hidden_dim, (const bf16*)ans_w, n_ids, true_cols, n_true,
         false_cols, n_false, margin_out, bits_out, status);
     return launch_status("qb_answer_margin");
+}
+
+extern "C" int qb_answer_score(const void* normed, int64_t n_rows, int64_t hidden_dim,
+                               const void* ans_w, int n_ids, const int32_t* true_cols, int n_true,
+                               const int32_t* false_cols, int n_false, float* score_out,
+                               void* stream) {
+    int st = check_hdim(hidden_dim, "qb_answer_score");
+    if (st) return st;
+    if (n_ids <= 0 || n_ids > MAX_IDS) return invalid("qb_answer_score: 1 <= n_ids <= 16");
+    if (n_true <= 0 || n_false <= 0) return invalid("qb_answer_score: empty answer class");
+    if (n_rows < 0) return invalid("qb_answer_score: negative size");
+    if (!aligned(normed, 16) || !aligned(ans_w, 16))
+        return invalid("qb_answer_score: pointers must be 16-byte aligned");
+    if (n_rows == 0) return QB_OK;
+    if (n_rows > 0x7fffffffLL) return invalid("qb_answer_score: too many rows");
+    uint32_t* status = device_status_ptr();
+    if (!status) return launch_status("qb_answer_score: status word");
+    answer_margin_kernel<true><<<(unsigned)n_rows, (unsigned)(hidden_dim / 8), 0,
+                                 (cudaStream_t)stream>>>(
+        (const bf16*)normed, (int)hidden_dim, (const bf16*)ans_w, n_ids, true_cols, n_true,
+        false_cols, n_false, score_out, nullptr, status);
+    return launch_status("qb_answer_score");
 }

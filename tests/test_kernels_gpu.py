@@ -288,3 +288,24 @@ def test_final_norm_and_answer_margin(dev):
     assert_bits_equal(margin, m_ref, "margins")
     assert_bits_equal(bits, b_ref, "bits")
     assert_status_clean()
+
+
+def test_answer_score_readout(dev):
+    """AI.SCORE: fp32 yes/no logits and sigmoid, through AsyncScores, against
+    the oracle bit for bit and torch's fp32 sigmoid within float tolerance."""
+    cfg = TINY
+    g = torch.Generator().manual_seed(12)
+    rows = 57
+    normed = torch.randn(rows, cfg.hidden, generator=g).to(torch.bfloat16)
+    w = random_weights(cfg, seed=3, device="cpu")
+    from quail_b200.readout import AnswerRows, AsyncScores
+    scorer = AsyncScores(torch, AnswerRows(torch, w.to(dev)))
+    got = scorer.result(scorer.submit(normed.to(dev)))
+    allowed, ans_w, tc, fc = w.answer_rows()
+    ref = nx.answer_score(normed, ans_w, tc, fc)
+    assert got.dtype == np.float32 and got.shape == (rows,)
+    assert np.array_equal(got.view(np.int32), ref.numpy().view(np.int32))
+    logits = normed.float() @ ans_w.float().t()
+    plain = torch.sigmoid(logits[:, tc].amax(1) - logits[:, fc].amax(1))
+    assert float((torch.from_numpy(got) - plain).abs().max()) < 1e-5
+    assert_status_clean()

@@ -92,3 +92,18 @@ def test_tcgen05_f16_probe_matches_model():
         want = torch.from_numpy(data[key + "_d"])
         got = tc.mma_bf16(a, b_nk, c0)
         assert torch.equal(got.view(torch.int32), want.view(torch.int32)), key
+
+
+def test_answer_score_restatement():
+    """The oracle's AI.SCORE readout against plain torch fp32 (AsyncScores'
+    own arithmetic: F.linear in fp32, amax per class, sigmoid)."""
+    from oracle import numerics as nx
+    g = torch.Generator().manual_seed(4)
+    normed = torch.randn(33, 512, generator=g).to(torch.bfloat16)
+    ans_w = (0.02 * torch.randn(8, 512, generator=g)).to(torch.bfloat16)
+    tcols, fcols = [0, 2, 4, 6], [1, 3, 5, 7]
+    got = nx.answer_score(normed, ans_w, tcols, fcols)
+    logits = torch.nn.functional.linear(normed.float(), ans_w.float())
+    want = torch.sigmoid(logits[:, tcols].amax(1) - logits[:, fcols].amax(1))
+    assert got.dtype == torch.float32
+    assert float((got - want).abs().max()) < 2e-6
