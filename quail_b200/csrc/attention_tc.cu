@@ -115,14 +115,19 @@ __device__ __forceinline__ uint32_t bf16x2_bits(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// One merged output value: a = bf16(o * inv); with call B,
-// bf16(a + (b - a) w), b the call-B output (high or low half of ob).
-__device__ __forceinline__ float merge_value(uint32_t o_bits, uint32_t ob, int high, float inv,
-                                             float w, bool has_b) {
-    const float a = bf16_round(__fmul_rn(__uint_as_float(o_bits), inv));
-    if (!has_b) return a;
-    const float b = __uint_as_float(high ? (ob & 0xFFFF0000u) : (ob << 16));
-    return bf16_round(__fadd_rn(a, __fmul_rn(__fsub_rn(b, a), w)));
+// Two merged outputs as a bf16 pair (f32x2 arithmetic): a = bf16(o inv);
+// with call B, bf16(a + (b - a) w), b the call-B output (bf16 pair ob).
+__device__ __forceinline__ uint32_t merge_pair(uint32_t o0, uint32_t o1, uint32_t ob,
+                                               uint64_t inv2, uint64_t w2, bool has_b) {
+    float a0, a1;
+    f2unpack(f2mul(f2pack(__uint_as_float(o0), __uint_as_float(o1)), inv2), a0, a1);
+    const uint32_t y = bf16x2_bits(a0, a1);
+    if (!has_b) return y;
+    const uint64_t a = f2pack(__uint_as_float(y << 16), __uint_as_float(y & 0xFFFF0000u));
+    const uint64_t b = f2pack(__uint_as_float(ob << 16), __uint_as_float(ob & 0xFFFF0000u));
+    float s0, s1;
+    f2unpack(f2add(a, f2mul(f2sub(b, a), w2)), s0, s1);
+    return bf16x2_bits(s0, s1);
 }
 
 // Operand descriptors. Q: [mt][half][128 rows][128 B]; K, V: [half][64][128 B].
@@ -380,7 +385,6 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
         // jq = items with tiles whose Q the S cursor consumed
         int s_item = blockIdx.x, ks = 0, cs = 0, ts = 0, gs = 0, jq = 0;
         bool s_have_info = false;  // the S cursor's item info is acquired
-        int s_mask = 0;            // M tiles whose S of tile gs is issued
         // moves the S cursor to its next tile; false when the items are done
         // or a wait gave up. Blocking only when told so.
         auto s_seek = [&](bool block, bool& ready) -> bool {
@@ -419,45 +423,39 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             }
             return true;
         };
-        // S of the cursor's tile for one M tile; the cursor moves on once
-        // every M tile's S is issued
-        auto s_issue = [&](int mt) {
+        auto s_issue = [&]() {
             const Info* inf = &aux->info[ks & 1];
             const int st = gs % NST;
             const uint32_t k_base = smem_u32(smem + OFF_KV + st * STAGE_BYTES);
             tc_fence_after();
             if (lane == 0) {
+                for (int mt = 0; mt < nmt; ++mt) {
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk)
-                    mma_bf16_ss(tmem + TM_S + (uint32_t)(mt * 64), q_desc(q_base, mt, kk),
-                                k_desc(k_base, kk), IDESC_S, kk > 0 ? 1u : 0u);
-                mma_commit(&aux->s_full[mt]);
-            }
-            s_mask |= 1 << mt;
-            if (s_mask == (1 << nmt) - 1) {
-                if (ts == 0 && cs == 0) ++jq;
-                s_mask = 0;
-                ++gs;
-                ++ts;
-                // the item's last S: Q may be reloaded once these MMAs are done
-                int c = cs, t = ts;
-                while (c < inf->n_calls && t >= inf->calls[c].n_tiles) {
-                    ++c;
-                    t = 0;
+                    for (int kk = 0; kk < D / 16; ++kk)
+                        mma_bf16_ss(tmem + TM_S + (uint32_t)(mt * 64), q_desc(q_base, mt, kk),
+                                    k_desc(k_base, kk), IDESC_S, kk > 0 ? 1u : 0u);
+                    mma_commit(&aux->s_full[mt]);
                 }
-                if (c >= inf->n_calls && lane == 0) mma_commit(&aux->q_empty);
             }
+            ++gs;
+            ++ts;
+            // the item's last S: Q may be reloaded once these MMAs are done
+            int c = cs, t = ts;
+            while (c < inf->n_calls && t >= inf->calls[c].n_tiles) {
+                ++c;
+                t = 0;
+            }
+            if (c >= inf->n_calls && lane == 0) mma_commit(&aux->q_empty);
             __syncwarp();
         };
-        // S of the cursor's tile for M tile mt can go: the item's Q (first
-        // tile), the K tile, mt's S buffer
-        auto s_ready = [&](int mt) -> bool {
+        // S of the cursor's tile can go: its item's Q, its K tile, the S buffers
+        auto s_ready = [&]() -> bool {
             int r = 1;
             if (lane == 0) {
-                if (ts == 0 && cs == 0)
+                if (ts == 0 && cs == 0)  // the item's first S: its Q
                     r = mbar_try_wait(smem_u32(&aux->q_full), (uint32_t)jq & 1u);
                 if (r) r = mbar_try_wait(smem_u32(&aux->kv_full[gs % NST]), (uint32_t)(gs / NST) & 1u);
-                if (r && gs > 0)
+                for (int mt = 0; mt < nmt && r && gs > 0; ++mt)
                     r = mbar_try_wait(smem_u32(&aux->s_empty[mt]), (uint32_t)(gs - 1) & 1u);
             }
             return __shfl_sync(0xffffffffu, r, 0) != 0;
@@ -469,24 +467,16 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                     mbar_try_wait(smem_u32(&aux->o_ready[mt]), (uint32_t)g & 1u);
             return __shfl_sync(0xffffffffu, r, 0) != 0;
         };
-        // issues what is ready of the S cursor's tile; false on give-up
+        // issues the S cursor's tile when ready; returns false on give-up
         auto try_s = [&](bool block, bool& issued) -> bool {
             issued = false;
             bool ready;
             if (!s_seek(block, ready)) return false;
-            if (!ready) return true;
-            for (int mt = 0; mt < nmt; ++mt) {
-                if ((s_mask >> mt) & 1) continue;
-                if (!s_ready(mt)) continue;
-                s_issue(mt);
-                issued = true;
-                if (s_mask == 0) break;  // the tile is complete: the cursor moved
-            }
+            if (!ready || !s_ready()) return true;
+            if (ts == 0 && cs == 0) ++jq;
+            s_issue();
+            issued = true;
             return true;
-        };
-        // S of tile g for M tile mt is issued
-        auto s_done = [&](int g, int mt) -> bool {
-            return gs > g || (gs == g && ((s_mask >> mt) & 1));
         };
         int g = 0;
         for (int item = blockIdx.x, k = 0; item < n_items && ok; item += gridDim.x, ++k) {
@@ -518,8 +508,8 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                             }
                             progress |= issued;
                         }
-                        for (int mt = 0; mt < nmt; ++mt) {
-                            if (pv_issued[mt] || !s_done(g, mt) || !pv_ready(g, mt)) continue;
+                        for (int mt = 0; mt < nmt && gs > g; ++mt) {
+                            if (pv_issued[mt] || !pv_ready(g, mt)) continue;
                             const int valid = cl.n_keys - t * KT;
                             if (!zeroed && cl.kind != CALL_OWN && valid < KT) {
                                 // the V rows past the last key: zeros (the tile
@@ -624,21 +614,16 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         }
                         tc_fence_after();
                         const int lim = visible - t * KT;  // keys [0, lim) of the tile exist
-                        // pass 1: the whole S row into registers (one wait), the S
-                        // buffer handed back at once (the next tile's S may run
-                        // during pass 2), masked keys set to -inf, the row max
-                        uint32_t sr[KT];
-                        tmem_ld32_nowait(s_addr, sr);
-                        tmem_ld32_nowait(s_addr + 32, sr + 32);
-                        tmem_wait_ld();
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&aux->s_empty[mt]);
+                        // pass 1: the masked row max
                         float mx = -INFINITY;
+#pragma unroll 1
+                        for (int c0 = 0; c0 < KT; c0 += 16) {
+                            uint32_t sr[16];
+                            tmem_ld16_nowait(s_addr + (uint32_t)c0, sr);
+                            tmem_wait_ld();
 #pragma unroll
-                        for (int k = 0; k < KT; ++k) {
-                            if (k >= lim) sr[k] = 0xFF800000u;  // -inf
-                            mx = fmaxf(mx, __uint_as_float(sr[k]));
+                            for (int k = 0; k < 16; ++k)
+                                mx = fmaxf(mx, c0 + k < lim ? __uint_as_float(sr[k]) : -INFINITY);
                         }
                         const float m_new = fmaxf(m, mx);
                         float alpha, msl;
@@ -660,49 +645,55 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         }
                         uint8_t* prow = smem + OFF_P + ((g & 1) * 2 + mt) * P_TILE + i * 128;
                         const uint64_t nm = f2pack(-msl, -msl);
-                        // pass 2 (registers): p = exp2(s sl2 - m sl2), the row-sum
-                        // partials, bf16 P; 8 keys (one 16-byte chunk of P) per step
-#pragma unroll
-                        for (int c0 = 0; c0 < KT; c0 += 8) {
-                            float pv[8];
+                        // pass 2: p = exp2(s sl2 - m sl2), the row-sum partials, bf16 P
+#pragma unroll 1
+                        for (int c0 = 0; c0 < KT; c0 += 16) {
+                            uint32_t sr[16];
+                            tmem_ld16_nowait(s_addr + (uint32_t)c0, sr);
+                            tmem_wait_ld();
+                            float pv[16];
                             bool rare = false;
 #pragma unroll
-                            for (int k = 0; k < 8; k += 2) {
-                                f2unpack(f2fma(f2pack(__uint_as_float(sr[c0 + k]),
-                                                      __uint_as_float(sr[c0 + k + 1])),
-                                               sl, nm),
-                                         pv[k], pv[k + 1]);
-                                qexp2f_x2_fast(pv[k], pv[k + 1], rare);
+                            for (int k = 0; k < 16; k += 2) {
+                                const float s0 = c0 + k < lim ? __uint_as_float(sr[k]) : -INFINITY;
+                                const float s1 = c0 + k + 1 < lim ? __uint_as_float(sr[k + 1]) : -INFINITY;
+                                f2unpack(f2fma(f2pack(s0, s1), sl, nm), pv[k], pv[k + 1]);
+                                qexp2f_x2_low(pv[k], pv[k + 1], rare);
                             }
                             if (rare) {  // a subnormal p: the exact two-step scaling
 #pragma unroll
-                                for (int k = 0; k < 8; k += 2) {
-                                    float x, y;
-                                    f2unpack(f2fma(f2pack(__uint_as_float(sr[c0 + k]),
-                                                          __uint_as_float(sr[c0 + k + 1])),
-                                                   sl, nm),
-                                             x, y);
-                                    qexp2f_x2(x, y);
-                                    pv[k] = x;
-                                    pv[k + 1] = y;
+                                for (int k = 0; k < 16; k += 2) {
+                                    const float s0 = c0 + k < lim ? __uint_as_float(sr[k]) : -INFINITY;
+                                    const float s1 =
+                                        c0 + k + 1 < lim ? __uint_as_float(sr[k + 1]) : -INFINITY;
+                                    float a, b;
+                                    f2unpack(f2fma(f2pack(s0, s1), sl, nm), a, b);
+                                    qexp2f_x2(a, b);
+                                    pv[k] = a;
+                                    pv[k + 1] = b;
                                 }
                             }
-                            uint32_t pk[4];
+                            uint32_t pk[8];
 #pragma unroll
-                            for (int k = 0; k < 8; k += 2) {
+                            for (int k = 0; k < 16; k += 2) {
                                 // keys c0 + k, c0 + k + 1 belong to partial (k / 2) % 4 (c0 % 8 == 0)
-                                lp[k >> 1] = __fadd_rn(__fadd_rn(lp[k >> 1], pv[k]), pv[k + 1]);
+                                lp[(k >> 1) & 3] = __fadd_rn(__fadd_rn(lp[(k >> 1) & 3], pv[k]), pv[k + 1]);
                                 pk[k >> 1] = bf16x2_bits(pv[k], pv[k + 1]);
                             }
-                            const int ch = c0 >> 3;  // this step's 16-byte chunk of the row
+                            const int ch = c0 >> 3;  // 16-byte chunks ch, ch + 1 of the row
                             *reinterpret_cast<uint4*>(prow + ((ch ^ (i & 7)) << 4)) =
                                 make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                            *reinterpret_cast<uint4*>(prow + (((ch + 1) ^ (i & 7)) << 4)) =
+                                make_uint4(pk[4], pk[5], pk[6], pk[7]);
                         }
                         tc_fence_before();
                         aux->alpha[g & 1][mt][i] = alpha;
                         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(&aux->p_full[g & 1][mt]);
+                        if (lane == 0) {
+                            mbar_arrive(&aux->s_empty[mt]);
+                            mbar_arrive(&aux->p_full[g & 1][mt]);
+                        }
                     }
                     if (!ok) break;
                     // ---- epilogue of call c for this row: the last P V must be done ----
@@ -739,6 +730,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         const bool has_b = !UNIFIED && inf->s_grp[qi] >= 0;
                         float w = 0.0f;
                         if (has_b) w = bf16_round(sigmoidf_ref(__fsub_rn(lse_b, lse_a)));
+                        const uint64_t inv2 = f2pack(inv, inv), w2 = f2pack(w, w);
                         // pass 1: the merged row (bf16) into this M tile's two P
                         // buffers (free: its last P V finished) and its amax; pass 2:
                         // from there, quantised and stored. A row's 16-byte chunk j
@@ -755,10 +747,9 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                             uint32_t yv[16];
 #pragma unroll
                             for (int j = 0; j < 16; ++j) {
-                                const float a = merge_value(r[2 * j], ob[j], 0, inv, w, has_b);
-                                const float b = merge_value(r[2 * j + 1], ob[j], 1, inv, w, has_b);
-                                amax = fmaxf(amax, fmaxf(fabsf(a), fabsf(b)));
-                                yv[j] = bf16x2_bits(a, b);
+                                yv[j] = merge_pair(r[2 * j], r[2 * j + 1], ob[j], inv2, w2, has_b);
+                                amax = fmaxf(amax, fabsf(__uint_as_float(yv[j] << 16)));
+                                amax = fmaxf(amax, fabsf(__uint_as_float(yv[j] & 0xFFFF0000u)));
                             }
 #pragma unroll
                             for (int u = 0; u < 4; ++u) {

@@ -288,6 +288,33 @@ __device__ __forceinline__ void qexp2f_x2_fast(float& a, float& b, bool& rare) {
     b = sb ? 0.0f : b;
 }
 
+// qexp2f_x2_fast for exponents below 128 (softmax: s sl2 - m sl2 <= 0): the
+// clamp is -160 below only, so x <= -150.5 gives exactly 0 as qexp2f does
+// (2^-150.5 is under half the smallest subnormal); *rare is set when a
+// lane's n is in [-150, -127] (a subnormal, or 0 from qexp2f's clamp at
+// -150), and the caller redoes the pair with qexp2f_x2. NaN stays NaN.
+__device__ __forceinline__ void qexp2f_x2_low(float& a, float& b, bool& rare) {
+    const uint64_t M = f2pack(12582912.0f, 12582912.0f);
+    float ac, bc;
+    asm("max.NaN.f32 %0, %1, 0fC3200000;" : "=f"(ac) : "f"(a));  // -160
+    asm("max.NaN.f32 %0, %1, 0fC3200000;" : "=f"(bc) : "f"(b));
+    const uint64_t x = f2pack(ac, bc);
+    const uint64_t t = f2add(x, M);
+    const uint64_t f = f2sub(x, f2sub(t, M));
+    uint64_t p = f2pack(QB_EXP2_C7, QB_EXP2_C7);
+#define QB_STEP4(c) p = f2fma(p, f, f2pack(c, c));
+    QB_EXP2_POLY(QB_STEP4)
+#undef QB_STEP4
+    float ta, tb;
+    f2unpack(t, ta, tb);
+    const int na = __float_as_int(ta) - 0x4B400000, nb = __float_as_int(tb) - 0x4B400000;
+    rare |= ((unsigned)(na + 150) < 24u) | ((unsigned)(nb + 150) < 24u);
+    f2unpack(f2mul(p, f2pack(__int_as_float((na + 127) << 23), __int_as_float((nb + 127) << 23))),
+             a, b);
+    a = na < -126 ? 0.0f : a;
+    b = nb < -126 ? 0.0f : b;
+}
+
 // two sigmoidf_ref at once (same bits on each)
 __device__ __forceinline__ void sigmoidf_ref_x2(float& a, float& b) {
     float ea, eb;
