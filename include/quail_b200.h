@@ -204,6 +204,25 @@ int qb_silu_mul_quant(const void* gate_up, int64_t rows, int64_t inter,
                       void* stream);
 
 /*
+ * The MLP's gate_up projection and its SiLU-gated quantisation in one
+ * kernel: the same bits as qb_gemm_fp8_bs(a, w, n = 2 * inter) into bf16
+ * gate_up followed by qb_silu_mul_quant, without the bf16 [rows, 2 * inter]
+ * intermediate. Replaces the MLP's engine.gemm(gate_up_proj) +
+ * engine.activation_quant pair (quail/backends/quail/executor/models/
+ * qwen3.py:69-70; Engine.gemm and custom_silu_quant, attention.py:129-140,
+ * 644-656, 771-775). a, a_scale, a_scale_ld: as qb_gemm_fp8_bs;
+ * w: fp8 [2 * inter, k] (gate rows, then up rows); w_scale: f32
+ * [2 * inter / 128, k / 128]; q_out: fp8 [m, inter]; scale_out: f32
+ * [inter / 128, scale_ld]. inter % 128 == 0, k % 128 == 0; a, w, q_out
+ * 16-byte aligned.
+ */
+int qb_gemm_fp8_silu_quant(const void* a, const float* a_scale,
+                           int64_t a_scale_ld, const void* w,
+                           const float* w_scale, void* q_out, float* scale_out,
+                           int64_t scale_ld, int64_t m, int64_t inter,
+                           int64_t k, void* stream);
+
+/*
  * Final norm over the answer rows only: for each final row f,
  * x = hidden[f] + residual[f] (fp32); rstd = rsqrt(mean(x^2) + eps);
  * normed_out[i] = bf16(bf16(x * rstd) * final_w).

@@ -24,10 +24,22 @@
 //   warps 3-18  epilogue: warp w reads TMEM lanes 32*(w%4).. (its rows) and
 //               columns (w-3)/4 * BN/4 .. (its slice), scales and accumulates.
 // No cluster launch and no TMA multicast: every block loads its own tiles.
+//
+// SILU (the MLP's gate_up projection, weights [gate; up] of inter rows
+// each): a 256-wide tile is 128 gate columns j*128.. and the same 128 up
+// columns inter + j*128.. (two 128-row weight boxes), and the epilogue
+// writes q = fp8(silu(bf16 gate) * bf16 up / scale) with one scale per row
+// and tile (one 128-column quantisation group) instead of the bf16
+// product: the same bits as the bf16 GEMM followed by qb_silu_mul_quant.
+// Epilogue warp w holds gate columns 32*(w-3)/4.. and the matching up
+// columns of its rows; the row's group max is exchanged between the four
+// warps of the same rows through shared memory and an mbarrier.
 // Every mbarrier wait is bounded (about one second); a wait that gives up
 // sets a status bit, makes the other roles stop, drains the copies and MMAs
 // in flight and frees TMEM before the block exits.
 #include <cudaTypedefs.h>
+
+#include <type_traits>
 
 #include "tc_common.cuh"
 
@@ -48,7 +60,7 @@ constexpr int SCALE_SLOTS = 8;
 // written through a 128-byte-swizzled shared-memory staging area by TMA
 // stores (one 32 x 64 box per epilogue warp) instead of per-thread row
 // stores, so the epilogue returns to the next tile at once.
-template <int BN, int NST = MAX_STAGES, bool TSTORE = false>
+template <int BN, int NST = MAX_STAGES, bool TSTORE = false, bool SILU = false>
 struct Cfg {
     static constexpr int STAGES = NST;
     static_assert(NST >= 2 && NST <= MAX_STAGES, "stages");
@@ -61,7 +73,11 @@ struct Cfg {
     static_assert(!TSTORE || SLICE == 64, "TMA-store staging rows are 128 bytes");
     static constexpr int OUT_BYTES = TSTORE ? EPI_WARPS * 32 * SLICE * 2 : 0;
     static constexpr int SCALE_OFF = STAGES * STAGE_BYTES + OUT_BYTES;
-    static constexpr int BAR_OFF = SCALE_OFF + SCALE_SLOTS * 528;
+    static_assert(!SILU || (BN == 256 && !TSTORE), "SILU tiles are 128 gate + 128 up columns");
+    // SILU: per-row group max partials, [2 tile parities][4 slices][BM rows]
+    static constexpr int RED_OFF = SCALE_OFF + SCALE_SLOTS * 528;
+    static constexpr int RED_BYTES = SILU ? 2 * 4 * BM * 4 : 0;
+    static constexpr int BAR_OFF = RED_OFF + RED_BYTES;
     static constexpr int BAR_BYTES = 512;
     static constexpr int SMEM = BAR_OFF + BAR_BYTES + 1024;
     // instruction descriptor: D f32, A/B e4m3, both K-major, N, M=128
@@ -85,6 +101,7 @@ struct Barriers {
     uint64_t scale_full[SCALE_SLOTS];
     uint64_t scale_empty[SCALE_SLOTS];
     uint64_t drain;
+    uint64_t red_full[2];  // SILU: a tile's group-max partials are in shared memory
     uint32_t tmem_base;
     int abort;
 };
@@ -110,18 +127,23 @@ __device__ __forceinline__ void fma2(float* acc, const uint32_t* v, float s) {
     asm("mov.b64 {%0, %1}, %2;" : "=f"(acc[0]), "=f"(acc[1]) : "l"(a));
 }
 
-// OutT = bf16 (the library) or float (numerics probes: the fp32 accumulator).
+// OutT = bf16 (the library) or float (numerics probes: the fp32 accumulator);
+// uint8_t with SILU (fp8 e4m3 rows of N/2 columns, their scales at
+// q_scale[j * q_scale_ld + row]).
 // map_c (bf16 out, box 64 x 32, 128-byte swizzle) is read only when TSTORE.
-template <int BN, typename OutT = bf16, int NST = MAX_STAGES, bool TSTORE = false>
+template <int BN, typename OutT = bf16, int NST = MAX_STAGES, bool TSTORE = false,
+          bool SILU = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                    const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_c, const float* __restrict__ a_scale,
                    int64_t a_scale_ld, const float* __restrict__ w_scale, OutT* __restrict__ out,
-                   int M, int N, int K, uint32_t* status) {
-    using C = Cfg<BN, NST, TSTORE>;
+                   float* __restrict__ q_scale, int64_t q_scale_ld, int M, int N, int K,
+                   uint32_t* status) {
+    using C = Cfg<BN, NST, TSTORE, SILU>;
     constexpr int STAGES = C::STAGES;
     static_assert(!TSTORE || sizeof(OutT) == 2, "TMA stores write bf16");
+    static_assert(!SILU || sizeof(OutT) == 1, "SILU writes fp8");
     extern __shared__ uint8_t smem_raw[];
     // SWIZZLE_128B tiles need 1024-byte aligned shared memory
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -150,6 +172,8 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
             mbar_init(&bars->scale_empty[s], EPI_WARPS);
         }
         mbar_init(&bars->drain, 1);
+        mbar_init(&bars->red_full[0], EPI_WARPS);
+        mbar_init(&bars->red_full[1], EPI_WARPS);
         bars->abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -187,7 +211,17 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                     uint8_t* sa = smem + s * C::STAGE_BYTES;
                     mbar_arrive_expect_tx(&bars->full[s], C::STAGE_BYTES);
                     tma_load_2d(smem_u32(sa), &map_a, kb * BK, m0, &bars->full[s]);
-                    tma_load_2d(smem_u32(sa + C::A_BYTES), &map_b, kb * BK, n0, &bars->full[s]);
+                    if constexpr (SILU) {
+                        // gate rows j*128.., up rows N/2 + j*128..: one 256-row tile
+                        const int j0 = (tile % num_n) * 128;
+                        tma_load_2d(smem_u32(sa + C::A_BYTES), &map_b, kb * BK, j0,
+                                    &bars->full[s]);
+                        tma_load_2d(smem_u32(sa + C::A_BYTES + 128 * BK), &map_b, kb * BK,
+                                    N / 2 + j0, &bars->full[s]);
+                    } else {
+                        tma_load_2d(smem_u32(sa + C::A_BYTES), &map_b, kb * BK, n0,
+                                    &bars->full[s]);
+                    }
                 }
             }
             // no copy may still be landing when the block exits: wait for the
@@ -263,9 +297,11 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                     cp_async4(smem_u32(&sl->a[r]), valid ? col + m0 + r : a_scale,
                               valid ? 4u : 0u);
                 }
-                if (lane < NB)
-                    cp_async4(smem_u32(&sl->w[lane]),
-                              w_scale + (int64_t)(n0 / 128 + lane) * n_kb + kb, 4u);
+                if (lane < NB) {
+                    // the weight block of the tile's lane-th 128 columns
+                    const int wb = SILU ? (tile % num_n) + lane * (N / 256) : n0 / 128 + lane;
+                    cp_async4(smem_u32(&sl->w[lane]), w_scale + (int64_t)wb * n_kb + kb, 4u);
+                }
                 cp_async_arrive(&bars->scale_full[slot]);
             }
             if (!ok) break;
@@ -276,12 +312,13 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
         // ---------------- epilogue: promote, accumulate, store ----------------
         const int ew = warp - FIRST_EPI_WARP;
         const int quarter = warp & 3;          // TMEM lanes this warp may access
-        const int col0 = (ew >> 2) * C::SLICE; // its column slice
+        // its column slice (SILU: gate columns col0.., up columns 128 + col0..)
+        const int col0 = (ew >> 2) * (SILU ? 32 : C::SLICE);
         const int row_in_tile = quarter * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-        int acc_it = 0;
+        int acc_it = 0, tcount = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++tcount) {
             const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
             const int m = m0 + row_in_tile;
             const bool valid = m < M;
@@ -296,7 +333,9 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                     ok = false;
                     break;
                 }
-                const float sc = scales[slot].a[row_in_tile] * scales[slot].w[wblk];
+                const float a_sc = scales[slot].a[row_in_tile];
+                const float sc = a_sc * scales[slot].w[SILU ? 0 : wblk];
+                const float sc_up = SILU ? a_sc * scales[slot].w[1] : sc;
                 const int buf = acc_it % C::NBUF;
                 if (!mbar_wait(&bars->tmem_full[buf], (uint32_t)(acc_it / C::NBUF) & 1u, abort_flag,
                                status, STATUS_GEMM_EPILOGUE)) {
@@ -309,8 +348,10 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                 for (int c = 0; c < C::SLICE; c += 32) {
                     // two loads in flight per wait
                     uint32_t v[32];
-                    tmem_ld16_nowait(taddr + (uint32_t)c, v);
-                    tmem_ld16_nowait(taddr + (uint32_t)c + 16u, v + 16);
+                    // SILU: the second 32 columns are the up half's
+                    const uint32_t cc = (SILU && c > 0) ? 128u : (uint32_t)c;
+                    tmem_ld16_nowait(taddr + cc, v);
+                    tmem_ld16_nowait(taddr + cc + 16u, v + 16);
                     tmem_wait_ld();
                     if (c + 32 >= C::SLICE) {
                         // the buffer's last columns are in registers: hand it
@@ -323,11 +364,59 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                         }
                     }
 #pragma unroll
-                    for (int j = 0; j < 32; j += 2) fma2(acc + c + j, v + j, sc);
+                    for (int j = 0; j < 32; j += 2)
+                        fma2(acc + c + j, v + j, (SILU && c > 0) ? sc_up : sc);
                 }
             }
             if (!ok) break;
-            if constexpr (TSTORE) {
+            if constexpr (SILU) {
+                // y = (g sigmoid(g)) u on the bf16-rounded accumulators, as
+                // qb_silu_mul_quant computes it from the bf16 GEMM output
+                float amax = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    const bf162 g2 = __floats2bfloat162_rn(acc[i], acc[i + 1]);
+                    const bf162 u2 = __floats2bfloat162_rn(acc[32 + i], acc[33 + i]);
+                    const float g0 = __low2float(g2), g1 = __high2float(g2);
+                    float sa = g0, sb = g1;
+                    sigmoidf_ref_x2(sa, sb);
+                    const uint64_t gs = f2mul(f2pack(g0, g1), f2pack(sa, sb));
+                    f2unpack(f2mul(gs, f2pack(__low2float(u2), __high2float(u2))), acc[i],
+                             acc[i + 1]);
+                    amax = fmaxf(amax, fabsf(acc[i]));
+                    amax = fmaxf(amax, fabsf(acc[i + 1]));
+                }
+                // the row's group max over the four warps of its 128 columns
+                float* red = reinterpret_cast<float*>(smem + C::RED_OFF) + (tcount & 1) * 4 * BM;
+                red[(ew >> 2) * BM + row_in_tile] = amax;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->red_full[tcount & 1]);
+                if (!mbar_wait(&bars->red_full[tcount & 1], (uint32_t)(tcount >> 1) & 1u,
+                               abort_flag, status, STATUS_GEMM_EPILOGUE)) {
+                    ok = false;
+                    break;
+                }
+                amax = fmaxf(fmaxf(red[row_in_tile], red[BM + row_in_tile]),
+                             fmaxf(red[2 * BM + row_in_tile], red[3 * BM + row_in_tile]));
+                const float scale = group_scale(amax);
+                const GroupDivider dv(scale);
+                uint32_t pk[8];
+#pragma unroll
+                for (int i = 0; i < 32; i += 4) {
+                    float a = acc[i], b = acc[i + 1], c = acc[i + 2], d = acc[i + 3];
+                    dv.quant2(a, b);
+                    dv.quant2(c, d);
+                    pk[i >> 2] = (uint32_t)fp8x2(a, b) | ((uint32_t)fp8x2(c, d) << 16);
+                }
+                if (valid) {
+                    const int j = tile % num_n;
+                    uint8_t* dst = reinterpret_cast<uint8_t*>(out) + (int64_t)m * (N / 2) +
+                                   j * 128 + col0;
+                    *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    *reinterpret_cast<uint4*>(dst + 16) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                    if (col0 == 0) q_scale[(int64_t)j * q_scale_ld + m] = scale;
+                }
+            } else if constexpr (TSTORE) {
                 // this warp's 32 rows x 64 columns, row r's 16-byte chunk j at
                 // r * 128 + (j ^ r % 8) * 16: the 128-byte swizzle of map_c,
                 // and conflict-free for one row per lane
@@ -415,21 +504,24 @@ int make_out_map(CUtensorMap* map, void* base, int64_t rows, int64_t n) {
     return QB_OK;
 }
 
-template <int BN, int NST = MAX_STAGES, bool TSTORE = false>
+// SILU: n = 2 * inter weight rows, out fp8 [m, inter], q_scale [inter / 128, q_scale_ld]
+template <int BN, int NST = MAX_STAGES, bool TSTORE = false, bool SILU = false>
 int launch(const void* a, const float* a_scale, int64_t a_scale_ld, const void* w,
-           const float* w_scale, void* out, int64_t m, int64_t n, int64_t k, cudaStream_t stream) {
-    using C = Cfg<BN, NST, TSTORE>;
+           const float* w_scale, void* out, int64_t m, int64_t n, int64_t k, cudaStream_t stream,
+           float* q_scale = nullptr, int64_t q_scale_ld = 0) {
+    using C = Cfg<BN, NST, TSTORE, SILU>;
+    using OutT = typename std::conditional<SILU, uint8_t, bf16>::type;
     CUtensorMap map_a, map_b, map_c;
     memset(&map_c, 0, sizeof(map_c));
     int st = make_map(&map_a, a, m, k, BM);
     if (st) return st;
-    st = make_map(&map_b, w, n, k, BN);
+    st = make_map(&map_b, w, n, k, SILU ? 128 : BN);
     if (st) return st;
     if (TSTORE) {
         st = make_out_map(&map_c, out, m, n);
         if (st) return st;
     }
-    auto kernel = gemm_fp8_bs_kernel<BN, bf16, NST, TSTORE>;
+    auto kernel = gemm_fp8_bs_kernel<BN, OutT, NST, TSTORE, SILU>;
     static bool attr[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -444,9 +536,9 @@ int launch(const void* a, const float* a_scale, int64_t a_scale_ld, const void* 
     const int64_t tiles = ((m + BM - 1) / BM) * (n / BN);
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
     kernel<<<grid, NUM_THREADS, C::SMEM, stream>>>(map_a, map_b, map_c, a_scale, a_scale_ld,
-                                                   w_scale, (bf16*)out, (int)m, (int)n, (int)k,
-                                                   status);
-    return launch_status("qb_gemm_fp8_bs");
+                                                   w_scale, (OutT*)out, q_scale, q_scale_ld,
+                                                   (int)m, (int)n, (int)k, status);
+    return launch_status(SILU ? "qb_gemm_fp8_silu_quant" : "qb_gemm_fp8_bs");
 }
 
 }  // namespace
@@ -472,4 +564,25 @@ extern "C" int qb_gemm_fp8_bs(const void* a, const float* a_scale, int64_t a_sca
     if (n % 256 == 0)
         return launch<256, 3, true>(a, a_scale, a_scale_ld, w, w_scale, out, m, n, k, s);
     return launch<128, 4, false>(a, a_scale, a_scale_ld, w, w_scale, out, m, n, k, s);
+}
+
+extern "C" int qb_gemm_fp8_silu_quant(const void* a, const float* a_scale, int64_t a_scale_ld,
+                                      const void* w, const float* w_scale, void* q_out,
+                                      float* scale_out, int64_t scale_ld, int64_t m,
+                                      int64_t inter, int64_t k, void* stream) {
+    if (m < 0 || inter <= 0 || k <= 0) return invalid("qb_gemm_fp8_silu_quant: bad sizes");
+    if (k % BK != 0) return invalid("qb_gemm_fp8_silu_quant: k must be a multiple of 128");
+    if (inter % 128 != 0)
+        return invalid("qb_gemm_fp8_silu_quant: inter must be a multiple of 128");
+    if (m > 0x7fffffffLL || 2 * inter > 0x7fffffffLL || k > 0x7fffffffLL)
+        return invalid("qb_gemm_fp8_silu_quant: sizes exceed int32");
+    if (a_scale_ld < m) return invalid("qb_gemm_fp8_silu_quant: a_scale_ld < m");
+    if (scale_ld < m) return invalid("qb_gemm_fp8_silu_quant: scale_ld < m");
+    if (!aligned(a, 16) || !aligned(w, 16) || !aligned(q_out, 16))
+        return invalid("qb_gemm_fp8_silu_quant: a, w and q_out must be 16-byte aligned");
+    if (!a_scale || !w_scale || !scale_out)
+        return invalid("qb_gemm_fp8_silu_quant: NULL scales");
+    if (m == 0) return QB_OK;
+    return launch<256, 4, false, true>(a, a_scale, a_scale_ld, w, w_scale, q_out, m, 2 * inter,
+                                       k, (cudaStream_t)stream, scale_out, scale_ld);
 }

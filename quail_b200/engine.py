@@ -107,6 +107,29 @@ class Engine:
             self.gemm_events.append((start, end, 2.0 * m * n * k, nbytes))
         return out
 
+    def gemm_silu_quant(self, x: QuantRows, weight, weight_scale):
+        """activation_quant(gemm(x, gate_up)) in one kernel: the quantised
+        silu(gate) * up, without the bf16 gate_up intermediate."""
+        t = self.torch
+        m, k = x.q.shape
+        inter = weight.shape[0] // 2
+        out = self._quant_buffers(m, inter)
+        timed = self.gemm_events is not None
+        if timed:
+            start, end = t.cuda.Event(enable_timing=True), t.cuda.Event(enable_timing=True)
+            start.record()
+        nat.call("qb_gemm_fp8_silu_quant", nat.ptr(x.q), nat.ptr(x.scale), x.ld,
+                 nat.ptr(weight), nat.ptr(weight_scale), nat.ptr(out.q), nat.ptr(out.scale),
+                 out.ld, m, inter, k, self._stream())
+        if timed:
+            end.record()
+            n = 2 * inter
+            # A and W once, the fp8 product and its scales once, both input scales
+            nbytes = (m * k + n * k + m * inter + 4 * m * (inter // 128)
+                      + 4 * (m * (k // 128) + (n // 128) * (k // 128)))
+            self.gemm_events.append((start, end, 2.0 * m * n * k, nbytes))
+        return out
+
     # ---- rotary + KV append -------------------------------------------------
 
     def kv_row_map(self, kv_src, kv_dst, rows):

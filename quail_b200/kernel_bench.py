@@ -13,6 +13,8 @@ a profiler capture of one kernel runs on.
 
 Ops:
   gemm       qb_gemm_fp8_bs on (m, n, k); default the 4B qkv projection
+  gate_up    qb_gemm_fp8_silu_quant on (m, inter, hidden) beside the unfused
+             qb_gemm_fp8_bs (n = 2 inter) + qb_silu_mul_quant pair
   layer      the four GEMMs of one 4B layer back to back (m rows)
   silu       qb_silu_mul_quant on (rows, inter)
   norm       qb_add_rmsnorm_quant on (rows, hidden)
@@ -85,6 +87,30 @@ def op_gemm(torch, args):
     flops = 2.0 * m * n * k
     return {"shape": [m, n, k], "ms": ms, "tflops": flops / ms / 1e9, "bound": "tensor",
             "algorithmic": flops}
+
+
+def op_gate_up(torch, args):
+    m, inter, k = args.m, args.inter, args.hidden
+    a, a_s = fp8_rows(torch, m, k)
+    w, w_s = fp8_weight(torch, 2 * inter, k)
+    q = torch.empty(m, inter, dtype=torch.float8_e4m3fn, device="cuda")
+    s = torch.empty(inter // 128, m, dtype=torch.float32, device="cuda")
+    gu = torch.empty(m, 2 * inter, dtype=torch.bfloat16, device="cuda")
+
+    def fused():
+        nat.call("qb_gemm_fp8_silu_quant", nat.ptr(a), nat.ptr(a_s), m, nat.ptr(w),
+                 nat.ptr(w_s), nat.ptr(q), nat.ptr(s), m, m, inter, k, nat.stream_handle(torch))
+
+    def unfused():
+        nat.call("qb_gemm_fp8_bs", nat.ptr(a), nat.ptr(a_s), m, nat.ptr(w), nat.ptr(w_s),
+                 nat.ptr(gu), m, 2 * inter, k, nat.stream_handle(torch))
+        nat.call("qb_silu_mul_quant", nat.ptr(gu), m, inter, nat.ptr(q), nat.ptr(s), m,
+                 nat.stream_handle(torch))
+    ms = time_launches(torch, fused, args.warmup, args.iters)
+    ms_unfused = time_launches(torch, unfused, args.warmup, args.iters)
+    flops = 2.0 * m * 2 * inter * k
+    return {"shape": [m, inter, k], "ms": ms, "tflops": flops / ms / 1e9, "bound": "tensor",
+            "algorithmic": flops, "ms_unfused": ms_unfused}
 
 
 def op_layer(torch, args):
@@ -230,7 +256,8 @@ def op_attention(torch, args):
 
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    p.add_argument("op", choices=["gemm", "layer", "silu", "norm", "rope", "attention"])
+    p.add_argument("op", choices=["gemm", "gate_up", "layer", "silu", "norm", "rope",
+                                  "attention"])
     p.add_argument("--m", type=int, default=65536)
     p.add_argument("--n", type=int, default=6144)
     p.add_argument("--k", type=int, default=2560)

@@ -92,10 +92,12 @@ class Qwen3Pipeline(ModelPipeline):
                               (index, "o", hidden), (index, "residual_mid_in",
                                                      residual.clone())])
             x = eng.norm_quant(hidden, layer.post_ln, residual)
-            gate_up = eng.gemm(x, layer.gate_up_w, layer.gate_up_s)
-            x2 = eng.activation_quant(gate_up)
+            # gate_up GEMM + SiLU quantisation in one kernel
+            x2 = eng.gemm_silu_quant(x, layer.gate_up_w, layer.gate_up_s)
             hidden = eng.gemm(x2, layer.down_w, layer.down_s)
             if trace is not None:
+                # the bf16 gate_up the fused kernel never writes, for the trace
+                gate_up = eng.gemm(x, layer.gate_up_w, layer.gate_up_s)
                 trace.extend([(index, "g_in", x), (index, "gate_up", gate_up),
                               (index, "d_in", x2), (index, "down", hidden)])
         return eng.final_norm(hidden, residual, chunk.final_indices, w.final_norm)

@@ -134,6 +134,29 @@ def test_gemm_fp8_block_scaled(dev, m, n, k):
     assert_status_clean()
 
 
+@pytest.mark.parametrize("m,inter,k,oracle", [(1, 128, 256, True), (7, 384, 512, True),
+                                              (300, 1024, 2560, True), (257, 9728, 2560, False),
+                                              (4096 + 5, 2048, 256, False)])
+def test_gemm_silu_quant(dev, m, inter, k, oracle):
+    """gate_up GEMM + SiLU quantisation in one kernel: the same fp8 codes and
+    scales as the bf16 GEMM followed by qb_silu_mul_quant (and the oracle)."""
+    g = torch.Generator().manual_seed(m + inter + k)
+    aq, as_, wq, ws = _fp8_operands(g, m, 2 * inter, k)
+    eng = engine_for(TINY)
+    x = QuantRows(aq.to(dev), as_.to(dev).contiguous(), m)
+    out = eng.gemm_silu_quant(x, wq.to(dev), ws.to(dev))
+    torch.cuda.synchronize()
+    assert_status_clean()
+    if oracle:
+        q_ref, s_ref = nx.silu_mul_quant(nx.gemm_fp8_bs(aq, as_, wq, ws))
+        assert_bits_equal(out.scale[:, :m], s_ref, "scales")
+        assert_bits_equal(out.q, q_ref, "fp8 codes")
+    if inter % 256 == 0:
+        ref = eng.activation_quant(eng.gemm(x, wq.to(dev), ws.to(dev)))
+        assert_bits_equal(out.scale[:, :m], ref.scale[:, :m], "scales vs unfused")
+        assert_bits_equal(out.q, ref.q, "fp8 codes vs unfused")
+
+
 def test_gemm_large_against_dequantised_matmul(dev):
     """A full 4B QKV-shaped GEMM against fp32 torch on the dequantised operands."""
     g = torch.Generator(device="cuda").manual_seed(5)

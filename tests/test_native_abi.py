@@ -52,6 +52,19 @@ def test_invalid_gemm_shapes_are_rejected_before_launch(lib):
                  unaligned, 8, 256, 256, None)
 
 
+def test_invalid_fused_silu_gemm_calls_are_rejected(lib):
+    with pytest.raises(ValueError, match="inter must be a multiple of 128"):
+        nat.call("qb_gemm_fp8_silu_quant", None, None, 8, None, None, None, None, 8, 8, 100,
+                 256, None)
+    with pytest.raises(ValueError, match="scale_ld"):
+        nat.call("qb_gemm_fp8_silu_quant", None, None, 8, None, None, None, None, 4, 8, 128,
+                 256, None)
+    unaligned = ctypes.c_void_p(0x1001)
+    with pytest.raises(ValueError, match="aligned"):
+        nat.call("qb_gemm_fp8_silu_quant", unaligned, unaligned, 8, unaligned, unaligned,
+                 unaligned, unaligned, 8, 8, 128, 256, None)
+
+
 def test_invalid_attention_and_norm_calls_are_rejected(lib):
     with pytest.raises(ValueError, match="head_dim"):
         nat.call("qb_tree_attention", None, None, None, 4, 4, 2, 64, None, 1, None, 1,
