@@ -66,8 +66,16 @@ __device__ __forceinline__ float bf16_round(float x) {
 // The reference quantiser (per_token_group_quant_fp8 and the fused Triton
 // kernels): scale = max(amax, 1e-10) / 448; q = clamp(y / scale, +-448),
 // rounded to nearest even e4m3.
+// The division by 448 is Markstein's correction with r = RN(1/448)
+// (q0 = RN(a r), e = a - 448 q0 exact by FMA, q = RN(q0 + e r)): the
+// correctly rounded quotient for every a in [1e-10, inf] (checked against
+// __fdiv_rn on all of them).
 __device__ __forceinline__ float group_scale(float amax) {
-    return fmaxf(amax, 1e-10f) / QB_FP8_MAX;
+    const float a = fmaxf(amax, 1e-10f);
+    constexpr float r = 1.0f / QB_FP8_MAX;
+    const float q0 = __fmul_rn(a, r);
+    const float e = __fmaf_rn(-QB_FP8_MAX, q0, a);
+    return a < INFINITY ? __fmaf_rn(e, r, q0) : q0;  // inf: e would be NaN
 }
 
 // y / scale for many y of one group: the correctly rounded quotient from
@@ -88,7 +96,8 @@ struct GroupDivider {
     }
     __device__ __forceinline__ float div(float y) const {
         const float a = fabsf(y);
-        if (!(a >= 0x1p-96f && a < 0x1p+100f)) return div_slow(y, s);
+        // (an infinite scale has r = 0, and the residual would be NaN)
+        if (!(a >= 0x1p-96f && a < 0x1p+100f && s < INFINITY)) return div_slow(y, s);
         const float q0 = __fmul_rn(y, r);
         const float e = __fmaf_rn(-s, q0, y);
         return __fmaf_rn(e, r, q0);
@@ -102,6 +111,13 @@ struct GroupDivider {
     // [2^-96, 2^100) in magnitude (or not finite), which sets *rare; the
     // caller then redoes the values with quant2
     __device__ __forceinline__ void quant2_fast(float& a, float& b, bool& rare) const;
+    // quant2 for the saturating e4m3 conversion, which clamps a finite
+    // quotient to +-448 as quant2 does: RN(y / s) without the clamp. Exact
+    // for |y| in [2^-96, 2^100); *rare is set for |y| < 2^-96 (zeros too: the
+    // residual step would turn -0 into +0) and NaN. The caller checks the
+    // upper bound once on the group max (!(amax < 2^100)) and redoes rare
+    // values with quant2.
+    __device__ __forceinline__ void quant2_sat(float& a, float& b, bool& rare) const;
 };
 
 // two floats -> two e4m3 bytes (low byte = first value)
@@ -176,7 +192,7 @@ __device__ __forceinline__ float exp2_finish(float p, float t) {
 
 __device__ __forceinline__ void GroupDivider::quant2(float& a, float& b) const {
     const float fa = fabsf(a), fb = fabsf(b);
-    if (fa >= 0x1p-96f && fa < 0x1p+100f && fb >= 0x1p-96f && fb < 0x1p+100f) {
+    if (fa >= 0x1p-96f && fa < 0x1p+100f && fb >= 0x1p-96f && fb < 0x1p+100f && s < INFINITY) {
         const uint64_t y = f2pack(a, b), rr = f2pack(r, r);
         const uint64_t q0 = f2mul(y, rr);
         const uint64_t e = f2fma(f2pack(-s, -s), q0, y);
@@ -191,13 +207,36 @@ __device__ __forceinline__ void GroupDivider::quant2(float& a, float& b) const {
 
 __device__ __forceinline__ void GroupDivider::quant2_fast(float& a, float& b, bool& rare) const {
     const float fa = fabsf(a), fb = fabsf(b);
-    rare |= !(fa >= 0x1p-96f && fa < 0x1p+100f && fb >= 0x1p-96f && fb < 0x1p+100f);
+    rare |= !(fa >= 0x1p-96f && fa < 0x1p+100f && fb >= 0x1p-96f && fb < 0x1p+100f &&
+              s < INFINITY);
     const uint64_t y = f2pack(a, b), rr = f2pack(r, r);
     const uint64_t q0 = f2mul(y, rr);
     const uint64_t e = f2fma(f2pack(-s, -s), q0, y);
     f2unpack(f2fma(e, rr, q0), a, b);
     a = fminf(fmaxf(a, -QB_FP8_MAX), QB_FP8_MAX);
     b = fminf(fmaxf(b, -QB_FP8_MAX), QB_FP8_MAX);
+}
+
+__device__ __forceinline__ void GroupDivider::quant2_sat(float& a, float& b, bool& rare) const {
+    rare |= !(fabsf(a) >= 0x1p-96f) | !(fabsf(b) >= 0x1p-96f);
+    const uint64_t y = f2pack(a, b), rr = f2pack(r, r);
+    const uint64_t q0 = f2mul(y, rr);
+    const uint64_t e = f2fma(f2pack(-s, -s), q0, y);
+    f2unpack(f2fma(e, rr, q0), a, b);
+}
+
+// 1 / d, correctly rounded, for two d in [2^-126, 2^126) (normal d with a
+// normal reciprocal), by Markstein's correction of the hardware
+// approximation: r0 = rcp.approx(d), e = RN(1 - d r0) (exact by FMA),
+// r = RN(r0 + e r0). Equal to __frcp_rn on every float of that range
+// (exhaustive check on the B200).
+__device__ __forceinline__ void rcp_rn_normal_x2(float& a, float& b) {
+    float ra, rb;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(ra) : "f"(a));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(rb) : "f"(b));
+    const uint64_t r = f2pack(ra, rb);
+    const uint64_t e = f2fma(f2pack(-a, -b), r, f2pack(1.0f, 1.0f));
+    f2unpack(f2fma(e, r, r), a, b);
 }
 
 // 2^f on [-1/2, 1/2]: Taylor coefficients (ln 2)^k / k!, k = 7 .. 0, Horner
@@ -323,6 +362,37 @@ __device__ __forceinline__ void sigmoidf_ref_x2(float& a, float& b) {
     f2unpack(f2add(f2pack(1.0f, 1.0f), f2pack(ea, eb)), ea, eb);
     a = __frcp_rn(ea);
     b = __frcp_rn(eb);
+}
+
+// sigmoidf_ref_x2, branch-free: the same bits unless *rare is set, for
+// x = -g log2(e) above 125 (1 + 2^x reaches 2^125.5: the reciprocal leaves
+// rcp_rn_normal_x2's range) or NaN; the caller then redoes the pair with
+// sigmoidf_ref_x2. Below, x is clamped at -127 instead of -150: n = rint(x)
+// = -127 gives the scale bits 0, so 2^x becomes 0 there, and any 2^x under
+// 2^-24 leaves 1 + 2^x = 1 exactly as qexp2f's value would.
+__device__ __forceinline__ void sigmoidf_ref_x2_fast(float& a, float& b, bool& rare) {
+    float xa, xb;
+    f2unpack(f2mul(f2pack(a, b), f2pack(-1.44269504088896341f, -1.44269504088896341f)), xa, xb);
+    rare |= !(xa <= 125.0f) | !(xb <= 125.0f);
+    const uint64_t M = f2pack(12582912.0f, 12582912.0f);
+    const uint64_t x = f2pack(fmaxf(xa, -127.0f), fmaxf(xb, -127.0f));
+    const uint64_t t = f2add(x, M);
+    const uint64_t f = f2sub(x, f2sub(t, M));
+    uint64_t p = f2pack(QB_EXP2_C7, QB_EXP2_C7);
+#define QB_STEP5(c) p = f2fma(p, f, f2pack(c, c));
+    QB_EXP2_POLY(QB_STEP5)
+#undef QB_STEP5
+    float ta, tb;
+    f2unpack(t, ta, tb);
+    // 2^n: bits (n + 127) << 23, n = bits(t) - 0x4B400000, in one shift-add
+    constexpr uint32_t K = (127u - 0x4B400000u) << 23;
+    const uint64_t e = f2mul(p, f2pack(__uint_as_float((__float_as_uint(ta) << 23) + K),
+                                       __uint_as_float((__float_as_uint(tb) << 23) + K)));
+    float da, db;
+    f2unpack(f2add(f2pack(1.0f, 1.0f), e), da, db);
+    rcp_rn_normal_x2(da, db);
+    a = da;
+    b = db;
 }
 
 // ln x for normal positive x

@@ -379,7 +379,13 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                     const bf162 u2 = __floats2bfloat162_rn(acc[32 + i], acc[33 + i]);
                     const float g0 = __low2float(g2), g1 = __high2float(g2);
                     float sa = g0, sb = g1;
-                    sigmoidf_ref_x2(sa, sb);
+                    bool rare = false;
+                    sigmoidf_ref_x2_fast(sa, sb, rare);
+                    if (rare) {  // g below about -86 or NaN: the exact path
+                        sa = g0;
+                        sb = g1;
+                        sigmoidf_ref_x2(sa, sb);
+                    }
                     const uint64_t gs = f2mul(f2pack(g0, g1), f2pack(sa, sb));
                     f2unpack(f2mul(gs, f2pack(__low2float(u2), __high2float(u2))), acc[i],
                              acc[i + 1]);
@@ -400,12 +406,22 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                              fmaxf(red[2 * BM + row_in_tile], red[3 * BM + row_in_tile]));
                 const float scale = group_scale(amax);
                 const GroupDivider dv(scale);
+                const bool big = !(amax < 0x1p+100f);
                 uint32_t pk[8];
 #pragma unroll
                 for (int i = 0; i < 32; i += 4) {
                     float a = acc[i], b = acc[i + 1], c = acc[i + 2], d = acc[i + 3];
-                    dv.quant2(a, b);
-                    dv.quant2(c, d);
+                    bool rare = big;
+                    dv.quant2_sat(a, b, rare);
+                    dv.quant2_sat(c, d, rare);
+                    if (rare) {  // a zero, tiny or non-finite value: the exact path
+                        a = acc[i];
+                        b = acc[i + 1];
+                        c = acc[i + 2];
+                        d = acc[i + 3];
+                        dv.quant2(a, b);
+                        dv.quant2(c, d);
+                    }
                     pk[i >> 2] = (uint32_t)fp8x2(a, b) | ((uint32_t)fp8x2(c, d) << 16);
                 }
                 if (valid) {

@@ -24,14 +24,26 @@ __device__ __forceinline__ void quant_store8(const float* y, uint8_t* q_row, flo
     amax = group_amax(amax);
     const float scale = group_scale(amax);
     const GroupDivider dv(scale);
+    float q[8];
+    bool rare = !(amax < 0x1p+100f);
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        q[i] = y[i];
+        q[i + 1] = y[i + 1];
+        dv.quant2_sat(q[i], q[i + 1], rare);
+    }
+    if (rare) {  // a zero, tiny or non-finite value: the exact path
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+            q[i] = y[i];
+            q[i + 1] = y[i + 1];
+            dv.quant2(q[i], q[i + 1]);
+        }
+    }
     uint2 packed;
     uint16_t* p = reinterpret_cast<uint16_t*>(&packed);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        float a = y[2 * i], b = y[2 * i + 1];
-        dv.quant2(a, b);
-        p[i] = fp8x2(a, b);
-    }
+    for (int i = 0; i < 4; ++i) p[i] = fp8x2(q[2 * i], q[2 * i + 1]);
     *reinterpret_cast<uint2*>(q_row + col8 * 8) = packed;
     if ((threadIdx.x & 15) == 0) scale_out[(int64_t)(col8 / 16) * scale_ld + row] = scale;
 }
@@ -104,15 +116,28 @@ __global__ void silu_mul_quant_kernel(const bf16* __restrict__ gate_up, int64_t 
     const int64_t row = warp / per_row;
     const int col8 = (int)(warp % per_row) * 32 + lane;  // 8-column vector index
     const bf16* base = gate_up + row * (int64_t)(2 * inter);
-    float g[8], u[8], y[8];
+    float g[8], u[8], sg[8], y[8];
     bf16x8_to_float(*reinterpret_cast<const uint4*>(base + col8 * 8), g);
     bf16x8_to_float(*reinterpret_cast<const uint4*>(base + inter + col8 * 8), u);
+    bool rare = false;
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        sg[i] = g[i];
+        sg[i + 1] = g[i + 1];
+        sigmoidf_ref_x2_fast(sg[i], sg[i + 1], rare);
+    }
+    if (rare) {  // g below about -86 or NaN: the exact path
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+            sg[i] = g[i];
+            sg[i + 1] = g[i + 1];
+            sigmoidf_ref_x2(sg[i], sg[i + 1]);
+        }
+    }
 #pragma unroll
     for (int i = 0; i < 8; i += 2) {
         // y = (g * sigmoid(g)) * u, two lanes per instruction
-        float sa = g[i], sb = g[i + 1];
-        sigmoidf_ref_x2(sa, sb);
-        const uint64_t gs = f2mul(f2pack(g[i], g[i + 1]), f2pack(sa, sb));
+        const uint64_t gs = f2mul(f2pack(g[i], g[i + 1]), f2pack(sg[i], sg[i + 1]));
         f2unpack(f2mul(gs, f2pack(u[i], u[i + 1])), y[i], y[i + 1]);
     }
     quant_store8(y, q_out + row * inter, scale_out, scale_ld, row, col8);
