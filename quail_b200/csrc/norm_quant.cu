@@ -48,8 +48,10 @@ __device__ __forceinline__ void quant_store8(const float* y, uint8_t* q_row, flo
     if ((threadIdx.x & 15) == 0) scale_out[(int64_t)(col8 / 16) * scale_ld + row] = scale;
 }
 
-// blockDim.x == hidden / 8; one row per block.
-__global__ void embed_rmsnorm_quant_kernel(const int64_t* __restrict__ ids,
+// blockDim.x == hidden / 8; one row per block. 32 registers (the bound
+// allows 2 x 1024 threads) keep six 320-thread blocks resident per SM for the
+// 4B hidden size: the memory parallelism this HBM-bound kernel lives on.
+__global__ void __launch_bounds__(1024, 2) embed_rmsnorm_quant_kernel(const int64_t* __restrict__ ids,
                                            const bf16* __restrict__ embed, int64_t vocab,
                                            int hidden, const bf16* __restrict__ w, float eps,
                                            bf16* __restrict__ residual_out,
@@ -79,8 +81,8 @@ __global__ void embed_rmsnorm_quant_kernel(const int64_t* __restrict__ ids,
     quant_store8(y, q_out + row * hidden, scale_out, scale_ld, row, t);
 }
 
-// blockDim.x == hidden / 8; one row per block.
-__global__ void add_rmsnorm_quant_kernel(const bf16* __restrict__ hidden_in,
+// blockDim.x == hidden / 8; one row per block; 32 registers as above.
+__global__ void __launch_bounds__(1024, 2) add_rmsnorm_quant_kernel(const bf16* __restrict__ hidden_in,
                                          bf16* __restrict__ residual,
                                          const bf16* __restrict__ w, float eps, int hidden,
                                          uint8_t* __restrict__ q_out,
