@@ -45,11 +45,12 @@ METRIC = "AI.IF rows/sec (Qwen3-4B FP8 filter, config 1)"
 UNIT = "rows/s"
 
 
-# DRAM bytes (read + write) per qb_gemm_fp8_bs launch, averaged over the 144
-# launches of one config-1 chunk (qkv, o, gate_up, down x 36 layers), from the
-# ncu launch list in profiles/launch_list_config1.md (dram__bytes_read.sum +
+# DRAM bytes (read + write) per GEMM launch, averaged over the 144 launches
+# of one config-1 chunk (qkv, o, down: qb_gemm_fp8_bs; gate_up:
+# qb_gemm_fp8_silu_quant; x 36 layers), from the ncu launch list in
+# profiles/launch_list_config1.md (dram__bytes_read.sum +
 # dram__bytes_write.sum, one pass, same workload as this bench)
-GEMM_DRAM_BYTES_PER_LAUNCH = 2.635e9
+GEMM_DRAM_BYTES_PER_LAUNCH = 1.6245e9
 GEMM_TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/launch_list_config1.md"
 
 
@@ -405,7 +406,8 @@ def main():
                        "prefill_tokens_per_s": tokens_all / (ms / 1000.0),
                        "l2": "inputs larger than L2 (>=0.5 GB activations per chunk)",
                        "status_word": status},
-            "roofline": {"bound": "tensor", "kernel": "qb_gemm_fp8_bs",
+            "roofline": {"bound": "tensor",
+                         "kernel": "qb_gemm_fp8_bs + qb_gemm_fp8_silu_quant (all GEMMs)",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak if peak else None,
                          "traffic": GEMM_DRAM_BYTES_PER_LAUNCH,
