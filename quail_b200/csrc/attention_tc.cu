@@ -45,7 +45,8 @@ using namespace qb::tc;
 constexpr int D = 128;
 constexpr int QR = 64;  // query rows per block
 constexpr int KT = 64;  // keys per tile
-constexpr int NST = 2;  // K/V stages
+constexpr int KST = 3;  // K stages: a K tile is free once its S MMAs are done
+constexpr int VST = 2;  // V stages: a V tile is free once its P V MMAs are done
 constexpr int MAX_CALLS = QR + 1;
 constexpr int FIRST_SOFT = 2, FIRST_CORR = 10;
 constexpr int NUM_THREADS = 14 * 32;
@@ -53,10 +54,10 @@ constexpr int NUM_THREADS = 14 * 32;
 constexpr int Q_BYTES = 2 * 2 * 128 * 128;  // [mt][half][128 rows][128 B]
 constexpr int KV_HALF = 64 * 128;           // [64 keys][64 dims]
 constexpr int KV_TILE = 2 * KV_HALF;        // K or V: two 64-dim halves
-constexpr int STAGE_BYTES = 2 * KV_TILE;    // K then V
 constexpr int P_TILE = 128 * 128;           // [128 rows][64 keys]
-constexpr int OFF_KV = Q_BYTES;
-constexpr int OFF_P = OFF_KV + NST * STAGE_BYTES;
+constexpr int OFF_K = Q_BYTES;
+constexpr int OFF_V = OFF_K + KST * KV_TILE;
+constexpr int OFF_P = OFF_V + VST * KV_TILE;
 constexpr int OFF_AUX = OFF_P + 4 * P_TILE;  // P: [buffer 2][mt 2]
 
 constexpr uint32_t TM_O = 0, TM_S = 256, TM_OB = 384;
@@ -85,7 +86,7 @@ struct Info {
 struct Aux {
     uint64_t q_full, q_empty;
     uint64_t info_full[2], info_empty[2];
-    uint64_t kv_full[NST], kv_empty[NST];
+    uint64_t k_full[KST], k_empty[KST], v_full[VST], v_empty[VST];
     uint64_t s_full[2], s_empty[2], o_ready[2];
     // per P buffer (tile parity) and M tile; phase = tile / 2, so a producer
     // can only complete a buffer's next phase after every waiter observed
@@ -178,9 +179,13 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             // correction warps
             mbar_init(&aux->info_empty[b], 1 + 4 * nmt + 4);
         }
-        for (int st = 0; st < NST; ++st) {
-            mbar_init(&aux->kv_full[st], 1);
-            mbar_init(&aux->kv_empty[st], 1);
+        for (int st = 0; st < KST; ++st) {
+            mbar_init(&aux->k_full[st], 1);
+            mbar_init(&aux->k_empty[st], 1);
+        }
+        for (int st = 0; st < VST; ++st) {
+            mbar_init(&aux->v_full[st], 1);
+            mbar_init(&aux->v_empty[st], 1);
         }
         for (int m = 0; m < 2; ++m) {
             mbar_init(&aux->s_full[m], 1);
@@ -208,7 +213,8 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
 
     if (warp == 0) {
         // ---------------- loader: item info, Q, K and V tiles ----------------
-        int g = 0, jq = 0;  // tiles loaded, Q loads issued
+        int g = 0, jq = 0;    // tiles loaded, Q loads issued
+        int nk = 0, nv = 0;   // K and V tiles whose loads were issued
         bool ok = true;
         for (int item = blockIdx.x, k = 0; item < n_items && ok; item += gridDim.x, ++k) {
             const int slot = k & 1;
@@ -313,53 +319,62 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                 for (int c = 0; c < nc && ok; ++c) {
                     const Call cl = inf->calls[c];
                     for (int t = 0; t < cl.n_tiles; ++t, ++g) {
-                        const int st = g % NST;
-                        if (!mbar_wait(&aux->kv_empty[st], ((uint32_t)(g / NST) & 1u) ^ 1u,
-                                       abort_flag, status, STATUS_ATTN_LOAD)) {
-                            ok = false;
-                            break;
-                        }
-                        uint8_t* kd = smem + OFF_KV + st * STAGE_BYTES;
-                        uint8_t* vd = kd + KV_TILE;
-                        mbar_arrive_expect_tx(&aux->kv_full[st], STAGE_BYTES);
+                        // K, then V: K may run KST tiles ahead of the S MMAs,
+                        // V VST tiles ahead of the P V MMAs
                         const int j0 = t * KT;
-                        if (cl.kind == CALL_OWN) {
-                            const int y = seg_start + j0;
-                            for (int half = 0; half < 2; ++half) {
-                                tma_load_2d(smem_u32(kd + half * KV_HALF), &map_k,
-                                            hk * D + half * 64, y, &aux->kv_full[st]);
-                                tma_load_2d(smem_u32(vd + half * KV_HALF), &map_v,
-                                            hk * D + half * 64, y, &aux->kv_full[st]);
+                        const int32_t* trow =
+                            cl.kind == CALL_OWN
+                                ? nullptr
+                                : read_table +
+                                      (int64_t)(cl.kind == CALL_UNIFIED ? seg : cl.group) * table_width;
+                        for (int kv = 0; kv < 2 && ok; ++kv) {
+                            const int n = kv == 0 ? nk : nv;
+                            const int nst = kv == 0 ? KST : VST;
+                            const int st = n % nst;
+                            uint64_t* full = kv == 0 ? &aux->k_full[st] : &aux->v_full[st];
+                            uint64_t* empty = kv == 0 ? &aux->k_empty[st] : &aux->v_empty[st];
+                            if (!mbar_wait(empty, ((uint32_t)(n / nst) & 1u) ^ 1u, abort_flag,
+                                           status, STATUS_ATTN_LOAD)) {
+                                ok = false;
+                                break;
                             }
-                        } else {
-                            const int32_t* trow =
-                                read_table +
-                                (int64_t)(cl.kind == CALL_UNIFIED ? seg : cl.group) * table_width;
-                            for (int pg = 0; pg < KT / page_tokens; ++pg) {
-                                const int key = j0 + pg * page_tokens;
-                                int64_t page = 0;  // keys past the last one: any valid page
-                                if (key < cl.n_keys) {
-                                    page = trow[key / page_tokens];
-                                    if (page < 0 || page >= n_pages) {
-                                        atomicOr(status, STATUS_BAD_INDEX);
-                                        page = 0;
+                            uint8_t* dst = smem + (kv == 0 ? OFF_K : OFF_V) + st * KV_TILE;
+                            const CUtensorMap* own_map = kv == 0 ? &map_k : &map_v;
+                            const CUtensorMap* page_map = kv == 0 ? &map_kp : &map_vp;
+                            mbar_arrive_expect_tx(full, KV_TILE);
+                            if (cl.kind == CALL_OWN) {
+                                const int y = seg_start + j0;
+                                for (int half = 0; half < 2; ++half)
+                                    tma_load_2d(smem_u32(dst + half * KV_HALF), own_map,
+                                                hk * D + half * 64, y, full);
+                            } else {
+                                for (int pg = 0; pg < KT / page_tokens; ++pg) {
+                                    const int key = j0 + pg * page_tokens;
+                                    int64_t page = 0;  // keys past the last one: any valid page
+                                    if (key < cl.n_keys) {
+                                        page = trow[key / page_tokens];
+                                        if (page < 0 || page >= n_pages) {
+                                            atomicOr(status, STATUS_BAD_INDEX);
+                                            page = 0;
+                                        }
                                     }
-                                }
-                                const int y = (int)(page * page_tokens);
-                                const int off = pg * page_tokens * 128;
-                                for (int half = 0; half < 2; ++half) {
-                                    tma_load_2d(smem_u32(kd + half * KV_HALF + off), &map_kp,
-                                                hk * D + half * 64, y, &aux->kv_full[st]);
-                                    tma_load_2d(smem_u32(vd + half * KV_HALF + off), &map_vp,
-                                                hk * D + half * 64, y, &aux->kv_full[st]);
+                                    const int y = (int)(page * page_tokens);
+                                    const int off = pg * page_tokens * 128;
+                                    for (int half = 0; half < 2; ++half)
+                                        tma_load_2d(smem_u32(dst + half * KV_HALF + off), page_map,
+                                                    hk * D + half * 64, y, full);
                                 }
                             }
+                            if (kv == 0) ++nk; else ++nv;
                         }
+                        if (!ok) break;
                     }
                 }
             }
             ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
             g = __shfl_sync(0xffffffffu, g, 0);
+            nk = __shfl_sync(0xffffffffu, nk, 0);
+            nv = __shfl_sync(0xffffffffu, nv, 0);
             jq = __shfl_sync(0xffffffffu, jq, 0);
         }
         // no copy may still be landing when the block exits
@@ -367,10 +382,16 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             int flag = 0;
             if (jq > 0 && !mbar_try_wait(smem_u32(&aux->q_full), (uint32_t)(jq - 1) & 1u))
                 mbar_wait(&aux->q_full, (uint32_t)(jq - 1) & 1u, &flag, status, STATUS_ATTN_LOAD);
-            for (int j = (g > NST ? g - NST : 0); j < g; ++j) {
-                const int st = j % NST;
-                if (!mbar_try_wait(smem_u32(&aux->kv_full[st]), (uint32_t)(j / NST) & 1u))
-                    mbar_wait(&aux->kv_full[st], (uint32_t)(j / NST) & 1u, &flag, status,
+            for (int j = (nk > KST ? nk - KST : 0); j < nk; ++j) {
+                const int st = j % KST;
+                if (!mbar_try_wait(smem_u32(&aux->k_full[st]), (uint32_t)(j / KST) & 1u))
+                    mbar_wait(&aux->k_full[st], (uint32_t)(j / KST) & 1u, &flag, status,
+                              STATUS_ATTN_LOAD);
+            }
+            for (int j = (nv > VST ? nv - VST : 0); j < nv; ++j) {
+                const int st = j % VST;
+                if (!mbar_try_wait(smem_u32(&aux->v_full[st]), (uint32_t)(j / VST) & 1u))
+                    mbar_wait(&aux->v_full[st], (uint32_t)(j / VST) & 1u, &flag, status,
                               STATUS_ATTN_LOAD);
             }
         }
@@ -425,8 +446,8 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
         };
         auto s_issue = [&]() {
             const Info* inf = &aux->info[ks & 1];
-            const int st = gs % NST;
-            const uint32_t k_base = smem_u32(smem + OFF_KV + st * STAGE_BYTES);
+            const int st = gs % KST;
+            const uint32_t k_base = smem_u32(smem + OFF_K + st * KV_TILE);
             tc_fence_after();
             if (lane == 0) {
                 for (int mt = 0; mt < nmt; ++mt) {
@@ -436,6 +457,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                                     k_desc(k_base, kk), IDESC_S, kk > 0 ? 1u : 0u);
                     mma_commit(&aux->s_full[mt]);
                 }
+                mma_commit(&aux->k_empty[st]);  // the K tile is free once these are done
             }
             ++gs;
             ++ts;
@@ -454,7 +476,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             if (lane == 0) {
                 if (ts == 0 && cs == 0)  // the item's first S: its Q
                     r = mbar_try_wait(smem_u32(&aux->q_full), (uint32_t)jq & 1u);
-                if (r) r = mbar_try_wait(smem_u32(&aux->kv_full[gs % NST]), (uint32_t)(gs / NST) & 1u);
+                if (r) r = mbar_try_wait(smem_u32(&aux->k_full[gs % KST]), (uint32_t)(gs / KST) & 1u);
                 for (int mt = 0; mt < nmt && r && gs > 0; ++mt)
                     r = mbar_try_wait(smem_u32(&aux->s_empty[mt]), (uint32_t)(gs - 1) & 1u);
             }
@@ -463,7 +485,8 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
         auto pv_ready = [&](int g, int mt) -> bool {
             int r = 0;
             if (lane == 0)
-                r = mbar_try_wait(smem_u32(&aux->p_full[g & 1][mt]), (uint32_t)(g >> 1) & 1u) &&
+                r = mbar_try_wait(smem_u32(&aux->v_full[g % VST]), (uint32_t)(g / VST) & 1u) &&
+                    mbar_try_wait(smem_u32(&aux->p_full[g & 1][mt]), (uint32_t)(g >> 1) & 1u) &&
                     mbar_try_wait(smem_u32(&aux->o_ready[mt]), (uint32_t)g & 1u);
             return __shfl_sync(0xffffffffu, r, 0) != 0;
         };
@@ -491,8 +514,8 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             for (int c = 0; c < n_calls && ok; ++c) {
                 const Call cl = inf->calls[c];
                 for (int t = 0; t < cl.n_tiles; ++t, ++g) {
-                    const int st = g % NST;
-                    uint8_t* vd = smem + OFF_KV + st * STAGE_BYTES + KV_TILE;
+                    const int st = g % VST;
+                    uint8_t* vd = smem + OFF_V + st * KV_TILE;
                     const uint32_t v_base = smem_u32(vd);
                     bool pv_issued[2] = {nmt < 1, nmt < 2};
                     bool zeroed = false;
@@ -513,7 +536,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                             const int valid = cl.n_keys - t * KT;
                             if (!zeroed && cl.kind != CALL_OWN && valid < KT) {
                                 // the V rows past the last key: zeros (the tile
-                                // landed: this tile's S waited for it)
+                                // landed: pv_ready waited for it)
                                 const int first = valid < 0 ? 0 : valid;
                                 for (int idx = first * 8 + lane; idx < KT * 8; idx += 32) {
                                     const int r = idx >> 3, ch = idx & 7;
@@ -561,7 +584,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         }
                     }
                     if (!ok) break;
-                    if (lane == 0) mma_commit(&aux->kv_empty[st]);
+                    if (lane == 0) mma_commit(&aux->v_empty[st]);
                     __syncwarp();
                 }
             }
