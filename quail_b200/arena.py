@@ -205,6 +205,12 @@ class KVArena:
         self._set_rows(key)
         return pages
 
+    def growth_cost(self, key, capacity_tokens: int) -> int:
+        """Pages a resident key needs to grow to capacity (arena.py:772-786,
+        without the sliding pool)."""
+        return max(0, self.accounting.pages_needed(capacity_tokens)
+                   - len(self.accounting.table_pages(key)))
+
     def can_borrow(self, parent, shared: int) -> bool:
         return (parent in self.accounting.owned
                 and shared <= self.accounting.tokens[parent])

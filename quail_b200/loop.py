@@ -5,14 +5,16 @@ loop.py): ``pack_chunk`` lays out one forward pass's rows and attention
 bookkeeping (loop.py:219-577), ``FilterStream`` runs one chunk per
 ``next()`` and reads the previous chunk's answers while the new one runs
 (loop.py:1195-1532), and ``run_filter`` drives it to the end
-(loop.py:1535-1559). Page indices, scatter maps, block tables, reader
+(loop.py:1535-1559); ``run_join`` streams partner lists against anchors
+for AI joins and AI.SCORE (loop.py:609-978). Page indices, scatter maps, block tables, reader
 rows, the merge source map and the answer rows are bit-identical to the
 reference's for the same inputs.
 
 Packing happens on the host in numpy (``HostChunk``); ``HostChunk.upload``
 copies it to the device in one pinned transfer per array. Not built here:
-diffusion canvas rows, sliding-window pools, survivor retention and held
-survivors for joins (outside the AI.IF prefill path).
+diffusion canvas rows, sliding-window pools, survivor retention, held
+survivors and a streaming anchor source for joins (outside the AI.IF
+prefill path).
 """
 
 import time
@@ -20,7 +22,7 @@ from dataclasses import dataclass, field
 
 import numpy as np
 
-from quail_b200.pack import FilterAdmission
+from quail_b200.pack import FilterAdmission, JoinAdmission, partner_pages
 
 ATTENTION_PATHS = ("unified", "tree")
 ATTN_TILE = 64   # query rows per attention block
@@ -622,3 +624,196 @@ def run_filter(torch, arena, pipeline, async_ans, doc_ids, question_ids, budget,
         stats["h2d_bytes"] = stream.h2d_bytes
         stats["chunks"] = stream.chunks
     return stream.answers, stream.spans, stream.tokens
+
+
+def run_join(torch, arena, pipeline, async_ans, anchor_prefixes, stage_suffixes, budget,
+             stage_frames=None, anchor_keys=None, anchor_done=None, anchor_source=None,
+             anchor_partners=None, anchor_batch=None, attention_mode=None, prefix_tree=None,
+             stats=None, device="cuda", on_chunk=None):
+    """Stream partner lists against anchors, gating survivors between stages
+    (Quail's run_join, loop.py:609-978; arguments as there).
+
+    Each chunk packs anchors' prefixes (fresh anchors; a tree borrower only
+    past its shared tokens), the stage frame written after the anchor's
+    document rows (a frame entry, whose answer is skipped) and runs of
+    partner suffixes read against the anchor's kept KV. The readout's dtype
+    picks the answer rows: None for 0/1 lists (AI joins), float32 arrays for
+    AI.SCORE.
+
+    Returns:
+        (answers, spans, tokens): answers[j][a] is anchor a's row over the
+        stage-j partners it streams; spans (stage, start, end) CUDA events
+        per forward; tokens the fresh tokens packed.
+    """
+    if anchor_source is not None or anchor_batch is not None:
+        raise NotImplementedError("run_join: a streaming anchor source is not built here")
+    if tuple(getattr(pipeline, "canvas_ids", ()) or ()):
+        raise NotImplementedError("run_join: diffusion canvas rows are not built here")
+    k = len(stage_suffixes)
+    prefixes = list(anchor_prefixes)
+    keys = list(range(len(prefixes))) if anchor_keys is None else list(anchor_keys)
+    if len(keys) != len(prefixes):
+        raise ValueError("anchor_keys must match anchor_prefixes")
+    frames = stage_frames or [[] for _ in range(k)]
+    mode = attention_path(pipeline, attention_mode, default="tree")
+    if k == 0:
+        return [], [], 0
+    frame_max = max(len(f) for f in frames)
+
+    def entry_rows(a, j, start, end, carried):
+        rows = (len(prefixes[a]) if carried else 0) + sum(
+            len(stage_suffixes[j][i]) for i in sched.partner_indices(a, j, start, end))
+        if frames[j] and start == 0:
+            rows += len(frames[j])
+        return rows
+
+    def held_pages(key, prefix_tokens):
+        capacity = prefix_tokens + frame_max
+        return arena.page_cost(capacity) - arena.growth_cost(key, capacity)
+
+    resident = {a: held_pages(keys[a], len(prefixes[a]))
+                for a in range(len(keys)) if arena.is_resident(keys[a])}
+    for a in resident:
+        arena.pin(keys[a])
+    if prefix_tree is not None and not prefix_tree.shared_tokens:
+        prefix_tree = None
+    partners_of = (lambda key: None) if anchor_partners is None else anchor_partners
+    sched = JoinAdmission(
+        [len(p) for p in prefixes], [[len(s) for s in sufs] for sufs in stage_suffixes],
+        budget, arena.n_pages, arena.page_tokens, frame_tokens=[len(f) for f in frames],
+        resident=resident, anchor_partners={a: partners_of(keys[a]) for a in range(len(keys))},
+        temporary_suffix_pages=mode == "unified", answer_dtype=async_ans.dtype,
+        page_cost=arena.page_cost, tree=prefix_tree)
+    borrowing = sched.borrowing
+    borrowing.can_borrow = borrow_check(arena, keys, borrowing)
+    borrowers = borrowing.borrowers()
+    lowest_borrow = lowest_borrows(borrowing)
+    held = [keys[a] for a, n in enumerate(borrowers) if n]
+    spans, outstanding = [], []
+    tokens = 0
+    h2d = [0, 0]  # bytes, chunks
+
+    def build(part):
+        specs = []
+        for a, j, start, end, carried in part:
+            key, f, frame = keys[a], len(prefixes[a]), frames[j]
+            parent, shared = ((borrowing.parent(a), borrowing.shared(a)) if carried
+                              else (None, 0))
+            fresh = not arena.is_resident(key)
+            got = arena.activate(key, f, capacity_tokens=f + frame_max, base_tokens=f,
+                                 borrow=(keys[parent], shared) if shared else None)
+            assert got is not None, "scheduler admitted an anchor the arena cannot hold"
+            if fresh and a < len(borrowers) and borrowers[a]:
+                arena.hold(key, borrowers[a])
+                arena.keep_window(key, lowest_borrow[a])
+            prefix = None
+            if carried:
+                prefix = prefixes[a][shared:] if shared else prefixes[a]
+            sufs = [stage_suffixes[j][i] for i in sched.partner_indices(a, j, start, end)]
+            if frame and start == 0:
+                # the frame goes into the anchor's KV after its document rows
+                # (this entry's answer means nothing); the partners read both
+                specs.append(dict(key=key, prefix=prefix, start=shared, f=f, suffixes=[frame],
+                                  write_suffix_tokens=len(frame)))
+                specs.append(dict(key=key, prefix=None, f=f + len(frame), suffixes=sufs))
+            else:
+                specs.append(dict(key=key, prefix=prefix, start=shared, f=f + len(frame),
+                                  suffixes=sufs))
+        return pack_chunk(arena, specs, attention_mode=mode)
+
+    def settle(anchor):
+        if anchor_done is None:
+            if arena.is_resident(keys[anchor]):
+                arena.free_key(keys[anchor])
+        else:
+            anchor_done(anchor, sched.answers[k - 1].get(anchor, []))
+
+    def event(kind, anchor):
+        if kind == "finished":
+            settle(anchor)
+        elif arena.is_resident(keys[anchor]):
+            arena.free_key(keys[anchor])
+
+    def report(entry):
+        part, handle = entry
+        bits = async_ans.result(handle)
+        pos = 0
+        for a, j, start, end, _ in part:
+            if frames[j] and start == 0:
+                pos += 1
+            for kind, anchor in sched.report(a, j, start, end, bits[pos:pos + end - start]):
+                event(kind, anchor)
+            pos += end - start
+
+    def run_one(part):
+        nonlocal tokens
+        host = build(part)
+        chunk = host.upload(torch, device)
+        h2d[0] += host.h2d_bytes
+        h2d[1] += 1
+        if on_chunk is not None:
+            on_chunk(host, part)
+        tokens += chunk.tokens
+        e0 = e1 = None
+        if device != "cpu":
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+        normed = _forward(pipeline, arena, chunk)
+        if e1 is not None:
+            e1.record()
+        for key in chunk.fresh_keys:
+            arena.trim_window(key)
+        spans.append((part[0][1], e0, e1))
+        outstanding.append((part, async_ans.submit(normed)))
+        while len(outstanding) > 1:
+            report(outstanding.pop(0))
+
+    def run_part(part):
+        # a chunk whose temporary suffix pages do not fit (the packer takes
+        # them a page at a time) is retried after evicting retained KV, or
+        # halved
+        try:
+            run_one(part)
+        except ArenaFullError:
+            need = arena.page_cost(sum(entry_rows(*e) for e in part))
+            if arena.evict_retained(need):
+                run_part(part)
+                return
+            if len(part) < 2:
+                raise
+            half = len(part) // 2
+            run_part(part[:half])
+            run_part(part[half:])
+
+    while True:
+        for kind, anchor in sched.take_settled():
+            event(kind, anchor)
+        if sched.done():
+            break
+        if sched.blocked_pages:
+            arena.evict_retained(sched.blocked_pages)
+        groups = sched.next_chunk(arena.free_pages)
+        if not groups:
+            if outstanding:
+                report(outstanding.pop(0))
+                continue
+            if sched.blocked_pages and arena.evict_retained(sched.blocked_pages):
+                continue
+            if arena.drop_holds(held):
+                continue
+            raise AssertionError("nothing buildable and nothing in flight")
+        run_part(groups)
+        # the packed children hold their parents' pages now
+        for a, _, start, _, carried in groups:
+            parent = borrowing.tree_parent[a] if a < len(borrowing.tree_parent) else None
+            if carried and start == 0 and parent is not None:
+                arena.release(keys[parent])
+    while outstanding:
+        report(outstanding.pop(0))
+    arena.drop_holds(held)
+    if stats is not None:
+        stats["borrowed_tokens"] = borrowing.borrowed_tokens
+        stats["h2d_bytes"] = h2d[0]
+        stats["chunks"] = h2d[1]
+    return sched.answers, spans, tokens

@@ -2,7 +2,7 @@
 
 Run in a container that has the reference checkout (not on the GPU box):
 
-    python tests/golden/make_golden.py /path/to/quail
+    python tests/golden/make_golden.py /path/to/quail [scenario ...]
 
 Two kinds of fixtures:
 
@@ -11,7 +11,9 @@ Two kinds of fixtures:
   documents with a CPU KVArena and a recording pipeline; every packed
   chunk's arrays (ids, positions, finals, KV scatter, reads, source map,
   unified tables) and the final answers. quail_b200's packer must match
-  them bit for bit.
+  them bit for bit. host_join_* / host_score_*: the same record of the
+  reference's run_join (loop.py:609) over config-2-shaped anchors and
+  partners, with 0/1 answers (AI joins) or float32 scores (AI.SCORE).
 - kernels.npz: seeded inputs and outputs of the reference's fused Triton
   kernels (add_rms_norm_quant, qk_norm_rope, silu_mul_quant,
   merge_attn_quant, kv_row_scatter; attention.py:293-642) run on CPU
@@ -160,12 +162,8 @@ def chunk_record(chunk, arrays, index):
     return entry
 
 
-def run_reference_scenario(name):
-    from quail.backends.quail.executor import loop
-    from quail.backends.quail.executor.arena import KVArena
-    from quail.backends.quail.executor.models.base import ModelPipeline
-    from quail.execution.tokens import prefix_tree
-
+def _cpu_staging(loop):
+    """The reference loop's pinned-memory uploads, as plain CPU tensors."""
     def staged(torch_, data, dtype, pinned=True):
         if isinstance(data, np.ndarray) or torch.is_tensor(data):
             return torch.as_tensor(data, dtype=dtype)
@@ -178,6 +176,15 @@ def run_reference_scenario(name):
 
     loop._staged = staged
     loop._staged_token_parts = token_parts
+
+
+def run_reference_scenario(name):
+    from quail.backends.quail.executor import loop
+    from quail.backends.quail.executor.arena import KVArena
+    from quail.backends.quail.executor.models.base import ModelPipeline
+    from quail.execution.tokens import prefix_tree
+
+    _cpu_staging(loop)
     docs, questions, budget, pages, attention, use_tree, writes = scenario_docs(name)
     arena = KVArena(1, pages, 16, 1, 8, dtype=torch.bfloat16, device="cpu")
     chunks, arrays, entries = [], {}, []
@@ -211,6 +218,98 @@ def run_reference_scenario(name):
                    tree=None if tree is None else dict(order=list(map(int, tree.order)),
                                                        parent=tree.parent,
                                                        shared=list(map(int, tree.shared))))
+    np.savez_compressed(HERE / f"host_{name}.npz", **arrays)
+    (HERE / f"host_{name}.json").write_text(json.dumps(summary, separators=(",", ":")))
+    return summary
+
+
+# ---- join scenarios (run_join, loop.py:609-978) ------------------------------
+
+JOIN_SCENARIOS = ("join_tree", "join_unified", "join_stages_tree", "join_stages_unified",
+                  "join_tight_unified", "score_tree", "score_unified")
+
+
+def join_inputs(name):
+    """(anchors, stage_suffixes, frames, partners, budget, n_pages, attention).
+
+    Config 2's shape scaled down: every anchor is a 48-token shared
+    instruction + a left document (two-level prefix sharing through the
+    prefix tree), partners are right documents; joins frame each stage,
+    AI.SCORE streams a per-anchor subset of the partners."""
+    seed = {"join_tree": 10, "join_unified": 10, "join_stages_tree": 11,
+            "join_stages_unified": 11, "join_tight_unified": 12, "score_tree": 13,
+            "score_unified": 13}[name]
+    rng = np.random.default_rng(seed)
+    instr = rng.integers(1000, 150000, 48).tolist()
+    anchors = [instr + rng.integers(1000, 150000, int(rng.integers(20, 100))).tolist()
+               for _ in range(10)]
+    n_stages = 2 if "stages" in name else 1
+    stage_suffixes = [[rng.integers(1000, 150000, int(rng.integers(8, 40))).tolist()
+                       for _ in range(12 - 3 * j)] for j in range(n_stages)]
+    score = name.startswith("score")
+    frames = None if score else [rng.integers(1000, 150000, 3 - j).tolist()
+                                 for j in range(n_stages)]
+    partners = None
+    if score:
+        partners = [sorted(int(i) for i in rng.choice(12, size=int(rng.integers(1, 12)),
+                                                       replace=False))
+                    for _ in anchors]
+    budget, pages = 400, 300
+    if "tight" in name:
+        budget, pages = 500, 40
+    attention = "unified" if name.endswith("unified") else "tree"
+    return anchors, stage_suffixes, frames, partners, budget, pages, attention
+
+
+def score_values(input_ids, positions, finals):
+    """The recording readout's AI.SCORE values: a float32 per final row."""
+    ids = np.asarray(input_ids)
+    pos = np.asarray(positions)
+    fin = np.asarray(finals)
+    return ((ids[fin] * 7 + pos[fin]) % 1000).astype(np.float32) / np.float32(1000.0)
+
+
+def run_reference_join(name):
+    from quail.backends.quail.executor import loop
+    from quail.backends.quail.executor.arena import KVArena
+    from quail.backends.quail.executor.models.base import ModelPipeline
+    from quail.execution.tokens import prefix_tree
+
+    _cpu_staging(loop)
+    anchors, stage_suffixes, frames, partners, budget, pages, attention = join_inputs(name)
+    arena = KVArena(1, pages, 16, 1, 8, dtype=torch.bfloat16, device="cpu")
+    arrays, entries = {}, []
+    score = name.startswith("score")
+
+    class Recorder(ModelPipeline):
+        tree_attention = True
+
+        def forward_chunk(self, chunk):
+            entries.append(chunk_record(chunk, arrays, len(entries)))
+            return chunk
+
+    class Answers:
+        dtype = np.float32 if score else None
+
+        def submit(self, chunk):
+            f = score_values if score else answer_bits
+            return f(chunk.input_ids, chunk.positions, chunk.final_indices)
+
+        def result(self, handle):
+            return handle
+
+    keys = [("a", i) for i in range(len(anchors))]
+    stats = {}
+    answers, _, tokens = loop.run_join(
+        _Torch(), arena, Recorder(), Answers(), anchors, stage_suffixes, budget,
+        stage_frames=frames, anchor_keys=keys, attention_mode=attention,
+        anchor_partners=None if partners is None else (lambda key: [partners[key[1]]]),
+        prefix_tree=prefix_tree(anchors, 16), stats=stats)
+    summary = dict(name=name, chunks=entries, tokens=int(tokens),
+                   borrowed_tokens=int(stats.get("borrowed_tokens", 0)),
+                   answers=[{str(a): [float(x) for x in row] for a, row in sorted(st.items())}
+                            for st in answers],
+                   free_pages_after=int(arena.free_pages))
     np.savez_compressed(HERE / f"host_{name}.npz", **arrays)
     (HERE / f"host_{name}.json").write_text(json.dumps(summary, separators=(",", ":")))
     return summary
@@ -309,9 +408,19 @@ def main():
     if not (ref / "quail").is_dir():
         sys.exit("usage: make_golden.py <reference checkout>")
     _install_reference(ref)
+    only = sys.argv[2:]
     for name in SCENARIOS:
+        if only and name not in only:
+            continue
         summary = run_reference_scenario(name)
         print(name, "chunks", len(summary["chunks"]), "tokens", summary["tokens"])
+    for name in JOIN_SCENARIOS:
+        if only and name not in only:
+            continue
+        summary = run_reference_join(name)
+        print(name, "chunks", len(summary["chunks"]), "tokens", summary["tokens"])
+    if only and "kernels" not in only:
+        return
     make_kernel_vectors()
     print("kernels.npz written")
 

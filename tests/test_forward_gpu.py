@@ -25,7 +25,7 @@ from quail_b200 import loop
 from quail_b200.arena import KVArena
 from quail_b200.model import QWEN3_4B, TINY, random_weights
 from quail_b200.pipeline import Qwen3Pipeline
-from quail_b200.readout import AnswerRows, AsyncAnswers
+from quail_b200.readout import AnswerRows, AsyncAnswers, AsyncScores
 from quail_b200.tokens import prefix_tree
 
 pytestmark = pytest.mark.gpu
@@ -102,3 +102,88 @@ def test_qwen3_4b_shaped_rows_match_oracle():
     weights = random_weights(cfg, seed=0, device="cuda")
     docs, questions = rows_with_prefix(0, 3, 64, 16, 48, 1000, 150000)
     run_and_compare(cfg, weights, docs, questions, budget=4096, n_pages=200, mode="tree")
+
+
+def join_rows(seed, cfg, n_anchors, n_partners, n_stages):
+    """Config 2's shape, small: a shared instruction + left document per
+    anchor, right documents as partners, a frame per stage."""
+    rng = np.random.default_rng(seed)
+    instr = rng.integers(16, cfg.vocab, 48).tolist()
+    anchors = [instr + rng.integers(16, cfg.vocab, int(rng.integers(20, 120))).tolist()
+               for _ in range(n_anchors)]
+    stages = [[rng.integers(16, cfg.vocab, int(rng.integers(8, 48))).tolist()
+               for _ in range(n_partners)] for _ in range(n_stages)]
+    frames = [rng.integers(16, cfg.vocab, 3).tolist() for _ in range(n_stages)]
+    return anchors, stages, frames
+
+
+class RecordingScores(AsyncScores):
+    """AsyncScores that keeps each chunk's scores for the comparison."""
+
+    def __init__(self, torch_, rows):
+        super().__init__(torch_, rows)
+        self.kept = []
+
+    def result(self, handle):
+        out = super().result(handle)
+        self.kept.append(out.copy())
+        return out
+
+
+def run_join_and_compare(cfg, weights, anchors, stages, frames, budget, n_pages, mode,
+                         score=False, partners=None):
+    dev = torch.device("cuda")
+    arena = KVArena(cfg.n_layers, n_pages, 16, cfg.n_kv, cfg.head_dim, device=dev)
+    arena.pools.zero_()
+    pipe = Qwen3Pipeline(torch, weights, arena)
+    rows = AnswerRows(torch, weights)
+    ans = RecordingScores(torch, rows) if score else AsyncAnswers(torch, rows, keep_margins=True)
+    hosts = []
+    answers, _, _ = loop.run_join(
+        torch, arena, pipe, ans, anchors, stages, budget, stage_frames=frames,
+        attention_mode=mode, prefix_tree=prefix_tree(anchors, 16), device=dev,
+        anchor_partners=None if partners is None else (lambda key: [partners[key]]),
+        on_chunk=lambda host, groups: hosts.append(host))
+    torch.cuda.synchronize()
+    assert nat.kernel_status(torch.cuda.current_device()) == 0
+    got_rows = ans.kept if score else ans.margins
+    assert len(got_rows) == len(hosts)
+    cpu_w = weights.to("cpu")
+    cpu_arena = of.CpuArena(cfg.n_layers, arena.pool_rows, cfg.n_kv, cfg.head_dim)
+    _, ans_w, tc, fc = cpu_w.answer_rows()
+    for host, got in zip(hosts, got_rows):
+        normed = of.forward_chunk(cpu_w, host, cpu_arena)
+        if score:
+            want = nx.answer_score(normed, ans_w, tc, fc).numpy()
+        else:
+            want = nx.answer_margin(normed, ans_w, tc, fc)[0].numpy()
+        assert np.array_equal(got.view(np.int32), want.astype(np.float32).view(np.int32)), \
+            (got, want)
+    assert not arena.accounting.owned  # every anchor settled and freed
+    return answers
+
+
+@pytest.mark.parametrize("mode", ["tree", "unified"])
+def test_tiny_join_matches_oracle(mode):
+    """AI join (run_join): two stages with frames, prefix-sharing anchors."""
+    cfg = TINY
+    weights = random_weights(cfg, seed=5, device="cuda")
+    anchors, stages, frames = join_rows(6, cfg, 8, 10, 2)
+    answers = run_join_and_compare(cfg, weights, anchors, stages, frames, budget=700,
+                                   n_pages=300, mode=mode)
+    assert len(answers) == 2 and answers[0]
+
+
+def test_tiny_score_matches_oracle():
+    """AI.SCORE (run_join with AsyncScores): float32 scores per partner."""
+    cfg = TINY
+    weights = random_weights(cfg, seed=6, device="cuda")
+    anchors, stages, _ = join_rows(7, cfg, 8, 10, 1)
+    rng = np.random.default_rng(8)
+    partners = [sorted(int(i) for i in rng.choice(10, size=int(rng.integers(1, 10)),
+                                                   replace=False)) for _ in anchors]
+    answers = run_join_and_compare(cfg, weights, anchors, stages, None, budget=600,
+                                   n_pages=300, mode="tree", score=True, partners=partners)
+    assert sorted(answers[0]) == list(range(len(anchors)))
+    for a, row in answers[0].items():
+        assert row.dtype == np.float32 and len(row) == len(partners[a])

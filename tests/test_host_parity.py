@@ -1,9 +1,10 @@
 """quail_b200's host loop against the reference's own, chunk by chunk.
 
 The fixtures (tests/golden/host_*.npz/.json) were produced by running the
-reference's run_filter with a recording pipeline (tests/golden/
-make_golden.py). The same documents go through quail_b200.loop.run_filter
-here; every packed array must match bit for bit: token ids, positions,
+reference's run_filter and run_join with a recording pipeline (tests/golden/
+make_golden.py). The same documents (anchors and partners for the joins)
+go through quail_b200.loop.run_filter / run_join here; every packed array
+must match bit for bit: token ids, positions,
 answer rows, KV scatter rows, segment bounds, reader rows, block tables,
 the merge source map, unified tables, chunk layouts and final answers.
 """
@@ -73,6 +74,62 @@ def test_packed_chunks_match_reference(name):
         assert list(got["tree"].order) == want["tree"]["order"]
         assert got["tree"].parent == want["tree"]["parent"]
         assert list(got["tree"].shared) == want["tree"]["shared"]
+
+
+def run_ours_join(name):
+    anchors, stage_suffixes, frames, partners, budget, pages, attention = mg.join_inputs(name)
+    arena = KVArena(1, pages, 16, 1, 8, device=None)
+    arrays, entries = {}, []
+    score = name.startswith("score")
+
+    class Recorder(ModelPipeline):
+        tree_attention = True
+
+        def forward_chunk(self, chunk):
+            entries.append(mg.chunk_record(chunk.host, arrays, len(entries)))
+            return chunk.host
+
+    class Answers:
+        dtype = np.float32 if score else None
+
+        def submit(self, host):
+            f = mg.score_values if score else mg.answer_bits
+            return f(host.input_ids, host.positions, host.final_indices)
+
+        def result(self, handle):
+            return handle
+
+    keys = [("a", i) for i in range(len(anchors))]
+    stats = {}
+    answers, _, tokens = loop.run_join(
+        torch, arena, Recorder(), Answers(), anchors, stage_suffixes, budget,
+        stage_frames=frames, anchor_keys=keys, attention_mode=attention,
+        anchor_partners=None if partners is None else (lambda key: [partners[key[1]]]),
+        prefix_tree=prefix_tree(anchors, 16), stats=stats, device="cpu")
+    return dict(entries=entries, arrays=arrays, tokens=tokens, answers=answers, stats=stats,
+                arena=arena)
+
+
+@pytest.mark.parametrize("name", mg.JOIN_SCENARIOS)
+def test_join_chunks_match_reference(name):
+    """run_join (AI joins and AI.SCORE) against the reference's, chunk by chunk."""
+    want = json.loads((GOLDEN / f"host_{name}.json").read_text())
+    want_arrays = np.load(GOLDEN / f"host_{name}.npz")
+    got = run_ours_join(name)
+    assert len(got["entries"]) == len(want["chunks"])
+    for i, (g, w) in enumerate(zip(got["entries"], want["chunks"])):
+        assert g == w, f"chunk {i} metadata differs"
+    assert sorted(got["arrays"]) == sorted(want_arrays.files)
+    for key in want_arrays.files:
+        a, b = got["arrays"][key], want_arrays[key]
+        assert a.shape == b.shape, key
+        assert np.array_equal(a.astype(np.int64), b.astype(np.int64)), key
+    assert got["tokens"] == want["tokens"]
+    assert got["stats"]["borrowed_tokens"] == want["borrowed_tokens"]
+    answers = [{str(a): [float(x) for x in row] for a, row in sorted(st.items())}
+               for st in got["answers"]]
+    assert answers == want["answers"]
+    assert got["arena"].free_pages == want["free_pages_after"]
 
 
 def test_prefix_tree_shapes():
