@@ -1,11 +1,15 @@
-"""The public entry point of the B200 AI.IF path: one loaded GPU, one filter.
+"""The public entry point of the B200 AI.IF path: one loaded GPU.
 
 ``B200Executor`` is what Quail's per-GPU state holds after boot
-(quail/backends/quail/worker.py:46-148: model, KVArena, pipeline) and
+(quail/backends/quail/worker.py:46-148: model, KVArena, pipeline).
 ``filter`` is the AiFilter branch of QuailModelExecution._execute_quail_node
 (quail/backends/quail/backend.py:107-162): build the prefix tree when the
 plan shares prefixes, run the filter loop to the end, return per-document
 answers. Margins (yes - no logits) come back too, for parity checks.
+``join`` is its AI join branch (backend.py:166-214: run_join over anchors
+and per-stage partner lists) and ``score`` the AI.SCORE reranker
+(quail/backends/quail/executor/score.py:46-66: run_join with the sigmoid
+readout).
 """
 
 import time
@@ -17,7 +21,7 @@ from quail_b200 import loop
 from quail_b200.arena import KVArena
 from quail_b200.model import random_weights
 from quail_b200.pipeline import build_pipeline
-from quail_b200.readout import AnswerRows, AsyncAnswers
+from quail_b200.readout import AnswerRows, AsyncAnswers, AsyncScores
 from quail_b200.tokens import prefix_tree
 
 
@@ -34,6 +38,18 @@ class FilterResult:
     gpu_s: float
     wall_s: float
     timing: dict = field(default_factory=dict)
+
+
+@dataclass
+class JoinResult:
+    answers: list                      # per stage: anchor -> row over its partners
+    fresh_tokens: int
+    borrowed_tokens: int
+    chunks: int
+    h2d_bytes: int
+    d2h_bytes: int
+    gpu_s: float
+    wall_s: float
 
 
 class B200Executor:
@@ -99,3 +115,41 @@ class B200Executor:
                             borrowed_tokens=stats.get("borrowed_tokens", 0),
                             chunks=stats.get("chunks", 0), h2d_bytes=stats.get("h2d_bytes", 0),
                             d2h_bytes=ans.d2h_bytes, gpu_s=gpu_s, wall_s=wall, timing=timing)
+
+    def _join(self, readout, anchors, stage_suffixes, stage_frames, budget, attention,
+              share_prefixes, partners):
+        torch = self.torch
+        t0 = time.perf_counter()
+        tree = prefix_tree(anchors, self.arena.page_tokens) if share_prefixes else None
+        stats = {}
+        answers, spans, tokens = loop.run_join(
+            torch, self.arena, self.pipeline, readout, anchors,
+            [[list(s) for s in sufs] for sufs in stage_suffixes], budget or self.budget,
+            stage_frames=stage_frames, attention_mode=attention, prefix_tree=tree,
+            anchor_partners=None if partners is None else (lambda key: partners[key]),
+            stats=stats, device=self.device)
+        torch.cuda.synchronize(self.device)
+        wall = time.perf_counter() - t0
+        gpu_s = sum(a.elapsed_time(b) for _, a, b in spans if a is not None) / 1000.0
+        return JoinResult(answers=answers, fresh_tokens=tokens,
+                          borrowed_tokens=stats.get("borrowed_tokens", 0),
+                          chunks=stats.get("chunks", 0), h2d_bytes=stats.get("h2d_bytes", 0),
+                          d2h_bytes=readout.d2h_bytes, gpu_s=gpu_s, wall_s=wall)
+
+    def join(self, anchors, stage_suffixes, *, stage_frames=None, budget=None,
+             attention="tree", share_prefixes=True, partners=None) -> JoinResult:
+        """Run one AI join: every anchor against its partners, stage by stage
+        (an anchor continues to stage j + 1 once a stage-j partner answered
+        TRUE). partners: per anchor, per stage, partner indices or None."""
+        ans = AsyncAnswers(self.torch, self.answer_rows)
+        return self._join(ans, anchors, stage_suffixes, stage_frames, budget, attention,
+                          share_prefixes, partners)
+
+    def score(self, anchors, suffixes, *, budget=None, attention="tree",
+              share_prefixes=True, partners=None) -> JoinResult:
+        """AI.SCORE: sigmoid(yes - no) per (anchor, partner) as float32 rows;
+        partners: per anchor, the partner indices it scores, or None for all."""
+        ans = AsyncScores(self.torch, self.answer_rows)
+        per = None if partners is None else [[p] for p in partners]
+        return self._join(ans, anchors, [suffixes], None, budget, attention, share_prefixes,
+                          per)

@@ -1,0 +1,123 @@
+"""AI join throughput on one GPU: config 2 (Qwen3-4B FP8, two-level prefix sharing).
+
+``python -m quail_b200.join_bench [--left N] [--right M] [--cpu]`` runs
+``B200Executor.join`` over the first N left rows of config 2, each streaming
+every one of the M right rows (pairs = N x M). Config 2 shards by left row,
+so a GPU's share is a contiguous run of anchors against the whole right
+table; N anchors out of 200 is one GPU's slice of a larger run. One
+untimed warm-up join of one anchor precedes the timed one. Prints one JSON
+line:
+
+- ``e2e``: pairs/s through the public call (prefix tree, admission and
+  packing on the host, pinned H2D, the forwards, D2H of the answer bits),
+  timed on the wall clock around the call after a device synchronize;
+- ``value``: pairs/s over the summed CUDA-event time of the forwards
+  (``gpu_s``), the device-side rate;
+- tokens: logical prompt tokens of the pairs, fresh tokens packed (the
+  instruction and each left document are computed once per GPU), tokens
+  read from borrowed pages;
+- ``cpu_baseline`` (``--cpu``): the CPU oracle (BLAS mode, all host cores)
+  on one anchor against the first ``--cpu-partners`` right rows.
+"""
+
+import argparse
+import json
+import os
+import time
+
+from quail_b200.api import B200Executor
+from quail_b200.model import QWEN3_4B
+from quail_b200.workload import config2
+
+
+def cpu_sample(torch, weights, wl, partners, page_tokens=16):
+    """(seconds, pairs, tokens) of the CPU oracle on anchor 0 x partners."""
+    from oracle import forward as of
+    from oracle import numerics as nx
+    from quail_b200 import loop
+    from quail_b200.arena import KVArena
+    from quail_b200.tokens import prefix_tree
+
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
+    nx.MODE["exact"] = False
+    cpu_w = weights.to("cpu")
+    anchors = [wl.anchors[0]]
+    sufs = [wl.partners[:partners]]
+    arena = KVArena(1, 4096, page_tokens, 1, 8, device=None)
+    hosts = []
+
+    class Rec:
+        tree_attention = True
+        canvas_ids = ()
+
+        def forward_chunk(self, chunk):
+            hosts.append(chunk.host)
+            return len(chunk.host.final_indices)  # one answer per final row
+
+    class Ans:
+        dtype = None
+
+        def submit(self, n):
+            return [1] * n
+
+        def result(self, h):
+            return h
+
+    loop.run_join(torch, arena, Rec(), Ans(), anchors, sufs, 1 << 20, attention_mode="tree",
+                  prefix_tree=prefix_tree(anchors, page_tokens), device="cpu")
+    cfg = cpu_w.config
+    _, ans_w, tc, fc = cpu_w.answer_rows()
+    t0 = time.perf_counter()
+    cpu_arena = of.CpuArena(cfg.n_layers, 4096 * page_tokens, cfg.n_kv, cfg.head_dim)
+    for host in hosts:
+        nx.answer_margin(of.forward_chunk(cpu_w, host, cpu_arena), ans_w, tc, fc)
+    return time.perf_counter() - t0, partners, sum(h.tokens for h in hosts)
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    p.add_argument("--left", type=int, default=8, help="anchors (left rows) timed")
+    p.add_argument("--right", type=int, default=500, help="partners (right rows)")
+    p.add_argument("--pages", type=int, default=16384)
+    p.add_argument("--budget", type=int, default=0)
+    p.add_argument("--cpu", action="store_true")
+    p.add_argument("--cpu-partners", type=int, default=2)
+    args = p.parse_args(argv)
+    import torch
+
+    wl = config2(right=args.right)
+    ex = B200Executor(torch, QWEN3_4B, args.pages)
+    budget = args.budget or None
+    ex.join([wl.anchors[0]], [wl.partners], budget=budget)  # warm-up
+    ex.reset_arena()
+    anchors = [wl.anchors[i] for i in range(1, 1 + args.left)]
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    res = ex.join(anchors, [wl.partners], budget=budget)
+    wall = time.perf_counter() - t0
+    pairs = len(anchors) * len(wl.partners)
+    answered = sum(len(row) for row in res.answers[0].values())
+    logical = wl.logical_tokens(1, 1 + args.left)
+    line = {
+        "metric": "AI join pairs/s (Qwen3-4B FP8, config 2)", "unit": "pairs/s",
+        "value": pairs / res.gpu_s, "e2e": pairs / wall, "pairs": pairs, "answered": answered,
+        "gpu_s": res.gpu_s, "wall_s": wall, "chunks": res.chunks,
+        "logical_tokens": logical, "fresh_tokens": res.fresh_tokens,
+        "borrowed_tokens": res.borrowed_tokens,
+        "prefill_tokens_per_s": res.fresh_tokens / res.gpu_s,
+        "h2d_bytes": res.h2d_bytes, "d2h_bytes": res.d2h_bytes,
+        "config": {"workload": f"config2: {args.left} left x {args.right} right rows, tree "
+                               f"attention, one GPU's slice", "budget": budget or ex.budget},
+        "data": "synthetic (seeded config-2 shapes; random-init Qwen3-4B FP8 weights)",
+    }
+    if args.cpu:
+        dt, n, tokens = cpu_sample(torch, ex.weights, wl, args.cpu_partners)
+        line["cpu_baseline"] = {"value": n / dt, "unit": "pairs/s",
+                                "cores": len(os.sched_getaffinity(0)), "kind": "port",
+                                "sample": f"anchor 0 x {n} partners ({tokens} tokens) through "
+                                          f"the CPU oracle, {dt:.1f} s"}
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

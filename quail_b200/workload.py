@@ -95,6 +95,43 @@ def config3(rows=50_000, seed=0) -> Workload:
                     [_question()], 96)
 
 
+@dataclass
+class JoinWorkload:
+    """An AI join: anchors (left rows) stream every partner (right row)."""
+    name: str
+    model: str
+    anchors: Sequence           # instruction | left document, per left row
+    partners: list              # right document | question tail, per right row
+    instruction_tokens: int
+
+    @property
+    def pairs(self) -> int:
+        return len(self.anchors) * len(self.partners)
+
+    def logical_tokens(self, lo=0, hi=None) -> int:
+        """Prompt tokens of every pair whose anchor is in [lo, hi)."""
+        hi = len(self.anchors) if hi is None else hi
+        anchor = sum(len(self.anchors[a]) for a in range(lo, hi))
+        partner = sum(len(p) for p in self.partners)
+        return (hi - lo) * partner + anchor * len(self.partners)
+
+
+def config2(left=200, right=500, seed=0) -> JoinWorkload:
+    """Qwen3-4B FP8 AI join: a 48-token shared instruction, left documents
+    uniform in [128, 512] tokens (one anchor each), right documents uniform
+    in [64, 256] (each followed by the one-token question tail), ids uniform
+    in [1000, 150000); shard by left row."""
+    rng = np.random.default_rng(seed)
+    instruction = rng.integers(1000, 150000, 48)
+    left_lens = rng.integers(128, 513, left)
+    right_lens = rng.integers(64, 257, right)
+    anchors = DocRows(instruction, left_lens, 1000, 150000, seed + 1)
+    tail = _question()
+    prng = np.random.default_rng(seed + 2)
+    partners = [prng.integers(1000, 150000, int(n)).tolist() + tail for n in right_lens]
+    return JoinWorkload("config2", "qwen3-4b-fp8", anchors, partners, 48)
+
+
 def shard(n_rows: int, rank: int, world: int) -> tuple:
     """Contiguous row slice [lo, hi) of one rank."""
     per = -(-n_rows // world)

@@ -187,3 +187,23 @@ def test_tiny_score_matches_oracle():
     assert sorted(answers[0]) == list(range(len(anchors)))
     for a, row in answers[0].items():
         assert row.dtype == np.float32 and len(row) == len(partners[a])
+
+
+def test_executor_join_and_score_api():
+    """B200Executor.join / .score (the public calls) on the tiny model: rows
+    per anchor over its partners, every page back on the free list."""
+    from quail_b200.api import B200Executor
+    cfg = TINY
+    ex = B200Executor(torch, cfg, 300, seed=5)
+    anchors, stages, frames = join_rows(9, cfg, 5, 7, 2)
+    res = ex.join(anchors, stages, stage_frames=frames, budget=700)
+    assert len(res.answers) == 2
+    assert all(len(row) == 7 for row in res.answers[0].values())
+    assert res.fresh_tokens > 0 and res.gpu_s > 0
+    assert ex.arena.free_pages == 300
+    partners = [[0, 2, 4], [1], [0, 1, 2, 3, 4, 5, 6], [6], [3, 5]]
+    scores = ex.score(anchors, stages[0], budget=700, partners=partners)
+    for a, row in scores.answers[0].items():
+        assert row.dtype == np.float32 and len(row) == len(partners[a])
+        assert np.all((row >= 0) & (row <= 1))
+    assert ex.arena.free_pages == 300
