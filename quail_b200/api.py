@@ -50,6 +50,18 @@ class JoinResult:
     d2h_bytes: int
     gpu_s: float
     wall_s: float
+    n_anchors: int = 0
+
+    def survivors(self, semantics="semi"):
+        """Anchors the join keeps (backend.py:231-240): with "semi" (EXISTS)
+        those with a TRUE partner at the last stage, with "anti" (NOT EXISTS)
+        the rest, in anchor order."""
+        if semantics not in ("semi", "anti"):
+            raise ValueError(f"join semantics {semantics!r}: semi or anti")
+        last = self.answers[-1] if self.answers else {}
+        matched = {a for a, row in last.items() if any(row)}
+        keep = (lambda a: a in matched) if semantics == "semi" else (lambda a: a not in matched)
+        return [a for a in range(self.n_anchors) if keep(a)]
 
 
 class B200Executor:
@@ -134,7 +146,8 @@ class B200Executor:
         return JoinResult(answers=answers, fresh_tokens=tokens,
                           borrowed_tokens=stats.get("borrowed_tokens", 0),
                           chunks=stats.get("chunks", 0), h2d_bytes=stats.get("h2d_bytes", 0),
-                          d2h_bytes=readout.d2h_bytes, gpu_s=gpu_s, wall_s=wall)
+                          d2h_bytes=readout.d2h_bytes, gpu_s=gpu_s, wall_s=wall,
+                          n_anchors=len(anchors))
 
     def join(self, anchors, stage_suffixes, *, stage_frames=None, budget=None,
              attention="tree", share_prefixes=True, partners=None) -> JoinResult:

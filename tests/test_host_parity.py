@@ -184,3 +184,13 @@ def test_arena_free_stack_and_borrow_holds():
     assert arena.free_pages == 8
     # LIFO: freed pages come back in release order
     assert arena.alloc("c", 16) == [3]
+
+
+def test_join_survivors_semi_and_anti():
+    """EXISTS / NOT EXISTS over a join's last-stage rows (backend.py:231-240)."""
+    from quail_b200.api import JoinResult
+    res = JoinResult(answers=[{0: [1, 0], 1: [0, 0], 3: [0, 1]}, {0: [0, 1], 3: [0, 0]}],
+                     fresh_tokens=0, borrowed_tokens=0, chunks=0, h2d_bytes=0, d2h_bytes=0,
+                     gpu_s=0.0, wall_s=0.0, n_anchors=5)
+    assert res.survivors("semi") == [0]
+    assert res.survivors("anti") == [1, 2, 3, 4]
