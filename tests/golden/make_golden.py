@@ -14,6 +14,8 @@ Two kinds of fixtures:
   them bit for bit. host_join_* / host_score_*: the same record of the
   reference's run_join (loop.py:609) over config-2-shaped anchors and
   partners, with 0/1 answers (AI joins) or float32 scores (AI.SCORE).
+- token_store.arrow + .json: a token store file written by the
+  reference's TokenStore (the host input format) and its documents.
 - kernels.npz: seeded inputs and outputs of the reference's fused Triton
   kernels (add_rms_norm_quant, qk_norm_rope, silu_mul_quant,
   merge_attn_quant, kv_row_scatter; attention.py:293-642) run on CPU
@@ -315,6 +317,50 @@ def run_reference_join(name):
     return summary
 
 
+# ---- token store (quail/execution/tokens.py:180-359) ---------------------------
+
+def make_token_store():
+    """token_store.arrow: a store written by the reference's TokenStore.write
+    (tokenizer: a fixed text -> ids map), and token_store.json: its
+    documents as lists. Also checks that a store written by
+    quail_b200.token_store opens in the reference's TokenStore with the
+    same documents (recorded as reads_ours)."""
+    import tempfile
+
+    import pyarrow as pa
+    from quail.execution.tokens import TokenStore as RefStore
+
+    sys.path.insert(0, str(HERE.parent.parent))
+    from quail_b200.token_store import write_token_store
+
+    rng = np.random.default_rng(21)
+    texts = [" ".join(str(int(x)) for x in rng.integers(1000, 150000, int(n)))
+             for n in rng.integers(1, 60, 23)]
+
+    def tokenizer(text):
+        return [int(t) for t in text.split()]
+
+    batches = [pa.RecordBatch.from_arrays([pa.array(texts[i:i + 8])], names=["doc"])
+               for i in range(0, len(texts), 8)]
+    path = HERE / "token_store.arrow"
+    store = RefStore.write(str(path), batches, document_column="doc", tokenizer=tokenizer,
+                           token_type=pa.int32())
+    def as_ints(view):
+        return [int(t.as_py()) if hasattr(t, "as_py") else int(t) for t in view]
+
+    docs = [as_ints(store[i]) for i in range(len(store))]
+    assert docs == [tokenizer(t) for t in texts]
+    with tempfile.TemporaryDirectory() as tmp:
+        write_token_store(f"{tmp}/ours.arrow", docs, batch_rows=5)
+        ref = RefStore(f"{tmp}/ours.arrow")
+        back = [as_ints(ref[i]) for i in range(len(ref))]
+        reads_ours = back == docs and list(ref.lengths) == [len(d) for d in docs]
+        ref.close()
+    store.close()
+    (HERE / "token_store.json").write_text(json.dumps(dict(documents=docs,
+                                                           reads_ours=reads_ours)))
+
+
 # ---- kernel vectors ---------------------------------------------------------------
 
 def make_kernel_vectors():
@@ -419,6 +465,9 @@ def main():
             continue
         summary = run_reference_join(name)
         print(name, "chunks", len(summary["chunks"]), "tokens", summary["tokens"])
+    if not only or "token_store" in only:
+        make_token_store()
+        print("token_store.arrow written")
     if only and "kernels" not in only:
         return
     make_kernel_vectors()

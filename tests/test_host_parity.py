@@ -194,3 +194,56 @@ def test_join_survivors_semi_and_anti():
                      gpu_s=0.0, wall_s=0.0, n_anchors=5)
     assert res.survivors("semi") == [0]
     assert res.survivors("anti") == [1, 2, 3, 4]
+
+
+def test_token_store_reads_reference_file():
+    """The host input format: a token store file written by the reference's
+    TokenStore opens here with the same documents and lengths, and (checked
+    when the fixture was made) one written here opens in the reference."""
+    from quail_b200.token_store import TokenStore
+    want = json.loads((GOLDEN / "token_store.json").read_text())
+    store = TokenStore(GOLDEN / "token_store.arrow")
+    assert len(store) == len(want["documents"])
+    for i, doc in enumerate(want["documents"]):
+        assert store[i].tolist() == doc
+        assert store.lengths[i] == len(doc)
+    assert want["reads_ours"]
+    store.close()
+
+
+def test_filter_over_token_store_matches_reference(tmp_path):
+    """run_filter over documents served from a memory-mapped token store
+    packs the same chunks as over lists (the cfg1_tree golden)."""
+    from quail_b200.token_store import write_token_store
+    name = "cfg1_tree"
+    docs, questions, budget, pages, attention, use_tree, writes = mg.scenario_docs(name)
+    store = write_token_store(tmp_path / "docs.arrow", docs, batch_rows=16)
+    want = json.loads((GOLDEN / f"host_{name}.json").read_text())
+    want_arrays = np.load(GOLDEN / f"host_{name}.npz")
+    arena = KVArena(1, pages, 16, 1, 8, device=None)
+    arrays, entries = {}, []
+
+    class Recorder(ModelPipeline):
+        tree_attention = True
+
+        def forward_chunk(self, chunk):
+            entries.append(mg.chunk_record(chunk.host, arrays, len(entries)))
+            return chunk.host
+
+    class Answers:
+        def submit(self, host):
+            return mg.answer_bits(host.input_ids, host.positions, host.final_indices)
+
+        def result(self, handle):
+            return handle
+
+    answers, _, tokens = loop.run_filter(
+        torch, arena, Recorder(), Answers(), store, questions, budget, arena_writes=writes,
+        attention_mode=attention, prefix_tree=prefix_tree(store, 16), device="cpu")
+    assert entries == want["chunks"]
+    for key in want_arrays.files:
+        assert np.array_equal(arrays[key].astype(np.int64), want_arrays[key].astype(np.int64)), key
+    assert {str(k): v for k, v in sorted(answers.items())} == want["answers"]
+    assert tokens == want["tokens"]
+    store.close()
+
