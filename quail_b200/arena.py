@@ -205,6 +205,10 @@ class KVArena:
         self._set_rows(key)
         return pages
 
+    def pin(self, key) -> None:
+        """Mark a resident key active (a join's anchor): eviction skips it."""
+        self.accounting.pin(key)
+
     def growth_cost(self, key, capacity_tokens: int) -> int:
         """Pages a resident key needs to grow to capacity (arena.py:772-786,
         without the sliding pool)."""

@@ -12,9 +12,8 @@ reference's for the same inputs.
 
 Packing happens on the host in numpy (``HostChunk``); ``HostChunk.upload``
 copies it to the device in one pinned transfer per array. Not built here:
-diffusion canvas rows, sliding-window pools, survivor retention, held
-survivors and a streaming anchor source for joins (outside the AI.IF
-prefill path).
+diffusion canvas rows, sliding-window pools and survivor retention
+(outside the AI.IF prefill path).
 """
 
 import time
@@ -417,6 +416,7 @@ class FilterStream:
 
     def __init__(self, torch, arena, pipeline, async_ans, doc_ids, question_ids, budget,
                  timing=None, limit=None, *, arena_writes, arena_keys=None,
+                 hold_survivors=False, hold_extra_tokens=0,
                  attention_mode=None, document_done=None, prefix_tree=None,
                  device="cuda", on_chunk=None):
         p = _shared_preamble_tokens(question_ids)
@@ -429,7 +429,7 @@ class FilterStream:
             if not tail:
                 raise ValueError(f"stage {i} question has no tokens beyond the shared "
                                  f"preamble ({p} tokens)")
-        if not arena_writes and len(question_ids) > 1:
+        if not arena_writes and (len(question_ids) > 1 or hold_survivors):
             raise ValueError("arena_writes=False needs a single stage")
         self.attention_mode = attention_path(pipeline, attention_mode)
         unified = self.attention_mode == "unified"
@@ -441,6 +441,9 @@ class FilterStream:
         temp_tail = max(0, *(len(q) - p for q in question_ids)) if unified and arena_writes \
             else 0
         capacity_extra = p + temp_tail
+        if hold_survivors:
+            # a held document's pages cover the consumer's largest frame
+            capacity_extra = max(capacity_extra, hold_extra_tokens)
         if arena.retention_cap_pages is None:
             arena.retention_cap_pages = max(0, arena.n_pages - arena.pages_needed(2 * budget))
         self.sched = FilterAdmission(
@@ -463,6 +466,8 @@ class FilterStream:
         self.keys = keys
         self.timing = timing
         self.arena_writes = arena_writes
+        self.hold = hold_survivors
+        self.reserve_pages = 0  # pages a join consumer needs free for its partners
         self.preamble = p
         self.capacity_extra = capacity_extra
         self.tails = tails
@@ -495,6 +500,14 @@ class FilterStream:
         return dict(key=self.keys[doc], prefix=None, f=len(self.doc_ids[doc]) + self.preamble,
                     suffixes=[self.tails[stage]])
 
+    def set_reserve(self, pages):
+        """Leave pages free for a join consumer's partner rows."""
+        for doc, ids in enumerate(self.doc_ids):
+            if self.arena.page_cost(len(ids) + self.capacity_extra) + pages > self.arena.n_pages:
+                raise ValueError(f"document {doc} needs more pages than the arena holds "
+                                 f"beside the join's {pages} pages of partner rows")
+        self.reserve_pages = pages
+
     def _activate(self, doc):
         borrowing = self.sched.borrowing
         key = self.keys[doc]
@@ -508,7 +521,7 @@ class FilterStream:
             self.arena.hold(key, self.borrowers[doc])
             self.arena.keep_window(key, self.lowest_borrow[doc])
 
-    def _report(self, entry):
+    def _report(self, entry, items):
         t = time.perf_counter() if self.timing is not None else 0.0
         groups, handle = entry
         bits = self.async_ans.result(handle)
@@ -517,44 +530,60 @@ class FilterStream:
         finished = []
         for (doc, stage, _fresh), bit in zip(groups, bits):
             passed = bool(bit)
-            for d in self.sched.report(doc, stage, passed):
+            # a held survivor keeps its pages: the join consumer frees them
+            hold = passed and stage == last_stage and self.hold
+            for d in self.sched.report(doc, stage, passed, release=not hold):
                 self.arena.free_key(self.keys[d])
+            if hold:
+                items.append((self.keys[doc], self.doc_ids[doc]))
             if not passed or stage == last_stage:
                 finished.append((doc, stage, passed))
         if finished and self.document_done is not None:
             self.document_done(finished)
         _tick(self.timing, "report_rest", t)
 
-    def _finish(self):
+    def _finish(self, items):
         while self.outstanding:
-            self._report(self.outstanding.pop(0))
+            self._report(self.outstanding.pop(0), items)
         for doc in self.sched.drain_ready():
             self.arena.free_key(self.keys[doc])
         self.arena.drop_holds([self.keys[doc] for doc, n in enumerate(self.borrowers) if n])
         self.done = True
 
-    def next(self):
-        """Run one chunk; reads the previous chunk's answers while it runs."""
+    def next(self, evict_retained=False):
+        """Run one chunk; reads the previous chunk's answers while it runs.
+
+        Returns (held, blocked) as Quail's FilterStream.next (loop.py:
+        1438-1532): the (key, prefix) pairs of survivors handed over with
+        their KV (hold_survivors), and whether fresh admission is short of
+        pages that only the join consumer can free."""
+        items = []
         if self.done:
-            return
+            return items, False
         sched, arena, timing = self.sched, self.arena, self.timing
         while True:
             if sched.done():
-                self._finish()
-                return
-            free = arena.free_pages if self.arena_writes else None
+                self._finish(items)
+                return items, False
+            free = (max(0, arena.free_pages - self.reserve_pages) if self.arena_writes
+                    else None)
             t = time.perf_counter() if timing is not None else 0.0
             groups = sched.next_chunk(free)
             t = _tick(timing, "next_chunk", t)
             if groups:
                 break
             if self.outstanding:
-                self._report(self.outstanding.pop(0))
+                self._report(self.outstanding.pop(0), items)
                 continue
-            if sched.blocked_pages and arena.evict_retained(sched.blocked_pages):
-                continue
+            if sched.blocked_pages and (evict_retained or not self.hold):
+                if arena.evict_retained(sched.blocked_pages):
+                    continue
+            if self.hold and sched.blocked_pages and not evict_retained:
+                return items, True  # the consumer frees pages first
             if arena.drop_holds([self.keys[doc] for doc, n in enumerate(self.borrowers) if n]):
                 continue
+            if self.hold and sched.blocked_pages:
+                return items, True
             raise AssertionError("nothing buildable and nothing in flight")
         if self.tree is not None and self.attention_mode != "unified":
             def borrow_order(group):
@@ -599,7 +628,8 @@ class FilterStream:
         self.chunks += 1
         _tick(timing, "submit", t)
         while len(self.outstanding) > 1:
-            self._report(self.outstanding.pop(0))
+            self._report(self.outstanding.pop(0), items)
+        return items, bool(self.hold and sched.blocked_pages)
 
 
 def run_filter(torch, arena, pipeline, async_ans, doc_ids, question_ids, budget, timing=None,
@@ -638,20 +668,25 @@ def run_join(torch, arena, pipeline, async_ans, anchor_prefixes, stage_suffixes,
     document rows (a frame entry, whose answer is skipped) and runs of
     partner suffixes read against the anchor's kept KV. The readout's dtype
     picks the answer rows: None for 0/1 lists (AI joins), float32 arrays for
-    AI.SCORE.
+    AI.SCORE. With anchor_source (a FilterStream with hold_survivors), the
+    filter's survivors stream in as resident anchors between join chunks.
 
     Returns:
         (answers, spans, tokens): answers[j][a] is anchor a's row over the
         stage-j partners it streams; spans (stage, start, end) CUDA events
         per forward; tokens the fresh tokens packed.
     """
-    if anchor_source is not None or anchor_batch is not None:
-        raise NotImplementedError("run_join: a streaming anchor source is not built here")
     if tuple(getattr(pipeline, "canvas_ids", ()) or ()):
         raise NotImplementedError("run_join: diffusion canvas rows are not built here")
     k = len(stage_suffixes)
-    prefixes = list(anchor_prefixes)
-    keys = list(range(len(prefixes))) if anchor_keys is None else list(anchor_keys)
+    if anchor_source is not None:
+        # the source hands over resident anchors; the join appends them
+        if anchor_prefixes or anchor_keys:
+            raise ValueError("anchor_source fills anchor_prefixes and anchor_keys")
+        prefixes, keys = anchor_prefixes, anchor_keys
+    else:
+        prefixes = list(anchor_prefixes)
+        keys = list(range(len(prefixes))) if anchor_keys is None else list(anchor_keys)
     if len(keys) != len(prefixes):
         raise ValueError("anchor_keys must match anchor_prefixes")
     frames = stage_frames or [[] for _ in range(k)]
@@ -659,6 +694,14 @@ def run_join(torch, arena, pipeline, async_ans, anchor_prefixes, stage_suffixes,
     if k == 0:
         return [], [], 0
     frame_max = max(len(f) for f in frames)
+    if anchor_source is not None and mode == "unified":
+        # the source leaves room for one partner's temporary rows, or held
+        # anchors could fill the arena before the join can run
+        longest = [max((len(x) for x in sufs), default=0) for sufs in stage_suffixes]
+        anchor_source.set_reserve(max(
+            (partner_pages(arena.page_cost, arena.page_tokens, len(doc), len(frame), rows)
+             for doc in anchor_source.doc_ids for frame, rows in zip(frames, longest)),
+            default=0))
 
     def entry_rows(a, j, start, end, carried):
         rows = (len(prefixes[a]) if carried else 0) + sum(
@@ -692,6 +735,35 @@ def run_join(torch, arena, pipeline, async_ans, anchor_prefixes, stage_suffixes,
     spans, outstanding = [], []
     tokens = 0
     h2d = [0, 0]  # bytes, chunks
+
+    def admit(items):
+        if anchor_batch is not None and items:
+            kept = set(anchor_batch([key for key, _ in items]))
+            for key, _ in items:
+                if key not in kept and arena.is_resident(key):
+                    arena.free_key(key)
+            items = [(key, prefix) for key, prefix in items if key in kept]
+        for key, prefix in items:
+            if not arena.is_resident(key):
+                raise ValueError(f"streamed anchor {key!r} has no KV in the arena")
+            arena.pin(key)
+            keys.append(key)
+            prefixes.append(prefix)
+            sched.admit(len(prefix), held_pages(key, len(prefix)), partners=partners_of(key))
+
+    def pull(evict_retained=False, force=False):
+        """Source chunks until a join chunk can fill or the source blocks;
+        whether the source ran a chunk or handed an anchor over."""
+        moved = False
+        while not anchor_source.done and (force or sched.buildable_tokens() < budget):
+            force = False
+            before = anchor_source.chunks
+            items, blocked = anchor_source.next(evict_retained=evict_retained)
+            admit(items)
+            moved = moved or bool(items) or anchor_source.chunks > before
+            if blocked:
+                break
+        return moved
 
     def build(part):
         specs = []
@@ -787,9 +859,11 @@ def run_join(torch, arena, pipeline, async_ans, anchor_prefixes, stage_suffixes,
             run_part(part[half:])
 
     while True:
+        if anchor_source is not None and not anchor_source.done:
+            pull()
         for kind, anchor in sched.take_settled():
             event(kind, anchor)
-        if sched.done():
+        if sched.done() and (anchor_source is None or anchor_source.done):
             break
         if sched.blocked_pages:
             arena.evict_retained(sched.blocked_pages)
@@ -798,6 +872,10 @@ def run_join(torch, arena, pipeline, async_ans, anchor_prefixes, stage_suffixes,
             if outstanding:
                 report(outstanding.pop(0))
                 continue
+            if anchor_source is not None and not anchor_source.done:
+                # the source has to move; it may evict retained KV to admit
+                if pull(evict_retained=True, force=True):
+                    continue
             if sched.blocked_pages and arena.evict_retained(sched.blocked_pages):
                 continue
             if arena.drop_holds(held):

@@ -14,6 +14,9 @@ Two kinds of fixtures:
   them bit for bit. host_join_* / host_score_*: the same record of the
   reference's run_join (loop.py:609) over config-2-shaped anchors and
   partners, with 0/1 answers (AI joins) or float32 scores (AI.SCORE).
+- host_feed_*: a filter whose survivors feed a join (FilterStream
+  hold_survivors as run_join's anchor_source): both streams' chunks in
+  launch order, the filter's answers, the admitted anchors and the join's.
 - token_store.arrow + .json: a token store file written by the
   reference's TokenStore (the host input format) and its documents.
 - kernels.npz: seeded inputs and outputs of the reference's fused Triton
@@ -317,6 +320,73 @@ def run_reference_join(name):
     return summary
 
 
+# ---- a filter feeding a join (FilterStream hold_survivors + anchor_source) ----
+
+FEED_SCENARIOS = ("feed_tree", "feed_unified")
+
+
+def feed_inputs(name):
+    """(docs, question, frame, partners, budget, n_pages, attention)."""
+    rng = np.random.default_rng(14)
+    instr = rng.integers(1000, 150000, 32).tolist()
+    docs = [instr + rng.integers(1000, 150000, int(rng.integers(10, 90))).tolist()
+            for _ in range(16)]
+    question = [int(rng.integers(1000, 150000)), 5]
+    frame = rng.integers(1000, 150000, 3).tolist()
+    partners = [rng.integers(1000, 150000, int(rng.integers(6, 30))).tolist()
+                for _ in range(9)]
+    attention = "unified" if name.endswith("unified") else "tree"
+    return docs, question, frame, partners, 350, 200, attention
+
+
+def run_reference_feed(name):
+    from quail.backends.quail.executor import loop
+    from quail.backends.quail.executor.arena import KVArena
+    from quail.backends.quail.executor.models.base import ModelPipeline
+    from quail.execution.tokens import prefix_tree
+
+    _cpu_staging(loop)
+    docs, question, frame, partners, budget, pages, attention = feed_inputs(name)
+    arena = KVArena(1, pages, 16, 1, 8, dtype=torch.bfloat16, device="cpu")
+    arrays, entries = {}, []
+
+    class Recorder(ModelPipeline):
+        tree_attention = True
+
+        def forward_chunk(self, chunk):
+            entries.append(chunk_record(chunk, arrays, len(entries)))
+            return chunk
+
+    class Answers:
+        dtype = None
+
+        def submit(self, chunk):
+            return answer_bits(chunk.input_ids, chunk.positions, chunk.final_indices)
+
+        def result(self, handle):
+            return handle
+
+    source = loop.FilterStream(
+        _Torch(), arena, Recorder(), Answers(), docs, [question], budget, pinned=False,
+        arena_writes=True, arena_keys=[("d", i) for i in range(len(docs))],
+        hold_survivors=True, hold_extra_tokens=len(frame), prefix_tree=prefix_tree(docs, 16),
+        attention_mode=attention)
+    keys = []
+    answers, _, tokens = loop.run_join(
+        _Torch(), arena, Recorder(), Answers(), [], [partners], budget, stage_frames=[frame],
+        anchor_keys=keys, anchor_source=source, attention_mode=attention)
+    summary = dict(name=name, chunks=entries, tokens=int(tokens),
+                   source_tokens=int(source.tokens),
+                   filter_answers={str(k): v for k, v in sorted(source.answers.items())},
+                   keys=[int(key[1]) for key in keys],
+                   answers=[{str(a): [float(x) for x in row] for a, row in sorted(st.items())}
+                            for st in answers],
+                   free_pages_after=int(arena.free_pages))
+    np.savez_compressed(HERE / f"host_{name}.npz", **arrays)
+    (HERE / f"host_{name}.json").write_text(json.dumps(summary, separators=(",", ":")))
+    return summary
+
+
 # ---- token store (quail/execution/tokens.py:180-359) ---------------------------
 
 def make_token_store():
@@ -465,6 +535,11 @@ def main():
             continue
         summary = run_reference_join(name)
         print(name, "chunks", len(summary["chunks"]), "tokens", summary["tokens"])
+    for name in FEED_SCENARIOS:
+        if only and name not in only:
+            continue
+        summary = run_reference_feed(name)
+        print(name, "chunks", len(summary["chunks"]), "anchors", len(summary["keys"]))
     if not only or "token_store" in only:
         make_token_store()
         print("token_store.arrow written")

@@ -207,3 +207,49 @@ def test_executor_join_and_score_api():
         assert row.dtype == np.float32 and len(row) == len(partners[a])
         assert np.all((row >= 0) & (row <= 1))
     assert ex.arena.free_pages == 300
+
+
+def test_tiny_filter_feeding_join_matches_oracle():
+    """A filter whose survivors stream into a join as resident anchors
+    (FilterStream hold_survivors as run_join's anchor_source): every chunk of
+    both loops, in launch order, bit-exact against the oracle."""
+    cfg = TINY
+    weights = random_weights(cfg, seed=7, device="cuda")
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(15)
+    instr = rng.integers(16, cfg.vocab, 32).tolist()
+    docs = [instr + rng.integers(16, cfg.vocab, int(rng.integers(10, 90))).tolist()
+            for _ in range(14)]
+    question = [int(rng.integers(16, cfg.vocab)), 5]
+    frame = rng.integers(16, cfg.vocab, 3).tolist()
+    partners = [rng.integers(16, cfg.vocab, int(rng.integers(6, 30))).tolist() for _ in range(7)]
+    arena = KVArena(cfg.n_layers, 200, 16, cfg.n_kv, cfg.head_dim, device=dev)
+    arena.pools.zero_()
+    pipe = Qwen3Pipeline(torch, weights, arena)
+    rows = AnswerRows(torch, weights)
+    readouts = {"filter": AsyncAnswers(torch, rows, keep_margins=True),
+                "join": AsyncAnswers(torch, rows, keep_margins=True)}
+    launched = []
+    source = loop.FilterStream(
+        torch, arena, pipe, readouts["filter"], docs, [question], 350, arena_writes=True,
+        arena_keys=[("d", i) for i in range(len(docs))], hold_survivors=True,
+        hold_extra_tokens=len(frame), prefix_tree=prefix_tree(docs, 16), attention_mode="tree",
+        device=dev, on_chunk=lambda host, groups: launched.append(("filter", host)))
+    keys = []
+    answers, _, _ = loop.run_join(
+        torch, arena, pipe, readouts["join"], [], [partners], 350, stage_frames=[frame],
+        anchor_keys=keys, anchor_source=source, attention_mode="tree", device=dev,
+        on_chunk=lambda host, groups: launched.append(("join", host)))
+    torch.cuda.synchronize()
+    assert nat.kernel_status(torch.cuda.current_device()) == 0
+    assert keys and len(answers[0]) == len(keys)
+    cpu_w = weights.to("cpu")
+    cpu_arena = of.CpuArena(cfg.n_layers, arena.pool_rows, cfg.n_kv, cfg.head_dim)
+    _, ans_w, tc, fc = cpu_w.answer_rows()
+    got = {kind: iter(r.margins) for kind, r in readouts.items()}
+    for kind, host in launched:
+        normed = of.forward_chunk(cpu_w, host, cpu_arena)
+        want = nx.answer_margin(normed, ans_w, tc, fc)[0].numpy()
+        g = next(got[kind])
+        assert np.array_equal(g.view(np.int32), want.astype(np.float32).view(np.int32)), kind
+    assert not arena.accounting.owned

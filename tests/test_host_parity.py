@@ -247,3 +247,52 @@ def test_filter_over_token_store_matches_reference(tmp_path):
     assert tokens == want["tokens"]
     store.close()
 
+
+@pytest.mark.parametrize("name", mg.FEED_SCENARIOS)
+def test_filter_feeding_join_matches_reference(name):
+    """A filter whose survivors stream into a join as resident anchors
+    (FilterStream hold_survivors as run_join's anchor_source): both loops'
+    chunks in launch order, the filter's answers, the anchors admitted and
+    the join's answers."""
+    docs, question, frame, partners, budget, pages, attention = mg.feed_inputs(name)
+    want = json.loads((GOLDEN / f"host_{name}.json").read_text())
+    want_arrays = np.load(GOLDEN / f"host_{name}.npz")
+    arena = KVArena(1, pages, 16, 1, 8, device=None)
+    arrays, entries = {}, []
+
+    class Recorder(ModelPipeline):
+        tree_attention = True
+
+        def forward_chunk(self, chunk):
+            entries.append(mg.chunk_record(chunk.host, arrays, len(entries)))
+            return chunk.host
+
+    class Answers:
+        dtype = None
+
+        def submit(self, host):
+            return mg.answer_bits(host.input_ids, host.positions, host.final_indices)
+
+        def result(self, handle):
+            return handle
+
+    source = loop.FilterStream(
+        torch, arena, Recorder(), Answers(), docs, [question], budget, arena_writes=True,
+        arena_keys=[("d", i) for i in range(len(docs))], hold_survivors=True,
+        hold_extra_tokens=len(frame), prefix_tree=prefix_tree(docs, 16),
+        attention_mode=attention, device="cpu")
+    keys = []
+    answers, _, tokens = loop.run_join(
+        torch, arena, Recorder(), Answers(), [], [partners], budget, stage_frames=[frame],
+        anchor_keys=keys, anchor_source=source, attention_mode=attention, device="cpu")
+    assert entries == want["chunks"]
+    assert sorted(arrays) == sorted(want_arrays.files)
+    for key in want_arrays.files:
+        assert np.array_equal(arrays[key].astype(np.int64), want_arrays[key].astype(np.int64)), key
+    assert {str(k): v for k, v in sorted(source.answers.items())} == want["filter_answers"]
+    assert [key[1] for key in keys] == want["keys"]
+    assert [{str(a): [float(x) for x in row] for a, row in sorted(st.items())}
+            for st in answers] == want["answers"]
+    assert tokens == want["tokens"] and source.tokens == want["source_tokens"]
+    assert arena.free_pages == want["free_pages_after"]
+
