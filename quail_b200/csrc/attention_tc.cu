@@ -785,6 +785,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         const int h = h0 + 2 * mt + (i >> 6);
                         const float sc = group_scale(amax);
                         const GroupDivider dv(sc);
+                        const bool big = !(amax < 0x1p+100f);  // the quotient range bound
                         uint8_t* out = q_out + ((int64_t)(row < seg_end ? row : row0) * n_q + h) * D;
 #pragma unroll 1
                         for (int c0 = 0; c0 < D; c0 += 32) {
@@ -799,14 +800,14 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                                 yv[4 * u + 3] = v4.w;
                             }
                             float qv[32];
-                            bool rare = false;
+                            bool rare = big;
 #pragma unroll
                             for (int j = 0; j < 16; ++j) {
                                 qv[2 * j] = __uint_as_float(yv[j] << 16);
                                 qv[2 * j + 1] = __uint_as_float(yv[j] & 0xFFFF0000u);
-                                dv.quant2_fast(qv[2 * j], qv[2 * j + 1], rare);
+                                dv.quant2_sat(qv[2 * j], qv[2 * j + 1], rare);
                             }
-                            if (rare) {  // a value outside the one-reciprocal range: IEEE division
+                            if (rare) {  // a zero, tiny or non-finite value: the exact path
 #pragma unroll
                                 for (int j = 0; j < 16; ++j) {
                                     float a = __uint_as_float(yv[j] << 16);
