@@ -104,6 +104,17 @@ def test_qwen3_4b_shaped_rows_match_oracle():
     run_and_compare(cfg, weights, docs, questions, budget=4096, n_pages=200, mode="tree")
 
 
+def test_qwen3_32b_width_rows_match_oracle():
+    """Qwen3-32B's layer shapes (hidden 5120, 64 query / 8 KV heads, inter
+    25600), two layers, on a few config-3-shaped rows."""
+    import dataclasses
+    from quail_b200.model import QWEN3_32B
+    cfg = dataclasses.replace(QWEN3_32B, name="qwen3-32b-2l", n_layers=2)
+    weights = random_weights(cfg, seed=2, device="cuda")
+    docs, questions = rows_with_prefix(3, 2, 96, 16, 48, 1000, 150000)
+    run_and_compare(cfg, weights, docs, questions, budget=4096, n_pages=100, mode="tree")
+
+
 def join_rows(seed, cfg, n_anchors, n_partners, n_stages):
     """Config 2's shape, small: a shared instruction + left document per
     anchor, right documents as partners, a frame per stage."""

@@ -212,7 +212,9 @@ def test_qk_norm_rope_and_kv_append(dev):
 # GQA groups of 2 and 4 run the tcgen05 kernel (one and two 128-row M tiles),
 # an odd group the mma.sync kernel
 ATTN_CONFIGS = {"g2": TINY, "g4": dataclasses.replace(TINY, name="tiny-g4", n_q=8),
-                "g3": dataclasses.replace(TINY, name="tiny-g3", n_q=3, n_kv=1)}
+                "g3": dataclasses.replace(TINY, name="tiny-g3", n_q=3, n_kv=1),
+                # Qwen3-32B's grouping (64 query heads over 8 KV heads)
+                "g8": dataclasses.replace(TINY, name="tiny-g8", n_q=16, n_kv=2)}
 
 
 def _attention_case(mode, dev, seed=0, cfg=TINY):
