@@ -95,6 +95,16 @@ def config3(rows=50_000, seed=0) -> Workload:
                     [_question()], 96)
 
 
+def config4(rows=4_000, seed=0) -> Workload:
+    """Qwen3-4B FP8 long-document filter: a 64-token shared prefix and
+    suffixes uniform in [4096, 16384] tokens, ids uniform in [1000, 150000)."""
+    rng = np.random.default_rng(seed)
+    prefix = rng.integers(1000, 150000, 64)
+    lens = rng.integers(4096, 16385, rows).astype(np.int64)
+    return Workload("config4", "qwen3-4b-fp8", DocRows(prefix, lens, 1000, 150000, seed),
+                    [_question()], 64)
+
+
 @dataclass
 class JoinWorkload:
     """An AI join: anchors (left rows) stream every partner (right row)."""

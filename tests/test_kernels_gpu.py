@@ -217,13 +217,17 @@ ATTN_CONFIGS = {"g2": TINY, "g4": dataclasses.replace(TINY, name="tiny-g4", n_q=
                 "g8": dataclasses.replace(TINY, name="tiny-g8", n_q=16, n_kv=2)}
 
 
-def _attention_case(mode, dev, seed=0, cfg=TINY):
-    """A packed chunk (our packer) with random q/k/v and random resident KV."""
+def _attention_case(mode, dev, seed=0, cfg=TINY, long=False):
+    """A packed chunk (our packer) with random q/k/v and random resident KV.
+    long: two documents past a thousand tokens (config 4's regime: many key
+    tiles per query tile, query tiles deep into a causal segment)."""
     rng = np.random.default_rng(seed)
     prefix = rng.integers(1000, 2000, 64).tolist()
-    lens = rng.integers(1, 150, 12)
+    lens = rng.integers(1, 150, 4 if long else 12)
     docs = [prefix + rng.integers(1000, 2000, int(n)).tolist() for n in lens]
     docs.append(prefix + rng.integers(1000, 2000, 300).tolist())
+    if long:
+        docs += [prefix + rng.integers(1000, 2000, n).tolist() for n in (1200, 700)]
     arena = KVArena(cfg.n_layers, 200, 16, cfg.n_kv, cfg.head_dim, device=dev)
     g = torch.Generator(device="cuda").manual_seed(seed)
     arena.pools.copy_(torch.randn(arena.pools.shape, device=dev, generator=g))
@@ -250,10 +254,11 @@ def _attention_case(mode, dev, seed=0, cfg=TINY):
     return cfg, arena, chunks
 
 
-@pytest.mark.parametrize("group", sorted(ATTN_CONFIGS))
+@pytest.mark.parametrize("case", sorted(ATTN_CONFIGS) + ["long"])
 @pytest.mark.parametrize("mode", ["tree", "unified"])
-def test_attention_against_oracle(dev, mode, group):
-    cfg, arena, chunks = _attention_case(mode, dev, cfg=ATTN_CONFIGS[group])
+def test_attention_against_oracle(dev, mode, case):
+    cfg, arena, chunks = _attention_case(mode, dev, cfg=ATTN_CONFIGS.get(case, TINY),
+                                         long=case == "long")
     eng = Engine(torch, arena, cfg)
     scale = cfg.head_dim ** -0.5
     checked = 0
