@@ -681,7 +681,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                                 const float s0 = c0 + k < lim ? __uint_as_float(sr[k]) : -INFINITY;
                                 const float s1 = c0 + k + 1 < lim ? __uint_as_float(sr[k + 1]) : -INFINITY;
                                 f2unpack(f2fma(f2pack(s0, s1), sl, nm), pv[k], pv[k + 1]);
-                                qexp2f_x2_low(pv[k], pv[k + 1], rare);
+                                qexp2f_x2_softmax(pv[k], pv[k + 1], rare);
                             }
                             if (rare) {  // a subnormal p: the exact two-step scaling
 #pragma unroll

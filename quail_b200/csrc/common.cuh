@@ -354,6 +354,32 @@ __device__ __forceinline__ void qexp2f_x2_low(float& a, float& b, bool& rare) {
     b = nb < -126 ? 0.0f : b;
 }
 
+// qexp2f_x2_low with the scale folded into the clamp: x is clamped at -127,
+// where n = -127 gives the scale bits 0 and so 2^x = 0 without a select;
+// *rare is set for x in [-150.5, -126.5) (a subnormal result, redone with
+// qexp2f_x2 by the caller); x below -150.5 (masked keys: -inf) gives 0 as
+// qexp2f does, NaN stays NaN. For x <= 1 (softmax exponents).
+__device__ __forceinline__ void qexp2f_x2_softmax(float& a, float& b, bool& rare) {
+    rare |= ((a < -126.5f) & (a >= -150.5f)) | ((b < -126.5f) & (b >= -150.5f));
+    const uint64_t M = f2pack(12582912.0f, 12582912.0f);
+    float ac, bc;
+    asm("max.NaN.f32 %0, %1, 0fC2FE0000;" : "=f"(ac) : "f"(a));  // -127
+    asm("max.NaN.f32 %0, %1, 0fC2FE0000;" : "=f"(bc) : "f"(b));
+    const uint64_t x = f2pack(ac, bc);
+    const uint64_t t = f2add(x, M);
+    const uint64_t f = f2sub(x, f2sub(t, M));
+    uint64_t p = f2pack(QB_EXP2_C7, QB_EXP2_C7);
+#define QB_STEP6(c) p = f2fma(p, f, f2pack(c, c));
+    QB_EXP2_POLY(QB_STEP6)
+#undef QB_STEP6
+    float ta, tb;
+    f2unpack(t, ta, tb);
+    constexpr uint32_t K = (127u - 0x4B400000u) << 23;  // 2^n bits: (bits(t) << 23) + K
+    f2unpack(f2mul(p, f2pack(__uint_as_float((__float_as_uint(ta) << 23) + K),
+                             __uint_as_float((__float_as_uint(tb) << 23) + K))),
+             a, b);
+}
+
 // two sigmoidf_ref at once (same bits on each)
 __device__ __forceinline__ void sigmoidf_ref_x2(float& a, float& b) {
     float ea, eb;

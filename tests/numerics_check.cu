@@ -10,14 +10,16 @@
 //      the positive NaNs)
 //   3  quant2_sat (+ the group bound and exact redo) vs quant2, e4m3 codes,
 //      on 64 group scales x 2^24 values of the group each
+//   4  qexp2f_x2_softmax (+ exact redo when rare) vs qexp2f, every x <= 1
+//      (every negative float, zeros, positives up to 1.0, -inf and NaNs)
 #include "common.cuh"
 
 using namespace qb;
 
 namespace {
 
-__device__ unsigned long long g_bad[4];
-__device__ unsigned int g_first[4];
+__device__ unsigned long long g_bad[5];
+__device__ unsigned int g_first[5];
 
 __device__ void record(int which, uint32_t bits) {
     atomicAdd(&g_bad[which], 1ull);
@@ -117,13 +119,43 @@ __global__ void check_quant(const float* amaxes) {
     }
 }
 
+// all bit patterns with sign 1 (negatives, -0, -inf, NaNs) and the
+// non-negative ones up to 1.0f
+__global__ void check_exp2_softmax() {
+    const uint64_t n = (1ull << 31) + 0x3F800001ull;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+         i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t ba = i < (1ull << 31) ? (uint32_t)i | 0x80000000u
+                                              : (uint32_t)(i - (1ull << 31));
+        const uint32_t bb = ba ^ 0x00400001u;  // a second lane value nearby
+        const float xa = __uint_as_float(ba);
+        const float xb = (__uint_as_float(bb) <= 1.0f || __uint_as_float(bb) != __uint_as_float(bb))
+                             ? __uint_as_float(bb) : xa;
+        float a = xa, b = xb;
+        bool rare = false;
+        qexp2f_x2_softmax(a, b, rare);
+        if (rare) {
+            a = xa;
+            b = xb;
+            qexp2f_x2(a, b);
+        }
+        const float wa = qexp2f(xa);
+        const bool nan_a = wa != wa;
+        if (nan_a ? (a == a) : (__float_as_uint(a) != __float_as_uint(wa))) record(4, ba);
+        const float wb = qexp2f(xb);
+        const bool nan_b = wb != wb;
+        if (nan_b ? (b == b) : (__float_as_uint(b) != __float_as_uint(wb)))
+            record(4, __float_as_uint(xb));
+    }
+}
+
 }  // namespace
 
-// bad[4], first[4] (host): mismatch counts and the smallest mismatching
+// bad[5], first[5] (host): mismatch counts and the smallest mismatching
 // input bits of each check. Returns a cudaError_t.
 extern "C" int qbn_run_checks(unsigned long long* bad, unsigned int* first) {
-    unsigned long long zero[4] = {0, 0, 0, 0};
-    unsigned int ones[4] = {0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu};
+    unsigned long long zero[5] = {0, 0, 0, 0, 0};
+    unsigned int ones[5] = {0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu};
     cudaMemcpyToSymbol(g_bad, zero, sizeof(zero));
     cudaMemcpyToSymbol(g_first, ones, sizeof(ones));
     check_rcp<<<148 * 8, 256>>>(0x00800000u, 0x7E800000u);
@@ -140,6 +172,7 @@ extern "C" int qbn_run_checks(unsigned long long* bad, unsigned int* first) {
     cudaMalloc(&amax_dev, sizeof(amax_host));
     cudaMemcpy(amax_dev, amax_host, sizeof(amax_host), cudaMemcpyHostToDevice);
     check_quant<<<dim3(256, 64), 256>>>(amax_dev);
+    check_exp2_softmax<<<148 * 8, 256>>>();
     cudaError_t err = cudaDeviceSynchronize();
     cudaFree(amax_dev);
     if (err != cudaSuccess) return (int)err;
