@@ -231,7 +231,8 @@ def run_reference_scenario(name):
 # ---- join scenarios (run_join, loop.py:609-978) ------------------------------
 
 JOIN_SCENARIOS = ("join_tree", "join_unified", "join_stages_tree", "join_stages_unified",
-                  "join_tight_unified", "score_tree", "score_unified")
+                  "join_tight_unified", "score_tree", "score_unified", "join_edges_tree",
+                  "join_resident_unified")
 
 
 def join_inputs(name):
@@ -243,12 +244,12 @@ def join_inputs(name):
     AI.SCORE streams a per-anchor subset of the partners."""
     seed = {"join_tree": 10, "join_unified": 10, "join_stages_tree": 11,
             "join_stages_unified": 11, "join_tight_unified": 12, "score_tree": 13,
-            "score_unified": 13}[name]
+            "score_unified": 13, "join_edges_tree": 16, "join_resident_unified": 17}[name]
     rng = np.random.default_rng(seed)
     instr = rng.integers(1000, 150000, 48).tolist()
     anchors = [instr + rng.integers(1000, 150000, int(rng.integers(20, 100))).tolist()
                for _ in range(10)]
-    n_stages = 2 if "stages" in name else 1
+    n_stages = 2 if ("stages" in name or "edges" in name) else 1
     stage_suffixes = [[rng.integers(1000, 150000, int(rng.integers(8, 40))).tolist()
                        for _ in range(12 - 3 * j)] for j in range(n_stages)]
     score = name.startswith("score")
@@ -256,14 +257,24 @@ def join_inputs(name):
                                  for j in range(n_stages)]
     partners = None
     if score:
-        partners = [sorted(int(i) for i in rng.choice(12, size=int(rng.integers(1, 12)),
-                                                       replace=False))
+        partners = [[sorted(int(i) for i in rng.choice(12, size=int(rng.integers(1, 12)),
+                                                        replace=False))]
                     for _ in anchors]
+    if "edges" in name:
+        # per-anchor partner lists with empty ones: anchor 1 has none at the
+        # first stage (settles without a chunk, dropped), anchor 2 none at
+        # the last (an empty row once it passes), anchor 3 one partner each
+        partners = [[None, None] for _ in anchors]
+        partners[1] = [[], None]
+        partners[2] = [None, []]
+        partners[3] = [[4], [0]]
     budget, pages = 400, 300
     if "tight" in name:
         budget, pages = 500, 40
+    # anchors already resident (their prefix KV in the arena): 0, 3, 7
+    resident = (0, 3, 7) if "resident" in name else ()
     attention = "unified" if name.endswith("unified") else "tree"
-    return anchors, stage_suffixes, frames, partners, budget, pages, attention
+    return anchors, stage_suffixes, frames, partners, budget, pages, attention, resident
 
 
 def score_values(input_ids, positions, finals):
@@ -281,8 +292,13 @@ def run_reference_join(name):
     from quail.execution.tokens import prefix_tree
 
     _cpu_staging(loop)
-    anchors, stage_suffixes, frames, partners, budget, pages, attention = join_inputs(name)
+    anchors, stage_suffixes, frames, partners, budget, pages, attention, resident = \
+        join_inputs(name)
     arena = KVArena(1, pages, 16, 1, 8, dtype=torch.bfloat16, device="cpu")
+    frame_max = max(len(f) for f in frames) if frames else 0
+    for a in resident:
+        assert arena.activate(("a", a), len(anchors[a]),
+                              capacity_tokens=len(anchors[a]) + frame_max) is not None
     arrays, entries = {}, []
     score = name.startswith("score")
 
@@ -308,7 +324,7 @@ def run_reference_join(name):
     answers, _, tokens = loop.run_join(
         _Torch(), arena, Recorder(), Answers(), anchors, stage_suffixes, budget,
         stage_frames=frames, anchor_keys=keys, attention_mode=attention,
-        anchor_partners=None if partners is None else (lambda key: [partners[key[1]]]),
+        anchor_partners=None if partners is None else (lambda key: partners[key[1]]),
         prefix_tree=prefix_tree(anchors, 16), stats=stats)
     summary = dict(name=name, chunks=entries, tokens=int(tokens),
                    borrowed_tokens=int(stats.get("borrowed_tokens", 0)),

@@ -77,8 +77,13 @@ def test_packed_chunks_match_reference(name):
 
 
 def run_ours_join(name):
-    anchors, stage_suffixes, frames, partners, budget, pages, attention = mg.join_inputs(name)
+    anchors, stage_suffixes, frames, partners, budget, pages, attention, resident = \
+        mg.join_inputs(name)
     arena = KVArena(1, pages, 16, 1, 8, device=None)
+    frame_max = max(len(f) for f in frames) if frames else 0
+    for a in resident:
+        assert arena.activate(("a", a), len(anchors[a]),
+                              capacity_tokens=len(anchors[a]) + frame_max) is not None
     arrays, entries = {}, []
     score = name.startswith("score")
 
@@ -104,7 +109,7 @@ def run_ours_join(name):
     answers, _, tokens = loop.run_join(
         torch, arena, Recorder(), Answers(), anchors, stage_suffixes, budget,
         stage_frames=frames, anchor_keys=keys, attention_mode=attention,
-        anchor_partners=None if partners is None else (lambda key: [partners[key[1]]]),
+        anchor_partners=None if partners is None else (lambda key: partners[key[1]]),
         prefix_tree=prefix_tree(anchors, 16), stats=stats, device="cpu")
     return dict(entries=entries, arrays=arrays, tokens=tokens, answers=answers, stats=stats,
                 arena=arena)
