@@ -107,10 +107,6 @@ struct GroupDivider {
     }
     // quant of two values with f32x2 arithmetic (same bits as quant on each)
     __device__ __forceinline__ void quant2(float& a, float& b) const;
-    // quant2 without its rare branch: exact unless a value is outside
-    // [2^-96, 2^100) in magnitude (or not finite), which sets *rare; the
-    // caller then redoes the values with quant2
-    __device__ __forceinline__ void quant2_fast(float& a, float& b, bool& rare) const;
     // quant2 for the saturating e4m3 conversion, which clamps a finite
     // quotient to +-448 as quant2 does: RN(y / s) without the clamp. Exact
     // for |y| in [2^-96, 2^100); *rare is set for |y| < 2^-96 (zeros too: the
@@ -205,18 +201,6 @@ __device__ __forceinline__ void GroupDivider::quant2(float& a, float& b) const {
     b = fminf(fmaxf(b, -QB_FP8_MAX), QB_FP8_MAX);
 }
 
-__device__ __forceinline__ void GroupDivider::quant2_fast(float& a, float& b, bool& rare) const {
-    const float fa = fabsf(a), fb = fabsf(b);
-    rare |= !(fa >= 0x1p-96f && fa < 0x1p+100f && fb >= 0x1p-96f && fb < 0x1p+100f &&
-              s < INFINITY);
-    const uint64_t y = f2pack(a, b), rr = f2pack(r, r);
-    const uint64_t q0 = f2mul(y, rr);
-    const uint64_t e = f2fma(f2pack(-s, -s), q0, y);
-    f2unpack(f2fma(e, rr, q0), a, b);
-    a = fminf(fmaxf(a, -QB_FP8_MAX), QB_FP8_MAX);
-    b = fminf(fmaxf(b, -QB_FP8_MAX), QB_FP8_MAX);
-}
-
 __device__ __forceinline__ void GroupDivider::quant2_sat(float& a, float& b, bool& rare) const {
     rare |= !(fabsf(a) >= 0x1p-96f) | !(fabsf(b) >= 0x1p-96f);
     const uint64_t y = f2pack(a, b), rr = f2pack(r, r);
@@ -301,64 +285,12 @@ __device__ __forceinline__ float sigmoidf_ref(float x) {
     return __frcp_rn(__fadd_rn(1.0f, qexpf(-x)));
 }
 
-// qexp2f_x2 without its rare branch: exact unless a lane's result is
-// subnormal (n < -126, x above the clamp), which sets *rare; the caller then
-// redoes the values with qexp2f_x2. Branch-free, so independent pairs
-// interleave.
-__device__ __forceinline__ void qexp2f_x2_fast(float& a, float& b, bool& rare) {
-    const uint64_t M = f2pack(12582912.0f, 12582912.0f);
-    const float ac = exp2_clamp(a), bc = exp2_clamp(b);
-    const uint64_t x = f2pack(ac, bc);
-    const uint64_t t = f2add(x, M);
-    const uint64_t f = f2sub(x, f2sub(t, M));
-    uint64_t p = f2pack(QB_EXP2_C7, QB_EXP2_C7);
-#define QB_STEP3(c) p = f2fma(p, f, f2pack(c, c));
-    QB_EXP2_POLY(QB_STEP3)
-#undef QB_STEP3
-    float ta, tb;
-    f2unpack(t, ta, tb);
-    // n < -126: a subnormal result, except at the clamp x = -150 (masked keys,
-    // -inf), where 2^-150 rounds to exactly 0
-    const bool sa = __float_as_int(ta) - 0x4B400000 < -126;
-    const bool sb = __float_as_int(tb) - 0x4B400000 < -126;
-    rare |= (sa & (ac > -150.0f)) | (sb & (bc > -150.0f));
-    f2unpack(f2mul(p, f2pack(exp2_scale(ta), exp2_scale(tb))), a, b);
-    a = sa ? 0.0f : a;
-    b = sb ? 0.0f : b;
-}
-
-// qexp2f_x2_fast for exponents below 128 (softmax: s sl2 - m sl2 <= 0): the
-// clamp is -160 below only, so x <= -150.5 gives exactly 0 as qexp2f does
-// (2^-150.5 is under half the smallest subnormal); *rare is set when a
-// lane's n is in [-150, -127] (a subnormal, or 0 from qexp2f's clamp at
-// -150), and the caller redoes the pair with qexp2f_x2. NaN stays NaN.
-__device__ __forceinline__ void qexp2f_x2_low(float& a, float& b, bool& rare) {
-    const uint64_t M = f2pack(12582912.0f, 12582912.0f);
-    float ac, bc;
-    asm("max.NaN.f32 %0, %1, 0fC3200000;" : "=f"(ac) : "f"(a));  // -160
-    asm("max.NaN.f32 %0, %1, 0fC3200000;" : "=f"(bc) : "f"(b));
-    const uint64_t x = f2pack(ac, bc);
-    const uint64_t t = f2add(x, M);
-    const uint64_t f = f2sub(x, f2sub(t, M));
-    uint64_t p = f2pack(QB_EXP2_C7, QB_EXP2_C7);
-#define QB_STEP4(c) p = f2fma(p, f, f2pack(c, c));
-    QB_EXP2_POLY(QB_STEP4)
-#undef QB_STEP4
-    float ta, tb;
-    f2unpack(t, ta, tb);
-    const int na = __float_as_int(ta) - 0x4B400000, nb = __float_as_int(tb) - 0x4B400000;
-    rare |= ((unsigned)(na + 150) < 24u) | ((unsigned)(nb + 150) < 24u);
-    f2unpack(f2mul(p, f2pack(__int_as_float((na + 127) << 23), __int_as_float((nb + 127) << 23))),
-             a, b);
-    a = na < -126 ? 0.0f : a;
-    b = nb < -126 ? 0.0f : b;
-}
-
-// qexp2f_x2_low with the scale folded into the clamp: x is clamped at -127,
-// where n = -127 gives the scale bits 0 and so 2^x = 0 without a select;
-// *rare is set for x in [-150.5, -126.5) (a subnormal result, redone with
-// qexp2f_x2 by the caller); x below -150.5 (masked keys: -inf) gives 0 as
-// qexp2f does, NaN stays NaN. For x <= 1 (softmax exponents).
+// qexp2f_x2 without its rare branch, for x <= 1 (softmax exponents): x is
+// clamped at -127, where n = -127 gives the scale bits 0 and so 2^x = 0
+// without a select; *rare is set for x in [-150.5, -126.5) (a subnormal
+// result, redone with qexp2f_x2 by the caller); x below -150.5 (masked
+// keys: -inf) gives 0 as qexp2f does (2^-150.5 is under half the smallest
+// subnormal), NaN stays NaN.
 __device__ __forceinline__ void qexp2f_x2_softmax(float& a, float& b, bool& rare) {
     rare |= ((a < -126.5f) & (a >= -150.5f)) | ((b < -126.5f) & (b >= -150.5f));
     const uint64_t M = f2pack(12582912.0f, 12582912.0f);
