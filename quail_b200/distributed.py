@@ -63,3 +63,40 @@ def run_sharded(torch, dist, n_rows, run_slice, device="cpu"):
     if len(all_bits) != n_rows:
         raise RankFailed(f"gathered {len(all_bits)} rows, expected {n_rows}")
     return all_bits.astype(np.uint8), all_margins
+
+
+def run_sharded_join(torch, dist, n_anchors, n_stages, run_slice, device="cpu"):
+    """A join sharded by anchor (config 2 shards by left row, coordinator.py:
+    125-207): run_slice(lo, hi) runs this rank's anchors [lo, hi) and returns
+    answers[stage][local anchor] -> row; every rank gets the rows of all
+    anchors, keyed by global anchor index. Raises RankFailed on every rank
+    when any rank raised."""
+    rank, world = dist.get_rank(), dist.get_world_size()
+    lo, hi = shard(n_anchors, rank, world)
+    error = None
+    answers = [dict() for _ in range(n_stages)]
+    try:
+        answers = run_slice(lo, hi)
+    except Exception as exc:  # reported to every rank below
+        error = exc
+    ok = torch.tensor([0 if error is not None else 1], dtype=torch.int32, device=device)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if int(ok) == 0:
+        raise RankFailed(f"rank {rank}: a rank failed during the sharded join") from error
+    out = []
+    for j in range(n_stages):
+        stage = answers[j] if j < len(answers) else {}
+        local = sorted(stage)
+        ids = np.asarray([lo + a for a in local], dtype=np.float32)
+        lens = np.asarray([len(stage[a]) for a in local], dtype=np.float32)
+        vals = (np.concatenate([np.asarray(stage[a], dtype=np.float32) for a in local])
+                if local else np.zeros(0, dtype=np.float32))
+        g_ids = gather_rows(torch, dist, ids, device).astype(np.int64)
+        g_lens = gather_rows(torch, dist, lens, device).astype(np.int64)
+        g_vals = gather_rows(torch, dist, vals, device)
+        rows, at = {}, 0
+        for a, n in zip(g_ids, g_lens):
+            rows[int(a)] = g_vals[at:at + n]
+            at += n
+        out.append(rows)
+    return out

@@ -20,7 +20,7 @@ import torch.multiprocessing as mp
 
 from quail_b200 import loop
 from quail_b200.arena import KVArena
-from quail_b200.distributed import RankFailed, run_sharded
+from quail_b200.distributed import RankFailed, run_sharded, run_sharded_join
 from quail_b200.pipeline import ModelPipeline
 from quail_b200.tokens import prefix_tree
 
@@ -58,6 +58,40 @@ def cpu_filter(docs):
     return bits, margins
 
 
+def make_join():
+    rng = np.random.default_rng(12)
+    instr = rng.integers(100, 900, 32).tolist()
+    anchors = [instr + rng.integers(100, 900, int(n)).tolist() for n in rng.integers(8, 60, 11)]
+    stages = [[rng.integers(100, 900, int(n)).tolist() for n in rng.integers(4, 20, k)]
+              for k in (7, 5)]
+    frames = [[3, 4], [5]]
+    return anchors, stages, frames
+
+
+def cpu_join(anchors, stages, frames):
+    """A two-stage join on the CPU with the same deterministic answer model."""
+    arena = KVArena(1, 256, 16, 1, 8, device=None)
+
+    class Rec(ModelPipeline):
+        def forward_chunk(self, chunk):
+            return chunk.host
+
+    class Ans:
+        dtype = None
+
+        def submit(self, host):
+            fin = host.final_indices
+            return list(((host.input_ids[fin] + host.positions[fin]) % 2).astype(int))
+
+        def result(self, h):
+            return h
+
+    answers, _, _ = loop.run_join(torch, arena, Rec(), Ans(), anchors, stages, 300,
+                                  stage_frames=frames, attention_mode="tree",
+                                  prefix_tree=prefix_tree(anchors, 16), device="cpu")
+    return answers
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -79,6 +113,17 @@ def _worker(rank, world, port, mode, out):
 
         if mode == "exit" and rank == 1:
             os._exit(0)    # leaves between steps; nothing in flight
+        if mode.startswith("join"):
+            anchors, stages, frames = make_join()
+
+            def run_join_slice(lo, hi):
+                if mode == "join_raise" and rank == 0:
+                    raise ValueError("injected host failure")
+                return cpu_join(anchors[lo:hi], stages, frames)
+
+            rows = run_sharded_join(torch, dist, len(anchors), len(stages), run_join_slice)
+            out.put((rank, "ok", [{a: r.tolist() for a, r in st.items()} for st in rows], None))
+            return
         bits, margins = run_sharded(torch, dist, len(docs), run_slice)
         out.put((rank, "ok", bits.tolist(), margins.tolist()))
     except RankFailed as exc:
@@ -134,3 +179,22 @@ def test_an_exiting_rank_ends_the_others_collective_with_an_error():
     results = run_ranks("exit")
     kind, msg, _ = results[0]
     assert kind != "ok"
+
+
+def test_two_ranks_reproduce_single_process_join():
+    """A two-stage join sharded by anchor over two gloo ranks: every rank
+    ends with the rows the single-process join gives, keyed by anchor."""
+    anchors, stages, frames = make_join()
+    want = cpu_join(anchors, stages, frames)
+    want = [{a: [float(x) for x in row] for a, row in st.items()} for st in want]
+    results = run_ranks("join")
+    for rank in (0, 1):
+        kind, rows, _ = results[rank]
+        assert kind == "ok"
+        assert rows == want
+
+
+def test_a_raising_rank_fails_every_rank_of_a_join():
+    results = run_ranks("join_raise")
+    assert {k for k, _, _ in results.values()} == {"RankFailed"}
+
