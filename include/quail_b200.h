@@ -113,6 +113,29 @@ int qb_qknorm_rope(const void* qkv, int64_t qkv_ld, const int64_t* positions,
                    int64_t pool_rows, void* stream);
 
 /*
+ * The qkv projection and qb_qknorm_rope in one kernel: the same bits as
+ * qb_gemm_fp8_bs(a, w, n = (n_q + 2 n_kv) * 128) into a bf16 qkv followed by
+ * qb_qknorm_rope(qkv, ...), without the bf16 [m, n] intermediate: q and k
+ * normalised and rotated, v copied, k and v appended to the pools at
+ * row_dst. Replaces engine.gemm(q_in, q_scale, attn.qkv_proj) +
+ * custom_qk_norm_rope + the v slice + kv_row_scatter (quail/backends/quail/
+ * executor/models/qwen3.py:61-64; attention.py:129-141, 363-409, 673-688,
+ * 725-736). a, a_scale, a_scale_ld, w, w_scale: as qb_gemm_fp8_bs with
+ * n = (n_q + 2 n_kv) * 128 weight rows (q | k | v heads), n_q + 2 n_kv even;
+ * the rest as qb_qknorm_rope, with cos_sin, q_w and k_w 16-byte aligned and
+ * pool_rows < 2^31. head_dim == 128.
+ */
+int qb_gemm_fp8_qknorm_rope(const void* a, const float* a_scale,
+                            int64_t a_scale_ld, const void* w,
+                            const float* w_scale, int64_t m, int64_t k,
+                            const int64_t* positions, const void* cos_sin,
+                            int64_t max_pos, const void* q_w, const void* k_w,
+                            float eps, int n_q, int n_kv, int head_dim,
+                            void* q_out, void* k_out, void* v_out,
+                            const int64_t* row_dst, void* k_pool, void* v_pool,
+                            int64_t pool_rows, void* stream);
+
+/*
  * Builds the per-row destination map the fused KV append reads:
  * row_dst[r] = dst[i] where src[i] == r, else -1.
  * Replaces nothing by itself; it turns the reference's (kv_src, kv_dst)

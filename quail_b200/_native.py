@@ -46,6 +46,8 @@ SIGNATURES = {
                              _P, _P, _I64, _I32, _F32, _P, _P, _I64, _P],
     "qb_silu_mul_quant": [_P, _I64, _I64, _P, _P, _I64, _P],
     "qb_gemm_fp8_silu_quant": [_P, _P, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P],
+    "qb_gemm_fp8_qknorm_rope": [_P, _P, _I64, _P, _P, _I64, _I64, _P, _P, _I64, _P, _P, _F32,
+                                _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _I64, _P],
     "qb_final_norm": [_P, _P, _I64, _I64, _P, _I64, _P, _F32, _P, _P],
     "qb_answer_margin": [_P, _I64, _I64, _P, _I32, _P, _I32, _P, _I32, _P, _P, _P],
     "qb_answer_score": [_P, _I64, _I64, _P, _I32, _P, _I32, _P, _I32, _P, _P],

@@ -394,6 +394,17 @@ __device__ __forceinline__ void bf16x8_to_float(const uint4& v, float* f) {
     }
 }
 
+// (a, b) rounded to nearest even bf16, a in the low half
+__device__ __forceinline__ uint32_t bf16x2_bits(float a, float b) {
+    const bf162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// the two bf16 halves of u (low first) as floats, exactly
+__device__ __forceinline__ float2 bf16x2_float2(uint32_t u) {
+    return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+
 __device__ __forceinline__ uint4 float_to_bf16x8(const float* f) {
     uint4 v;
     bf162* h = reinterpret_cast<bf162*>(&v);

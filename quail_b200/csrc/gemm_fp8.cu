@@ -60,7 +60,8 @@ constexpr int SCALE_SLOTS = 8;
 // written through a 128-byte-swizzled shared-memory staging area by TMA
 // stores (one 32 x 64 box per epilogue warp) instead of per-thread row
 // stores, so the epilogue returns to the next tile at once.
-template <int BN, int NST = MAX_STAGES, bool TSTORE = false, bool SILU = false>
+template <int BN, int NST = MAX_STAGES, bool TSTORE = false, bool SILU = false,
+          bool ROPE = false>
 struct Cfg {
     static constexpr int STAGES = NST;
     static_assert(NST >= 2 && NST <= MAX_STAGES, "stages");
@@ -71,12 +72,18 @@ struct Cfg {
     static constexpr int TMEM_COLS = NBUF * BN;  // all 512 columns
     static constexpr int SLICE = BN / 4;      // columns per epilogue warp
     static_assert(!TSTORE || SLICE == 64, "TMA-store staging rows are 128 bytes");
-    static constexpr int OUT_BYTES = TSTORE ? EPI_WARPS * 32 * SLICE * 2 : 0;
+    // TSTORE: one 32 x 64 bf16 staging box per epilogue warp; ROPE: the same
+    // 4 KB per warp holds the pair's sum-of-squares partials, then the two
+    // 32 x 32 output boxes (64-byte swizzle)
+    static constexpr int OUT_BYTES = (TSTORE || ROPE) ? EPI_WARPS * 32 * SLICE * 2 : 0;
     static constexpr int SCALE_OFF = STAGES * STAGE_BYTES + OUT_BYTES;
     static_assert(!SILU || (BN == 256 && !TSTORE), "SILU tiles are 128 gate + 128 up columns");
-    // SILU: per-row group max partials, [2 tile parities][4 slices][BM rows]
+    static_assert(!ROPE || (BN == 256 && !TSTORE && !SILU), "ROPE tiles are two heads");
+    // SILU: per-row group max partials, [2 tile parities][4 slices][BM rows];
+    // ROPE: the q and k norm weights (2 x 128 bf16), then each epilogue
+    // warp's 32 rows of (position, KV destination)
     static constexpr int RED_OFF = SCALE_OFF + SCALE_SLOTS * 528;
-    static constexpr int RED_BYTES = SILU ? 2 * 4 * BM * 4 : 0;
+    static constexpr int RED_BYTES = SILU ? 2 * 4 * BM * 4 : ROPE ? 512 + EPI_WARPS * 32 * 16 : 0;
     static constexpr int BAR_OFF = RED_OFF + RED_BYTES;
     static constexpr int BAR_BYTES = 512;
     static constexpr int SMEM = BAR_OFF + BAR_BYTES + 1024;
@@ -101,9 +108,35 @@ struct Barriers {
     uint64_t scale_full[SCALE_SLOTS];
     uint64_t scale_empty[SCALE_SLOTS];
     uint64_t drain;
-    uint64_t red_full[2];  // SILU: a tile's group-max partials are in shared memory
+    uint64_t red_full[2];  // SILU: a tile's partials are in shared memory
+    // ROPE: per warp pair (the two halves of a head's rows), [0] the pair's
+    // partials are staged, [1] both have read them
+    uint64_t pair[2][8];
     uint32_t tmem_base;
     int abort;
+};
+static_assert(sizeof(Barriers) <= 512, "barrier block");
+
+// ROPE: the q/k norm + rotary + KV append of qb_qknorm_rope, applied in the
+// qkv GEMM's epilogue (arguments as that entry point takes them)
+struct RopeArgs {
+    // bf16 [rows, width] maps, box 32 x 32, 64-byte swizzle: q_out, k_out,
+    // v_out, k_pool, v_pool (the pools only with row_dst)
+    CUtensorMap map_q, map_k, map_v, map_kp, map_vp;
+    const int64_t* positions;
+    const bf16* cos_sin;
+    int64_t max_pos;
+    const bf16* q_w;
+    const bf16* k_w;
+    float eps;
+    int n_q, n_kv;
+    bf16* q_out;
+    bf16* k_out;
+    bf16* v_out;
+    const int64_t* row_dst;
+    bf16* k_pool;
+    bf16* v_pool;
+    int64_t pool_rows;
 };
 
 __device__ __forceinline__ void mma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
@@ -132,15 +165,15 @@ __device__ __forceinline__ void fma2(float* acc, const uint32_t* v, float s) {
 // q_scale[j * q_scale_ld + row]).
 // map_c (bf16 out, box 64 x 32, 128-byte swizzle) is read only when TSTORE.
 template <int BN, typename OutT = bf16, int NST = MAX_STAGES, bool TSTORE = false,
-          bool SILU = false>
+          bool SILU = false, bool ROPE = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                    const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_c, const float* __restrict__ a_scale,
                    int64_t a_scale_ld, const float* __restrict__ w_scale, OutT* __restrict__ out,
                    float* __restrict__ q_scale, int64_t q_scale_ld, int M, int N, int K,
-                   uint32_t* status) {
-    using C = Cfg<BN, NST, TSTORE, SILU>;
+                   uint32_t* status, const __grid_constant__ RopeArgs rope) {
+    using C = Cfg<BN, NST, TSTORE, SILU, ROPE>;
     constexpr int STAGES = C::STAGES;
     static_assert(!TSTORE || sizeof(OutT) == 2, "TMA stores write bf16");
     static_assert(!SILU || sizeof(OutT) == 1, "SILU writes fp8");
@@ -174,6 +207,10 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
         mbar_init(&bars->drain, 1);
         mbar_init(&bars->red_full[0], EPI_WARPS);
         mbar_init(&bars->red_full[1], EPI_WARPS);
+        for (int p = 0; p < 8; ++p) {
+            mbar_init(&bars->pair[0][p], 2);
+            mbar_init(&bars->pair[1][p], 2);
+        }
         bars->abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -183,6 +220,14 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                      "r"(C::TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if constexpr (ROPE) {
+        // the norm weights, 16 bytes a lane: q_w by lanes 0-15, k_w by 16-31
+        if (warp == 2) {
+            const bf16* src = lane < 16 ? rope.q_w + lane * 8 : rope.k_w + (lane - 16) * 8;
+            reinterpret_cast<uint4*>(smem + C::RED_OFF)[lane] =
+                *reinterpret_cast<const uint4*>(src);
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -312,17 +357,34 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
         // ---------------- epilogue: promote, accumulate, store ----------------
         const int ew = warp - FIRST_EPI_WARP;
         const int quarter = warp & 3;          // TMEM lanes this warp may access
-        // its column slice (SILU: gate columns col0.., up columns 128 + col0..)
-        const int col0 = (ew >> 2) * (SILU ? 32 : C::SLICE);
+        // its column slice (SILU: gate columns col0.., up columns 128 + col0..;
+        // ROPE: head (ew / 4) / 2 of the tile, its columns 32 s.. and 64 + 32 s..
+        // for s = (ew / 4) % 2: the rotary lanes 16 s .. 16 s + 15)
+        const int col0 = SILU ? (ew >> 2) * 32
+                              : ROPE ? ((ew >> 2) >> 1) * 128 + ((ew >> 2) & 1) * 32
+                                     : (ew >> 2) * C::SLICE;
         const int row_in_tile = quarter * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-        int acc_it = 0, tcount = 0;
+        int acc_it = 0, tcount = 0, rcount = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++tcount) {
             const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
             const int m = m0 + row_in_tile;
             const bool valid = m < M;
             const int wblk = col0 / 128;
+            if constexpr (ROPE) {
+                // the row's position and KV destination, landed by the tile's end
+                if (valid) {
+                    const uint32_t pd = smem_u32(smem + C::RED_OFF + 512 + (ew * 32 + lane) * 16);
+                    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(pd),
+                                 "l"(rope.positions + m)
+                                 : "memory");
+                    if (rope.row_dst)
+                        asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(pd + 8),
+                                     "l"(rope.row_dst + m)
+                                     : "memory");
+                }
+            }
             float acc[C::SLICE];
 #pragma unroll
             for (int j = 0; j < C::SLICE; ++j) acc[j] = 0.0f;
@@ -348,8 +410,9 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                 for (int c = 0; c < C::SLICE; c += 32) {
                     // two loads in flight per wait
                     uint32_t v[32];
-                    // SILU: the second 32 columns are the up half's
-                    const uint32_t cc = (SILU && c > 0) ? 128u : (uint32_t)c;
+                    // SILU: the second 32 columns are the up half's; ROPE: the
+                    // head's second half
+                    const uint32_t cc = (SILU && c > 0) ? 128u : (ROPE && c > 0) ? 64u : (uint32_t)c;
                     tmem_ld16_nowait(taddr + cc, v);
                     tmem_ld16_nowait(taddr + cc + 16u, v + 16);
                     tmem_wait_ld();
@@ -432,6 +495,199 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                     *reinterpret_cast<uint4*>(dst + 16) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
                     if (col0 == 0) q_scale[(int64_t)j * q_scale_ld + m] = scale;
                 }
+            } else if constexpr (ROPE) {
+                // qb_qknorm_rope on this tile's two heads, bit for bit. Lane L
+                // of that kernel's warp holds columns 2L, 2L + 1, 64 + 2L,
+                // 65 + 2L of a head row; here warp sub (0 or 1) of a pair holds
+                // lanes 16 sub .. 16 sub + 15 of every row, and the pair swaps
+                // its sum-of-squares lane partials through the staging areas to
+                // run warp_sum's xor tree (16, 8, 4, 2, 1).
+                const int sl = ew >> 2, hh = sl >> 1, sub = sl & 1;
+                const int gh = n0 / 128 + hh;  // head in q | k | v
+                const int n_qk = rope.n_q + rope.n_kv;
+                const bool rot = gh < n_qk, kv = gh >= rope.n_q;
+                const int pair_id = hh * 4 + quarter;
+                const int sw = (lane >> 1) & 3;  // 64-byte swizzle of row lane
+                uint8_t* stage = smem + STAGES * C::STAGE_BYTES + ew * 4096;
+                const uint8_t* partner = smem + STAGES * C::STAGE_BYTES + (ew ^ 4) * 4096;
+                // the bf16 GEMM output that kernel reads: columns 32 sub + 2l,
+                // + 1 in p[l], 64 + 32 sub + 2l, + 1 in p[16 + l]
+                uint32_t p[32];
+#pragma unroll
+                for (int l = 0; l < 16; ++l) {
+                    p[l] = bf16x2_bits(acc[2 * l], acc[2 * l + 1]);
+                    p[16 + l] = bf16x2_bits(acc[32 + 2 * l], acc[33 + 2 * l]);
+                }
+                asm volatile("cp.async.wait_all;" ::: "memory");
+                const int64_t* pd =
+                    reinterpret_cast<const int64_t*>(smem + C::RED_OFF + 512 + (ew * 32 + lane) * 16);
+                int64_t pos = valid ? pd[0] : 0;
+                if (pos < 0 || pos >= rope.max_pos) {
+                    if (sl == 0) atomicOr(status, STATUS_BAD_INDEX);
+                    pos = 0;
+                }
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                __syncwarp();
+                if (rot) {
+                    // the staging area (free now that the last tile's stores read
+                    // it): the 16 lane partials of each row at [0, 2 KB), the
+                    // row's cos (columns 32 sub ..) at [2 KB, 4 KB)
+                    const bf16* tab = rope.cos_sin + pos * 128 + 32 * sub;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(
+                                         stage + 2048 + lane * 64 + ((j ^ sw) << 4))),
+                                     "l"(tab + 8 * j)
+                                     : "memory");
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        float ps[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int l = 4 * q + e;
+                            const float2 a = bf16x2_float2(p[l]), b = bf16x2_float2(p[16 + l]);
+                            float ss = __fmul_rn(a.x, a.x);
+                            ss = __fmaf_rn(a.y, a.y, ss);
+                            ss = __fmaf_rn(b.x, b.x, ss);
+                            ps[e] = __fmaf_rn(b.y, b.y, ss);
+                        }
+                        *reinterpret_cast<float4*>(stage + lane * 64 + ((q ^ sw) << 4)) =
+                            make_float4(ps[0], ps[1], ps[2], ps[3]);
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bars->pair[0][pair_id]);
+                    // the row's sin (columns 64 + 32 sub ..)
+                    uint4 sn4[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) sn4[j] = __ldg(reinterpret_cast<const uint4*>(tab + 64) + j);
+                    if (!mbar_wait(&bars->pair[0][pair_id], (uint32_t)rcount & 1u, abort_flag, status,
+                                   STATUS_GEMM_EPILOGUE)) {
+                        ok = false;
+                        break;
+                    }
+                    // lane partials l of both warps added (the tree's first
+                    // level), then l + 8, + 4, + 2, + 1
+                    float t8[8];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        float t[8];  // chunks h and h + 2: lanes 4h .. 4h + 3 and + 8
+#pragma unroll
+                        for (int k2 = 0; k2 < 2; ++k2) {
+                            const int q = h + 2 * k2;
+                            const float4 mine =
+                                *reinterpret_cast<const float4*>(stage + lane * 64 + ((q ^ sw) << 4));
+                            const float4 o =
+                                *reinterpret_cast<const float4*>(partner + lane * 64 + ((q ^ sw) << 4));
+                            t[4 * k2] = __fadd_rn(mine.x, o.x);
+                            t[4 * k2 + 1] = __fadd_rn(mine.y, o.y);
+                            t[4 * k2 + 2] = __fadd_rn(mine.z, o.z);
+                            t[4 * k2 + 3] = __fadd_rn(mine.w, o.w);
+                        }
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) t8[4 * h + e] = __fadd_rn(t[e], t[4 + e]);
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bars->pair[1][pair_id]);
+#pragma unroll
+                    for (int l = 0; l < 4; ++l) t8[l] = __fadd_rn(t8[l], t8[l + 4]);
+                    t8[0] = __fadd_rn(t8[0], t8[2]);
+                    t8[1] = __fadd_rn(t8[1], t8[3]);
+                    const float ss = __fadd_rn(t8[0], t8[1]);
+                    const float rstd = 1.0f / sqrtf(ss / 128.0f + rope.eps);
+                    const uint4* wt = reinterpret_cast<const uint4*>(smem + C::RED_OFF) +
+                                      (kv ? 16 : 0) + 4 * sub;
+                    asm volatile("cp.async.wait_all;" ::: "memory");
+                    // the partner has read this warp's partials: [0, 2 KB) is free
+                    if (!mbar_wait(&bars->pair[1][pair_id], (uint32_t)rcount & 1u, abort_flag, status,
+                                   STATUS_GEMM_EPILOGUE)) {
+                        ok = false;
+                        break;
+                    }
+                    ++rcount;
+                    // chunk j's outputs: the lo piece at [0, 2 KB), the hi piece
+                    // over the cos chunk it has just consumed
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        uint8_t* lo_at = stage + lane * 64 + ((j ^ sw) << 4);
+                        const uint4 c4 = *reinterpret_cast<const uint4*>(lo_at + 2048);
+                        const uint4 wa4 = wt[j], wb4 = wt[8 + j];
+                        const uint32_t c8[4] = {c4.x, c4.y, c4.z, c4.w};
+                        const uint32_t s8[4] = {sn4[j].x, sn4[j].y, sn4[j].z, sn4[j].w};
+                        const uint32_t wa8[4] = {wa4.x, wa4.y, wa4.z, wa4.w};
+                        const uint32_t wb8[4] = {wb4.x, wb4.y, wb4.z, wb4.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int l = 4 * j + e;
+                            const float2 c = bf16x2_float2(c8[e]), sn = bf16x2_float2(s8[e]);
+                            const float2 wa = bf16x2_float2(wa8[e]), wb = bf16x2_float2(wb8[e]);
+                            const float2 a = bf16x2_float2(p[l]), b = bf16x2_float2(p[16 + l]);
+                            const float ax = __fmul_rn(__fmul_rn(a.x, rstd), wa.x);
+                            const float ay = __fmul_rn(__fmul_rn(a.y, rstd), wa.y);
+                            const float bx = __fmul_rn(__fmul_rn(b.x, rstd), wb.x);
+                            const float by = __fmul_rn(__fmul_rn(b.y, rstd), wb.y);
+                            p[l] = bf16x2_bits(__fsub_rn(__fmul_rn(ax, c.x), __fmul_rn(bx, sn.x)),
+                                               __fsub_rn(__fmul_rn(ay, c.y), __fmul_rn(by, sn.y)));
+                            p[16 + l] =
+                                bf16x2_bits(__fadd_rn(__fmul_rn(bx, c.x), __fmul_rn(ax, sn.x)),
+                                            __fadd_rn(__fmul_rn(by, c.y), __fmul_rn(ay, sn.y)));
+                        }
+                        *reinterpret_cast<uint4*>(lo_at) =
+                            make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+                        *reinterpret_cast<uint4*>(lo_at + 2048) =
+                            make_uint4(p[16 + 4 * j], p[17 + 4 * j], p[18 + 4 * j], p[19 + 4 * j]);
+                    }
+                } else {
+                    // the row's two 32-column pieces: two 32 x 32 boxes
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        *reinterpret_cast<uint4*>(stage + lane * 64 + ((j ^ sw) << 4)) =
+                            make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+                        *reinterpret_cast<uint4*>(stage + 2048 + lane * 64 + ((j ^ sw) << 4)) =
+                            make_uint4(p[16 + 4 * j], p[17 + 4 * j], p[18 + 4 * j], p[19 + 4 * j]);
+                    }
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                // KV append: one box store when the 32 rows land on 32
+                // consecutive pool rows, else per-row stores
+                int64_t dst = (valid && rope.row_dst) ? pd[1] : -1;
+                if (dst >= rope.pool_rows) {
+                    if (sl == 0) atomicOr(status, STATUS_BAD_INDEX);
+                    dst = -1;
+                }
+                bool pool_box = false;
+                int64_t d0 = 0;
+                if (kv && __any_sync(0xffffffffu, dst >= 0)) {
+                    d0 = __shfl_sync(0xffffffffu, dst, 0);
+                    pool_box = __all_sync(0xffffffffu, dst == d0 + lane) && d0 >= 0 &&
+                               d0 + 32 <= rope.pool_rows;
+                    if (!pool_box && dst >= 0) {
+                        const int kvw = rope.n_kv * 128;
+                        bf16* pr = (rot ? rope.k_pool : rope.v_pool) + dst * kvw +
+                                   (rot ? gh - rope.n_q : gh - n_qk) * 128 + 32 * sub;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            *reinterpret_cast<uint4*>(pr + 8 * j) =
+                                make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+                            *reinterpret_cast<uint4*>(pr + 64 + 8 * j) = make_uint4(
+                                p[16 + 4 * j], p[17 + 4 * j], p[18 + 4 * j], p[19 + 4 * j]);
+                        }
+                    }
+                }
+                // rows past M are clipped by the maps' bounds
+                if (lane == 0 && m0 + quarter * 32 < M) {
+                    const CUtensorMap* mo = !kv ? &rope.map_q : rot ? &rope.map_k : &rope.map_v;
+                    const int x = (!kv ? gh : rot ? gh - rope.n_q : gh - n_qk) * 128 + 32 * sub;
+                    const int y = m0 + quarter * 32;
+                    tma_store_2d(mo, smem_u32(stage), x, y);
+                    tma_store_2d(mo, smem_u32(stage + 2048), x + 64, y);
+                    if (pool_box) {
+                        const CUtensorMap* mp = rot ? &rope.map_kp : &rope.map_vp;
+                        tma_store_2d(mp, smem_u32(stage), x, (int)d0);
+                        tma_store_2d(mp, smem_u32(stage + 2048), x + 64, (int)d0);
+                    }
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                }
             } else if constexpr (TSTORE) {
                 // this warp's 32 rows x 64 columns, row r's 16-byte chunk j at
                 // r * 128 + (j ^ r % 8) * 16: the 128-byte swizzle of map_c,
@@ -465,7 +721,7 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
             }
         }
         // the global writes of the last stores complete before the block exits
-        if (TSTORE && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        if ((TSTORE || ROPE) && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
 
     tc_fence_before();
@@ -499,6 +755,28 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, int bo
     return QB_OK;
 }
 
+// bf16 [rows, n] map, box 32 rows x 32 columns, 64-byte swizzle (the
+// ROPE epilogue's output boxes)
+int make_box32_map(CUtensorMap* map, void* base, int64_t rows, int64_t n) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = get_encoder();
+    if (!enc) {
+        set_error("qb_gemm_fp8_qknorm_rope: cuTensorMapEncodeTiled unavailable");
+        return QB_ERR_CUDA;
+    }
+    cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)n * 2};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("qb_gemm_fp8_qknorm_rope: cuTensorMapEncodeTiled (out) failed (%d)", (int)r);
+        return QB_ERR_CUDA;
+    }
+    return QB_OK;
+}
+
 // bf16 output map: rows x n, box 32 rows x 64 columns, 128-byte swizzle
 int make_out_map(CUtensorMap* map, void* base, int64_t rows, int64_t n) {
     PFN_cuTensorMapEncodeTiled_v12000 enc = get_encoder();
@@ -521,11 +799,12 @@ int make_out_map(CUtensorMap* map, void* base, int64_t rows, int64_t n) {
 }
 
 // SILU: n = 2 * inter weight rows, out fp8 [m, inter], q_scale [inter / 128, q_scale_ld]
-template <int BN, int NST = MAX_STAGES, bool TSTORE = false, bool SILU = false>
+template <int BN, int NST = MAX_STAGES, bool TSTORE = false, bool SILU = false,
+          bool ROPE = false>
 int launch(const void* a, const float* a_scale, int64_t a_scale_ld, const void* w,
            const float* w_scale, void* out, int64_t m, int64_t n, int64_t k, cudaStream_t stream,
-           float* q_scale = nullptr, int64_t q_scale_ld = 0) {
-    using C = Cfg<BN, NST, TSTORE, SILU>;
+           float* q_scale = nullptr, int64_t q_scale_ld = 0, const RopeArgs* rope = nullptr) {
+    using C = Cfg<BN, NST, TSTORE, SILU, ROPE>;
     using OutT = typename std::conditional<SILU, uint8_t, bf16>::type;
     CUtensorMap map_a, map_b, map_c;
     memset(&map_c, 0, sizeof(map_c));
@@ -537,7 +816,7 @@ int launch(const void* a, const float* a_scale, int64_t a_scale_ld, const void* 
         st = make_out_map(&map_c, out, m, n);
         if (st) return st;
     }
-    auto kernel = gemm_fp8_bs_kernel<BN, OutT, NST, TSTORE, SILU>;
+    auto kernel = gemm_fp8_bs_kernel<BN, OutT, NST, TSTORE, SILU, ROPE>;
     static bool attr[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -551,10 +830,15 @@ int launch(const void* a, const float* a_scale, int64_t a_scale_ld, const void* 
     if (!status) return launch_status("qb_gemm_fp8_bs: status word");
     const int64_t tiles = ((m + BM - 1) / BM) * (n / BN);
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
+    RopeArgs none;
+    memset(&none, 0, sizeof(none));
     kernel<<<grid, NUM_THREADS, C::SMEM, stream>>>(map_a, map_b, map_c, a_scale, a_scale_ld,
                                                    w_scale, (OutT*)out, q_scale, q_scale_ld,
-                                                   (int)m, (int)n, (int)k, status);
-    return launch_status(SILU ? "qb_gemm_fp8_silu_quant" : "qb_gemm_fp8_bs");
+                                                   (int)m, (int)n, (int)k, status,
+                                                   rope ? *rope : none);
+    return launch_status(SILU   ? "qb_gemm_fp8_silu_quant"
+                         : ROPE ? "qb_gemm_fp8_qknorm_rope"
+                                : "qb_gemm_fp8_bs");
 }
 
 }  // namespace
@@ -601,4 +885,61 @@ extern "C" int qb_gemm_fp8_silu_quant(const void* a, const float* a_scale, int64
     if (m == 0) return QB_OK;
     return launch<256, 4, false, true>(a, a_scale, a_scale_ld, w, w_scale, q_out, m, 2 * inter,
                                        k, (cudaStream_t)stream, scale_out, scale_ld);
+}
+
+extern "C" int qb_gemm_fp8_qknorm_rope(
+    const void* a, const float* a_scale, int64_t a_scale_ld, const void* w, const float* w_scale,
+    int64_t m, int64_t k, const int64_t* positions, const void* cos_sin, int64_t max_pos,
+    const void* q_w, const void* k_w, float eps, int n_q, int n_kv, int head_dim, void* q_out,
+    void* k_out, void* v_out, const int64_t* row_dst, void* k_pool, void* v_pool,
+    int64_t pool_rows, void* stream) {
+    if (head_dim != 128) return invalid("qb_gemm_fp8_qknorm_rope: head_dim must be 128");
+    if (m < 0 || k <= 0 || n_q <= 0 || n_kv <= 0 || n_q % n_kv != 0)
+        return invalid("qb_gemm_fp8_qknorm_rope: bad sizes or head counts");
+    const int64_t n = (int64_t)(n_q + 2 * n_kv) * 128;
+    if (n % 256 != 0)
+        return invalid("qb_gemm_fp8_qknorm_rope: n_q + 2 n_kv must be even (two heads a tile)");
+    if (k % BK != 0) return invalid("qb_gemm_fp8_qknorm_rope: k must be a multiple of 128");
+    if (m > 0x7fffffffLL || k > 0x7fffffffLL)
+        return invalid("qb_gemm_fp8_qknorm_rope: sizes exceed int32");
+    if (a_scale_ld < m) return invalid("qb_gemm_fp8_qknorm_rope: a_scale_ld < m");
+    if (!aligned(a, 16) || !aligned(w, 16) || !aligned(q_out, 16) || !aligned(k_out, 16) ||
+        !aligned(v_out, 16) || !aligned(q_w, 16) || !aligned(k_w, 16) || !aligned(cos_sin, 16))
+        return invalid(
+            "qb_gemm_fp8_qknorm_rope: a, w, the outputs, weights and cos_sin must be 16-byte "
+            "aligned");
+    if (row_dst && (!k_pool || !v_pool || !aligned(k_pool, 16) || !aligned(v_pool, 16)))
+        return invalid("qb_gemm_fp8_qknorm_rope: KV append needs 16-byte aligned pools");
+    if (!a_scale || !w_scale || !positions || !cos_sin || !q_w || !k_w)
+        return invalid("qb_gemm_fp8_qknorm_rope: NULL input");
+    if (max_pos <= 0) return invalid("qb_gemm_fp8_qknorm_rope: empty rotary cache");
+    if (pool_rows > 0x7fffffffLL) return invalid("qb_gemm_fp8_qknorm_rope: pool_rows exceeds int32");
+    if (m == 0) return QB_OK;
+    RopeArgs r;
+    memset(&r, 0, sizeof(r));
+    int st = make_box32_map(&r.map_q, q_out, m, (int64_t)n_q * 128);
+    if (!st) st = make_box32_map(&r.map_k, k_out, m, (int64_t)n_kv * 128);
+    if (!st) st = make_box32_map(&r.map_v, v_out, m, (int64_t)n_kv * 128);
+    if (!st && row_dst && pool_rows > 0) {
+        st = make_box32_map(&r.map_kp, k_pool, pool_rows, (int64_t)n_kv * 128);
+        if (!st) st = make_box32_map(&r.map_vp, v_pool, pool_rows, (int64_t)n_kv * 128);
+    }
+    if (st) return st;
+    r.positions = positions;
+    r.cos_sin = (const bf16*)cos_sin;
+    r.max_pos = max_pos;
+    r.q_w = (const bf16*)q_w;
+    r.k_w = (const bf16*)k_w;
+    r.eps = eps;
+    r.n_q = n_q;
+    r.n_kv = n_kv;
+    r.q_out = (bf16*)q_out;
+    r.k_out = (bf16*)k_out;
+    r.v_out = (bf16*)v_out;
+    r.row_dst = row_dst;
+    r.k_pool = (bf16*)k_pool;
+    r.v_pool = (bf16*)v_pool;
+    r.pool_rows = pool_rows;
+    return launch<256, 3, false, false, true>(a, a_scale, a_scale_ld, w, w_scale, nullptr, m, n,
+                                              k, (cudaStream_t)stream, nullptr, 0, &r);
 }

@@ -158,6 +158,37 @@ class Engine:
                  self._stream())
         return q, k, v
 
+    def gemm_qknorm_rope(self, x: QuantRows, weight, weight_scale, positions, cos_sin, q_w, k_w,
+                         layer, row_dst=None):
+        """qk_norm_rope(gemm(x, qkv)) in one kernel: (q, k, v), KV appended
+        where row_dst >= 0; the bf16 qkv intermediate is never written."""
+        t = self.torch
+        cfg = self.cfg
+        m, k_dim = x.q.shape
+        q = t.empty((m, cfg.n_q * cfg.head_dim), dtype=t.bfloat16, device="cuda")
+        k = t.empty((m, cfg.n_kv * cfg.head_dim), dtype=t.bfloat16, device="cuda")
+        v = t.empty_like(k)
+        kp = vp = None
+        if row_dst is not None:
+            kp, vp = self.arena.layer_kv(layer)
+        timed = self.gemm_events is not None
+        if timed:
+            start, end = t.cuda.Event(enable_timing=True), t.cuda.Event(enable_timing=True)
+            start.record()
+        nat.call("qb_gemm_fp8_qknorm_rope", nat.ptr(x.q), nat.ptr(x.scale), x.ld, nat.ptr(weight),
+                 nat.ptr(weight_scale), m, k_dim, nat.ptr(positions), nat.ptr(cos_sin),
+                 cos_sin.shape[0], nat.ptr(q_w), nat.ptr(k_w), cfg.eps, cfg.n_q, cfg.n_kv,
+                 cfg.head_dim, nat.ptr(q), nat.ptr(k), nat.ptr(v), nat.ptr(row_dst), nat.ptr(kp),
+                 nat.ptr(vp), self.arena.pool_rows, self._stream())
+        if timed:
+            end.record()
+            n = weight.shape[0]
+            # A and W once, q/k/v once, both scale arrays (the pool copy aside)
+            nbytes = m * k_dim + n * k_dim + 2 * m * n + 4 * (m * (k_dim // 128)
+                                                            + (n // 128) * (k_dim // 128))
+            self.gemm_events.append((start, end, 2.0 * m * n * k_dim, nbytes))
+        return q, k, v
+
     def kv_scatter(self, src_k, src_v, src, dst, layer, src_rows):
         kp, vp = self.arena.layer_kv(layer)
         row = self.cfg.n_kv * self.cfg.head_dim

@@ -15,6 +15,8 @@ Ops:
   gemm       qb_gemm_fp8_bs on (m, n, k); default the 4B qkv projection
   gate_up    qb_gemm_fp8_silu_quant on (m, inter, hidden) beside the unfused
              qb_gemm_fp8_bs (n = 2 inter) + qb_silu_mul_quant pair
+  qkv_rope   qb_gemm_fp8_qknorm_rope on m rows beside the unfused
+             qb_gemm_fp8_bs + qb_qknorm_rope pair (with the KV append)
   layer      the four GEMMs of one 4B layer back to back (m rows)
   silu       qb_silu_mul_quant on (rows, inter)
   norm       qb_add_rmsnorm_quant on (rows, hidden)
@@ -110,6 +112,44 @@ def op_gate_up(torch, args):
     ms_unfused = time_launches(torch, unfused, args.warmup, args.iters)
     flops = 2.0 * m * 2 * inter * k
     return {"shape": [m, inter, k], "ms": ms, "tflops": flops / ms / 1e9, "bound": "tensor",
+            "algorithmic": flops, "ms_unfused": ms_unfused}
+
+
+def op_qkv_rope(torch, args):
+    from quail_b200.model import QWEN3_4B as cfg, rotary_cache
+    m, k = args.m, cfg.hidden
+    n = (cfg.n_q + 2 * cfg.n_kv) * cfg.head_dim
+    a, a_s = fp8_rows(torch, m, k)
+    w, w_s = fp8_weight(torch, n, k)
+    pos = torch.arange(m, device="cuda", dtype=torch.int64) % 2048
+    cos_sin = rotary_cache(cfg, "cuda")
+    qw = torch.ones(cfg.head_dim, dtype=torch.bfloat16, device="cuda")
+    q = torch.empty(m, cfg.n_q * cfg.head_dim, dtype=torch.bfloat16, device="cuda")
+    kk = torch.empty(m, cfg.n_kv * cfg.head_dim, dtype=torch.bfloat16, device="cuda")
+    v = torch.empty_like(kk)
+    kp = torch.empty_like(kk)
+    vp = torch.empty_like(kk)
+    row_dst = torch.arange(m, device="cuda", dtype=torch.int64)
+    qkv = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    st = nat.stream_handle(torch)
+
+    def fused():
+        nat.call("qb_gemm_fp8_qknorm_rope", nat.ptr(a), nat.ptr(a_s), m, nat.ptr(w), nat.ptr(w_s),
+                 m, k, nat.ptr(pos), nat.ptr(cos_sin), cos_sin.shape[0], nat.ptr(qw), nat.ptr(qw),
+                 1e-6, cfg.n_q, cfg.n_kv, cfg.head_dim, nat.ptr(q), nat.ptr(kk), nat.ptr(v),
+                 nat.ptr(row_dst), nat.ptr(kp), nat.ptr(vp), m, st)
+
+    def unfused():
+        nat.call("qb_gemm_fp8_bs", nat.ptr(a), nat.ptr(a_s), m, nat.ptr(w), nat.ptr(w_s),
+                 nat.ptr(qkv), m, n, k, st)
+        nat.call("qb_qknorm_rope", nat.ptr(qkv), n, nat.ptr(pos), nat.ptr(cos_sin),
+                 cos_sin.shape[0], nat.ptr(qw), nat.ptr(qw), 1e-6, m, cfg.n_q, cfg.n_kv,
+                 cfg.head_dim, nat.ptr(q), nat.ptr(kk), nat.ptr(v), nat.ptr(row_dst), nat.ptr(kp),
+                 nat.ptr(vp), m, st)
+    ms = time_launches(torch, fused, args.warmup, args.iters)
+    ms_unfused = time_launches(torch, unfused, args.warmup, args.iters)
+    flops = 2.0 * m * n * k
+    return {"rows": m, "ms": ms, "tflops": flops / ms / 1e9, "bound": "tensor",
             "algorithmic": flops, "ms_unfused": ms_unfused}
 
 
@@ -256,8 +296,8 @@ def op_attention(torch, args):
 
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    p.add_argument("op", choices=["gemm", "gate_up", "layer", "silu", "norm", "rope",
-                                  "attention"])
+    p.add_argument("op", choices=["gemm", "gate_up", "qkv_rope", "layer", "silu", "norm",
+                                  "rope", "attention"])
     p.add_argument("--m", type=int, default=65536)
     p.add_argument("--n", type=int, default=6144)
     p.add_argument("--k", type=int, default=2560)

@@ -52,6 +52,9 @@ class Qwen3Pipeline(ModelPipeline):
         # a list records every op's output of the next forward passes as
         # (layer, name, tensor); parity diagnostics only
         self.trace = None
+        # the qkv GEMM carries the q/k norm, rotary and KV append when a
+        # 256-column tile holds two whole heads (n_q + 2 n_kv even)
+        self.fused_qkv = self.cfg.head_dim == 128 and (self.cfg.n_q + 2 * self.cfg.n_kv) % 2 == 0
 
     def linears(self):
         layer = self.layers[0]
@@ -78,9 +81,19 @@ class Qwen3Pipeline(ModelPipeline):
                 if trace is not None:
                     trace.append((index, "residual_in", residual.clone()))
                 x = eng.norm_quant(hidden, layer.input_ln, residual)
-            qkv = eng.gemm(x, layer.qkv_w, layer.qkv_s)
-            q, k, v = eng.qk_norm_rope(qkv, chunk.positions, w.cos_sin, layer.q_norm,
-                                       layer.k_norm, meta["layer"], row_dst)
+            if self.fused_qkv:
+                # qkv GEMM + q/k norm + rotary + KV append in one kernel
+                q, k, v = eng.gemm_qknorm_rope(x, layer.qkv_w, layer.qkv_s, chunk.positions,
+                                               w.cos_sin, layer.q_norm, layer.k_norm,
+                                               meta["layer"], row_dst)
+                qkv = None
+                if trace is not None:
+                    # the bf16 qkv the fused kernel never writes, for the trace
+                    qkv = eng.gemm(x, layer.qkv_w, layer.qkv_s)
+            else:
+                qkv = eng.gemm(x, layer.qkv_w, layer.qkv_s)
+                q, k, v = eng.qk_norm_rope(qkv, chunk.positions, w.cos_sin, layer.q_norm,
+                                           layer.k_norm, meta["layer"], row_dst)
             if tree:
                 o_in = eng.attention_tree(q, k, v, meta)
             else:

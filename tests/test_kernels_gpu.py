@@ -157,6 +157,53 @@ def test_gemm_silu_quant(dev, m, inter, k, oracle):
         assert_bits_equal(out.q, ref.q, "fp8 codes vs unfused")
 
 
+@pytest.mark.parametrize("cfg_name,m,runs", [("tiny", 1, False), ("tiny", 300, False),
+                                             ("tiny", 300, True), ("4b", 517, False),
+                                             ("4b", 517, True), ("32b", 130, True)])
+def test_gemm_qknorm_rope_matches_unfused(dev, cfg_name, m, runs):
+    """qkv GEMM + q/k norm + rotary + KV append in one kernel: the same q, k,
+    v and pool rows, bit for bit, as qb_gemm_fp8_bs then qb_qknorm_rope.
+    runs: KV destinations in consecutive runs (two of them, the second from
+    a row that is not a multiple of 32: box stores and per-row stores) instead
+    of every other row at random."""
+    from quail_b200.model import QWEN3_4B, QWEN3_32B, rotary_cache
+    cfg = {"tiny": TINY, "4b": QWEN3_4B, "32b": QWEN3_32B}[cfg_name]
+    g = torch.Generator().manual_seed(m + cfg.hidden)
+    n = (cfg.n_q + 2 * cfg.n_kv) * cfg.head_dim
+    aq, as_, wq, ws = _fp8_operands(g, m, n, cfg.hidden)
+    x = QuantRows(aq.to(dev), as_.to(dev).contiguous(), m)
+    pos = torch.randint(0, 4000, (m,), generator=g).to(dev)
+    cos_sin = rotary_cache(cfg, dev)
+    qw = (1 + 0.1 * torch.randn(cfg.head_dim, generator=g)).to(torch.bfloat16).to(dev)
+    kw = (1 + 0.1 * torch.randn(cfg.head_dim, generator=g)).to(torch.bfloat16).to(dev)
+    pool_rows = 2 * m + 16
+    arenas = [KVArena(1, (pool_rows + 15) // 16, 16, cfg.n_kv, cfg.head_dim, device=dev)
+              for _ in range(2)]
+    for a in arenas:
+        a.pools.zero_()
+    row_dst = torch.full((m,), -1, dtype=torch.int64)
+    if runs:
+        cut = (m * 2) // 3 + 5
+        row_dst[:cut] = 3 + torch.arange(cut)
+        row_dst[cut:] = m + 8 + torch.arange(m - cut)
+    else:
+        row_dst[::2] = torch.randperm(arenas[0].pool_rows, generator=g)[: (m + 1) // 2]
+    assert int(row_dst.max()) < arenas[0].pool_rows
+    row_dst = row_dst.to(dev)
+    eng_f = Engine(torch, arenas[0], cfg)
+    q_f, k_f, v_f = eng_f.gemm_qknorm_rope(x, wq.to(dev), ws.to(dev), pos, cos_sin, qw, kw, 0,
+                                           row_dst)
+    eng_u = Engine(torch, arenas[1], cfg)
+    qkv = eng_u.gemm(x, wq.to(dev), ws.to(dev))
+    q_u, k_u, v_u = eng_u.qk_norm_rope(qkv, pos, cos_sin, qw, kw, 0, row_dst)
+    torch.cuda.synchronize()
+    assert_status_clean()
+    assert_bits_equal(q_f, q_u, "q")
+    assert_bits_equal(k_f, k_u, "k")
+    assert_bits_equal(v_f, v_u, "v")
+    assert_bits_equal(arenas[0].pools, arenas[1].pools, "KV pools")
+
+
 def test_gemm_large_against_dequantised_matmul(dev):
     """A full 4B QKV-shaped GEMM against fp32 torch on the dequantised operands."""
     g = torch.Generator(device="cuda").manual_seed(5)

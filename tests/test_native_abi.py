@@ -65,6 +65,16 @@ def test_invalid_fused_silu_gemm_calls_are_rejected(lib):
                  unaligned, unaligned, 8, 8, 128, 256, None)
 
 
+def test_invalid_fused_qkv_calls_are_rejected(lib):
+    # 3 + 2 * 1 heads: a 256-column tile would split a head
+    with pytest.raises(ValueError, match="even"):
+        nat.call("qb_gemm_fp8_qknorm_rope", None, None, 8, None, None, 8, 256, None, None, 10,
+                 None, None, 1e-6, 3, 1, 128, None, None, None, None, None, None, 0, None)
+    with pytest.raises(ValueError, match="head_dim"):
+        nat.call("qb_gemm_fp8_qknorm_rope", None, None, 8, None, None, 8, 256, None, None, 10,
+                 None, None, 1e-6, 4, 2, 64, None, None, None, None, None, None, 0, None)
+
+
 def test_invalid_attention_and_norm_calls_are_rejected(lib):
     with pytest.raises(ValueError, match="head_dim"):
         nat.call("qb_tree_attention", None, None, None, 4, 4, 2, 64, None, 1, None, 1,
