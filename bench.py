@@ -46,11 +46,12 @@ UNIT = "rows/s"
 
 
 # DRAM bytes (read + write) per GEMM launch, averaged over the 144 launches
-# of one config-1 chunk (qkv, o, down: qb_gemm_fp8_bs; gate_up:
-# qb_gemm_fp8_silu_quant; x 36 layers), from the ncu launch list in
-# profiles/launch_list_config1.md (dram__bytes_read.sum +
-# dram__bytes_write.sum, one pass, same workload as this bench)
-GEMM_DRAM_BYTES_PER_LAUNCH = 1.6176e9
+# of one config-1 chunk (o, down: qb_gemm_fp8_bs; qkv with q/k norm, rotary
+# and KV append: qb_gemm_fp8_qknorm_rope; gate_up: qb_gemm_fp8_silu_quant;
+# x 36 layers), from the ncu launch list in profiles/launch_list_config1.md
+# (dram__bytes_read.sum + dram__bytes_write.sum, one pass, same workload as
+# this bench)
+GEMM_DRAM_BYTES_PER_LAUNCH = 1.8058e9
 GEMM_TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/launch_list_config1.md"
 
 
@@ -407,7 +408,8 @@ def main():
                        "l2": "inputs larger than L2 (>=0.5 GB activations per chunk)",
                        "status_word": status},
             "roofline": {"bound": "tensor",
-                         "kernel": "qb_gemm_fp8_bs + qb_gemm_fp8_silu_quant (all GEMMs)",
+                         "kernel": "qb_gemm_fp8_bs + qb_gemm_fp8_qknorm_rope + "
+                                   "qb_gemm_fp8_silu_quant (all GEMMs)",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak if peak else None,
                          "traffic": GEMM_DRAM_BYTES_PER_LAUNCH,

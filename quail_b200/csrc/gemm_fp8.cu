@@ -109,9 +109,12 @@ struct Barriers {
     uint64_t scale_empty[SCALE_SLOTS];
     uint64_t drain;
     uint64_t red_full[2];  // SILU: a tile's partials are in shared memory
-    // ROPE: per warp pair (the two halves of a head's rows), [0] the pair's
-    // partials are staged, [1] both have read them
-    uint64_t pair[2][8];
+    // ROPE: per row quarter (its four warps: two heads x two column halves),
+    // [0] the partials and rotary rows are staged, [1] all four have read them
+    uint64_t quad[2][4];
+    // ROPE: per warp pair (the two column halves of a head's rows): both
+    // have read each other's partials
+    uint64_t pair[8];
     uint32_t tmem_base;
     int abort;
 };
@@ -207,10 +210,12 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
         mbar_init(&bars->drain, 1);
         mbar_init(&bars->red_full[0], EPI_WARPS);
         mbar_init(&bars->red_full[1], EPI_WARPS);
-        for (int p = 0; p < 8; ++p) {
-            mbar_init(&bars->pair[0][p], 2);
-            mbar_init(&bars->pair[1][p], 2);
+        for (int q = 0; q < 4; ++q) {
+            // four warps' lane 0 and the 4 x 32 lanes' cp.async arrivals
+            mbar_init(&bars->quad[0][q], 4 + 4 * 32);
+            mbar_init(&bars->quad[1][q], 4);
         }
+        for (int q = 0; q < 8; ++q) mbar_init(&bars->pair[q], 2);
         bars->abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -365,7 +370,7 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                                      : (ew >> 2) * C::SLICE;
         const int row_in_tile = quarter * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-        int acc_it = 0, tcount = 0, rcount = 0;
+        int acc_it = 0, tcount = 0, gcount = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++tcount) {
             const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
@@ -499,25 +504,22 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                 // qb_qknorm_rope on this tile's two heads, bit for bit. Lane L
                 // of that kernel's warp holds columns 2L, 2L + 1, 64 + 2L,
                 // 65 + 2L of a head row; here warp sub (0 or 1) of a pair holds
-                // lanes 16 sub .. 16 sub + 15 of every row, and the pair swaps
-                // its sum-of-squares lane partials through the staging areas to
-                // run warp_sum's xor tree (16, 8, 4, 2, 1).
+                // lanes 16 sub .. 16 sub + 15 of every row. The four warps of
+                // a row quarter share one staging exchange: each stages its
+                // 16 sum-of-squares lane partials a row (for warp_sum's xor
+                // tree 16, 8, 4, 2, 1 across the pair) and one rotary half
+                // (head 0's warps the cos, head 1's the sin of their columns).
                 const int sl = ew >> 2, hh = sl >> 1, sub = sl & 1;
                 const int gh = n0 / 128 + hh;  // head in q | k | v
                 const int n_qk = rope.n_q + rope.n_kv;
                 const bool rot = gh < n_qk, kv = gh >= rope.n_q;
-                const int pair_id = hh * 4 + quarter;
-                const int sw = (lane >> 1) & 3;  // 64-byte swizzle of row lane
-                uint8_t* stage = smem + STAGES * C::STAGE_BYTES + ew * 4096;
-                const uint8_t* partner = smem + STAGES * C::STAGE_BYTES + (ew ^ 4) * 4096;
-                // the bf16 GEMM output that kernel reads: columns 32 sub + 2l,
-                // + 1 in p[l], 64 + 32 sub + 2l, + 1 in p[16 + l]
-                uint32_t p[32];
+                const bool group = n0 / 128 < n_qk;  // the tile's first head rotates
+                const int sw = (lane >> 1) & 3;      // 64-byte swizzle of row lane
+                uint8_t* const stages = smem + STAGES * C::STAGE_BYTES;
+                uint8_t* stage = stages + ew * 4096;
+                // the bf16 GEMM output that kernel reads
 #pragma unroll
-                for (int l = 0; l < 16; ++l) {
-                    p[l] = bf16x2_bits(acc[2 * l], acc[2 * l + 1]);
-                    p[16 + l] = bf16x2_bits(acc[32 + 2 * l], acc[33 + 2 * l]);
-                }
+                for (int j = 0; j < 64; ++j) acc[j] = bf16_round(acc[j]);
                 asm volatile("cp.async.wait_all;" ::: "memory");
                 const int64_t* pd =
                     reinterpret_cast<const int64_t*>(smem + C::RED_OFF + 512 + (ew * 32 + lane) * 16);
@@ -526,125 +528,152 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                     if (sl == 0) atomicOr(status, STATUS_BAD_INDEX);
                     pos = 0;
                 }
+                // the staging area is free once the last tile's stores read it
                 if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
                 __syncwarp();
-                if (rot) {
-                    // the staging area (free now that the last tile's stores read
-                    // it): the 16 lane partials of each row at [0, 2 KB), the
-                    // row's cos (columns 32 sub ..) at [2 KB, 4 KB)
-                    const bf16* tab = rope.cos_sin + pos * 128 + 32 * sub;
+                if (group) {
+                    // [2 KB, 4 KB): this warp's rotary half of the row's table
+                    // entry (head 0's warps cos, head 1's sin, columns 32 sub ..)
+                    const bf16* tab = rope.cos_sin + pos * 128 + 64 * hh + 32 * sub;
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
                         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(
                                          stage + 2048 + lane * 64 + ((j ^ sw) << 4))),
                                      "l"(tab + 8 * j)
                                      : "memory");
+                    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(
+                                     smem_u32(&bars->quad[0][quarter]))
+                                 : "memory");
+                    // [0, 2 KB): the row's 16 lane partials
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         float ps[4];
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
                             const int l = 4 * q + e;
-                            const float2 a = bf16x2_float2(p[l]), b = bf16x2_float2(p[16 + l]);
-                            float ss = __fmul_rn(a.x, a.x);
-                            ss = __fmaf_rn(a.y, a.y, ss);
-                            ss = __fmaf_rn(b.x, b.x, ss);
-                            ps[e] = __fmaf_rn(b.y, b.y, ss);
+                            float ss = __fmul_rn(acc[2 * l], acc[2 * l]);
+                            ss = __fmaf_rn(acc[2 * l + 1], acc[2 * l + 1], ss);
+                            ss = __fmaf_rn(acc[32 + 2 * l], acc[32 + 2 * l], ss);
+                            ps[e] = __fmaf_rn(acc[33 + 2 * l], acc[33 + 2 * l], ss);
                         }
                         *reinterpret_cast<float4*>(stage + lane * 64 + ((q ^ sw) << 4)) =
                             make_float4(ps[0], ps[1], ps[2], ps[3]);
                     }
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&bars->pair[0][pair_id]);
-                    // the row's sin (columns 64 + 32 sub ..)
-                    uint4 sn4[4];
+                    if (lane == 0) mbar_arrive(&bars->quad[0][quarter]);
+                }
+                // columns 32 sub + 2l, + 1 in p[l], 64 + 32 sub + 2l, + 1 in
+                // p[16 + l], exactly (the values are bf16 already)
+                uint32_t p[32];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) sn4[j] = __ldg(reinterpret_cast<const uint4*>(tab + 64) + j);
-                    if (!mbar_wait(&bars->pair[0][pair_id], (uint32_t)rcount & 1u, abort_flag, status,
+                for (int l = 0; l < 16; ++l) {
+                    p[l] = bf16x2_bits(acc[2 * l], acc[2 * l + 1]);
+                    p[16 + l] = bf16x2_bits(acc[32 + 2 * l], acc[33 + 2 * l]);
+                }
+                if (group) {
+                    if (!mbar_wait(&bars->quad[0][quarter], (uint32_t)gcount & 1u, abort_flag, status,
                                    STATUS_GEMM_EPILOGUE)) {
                         ok = false;
                         break;
                     }
-                    // lane partials l of both warps added (the tree's first
-                    // level), then l + 8, + 4, + 2, + 1
-                    float t8[8];
+                    float rstd = 0.0f;
+                    if (rot) {
+                        const uint8_t* partner = stages + (ew ^ 4) * 4096;
+                        // lane partials l of both warps added (the tree's first
+                        // level), then l + 8, + 4, + 2, + 1
+                        float t8[8];
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        float t[8];  // chunks h and h + 2: lanes 4h .. 4h + 3 and + 8
+                        for (int h = 0; h < 2; ++h) {
+                            float t[8];  // chunks h and h + 2: lanes 4h .. 4h + 3 and + 8
 #pragma unroll
-                        for (int k2 = 0; k2 < 2; ++k2) {
-                            const int q = h + 2 * k2;
-                            const float4 mine =
-                                *reinterpret_cast<const float4*>(stage + lane * 64 + ((q ^ sw) << 4));
-                            const float4 o =
-                                *reinterpret_cast<const float4*>(partner + lane * 64 + ((q ^ sw) << 4));
-                            t[4 * k2] = __fadd_rn(mine.x, o.x);
-                            t[4 * k2 + 1] = __fadd_rn(mine.y, o.y);
-                            t[4 * k2 + 2] = __fadd_rn(mine.z, o.z);
-                            t[4 * k2 + 3] = __fadd_rn(mine.w, o.w);
+                            for (int k2 = 0; k2 < 2; ++k2) {
+                                const int q = h + 2 * k2;
+                                const int at = lane * 64 + ((q ^ sw) << 4);
+                                const float4 mine = *reinterpret_cast<const float4*>(stage + at);
+                                const float4 o = *reinterpret_cast<const float4*>(partner + at);
+                                t[4 * k2] = __fadd_rn(mine.x, o.x);
+                                t[4 * k2 + 1] = __fadd_rn(mine.y, o.y);
+                                t[4 * k2 + 2] = __fadd_rn(mine.z, o.z);
+                                t[4 * k2 + 3] = __fadd_rn(mine.w, o.w);
+                            }
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) t8[4 * h + e] = __fadd_rn(t[e], t[4 + e]);
                         }
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) t8[4 * h + e] = __fadd_rn(t[e], t[4 + e]);
+                        for (int l = 0; l < 4; ++l) t8[l] = __fadd_rn(t8[l], t8[l + 4]);
+                        t8[0] = __fadd_rn(t8[0], t8[2]);
+                        t8[1] = __fadd_rn(t8[1], t8[3]);
+                        const float ss = __fadd_rn(t8[0], t8[1]);
+                        rstd = 1.0f / sqrtf(ss / 128.0f + rope.eps);
                     }
+                    // [0, 2 KB) takes the lo outputs once the pair has read both
+                    // partials (every pair of a rotating tile takes this step)
+                    const int pair_id = hh * 4 + quarter;
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&bars->pair[1][pair_id]);
-#pragma unroll
-                    for (int l = 0; l < 4; ++l) t8[l] = __fadd_rn(t8[l], t8[l + 4]);
-                    t8[0] = __fadd_rn(t8[0], t8[2]);
-                    t8[1] = __fadd_rn(t8[1], t8[3]);
-                    const float ss = __fadd_rn(t8[0], t8[1]);
-                    const float rstd = 1.0f / sqrtf(ss / 128.0f + rope.eps);
-                    const uint4* wt = reinterpret_cast<const uint4*>(smem + C::RED_OFF) +
-                                      (kv ? 16 : 0) + 4 * sub;
-                    asm volatile("cp.async.wait_all;" ::: "memory");
-                    // the partner has read this warp's partials: [0, 2 KB) is free
-                    if (!mbar_wait(&bars->pair[1][pair_id], (uint32_t)rcount & 1u, abort_flag, status,
+                    if (lane == 0) mbar_arrive(&bars->pair[pair_id]);
+                    if (!mbar_wait(&bars->pair[pair_id], (uint32_t)gcount & 1u, abort_flag, status,
                                    STATUS_GEMM_EPILOGUE)) {
                         ok = false;
                         break;
                     }
-                    ++rcount;
-                    // chunk j's outputs: the lo piece at [0, 2 KB), the hi piece
-                    // over the cos chunk it has just consumed
+                    if (rot) {
+                        const uint4* wt = reinterpret_cast<const uint4*>(smem + C::RED_OFF) +
+                                          (kv ? 16 : 0) + 4 * sub;
+                        // the cos and sin halves staged by this quarter's head-0
+                        // and head-1 warps of the same column half
+                        const uint8_t* cos_at = stages + ((ew & 3) + 4 * sub) * 4096 + 2048;
+                        const uint8_t* sin_at = stages + ((ew & 3) + 4 * (2 + sub)) * 4096 + 2048;
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        uint8_t* lo_at = stage + lane * 64 + ((j ^ sw) << 4);
-                        const uint4 c4 = *reinterpret_cast<const uint4*>(lo_at + 2048);
-                        const uint4 wa4 = wt[j], wb4 = wt[8 + j];
-                        const uint32_t c8[4] = {c4.x, c4.y, c4.z, c4.w};
-                        const uint32_t s8[4] = {sn4[j].x, sn4[j].y, sn4[j].z, sn4[j].w};
-                        const uint32_t wa8[4] = {wa4.x, wa4.y, wa4.z, wa4.w};
-                        const uint32_t wb8[4] = {wb4.x, wb4.y, wb4.z, wb4.w};
+                        for (int j = 0; j < 4; ++j) {
+                            const int at = lane * 64 + ((j ^ sw) << 4);
+                            const uint4 c4 = *reinterpret_cast<const uint4*>(cos_at + at);
+                            const uint4 s4 = *reinterpret_cast<const uint4*>(sin_at + at);
+                            const uint4 wa4 = wt[j], wb4 = wt[8 + j];
+                            const uint32_t c8[4] = {c4.x, c4.y, c4.z, c4.w};
+                            const uint32_t s8[4] = {s4.x, s4.y, s4.z, s4.w};
+                            const uint32_t wa8[4] = {wa4.x, wa4.y, wa4.z, wa4.w};
+                            const uint32_t wb8[4] = {wb4.x, wb4.y, wb4.z, wb4.w};
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int l = 4 * j + e;
-                            const float2 c = bf16x2_float2(c8[e]), sn = bf16x2_float2(s8[e]);
-                            const float2 wa = bf16x2_float2(wa8[e]), wb = bf16x2_float2(wb8[e]);
-                            const float2 a = bf16x2_float2(p[l]), b = bf16x2_float2(p[16 + l]);
-                            const float ax = __fmul_rn(__fmul_rn(a.x, rstd), wa.x);
-                            const float ay = __fmul_rn(__fmul_rn(a.y, rstd), wa.y);
-                            const float bx = __fmul_rn(__fmul_rn(b.x, rstd), wb.x);
-                            const float by = __fmul_rn(__fmul_rn(b.y, rstd), wb.y);
-                            p[l] = bf16x2_bits(__fsub_rn(__fmul_rn(ax, c.x), __fmul_rn(bx, sn.x)),
-                                               __fsub_rn(__fmul_rn(ay, c.y), __fmul_rn(by, sn.y)));
-                            p[16 + l] =
-                                bf16x2_bits(__fadd_rn(__fmul_rn(bx, c.x), __fmul_rn(ax, sn.x)),
-                                            __fadd_rn(__fmul_rn(by, c.y), __fmul_rn(ay, sn.y)));
+                            for (int e = 0; e < 4; ++e) {
+                                const int l = 4 * j + e;
+                                const float2 c = bf16x2_float2(c8[e]), sn = bf16x2_float2(s8[e]);
+                                const float2 wa = bf16x2_float2(wa8[e]), wb = bf16x2_float2(wb8[e]);
+                                const float2 a = bf16x2_float2(p[l]), b = bf16x2_float2(p[16 + l]);
+                                const float ax = __fmul_rn(__fmul_rn(a.x, rstd), wa.x);
+                                const float ay = __fmul_rn(__fmul_rn(a.y, rstd), wa.y);
+                                const float bx = __fmul_rn(__fmul_rn(b.x, rstd), wb.x);
+                                const float by = __fmul_rn(__fmul_rn(b.y, rstd), wb.y);
+                                p[l] = bf16x2_bits(__fsub_rn(__fmul_rn(ax, c.x), __fmul_rn(bx, sn.x)),
+                                                   __fsub_rn(__fmul_rn(ay, c.y), __fmul_rn(by, sn.y)));
+                                p[16 + l] =
+                                    bf16x2_bits(__fadd_rn(__fmul_rn(bx, c.x), __fmul_rn(ax, sn.x)),
+                                                __fadd_rn(__fmul_rn(by, c.y), __fmul_rn(ay, sn.y)));
+                            }
+                            // stored before the next chunk's operands are loaded:
+                            // one chunk's operands in registers at a time
+                            *reinterpret_cast<uint4*>(stage + at) =
+                                make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
                         }
-                        *reinterpret_cast<uint4*>(lo_at) =
-                            make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
-                        *reinterpret_cast<uint4*>(lo_at + 2048) =
-                            make_uint4(p[16 + 4 * j], p[17 + 4 * j], p[18 + 4 * j], p[19 + 4 * j]);
                     }
-                } else {
-                    // the row's two 32-column pieces: two 32 x 32 boxes
+                    // every staged partial and rotary half has been read
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bars->quad[1][quarter]);
+                    if (!mbar_wait(&bars->quad[1][quarter], (uint32_t)gcount & 1u, abort_flag, status,
+                                   STATUS_GEMM_EPILOGUE)) {
+                        ok = false;
+                        break;
+                    }
+                    ++gcount;
+                }
+                // the row's two 32-column pieces: two 32 x 32 boxes (the lo
+                // piece of a rotated head is in place already)
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
+                for (int j = 0; j < 4; ++j) {
+                    if (!rot)
                         *reinterpret_cast<uint4*>(stage + lane * 64 + ((j ^ sw) << 4)) =
                             make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
-                        *reinterpret_cast<uint4*>(stage + 2048 + lane * 64 + ((j ^ sw) << 4)) =
-                            make_uint4(p[16 + 4 * j], p[17 + 4 * j], p[18 + 4 * j], p[19 + 4 * j]);
-                    }
+                    *reinterpret_cast<uint4*>(stage + 2048 + lane * 64 + ((j ^ sw) << 4)) =
+                        make_uint4(p[16 + 4 * j], p[17 + 4 * j], p[18 + 4 * j], p[19 + 4 * j]);
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();

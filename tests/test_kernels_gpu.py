@@ -158,16 +158,19 @@ def test_gemm_silu_quant(dev, m, inter, k, oracle):
 
 
 @pytest.mark.parametrize("cfg_name,m,runs", [("tiny", 1, False), ("tiny", 300, False),
-                                             ("tiny", 300, True), ("4b", 517, False),
-                                             ("4b", 517, True), ("32b", 130, True)])
+                                             ("tiny", 300, True), ("mixed", 300, True),
+                                             ("4b", 517, False), ("4b", 517, True),
+                                             ("32b", 130, True)])
 def test_gemm_qknorm_rope_matches_unfused(dev, cfg_name, m, runs):
     """qkv GEMM + q/k norm + rotary + KV append in one kernel: the same q, k,
     v and pool rows, bit for bit, as qb_gemm_fp8_bs then qb_qknorm_rope.
     runs: KV destinations in consecutive runs (two of them, the second from
     a row that is not a multiple of 32: box stores and per-row stores) instead
-    of every other row at random."""
+    of every other row at random. mixed: 6 q and 3 kv heads, so one tile
+    holds the last k head and the first v head."""
     from quail_b200.model import QWEN3_4B, QWEN3_32B, rotary_cache
-    cfg = {"tiny": TINY, "4b": QWEN3_4B, "32b": QWEN3_32B}[cfg_name]
+    cfg = {"tiny": TINY, "4b": QWEN3_4B, "32b": QWEN3_32B,
+           "mixed": dataclasses.replace(TINY, n_q=6, n_kv=3)}[cfg_name]
     g = torch.Generator().manual_seed(m + cfg.hidden)
     n = (cfg.n_q + 2 * cfg.n_kv) * cfg.head_dim
     aq, as_, wq, ws = _fp8_operands(g, m, n, cfg.hidden)
