@@ -75,7 +75,10 @@ struct Cfg {
     // TSTORE: one 32 x 64 bf16 staging box per epilogue warp; ROPE: the same
     // 4 KB per warp holds the pair's sum-of-squares partials, then the two
     // 32 x 32 output boxes (64-byte swizzle)
-    static constexpr int OUT_BYTES = (TSTORE || ROPE) ? EPI_WARPS * 32 * SLICE * 2 : 0;
+    // SILU: one 32 x 32 fp8 box (1 KB) per epilogue warp
+    static constexpr int OUT_BYTES = (TSTORE || ROPE) ? EPI_WARPS * 32 * SLICE * 2
+                                     : SILU           ? EPI_WARPS * 32 * 32
+                                                      : 0;
     static constexpr int SCALE_OFF = STAGES * STAGE_BYTES + OUT_BYTES;
     static_assert(!SILU || (BN == 256 && !TSTORE), "SILU tiles are 128 gate + 128 up columns");
     static_assert(!ROPE || (BN == 256 && !TSTORE && !SILU), "ROPE tiles are two heads");
@@ -166,7 +169,8 @@ __device__ __forceinline__ void fma2(float* acc, const uint32_t* v, float s) {
 // OutT = bf16 (the library) or float (numerics probes: the fp32 accumulator);
 // uint8_t with SILU (fp8 e4m3 rows of N/2 columns, their scales at
 // q_scale[j * q_scale_ld + row]).
-// map_c (bf16 out, box 64 x 32, 128-byte swizzle) is read only when TSTORE.
+// map_c is read only when TSTORE (bf16 out, box 64 x 32, 128-byte swizzle)
+// or SILU (fp8 out, box 32 x 32, 32-byte swizzle).
 template <int BN, typename OutT = bf16, int NST = MAX_STAGES, bool TSTORE = false,
           bool SILU = false, bool ROPE = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -492,14 +496,26 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                     }
                     pk[i >> 2] = (uint32_t)fp8x2(a, b) | ((uint32_t)fp8x2(c, d) << 16);
                 }
-                if (valid) {
-                    const int j = tile % num_n;
-                    uint8_t* dst = reinterpret_cast<uint8_t*>(out) + (int64_t)m * (N / 2) +
-                                   j * 128 + col0;
-                    *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                    *reinterpret_cast<uint4*>(dst + 16) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-                    if (col0 == 0) q_scale[(int64_t)j * q_scale_ld + m] = scale;
+                // the warp's 32 rows x 32 codes leave as one TMA box: row r at
+                // r * 32, its 16-byte halves swapped when r % 8 >= 4 (the
+                // 32-byte swizzle of map_c; conflict-free for a row a lane)
+                const int j = tile % num_n;
+                uint8_t* stage = smem + STAGES * C::STAGE_BYTES + ew * 1024;
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                __syncwarp();
+                const int sw = (lane >> 2) & 1;
+                *reinterpret_cast<uint4*>(stage + lane * 32 + (sw << 4)) =
+                    make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                *reinterpret_cast<uint4*>(stage + lane * 32 + ((sw ^ 1) << 4)) =
+                    make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                // rows past M are clipped by the map's bounds
+                if (lane == 0 && m0 + quarter * 32 < M) {
+                    tma_store_2d(&map_c, smem_u32(stage), j * 128 + col0, m0 + quarter * 32);
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                 }
+                if (valid && col0 == 0) q_scale[(int64_t)j * q_scale_ld + m] = scale;
             } else if constexpr (ROPE) {
                 // qb_qknorm_rope on this tile's two heads, bit for bit. Lane L
                 // of that kernel's warp holds columns 2L, 2L + 1, 64 + 2L,
@@ -750,7 +766,8 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
             }
         }
         // the global writes of the last stores complete before the block exits
-        if ((TSTORE || ROPE) && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        if ((TSTORE || ROPE || SILU) && lane == 0)
+            asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
 
     tc_fence_before();
@@ -806,6 +823,28 @@ int make_box32_map(CUtensorMap* map, void* base, int64_t rows, int64_t n) {
     return QB_OK;
 }
 
+// fp8 [rows, n] map, box 32 rows x 32 columns, 32-byte swizzle (the SILU
+// epilogue's output boxes)
+int make_fp8_box32_map(CUtensorMap* map, void* base, int64_t rows, int64_t n) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = get_encoder();
+    if (!enc) {
+        set_error("qb_gemm_fp8_silu_quant: cuTensorMapEncodeTiled unavailable");
+        return QB_ERR_CUDA;
+    }
+    cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)n};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("qb_gemm_fp8_silu_quant: cuTensorMapEncodeTiled (out) failed (%d)", (int)r);
+        return QB_ERR_CUDA;
+    }
+    return QB_OK;
+}
+
 // bf16 output map: rows x n, box 32 rows x 64 columns, 128-byte swizzle
 int make_out_map(CUtensorMap* map, void* base, int64_t rows, int64_t n) {
     PFN_cuTensorMapEncodeTiled_v12000 enc = get_encoder();
@@ -843,6 +882,10 @@ int launch(const void* a, const float* a_scale, int64_t a_scale_ld, const void* 
     if (st) return st;
     if (TSTORE) {
         st = make_out_map(&map_c, out, m, n);
+        if (st) return st;
+    }
+    if (SILU) {
+        st = make_fp8_box32_map(&map_c, out, m, n / 2);
         if (st) return st;
     }
     auto kernel = gemm_fp8_bs_kernel<BN, OutT, NST, TSTORE, SILU, ROPE>;

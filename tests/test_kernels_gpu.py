@@ -207,6 +207,46 @@ def test_gemm_qknorm_rope_matches_unfused(dev, cfg_name, m, runs):
     assert_bits_equal(arenas[0].pools, arenas[1].pools, "KV pools")
 
 
+def test_gemm_qknorm_rope_bad_indices_flag_like_unfused(dev):
+    """A position past the rotary cache and a KV destination past the pool:
+    the fused kernel flags STATUS_BAD_INDEX, reads cos/sin row 0 and skips
+    the append, as qb_qknorm_rope does; every output equals the pair's."""
+    cfg = TINY
+    m = 96
+    g = torch.Generator().manual_seed(41)
+    n = (cfg.n_q + 2 * cfg.n_kv) * cfg.head_dim
+    aq, as_, wq, ws = _fp8_operands(g, m, n, cfg.hidden)
+    x = QuantRows(aq.to(dev), as_.to(dev).contiguous(), m)
+    from quail_b200.model import rotary_cache
+    cos_sin = rotary_cache(cfg, dev)
+    pos = torch.randint(0, 100, (m,), generator=g)
+    pos[5] = cos_sin.shape[0]
+    pos = pos.to(dev)
+    qw = torch.ones(cfg.head_dim, dtype=torch.bfloat16, device=dev)
+    arenas = [KVArena(1, 16, 16, cfg.n_kv, cfg.head_dim, device=dev) for _ in range(2)]
+    for a in arenas:
+        a.pools.zero_()
+    row_dst = torch.arange(m, dtype=torch.int64)
+    row_dst[37] = arenas[0].pool_rows + 3
+    row_dst = row_dst.to(dev)
+    out = []
+    for fused, arena in ((True, arenas[0]), (False, arenas[1])):
+        eng = Engine(torch, arena, cfg)
+        assert_status_clean()
+        if fused:
+            q, k, v = eng.gemm_qknorm_rope(x, wq.to(dev), ws.to(dev), pos, cos_sin, qw, qw, 0,
+                                           row_dst)
+        else:
+            qkv = eng.gemm(x, wq.to(dev), ws.to(dev))
+            q, k, v = eng.qk_norm_rope(qkv, pos, cos_sin, qw, qw, 0, row_dst)
+        torch.cuda.synchronize()
+        assert nat.kernel_status(torch.cuda.current_device()) == 1 << 9  # STATUS_BAD_INDEX
+        out.append((q, k, v))
+    for (name, a), b in zip((("q", out[0][0]), ("k", out[0][1]), ("v", out[0][2])), out[1]):
+        assert_bits_equal(a, b, name)
+    assert_bits_equal(arenas[0].pools, arenas[1].pools, "KV pools")
+
+
 def test_gemm_large_against_dequantised_matmul(dev):
     """A full 4B QKV-shaped GEMM against fp32 torch on the dequantised operands."""
     g = torch.Generator(device="cuda").manual_seed(5)
