@@ -768,6 +768,9 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
         // the global writes of the last stores complete before the block exits
         if ((TSTORE || ROPE || SILU) && lane == 0)
             asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        // ROPE: this thread's row and rotary copies land before the block
+        // exits, also when a bounded wait gave up mid-tile
+        if (ROPE) asm volatile("cp.async.wait_all;" ::: "memory");
     }
 
     tc_fence_before();
