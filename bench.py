@@ -377,6 +377,8 @@ def main():
                "h2d_bytes_per_step": int(res.h2d_bytes / max(res.chunks, 1)),
                "d2h_bytes_per_step": int(res.d2h_bytes / max(res.chunks, 1)),
                "rows": int(e2e_rows), "seconds": e2e_s,
+               "host_seconds": {k: round(v, 4) for k, v in sorted(res.timing.items())},
+               "forward_seconds": round(res.gpu_s, 4),
                "note": "host token lists -> prefix tree, packing, pinned H2D, forward, "
                        "D2H bits+margins" + (", NCCL all-gather" if world > 1 else "")}
 
