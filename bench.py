@@ -51,7 +51,7 @@ UNIT = "rows/s"
 # x 36 layers), from the ncu launch list in profiles/launch_list_config1.md
 # (dram__bytes_read.sum + dram__bytes_write.sum, one pass, same workload as
 # this bench)
-GEMM_DRAM_BYTES_PER_LAUNCH = 1.8058e9
+GEMM_DRAM_BYTES_PER_LAUNCH = 1.8043e9
 GEMM_TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/launch_list_config1.md"
 
 
