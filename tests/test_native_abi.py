@@ -73,6 +73,19 @@ def test_invalid_fused_qkv_calls_are_rejected(lib):
     with pytest.raises(ValueError, match="head_dim"):
         nat.call("qb_gemm_fp8_qknorm_rope", None, None, 8, None, None, 8, 256, None, None, 10,
                  None, None, 1e-6, 4, 2, 64, None, None, None, None, None, None, 0, None)
+    # the rotary table and norm weights are copied 16 bytes at a time: a
+    # 4-byte aligned cos_sin (enough for qb_qknorm_rope) is refused here
+    ok16, four = ctypes.c_void_p(0x1000), ctypes.c_void_p(0x1004)
+    with pytest.raises(ValueError, match="16-byte aligned"):
+        nat.call("qb_gemm_fp8_qknorm_rope", ok16, ok16, 8, ok16, ok16, 8, 256, ok16, four, 10,
+                 ok16, ok16, 1e-6, 4, 2, 128, ok16, ok16, ok16, None, None, None, 0, None)
+    with pytest.raises(ValueError, match="16-byte aligned"):
+        nat.call("qb_gemm_fp8_qknorm_rope", ok16, ok16, 8, ok16, ok16, 8, 256, ok16, ok16, 10,
+                 four, ok16, 1e-6, 4, 2, 128, ok16, ok16, ok16, None, None, None, 0, None)
+    # a KV pool whose rows do not fit a 32-bit TMA coordinate
+    with pytest.raises(ValueError, match="pool_rows"):
+        nat.call("qb_gemm_fp8_qknorm_rope", ok16, ok16, 8, ok16, ok16, 8, 256, ok16, ok16, 10,
+                 ok16, ok16, 1e-6, 4, 2, 128, ok16, ok16, ok16, ok16, ok16, ok16, 1 << 31, None)
 
 
 def test_invalid_attention_and_norm_calls_are_rejected(lib):
