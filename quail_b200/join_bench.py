@@ -5,8 +5,16 @@
 every one of the M right rows (pairs = N x M). Config 2 shards by left row,
 so a GPU's share is a contiguous run of anchors against the whole right
 table; N anchors out of 200 is one GPU's slice of a larger run. One
-untimed warm-up join of one anchor precedes the timed one. Prints one JSON
-line:
+untimed warm-up join of one anchor precedes the timed one.
+
+``--workload exists --outer N`` runs config 4's EXISTS variant instead: N
+outer rows (64-token shared prefix | 512-token context), each against its
+own 8 candidate documents of 4096-16384 tokens (pairs = 8 N), every
+candidate scored as the reference's join does (gate_group keeps an outer
+row with any TRUE answer; there is no early stop at the first TRUE). It
+reports outer rows/s and the EXISTS survivors as well.
+
+Prints one JSON line:
 
 - ``e2e``: pairs/s through the public call (prefix tree, admission and
   packing on the host, pinned H2D, the forwards, D2H of the answer bits),
@@ -27,7 +35,7 @@ import time
 
 from quail_b200.api import B200Executor
 from quail_b200.model import QWEN3_4B
-from quail_b200.workload import config2
+from quail_b200.workload import config2, config4_exists
 
 
 def cpu_sample(torch, weights, wl, partners, page_tokens=16):
@@ -74,8 +82,49 @@ def cpu_sample(torch, weights, wl, partners, page_tokens=16):
     return time.perf_counter() - t0, partners, sum(h.tokens for h in hosts)
 
 
+def exists_main(torch, args):
+    """Config 4's EXISTS variant: outer rows 1..N against their candidates."""
+    wl = config4_exists()
+    ex = B200Executor(torch, QWEN3_4B, args.pages)
+    budget = args.budget or None
+    # warm-up: outer row 0 against two of its candidates
+    ex.join([wl.anchors[0]], [wl.candidates(0)[:2]], budget=budget)
+    ex.reset_arena()
+    outer = list(range(1, 1 + args.outer))
+    anchors = [wl.anchors[a] for a in outer]
+    suffixes, partners = [], []
+    for a in outer:
+        first = len(suffixes)
+        suffixes.extend(wl.candidates(a))
+        partners.append([list(range(first, len(suffixes)))])
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    res = ex.join(anchors, [suffixes], budget=budget, partners=partners)
+    wall = time.perf_counter() - t0
+    pairs = len(suffixes)
+    logical = sum(len(anchors[i]) * wl.n_candidates for i in range(len(anchors))) + sum(
+        len(x) for x in suffixes)
+    survivors = res.survivors("semi")
+    return {
+        "metric": "EXISTS outer rows/s (Qwen3-4B FP8, config 4 EXISTS variant)",
+        "unit": "outer rows/s", "value": len(outer) / res.gpu_s, "e2e": len(outer) / wall,
+        "pairs_per_s": pairs / res.gpu_s, "outer_rows": len(outer), "pairs": pairs,
+        "exists_survivors": len(survivors), "gpu_s": res.gpu_s, "wall_s": wall,
+        "chunks": res.chunks, "logical_tokens": logical, "fresh_tokens": res.fresh_tokens,
+        "borrowed_tokens": res.borrowed_tokens,
+        "prefill_tokens_per_s": res.fresh_tokens / res.gpu_s,
+        "h2d_bytes": res.h2d_bytes, "d2h_bytes": res.d2h_bytes,
+        "config": {"workload": f"config4 EXISTS: outer rows 1..{len(outer)}, "
+                               f"{wl.n_candidates} candidates each, tree attention, every "
+                               f"candidate scored", "budget": budget or ex.budget},
+        "data": "synthetic (seeded config-4 EXISTS shapes; random-init Qwen3-4B FP8 weights)",
+    }
+
+
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    p.add_argument("--workload", choices=["config2", "exists"], default="config2")
+    p.add_argument("--outer", type=int, default=4, help="EXISTS outer rows timed")
     p.add_argument("--left", type=int, default=8, help="anchors (left rows) timed")
     p.add_argument("--right", type=int, default=500, help="partners (right rows)")
     p.add_argument("--pages", type=int, default=16384)
@@ -85,6 +134,9 @@ def main(argv=None):
     args = p.parse_args(argv)
     import torch
 
+    if args.workload == "exists":
+        print(json.dumps(exists_main(torch, args)))
+        return
     wl = config2(right=args.right)
     ex = B200Executor(torch, QWEN3_4B, args.pages)
     budget = args.budget or None

@@ -142,6 +142,47 @@ def config2(left=200, right=500, seed=0) -> JoinWorkload:
     return JoinWorkload("config2", "qwen3-4b-fp8", anchors, partners, 48)
 
 
+@dataclass
+class ExistsWorkload:
+    """Config 4's EXISTS variant: outer rows (anchors) each scored against
+    their own correlated candidate rows, not a cross product.
+
+    anchors[a] = the 64-token shared prefix | outer row a's 512-token
+    context (the second-level prefix its candidates share);
+    candidates(a) = its candidate documents, each followed by the question
+    tail. An outer row survives EXISTS when any candidate answers TRUE.
+    """
+    name: str
+    model: str
+    anchors: Sequence
+    n_candidates: int
+    candidate_lengths: np.ndarray   # [outer rows, n_candidates]
+    tail: list
+    seed: int
+
+    def candidates(self, a: int) -> list:
+        """Outer row a's candidate token lists (generated on access)."""
+        out = []
+        for j, n in enumerate(self.candidate_lengths[a]):
+            rng = np.random.default_rng([self.seed, a, j])
+            out.append(rng.integers(1000, 150000, int(n)).tolist() + self.tail)
+        return out
+
+
+def config4_exists(outer=4_000, candidates=8, seed=0) -> ExistsWorkload:
+    """Qwen3-4B FP8 EXISTS probe: a 64-token shared prefix and a 512-token
+    context per outer row (the second-level prefix), then 8 candidate
+    documents per outer row with config 4's lengths (uniform in [4096,
+    16384] tokens), ids uniform in [1000, 150000)."""
+    rng = np.random.default_rng(seed)
+    prefix = rng.integers(1000, 150000, 64)
+    context = np.full(outer, 512, dtype=np.int64)
+    lens = rng.integers(4096, 16385, (outer, candidates)).astype(np.int64)
+    return ExistsWorkload("config4-exists", "qwen3-4b-fp8",
+                          DocRows(prefix, context, 1000, 150000, seed + 1), candidates, lens,
+                          _question(), seed + 2)
+
+
 def shard(n_rows: int, rank: int, world: int) -> tuple:
     """Contiguous row slice [lo, hi) of one rank."""
     per = -(-n_rows // world)

@@ -201,6 +201,54 @@ def test_join_survivors_semi_and_anti():
     assert res.survivors("anti") == [1, 2, 3, 4]
 
 
+def test_exists_workload_scores_each_candidate_once():
+    """Config 4's EXISTS variant through run_join's per-anchor partner lists:
+    every outer row answers exactly its own candidates, each candidate is
+    packed once, the outer rows once with their shared 64-token prefix
+    computed by the first and borrowed by the others, and no chunk exceeds
+    the budget."""
+    from quail_b200.workload import config4_exists
+    wl = config4_exists(outer=6)
+    outer = [1, 2, 3]
+    anchors = [wl.anchors[a] for a in outer]
+    sufs, partners = [], []
+    for a in outer:
+        first = len(sufs)
+        sufs.extend(wl.candidates(a))
+        partners.append([list(range(first, len(sufs)))])
+    assert all(len(x) == 576 for x in anchors)
+    assert all(4096 + 1 <= len(x) <= 16384 + 1 for x in sufs)
+    arena = KVArena(1, 16384, 16, 1, 8, device=None)
+    budget = 110376
+    sizes = []
+
+    class Recorder(ModelPipeline):
+        tree_attention = True
+
+        def forward_chunk(self, chunk):
+            sizes.append(chunk.host.tokens)
+            return len(chunk.host.final_indices)
+
+    class Answers:
+        dtype = None  # 0/1 answer rows, as AsyncAnswers
+
+        def submit(self, n):
+            return [1] * n
+
+        def result(self, handle):
+            return handle
+
+    stats = {}
+    answers, _, tokens = loop.run_join(
+        torch, arena, Recorder(), Answers(), anchors, [sufs], budget, attention_mode="tree",
+        prefix_tree=prefix_tree(anchors, 16), anchor_partners=lambda k: partners[k],
+        stats=stats, device="cpu")
+    assert {a: len(row) for a, row in answers[0].items()} == {0: 8, 1: 8, 2: 8}
+    assert stats["borrowed_tokens"] == 64 * (len(anchors) - 1)
+    assert tokens == sum(map(len, anchors)) + sum(map(len, sufs)) - stats["borrowed_tokens"]
+    assert max(sizes) <= budget
+
+
 def test_token_store_reads_reference_file():
     """The host input format: a token store file written by the reference's
     TokenStore opens here with the same documents and lengths, and (checked
