@@ -48,11 +48,12 @@ UNIT = "rows/s"
 # DRAM bytes (read + write) per GEMM launch, averaged over the 144 launches
 # of one config-1 chunk (o, down: qb_gemm_fp8_bs; qkv with q/k norm, rotary
 # and KV append: qb_gemm_fp8_qknorm_rope; gate_up: qb_gemm_fp8_silu_quant;
-# x 36 layers), from the ncu launch list in profiles/launch_list_config1.md
-# (dram__bytes_read.sum + dram__bytes_write.sum, one pass, same workload as
-# this bench)
+# x 36 layers). A profile constant, not measured in this run: ncu's
+# dram__bytes_read.sum + dram__bytes_write.sum over the launch list of this
+# bench's own workload (one pass per launch).
 GEMM_DRAM_BYTES_PER_LAUNCH = 1.8043e9
-GEMM_TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/launch_list_config1.md"
+GEMM_TRAFFIC_SOURCE = ("profile constant: ncu dram__bytes_read.sum + dram__bytes_write.sum, "
+                       "mean over the GEMM launches of one config-1 chunk")
 
 
 def parse_args():
@@ -62,9 +63,14 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--pages", type=int, default=16384)
-    p.add_argument("--cpu-rows", type=int, default=2)
+    p.add_argument("--cpu-rows", type=int, default=4,
+                   help="config-1 rows 0..n-1 (the prefix parent and n-1 borrowing rows) "
+                        "of the CPU baseline's sample")
     p.add_argument("--ref-rows", type=int, default=1,
                    help="config-1 rows per step of the reference arm's CPU sample")
+    p.add_argument("--e2e-rows", type=int, default=25000,
+                   help="rows of the rank's share run end to end (the whole share when "
+                        "it is smaller)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--budget", type=int, default=0)
@@ -142,18 +148,26 @@ def setup_dist(args):
     return world, rank, local
 
 
-def rows_needed(wl, lo, chunks, budget):
-    lens = wl.docs.lengths[lo:]
-    per_row = wl.prefix_tokens + float(np.mean(lens[:20000])) + len(wl.questions[0])
-    return int((chunks + 1) * budget / per_row * 1.15) + 64
+def rows_needed(wl, lo, hi, chunks, budget):
+    """Rows of [lo, hi) whose fresh tokens fill `chunks` chunks, plus 5%.
+
+    A borrowing row puts only its suffix and question tail into a chunk
+    (the shared prefix pages are the tree parent's), so the estimate counts
+    those tokens, row by row, until `chunks` budgets are covered."""
+    fresh = np.cumsum(wl.fresh_row_tokens(lo, hi)) + wl.prefix_tokens
+    n = int(np.searchsorted(fresh, chunks * budget)) + 1
+    return min(hi - lo, int(n * 1.05) + 64)
 
 
-def prepack(torch, ex, docs, questions, budget, n_chunks):
-    """Pack n_chunks chunks through the real filter loop without computing.
+def pack_chunks(torch, arena, docs, questions, budget, n_chunks, device):
+    """Pack chunks through the real filter loop without computing them.
 
-    Returns the uploaded device chunks in launch order; the arena's page
-    tables evolve exactly as in a real run of a single-stage filter (pages
-    of chunk i are freed once chunk i+1 is launched)."""
+    Packs until n_chunks + 1 chunks exist, so the first n_chunks were each
+    closed by the budget (a stream's last chunk holds only what was left),
+    or until the rows run out. Returns (chunks in launch order, whether the
+    first n_chunks are all closed by the budget). The arena's page tables
+    evolve exactly as in a real run of a single-stage filter: the pages of
+    chunk i are freed once chunk i+1 is launched."""
     from quail_b200 import loop
     from quail_b200.pipeline import ModelPipeline
     from quail_b200.tokens import prefix_tree
@@ -174,14 +188,34 @@ def prepack(torch, ex, docs, questions, budget, n_chunks):
         def result(self, handle):
             return handle
 
-    stream = loop.FilterStream(torch, ex.arena, Recorder(), Answers(), docs, questions, budget,
+    stream = loop.FilterStream(torch, arena, Recorder(), Answers(), docs, questions, budget,
                                arena_writes=True, attention_mode="tree",
-                               prefix_tree=prefix_tree(docs, 16), device=ex.device)
-    while len(chunks) < n_chunks and not stream.done:
+                               prefix_tree=prefix_tree(docs, 16), device=device)
+    while len(chunks) < n_chunks + 1 and not stream.done:
         stream.next()
-    if len(chunks) < n_chunks:
-        raise RuntimeError(f"only {len(chunks)} chunks for {n_chunks} steps")
-    return chunks
+    full = len(chunks) > n_chunks
+    return chunks[:n_chunks], full
+
+
+def prepack(torch, arena, wl, lo, hi, budget, n_chunks, device):
+    """n_chunks budget-filled chunks from the rows [lo, hi) of the workload.
+
+    Starts from the rows_needed estimate and doubles the row count (with
+    a fresh arena) until the packer closes n_chunks chunks on the budget.
+    Raises when even the whole slice gives fewer than n_chunks chunks.
+    Returns (chunks, rows used)."""
+    n_rows = rows_needed(wl, lo, hi, n_chunks, budget)
+    while True:
+        docs = wl.docs[lo:lo + n_rows]
+        chunks, full = pack_chunks(torch, arena, docs, wl.questions, budget, n_chunks, device)
+        if full or (n_rows == hi - lo and len(chunks) == n_chunks):
+            return chunks, n_rows
+        if n_rows == hi - lo:
+            raise RuntimeError(f"rows [{lo}, {hi}) pack only {len(chunks)} chunks for "
+                               f"{n_chunks} steps")
+        del chunks
+        arena.reset()
+        n_rows = min(hi - lo, 2 * n_rows)
 
 
 def cpu_baseline(torch, weights, wl, rows, page_tokens=16):
@@ -277,7 +311,7 @@ def main():
     from quail_b200 import _native as nat
     from quail_b200.api import B200Executor
     from quail_b200.model import QWEN3_4B
-    from quail_b200.workload import config1, shard
+    from quail_b200.workload import config1, token_shard
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -288,12 +322,12 @@ def main():
     wl = config1()
     budget = args.budget or cfg.max_chunk_tokens
     ex = B200Executor(torch, cfg, args.pages, device=dev, seed=0)
-    lo, hi = shard(wl.rows, rank, world)
-    n_rows = min(hi - lo, rows_needed(wl, lo, args.warmup + args.steps, budget))
-    docs = wl.docs[lo:lo + n_rows]
+    lo, hi = token_shard(wl.row_tokens(), rank, world)
 
     # ---- device-resident timing: chunks packed and uploaded beforehand ----
-    chunks = prepack(torch, ex, docs, wl.questions, budget, args.warmup + args.steps)
+    chunks, n_rows = prepack(torch, ex.arena, wl, lo, hi, budget, args.warmup + args.steps,
+                             ex.device)
+    docs = wl.docs[lo:lo + n_rows]
     torch.cuda.synchronize()
 
     def run(chunk):
@@ -350,7 +384,7 @@ def main():
     e2e = None
     if not args.no_e2e:
         ex.reset_arena()
-        e2e_docs = [docs[d] for c in timed for d, _ in c.layout]
+        e2e_docs = wl.docs[lo:lo + min(hi - lo, args.e2e_rows)]
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()

@@ -41,7 +41,9 @@ int qb_version(void);
 const char* qb_last_error(void);
 
 /* Reads and clears the device status word the tcgen05 kernels set when a
- * bounded wait gives up (0 = no timeout seen). Synchronises the device. */
+ * bounded wait gives up (0 = no timeout seen). Synchronises the device,
+ * then takes the word and leaves 0 in one atomic exchange on the device,
+ * so no bit set meanwhile by another stream is lost. */
 int qb_kernel_status(int device, uint32_t* status_out);
 
 /*

@@ -514,16 +514,9 @@ int launch_attention(const char* who, const void* q, const void* k, const void* 
     uint32_t* status = device_status_ptr();
     if (!status) return launch_status(who);
     const size_t smem = smem_bytes(MAX_HP, !UNIFIED);
-    static bool attr_set[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        if (cudaFuncSetAttribute(tree_attention_kernel<UNIFIED>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem) != cudaSuccess)
-            return launch_status(who);
-        attr_set[dev] = true;
-    }
+    static std::atomic<bool> attr_set[MAX_DEVICES];
+    if (!set_smem_once(attr_set, tree_attention_kernel<UNIFIED>, (int)smem))
+        return launch_status(who);
     dim3 grid((unsigned)n_tiles, (unsigned)(n_kv * (group / hp)));
     tree_attention_kernel<UNIFIED><<<grid, ROW_GROUPS * 32 * hp, smem_bytes(hp, !UNIFIED),
                                      (cudaStream_t)stream>>>(

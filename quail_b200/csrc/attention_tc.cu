@@ -964,15 +964,8 @@ int launch_attention_tc(bool unified, const char* who, const void* q, const void
         mvp = mv;
     }
     auto kernel = unified ? attention_tc_kernel<true> : attention_tc_kernel<false>;
-    static bool attr[2][64] = {{false}};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr[unified][dev]) {
-        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)SMEM_BYTES) != cudaSuccess)
-            return launch_status(who);
-        attr[unified][dev] = true;
-    }
+    static std::atomic<bool> attr[2][MAX_DEVICES];
+    if (!set_smem_once(attr[unified], kernel, (int)SMEM_BYTES)) return launch_status(who);
     // persistent: one block per SM walks the items (query tile x head group,
     // head groups of a tile adjacent so they share K/V in L2)
     const int64_t items = n_tiles * (int64_t)(n_kv * (group / hp));

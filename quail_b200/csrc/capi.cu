@@ -22,16 +22,19 @@ void set_error(const char* fmt, ...) {
 }
 
 uint32_t* device_status_ptr() {
-    // cudaGetSymbolAddress is per device; cache the address per device id.
-    static uint32_t* cache[64] = {nullptr};
+    // cudaGetSymbolAddress is per device; the address is cached per device
+    // id (host threads that race here store the same value).
+    static std::atomic<uint32_t*> cache[MAX_DEVICES];
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    if (cache[dev] == nullptr) {
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return nullptr;
+    uint32_t* got = cache[dev].load(std::memory_order_acquire);
+    if (got == nullptr) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, qb_device_status) != cudaSuccess) return nullptr;
-        cache[dev] = static_cast<uint32_t*>(p);
+        got = static_cast<uint32_t*>(p);
+        cache[dev].store(got, std::memory_order_release);
     }
-    return cache[dev];
+    return got;
 }
 
 int launch_status(const char* what) {
@@ -49,14 +52,29 @@ extern "C" int qb_version(void) { return (0 << 16) | (1 << 8) | 0; }
 
 extern "C" const char* qb_last_error(void) { return g_last_error; }
 
+namespace {
+// Where status_exchange_kernel leaves the word it took.
+__device__ uint32_t qb_status_taken;
+
+// Takes the status word and leaves 0 in one atomic step, so a bit that
+// another stream's kernel sets meanwhile is either taken here or stays.
+__global__ void status_exchange_kernel() {
+    qb_status_taken = atomicExch(&qb_device_status, 0u);
+}
+}  // namespace
+
 extern "C" int qb_kernel_status(int device, uint32_t* status_out) {
     if (status_out == nullptr) return qb::invalid("qb_kernel_status: status_out is NULL");
     int prev = 0;
     cudaGetDevice(&prev);
     if (cudaSetDevice(device) != cudaSuccess) return qb::launch_status("qb_kernel_status: cudaSetDevice");
-    uint32_t zero = 0, value = 0;
-    cudaError_t e = cudaMemcpyFromSymbol(&value, qb_device_status, sizeof(value));
-    if (e == cudaSuccess) e = cudaMemcpyToSymbol(qb_device_status, &zero, sizeof(zero));
+    uint32_t value = 0;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) {
+        status_exchange_kernel<<<1, 1>>>();
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&value, qb_status_taken, sizeof(value));
     cudaSetDevice(prev);
     if (e != cudaSuccess) {
         qb::set_error("qb_kernel_status: %s", cudaGetErrorString(e));

@@ -14,6 +14,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
+
 #include "../../include/quail_b200.h"
 
 typedef __nv_bfloat16 bf16;
@@ -51,6 +53,27 @@ enum : uint32_t {
 inline int invalid(const char* what) {
     set_error("%s", what);
     return QB_ERR_INVALID;
+}
+
+// Devices a per-device "done once" flag covers (cudaGetDevice ids).
+constexpr int MAX_DEVICES = 64;
+
+// Raises a kernel's dynamic shared-memory limit once per device. `done`
+// is the kernel's own array of MAX_DEVICES flags; several host threads may
+// race here, and each then sets the same attribute (an idempotent call).
+// Returns false when the CUDA call fails (its error is left for
+// launch_status to report).
+template <typename Kernel>
+inline bool set_smem_once(std::atomic<bool>* done, Kernel kernel, int bytes) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    const bool cached = dev >= 0 && dev < MAX_DEVICES;
+    if (cached && done[dev].load(std::memory_order_acquire)) return true;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+        cudaSuccess)
+        return false;
+    if (cached) done[dev].store(true, std::memory_order_release);
+    return true;
 }
 
 inline bool aligned(const void* p, size_t bytes) {

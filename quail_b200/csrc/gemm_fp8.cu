@@ -892,15 +892,9 @@ int launch(const void* a, const float* a_scale, int64_t a_scale_ld, const void* 
         if (st) return st;
     }
     auto kernel = gemm_fp8_bs_kernel<BN, OutT, NST, TSTORE, SILU, ROPE>;
-    static bool attr[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             C::SMEM);
-        if (e != cudaSuccess) return launch_status("qb_gemm_fp8_bs: smem attribute");
-        attr[dev] = true;
-    }
+    static std::atomic<bool> attr[MAX_DEVICES];
+    if (!set_smem_once(attr, kernel, C::SMEM))
+        return launch_status("qb_gemm_fp8_bs: smem attribute");
     uint32_t* status = device_status_ptr();
     if (!status) return launch_status("qb_gemm_fp8_bs: status word");
     const int64_t tiles = ((m + BM - 1) / BM) * (n / BN);

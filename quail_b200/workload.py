@@ -71,6 +71,18 @@ class Workload:
         n = hi - lo
         return int(lengths.sum() + n * (self.prefix_tokens + len(self.questions[0])))
 
+    def row_tokens(self) -> np.ndarray:
+        """Logical tokens (prefix + suffix + tail) of every row, in row order."""
+        lengths = self.docs.lengths[self.docs.start:self.docs.start + len(self.docs)]
+        return lengths + self.prefix_tokens + len(self.questions[0])
+
+    def fresh_row_tokens(self, lo=0, hi=None) -> np.ndarray:
+        """Tokens each row of [lo, hi) puts into a chunk when its first
+        prefix_tokens are borrowed from a resident parent: suffix + tail."""
+        hi = len(self.docs) if hi is None else hi
+        lengths = self.docs.lengths[self.docs.start + lo:self.docs.start + hi]
+        return lengths + len(self.questions[0])
+
 
 def _question():
     return [int(np.random.default_rng(3).integers(1000, 150000))]
@@ -184,7 +196,34 @@ def config4_exists(outer=4_000, candidates=8, seed=0) -> ExistsWorkload:
 
 
 def shard(n_rows: int, rank: int, world: int) -> tuple:
-    """Contiguous row slice [lo, hi) of one rank."""
+    """Contiguous row slice [lo, hi) of one rank (equal row counts)."""
     per = -(-n_rows // world)
     lo = min(n_rows, rank * per)
     return lo, min(n_rows, lo + per)
+
+
+def token_shard(row_tokens, rank: int, world: int) -> tuple:
+    """Contiguous row slice [lo, hi) of one rank, balanced by tokens.
+
+    Rank k's slice ends at the row boundary nearest to k/world of the total
+    token count (running sums over row_tokens), so every rank gets about
+    the same prefill work whatever the length distribution. Quail's filter
+    planner splits ordered documents into token-balanced contiguous ranges
+    the same way (quail/planner/decide.py:308-338, contiguous_shards);
+    results are per row, so where the cut falls changes no answer.
+    """
+    c = np.cumsum(np.asarray(row_tokens, dtype=np.int64))
+    n = len(c)
+    total = int(c[-1]) if n else 0
+
+    def cut(k):
+        if k <= 0 or n == 0:
+            return 0
+        if k >= world:
+            return n
+        target = total * k / world
+        i = min(int(np.searchsorted(c, target)), n - 1)   # first row reaching target
+        before = int(c[i - 1]) if i else 0
+        return i + 1 if int(c[i]) - target <= target - before else i
+
+    return cut(rank), cut(rank + 1)

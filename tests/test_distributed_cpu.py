@@ -20,9 +20,10 @@ import torch.multiprocessing as mp
 
 from quail_b200 import loop
 from quail_b200.arena import KVArena
-from quail_b200.distributed import RankFailed, run_sharded, run_sharded_join
+from quail_b200.distributed import RankFailed, gather_rows, run_sharded, run_sharded_join
 from quail_b200.pipeline import ModelPipeline
 from quail_b200.tokens import prefix_tree
+from quail_b200.workload import token_shard
 
 N_ROWS = 37
 
@@ -124,7 +125,14 @@ def _worker(rank, world, port, mode, out):
             rows = run_sharded_join(torch, dist, len(anchors), len(stages), run_join_slice)
             out.put((rank, "ok", [{a: r.tolist() for a, r in st.items()} for st in rows], None))
             return
-        bits, margins = run_sharded(torch, dist, len(docs), run_slice)
+        if mode == "int64":
+            # ids past 2^24 survive the gather unchanged
+            mine = np.arange(3 + rank, dtype=np.int64) + (1 << 40) + (rank << 33) + 1
+            got = gather_rows(torch, dist, mine, "cpu", np.int64)
+            out.put((rank, "ok", [int(x) for x in got], str(got.dtype)))
+            return
+        row_tokens = [len(d) + 1 for d in docs] if mode == "tokens" else None
+        bits, margins = run_sharded(torch, dist, len(docs), run_slice, row_tokens=row_tokens)
         out.put((rank, "ok", bits.tolist(), margins.tolist()))
     except RankFailed as exc:
         out.put((rank, "RankFailed", str(exc), None))
@@ -166,6 +174,32 @@ def test_two_ranks_reproduce_single_process_answers():
         assert kind == "ok"
         assert np.array_equal(np.asarray(bits), want_bits.astype(np.uint8))
         assert np.allclose(margins, want_margins)
+
+
+def test_token_balanced_ranks_reproduce_single_process_answers():
+    """Slices balanced by tokens: the same per-row answers in row order."""
+    docs = make_docs()
+    tok = [len(d) + 1 for d in docs]
+    cuts = [token_shard(tok, r, 2) for r in range(2)]
+    assert cuts[0][1] == cuts[1][0]
+    want_bits, want_margins = (np.concatenate(x) for x in zip(
+        *(cpu_filter(docs[a:b]) for a, b in cuts)))
+    results = run_ranks("tokens")
+    for rank in (0, 1):
+        kind, bits, margins = results[rank]
+        assert kind == "ok"
+        assert np.array_equal(np.asarray(bits), want_bits.astype(np.uint8))
+        assert np.allclose(margins, want_margins)
+
+
+def test_int64_gather_keeps_large_ids():
+    results = run_ranks("int64")
+    want = [int(x) for r in range(2)
+            for x in np.arange(3 + r, dtype=np.int64) + (1 << 40) + (r << 33) + 1]
+    for rank in (0, 1):
+        kind, got, dtype = results[rank]
+        assert kind == "ok" and dtype == "int64"
+        assert got == want
 
 
 def test_a_raising_rank_fails_every_rank():
