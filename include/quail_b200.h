@@ -46,6 +46,15 @@ const char* qb_last_error(void);
  * so no bit set meanwhile by another stream is lost. */
 int qb_kernel_status(int device, uint32_t* status_out);
 
+/* Sets how long the kernels' bounded waits on `device` wait before they give
+ * up (ns; 0 restores the default of one second). Waits for copies and MMAs
+ * a block already issued keep their own one-second limit, so a shortened
+ * limit ends only the waits on other roles. A diagnostic for tests of the
+ * give-up path (status bits, abort fan-out, TMEM freed); it synchronises the
+ * device. Replaces nothing in the reference: Quail's workers detect a failed
+ * GPU child on the host (quail/backends/quail/worker.py:382-384). */
+int qb_set_wait_limit(int device, uint64_t limit_ns);
+
 /*
  * Layer-0 input norm: hidden = embed[ids]; residual_out = hidden;
  * y = bf16(bf16(hidden * rsqrt(mean(hidden^2) + eps)) * norm_w);

@@ -31,6 +31,7 @@ SIGNATURES = {
     "qb_version": [],
     "qb_last_error": [],
     "qb_kernel_status": [_I32, _P],
+    "qb_set_wait_limit": [_I32, ctypes.c_uint64],
     "qb_embed_rmsnorm_quant": [_P, _I64, _P, _I64, _I64, _P, _F32, _P, _P, _P, _I64, _P],
     "qb_add_rmsnorm_quant": [_P, _P, _P, _F32, _I64, _I64, _P, _P, _I64, _P],
     "qb_gemm_fp8_bs": [_P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _P],
@@ -95,7 +96,8 @@ def check(status: int, what: str) -> None:
 
 # entry points that launch a kernel; LAUNCHES counts them per process
 LAUNCHING = frozenset(n for n in SIGNATURES if n not in (
-    "qb_version", "qb_last_error", "qb_kernel_status", "qb_tree_attention_tiles"))
+    "qb_version", "qb_last_error", "qb_kernel_status", "qb_set_wait_limit",
+    "qb_tree_attention_tiles"))
 LAUNCHES = {"count": 0}
 
 
@@ -120,6 +122,12 @@ def kernel_status(device: int = 0) -> int:
     out = ctypes.c_uint32(0)
     call("qb_kernel_status", device, ctypes.byref(out))
     return out.value
+
+
+def set_wait_limit(device: int = 0, limit_ns: int = 0) -> None:
+    """Shorten (or, with 0, restore to one second) the kernels' bounded
+    waits on a device; a diagnostic for tests of the give-up path."""
+    call("qb_set_wait_limit", device, limit_ns)
 
 
 def version() -> tuple:

@@ -51,6 +51,7 @@ class JoinResult:
     gpu_s: float
     wall_s: float
     n_anchors: int = 0
+    skipped_pairs: int = 0             # EXISTS early stop: partners never computed
 
     def survivors(self, semantics="semi"):
         """Anchors the join keeps (backend.py:231-240): with "semi" (EXISTS)
@@ -129,7 +130,7 @@ class B200Executor:
                             d2h_bytes=ans.d2h_bytes, gpu_s=gpu_s, wall_s=wall, timing=timing)
 
     def _join(self, readout, anchors, stage_suffixes, stage_frames, budget, attention,
-              share_prefixes, partners):
+              share_prefixes, partners, stop_at_true=False, stream_step=None):
         torch = self.torch
         t0 = time.perf_counter()
         tree = prefix_tree(anchors, self.arena.page_tokens) if share_prefixes else None
@@ -139,7 +140,8 @@ class B200Executor:
             [[list(s) for s in sufs] for sufs in stage_suffixes], budget or self.budget,
             stage_frames=stage_frames, attention_mode=attention, prefix_tree=tree,
             anchor_partners=None if partners is None else (lambda key: partners[key]),
-            stats=stats, device=self.device)
+            stats=stats, device=self.device, stop_at_true=stop_at_true,
+            stream_step=stream_step)
         torch.cuda.synchronize(self.device)
         wall = time.perf_counter() - t0
         gpu_s = sum(a.elapsed_time(b) for _, a, b in spans if a is not None) / 1000.0
@@ -147,16 +149,23 @@ class B200Executor:
                           borrowed_tokens=stats.get("borrowed_tokens", 0),
                           chunks=stats.get("chunks", 0), h2d_bytes=stats.get("h2d_bytes", 0),
                           d2h_bytes=readout.d2h_bytes, gpu_s=gpu_s, wall_s=wall,
-                          n_anchors=len(anchors))
+                          n_anchors=len(anchors),
+                          skipped_pairs=stats.get("skipped_partners", 0))
 
     def join(self, anchors, stage_suffixes, *, stage_frames=None, budget=None,
-             attention="tree", share_prefixes=True, partners=None) -> JoinResult:
+             attention="tree", share_prefixes=True, partners=None,
+             exists_stop=False) -> JoinResult:
         """Run one AI join: every anchor against its partners, stage by stage
         (an anchor continues to stage j + 1 once a stage-j partner answered
-        TRUE). partners: per anchor, per stage, partner indices or None."""
+        TRUE). partners: per anchor, per stage, partner indices or None.
+        exists_stop: for an EXISTS (semi) or NOT EXISTS (anti) join, stop an
+        anchor's last-stage stream at its first TRUE answer (partners not yet
+        launched are skipped; survivors are unchanged), with the anchors'
+        streams interleaved one partner per anchor per chunk."""
         ans = AsyncAnswers(self.torch, self.answer_rows)
         return self._join(ans, anchors, stage_suffixes, stage_frames, budget, attention,
-                          share_prefixes, partners)
+                          share_prefixes, partners, stop_at_true=exists_stop,
+                          stream_step=1 if exists_stop else None)
 
     def score(self, anchors, suffixes, *, budget=None, attention="tree",
               share_prefixes=True, partners=None) -> JoinResult:

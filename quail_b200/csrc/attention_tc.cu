@@ -379,21 +379,13 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
         }
         // no copy may still be landing when the block exits
         if (lane == 0) {
-            int flag = 0;
-            if (jq > 0 && !mbar_try_wait(smem_u32(&aux->q_full), (uint32_t)(jq - 1) & 1u))
-                mbar_wait(&aux->q_full, (uint32_t)(jq - 1) & 1u, &flag, status, STATUS_ATTN_LOAD);
-            for (int j = (nk > KST ? nk - KST : 0); j < nk; ++j) {
-                const int st = j % KST;
-                if (!mbar_try_wait(smem_u32(&aux->k_full[st]), (uint32_t)(j / KST) & 1u))
-                    mbar_wait(&aux->k_full[st], (uint32_t)(j / KST) & 1u, &flag, status,
-                              STATUS_ATTN_LOAD);
-            }
-            for (int j = (nv > VST ? nv - VST : 0); j < nv; ++j) {
-                const int st = j % VST;
-                if (!mbar_try_wait(smem_u32(&aux->v_full[st]), (uint32_t)(j / VST) & 1u))
-                    mbar_wait(&aux->v_full[st], (uint32_t)(j / VST) & 1u, &flag, status,
-                              STATUS_ATTN_LOAD);
-            }
+            if (jq > 0) mbar_drain(&aux->q_full, (uint32_t)(jq - 1) & 1u, status, STATUS_ATTN_LOAD);
+            for (int j = (nk > KST ? nk - KST : 0); j < nk; ++j)
+                mbar_drain(&aux->k_full[j % KST], (uint32_t)(j / KST) & 1u, status,
+                           STATUS_ATTN_LOAD);
+            for (int j = (nv > VST ? nv - VST : 0); j < nv; ++j)
+                mbar_drain(&aux->v_full[j % VST], (uint32_t)(j / VST) & 1u, status,
+                           STATUS_ATTN_LOAD);
         }
     } else if (warp == 1) {
         // ------ MMA issuer (lane 0 issues; the warp zeroes V tails): S of the
@@ -571,7 +563,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                                 if (t0 == 0) t0 = now;
                                 if (*abort_flag) {
                                     stop = 1;
-                                } else if (now - t0 > TIMEOUT_NS) {
+                                } else if (now - t0 > wait_limit_ns(status)) {
                                     atomicOr(status, STATUS_ATTN_MMA);
                                     *abort_flag = 1;
                                     stop = 1;
@@ -595,8 +587,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
         // every MMA issued must finish before TMEM is freed
         if (lane == 0) mma_commit(&aux->drain);
         __syncwarp();
-        int flag = 0;
-        mbar_wait(&aux->drain, 0, &flag, status, STATUS_ATTN_MMA);
+        mbar_drain(&aux->drain, 0, status, STATUS_ATTN_MMA);
     } else if (warp < FIRST_CORR) {
         // ------- softmax, then each call's epilogue: one thread per row of an M tile -------
         const int mt = (warp - FIRST_SOFT) >> 2;

@@ -1,5 +1,6 @@
 // Library-wide entry points: version, error messages, device status word.
 #include <stdarg.h>
+#include <stddef.h>
 #include <string.h>
 
 #include "common.cuh"
@@ -8,9 +9,18 @@ namespace {
 thread_local char g_last_error[512] = "";
 }
 
-// Set by the tcgen05 kernels when a bounded wait gives up; read by
-// qb_kernel_status. One word per device that loaded the library.
-__device__ uint32_t qb_device_status;
+// Per device that loaded the library: the status word the kernels set when
+// a bounded wait gives up (read by qb_kernel_status), and the limit of those
+// waits in ns (qb_set_wait_limit). Kernels get the address of `status` and
+// read the limit as the 64-bit word 8 bytes after it (qb::tc::wait_limit_ns).
+struct DeviceHealth {
+    uint32_t status;
+    uint32_t pad;
+    uint64_t wait_limit_ns;
+};
+static_assert(offsetof(DeviceHealth, wait_limit_ns) == 8, "kernels read the limit at status + 2");
+constexpr uint64_t DEFAULT_WAIT_LIMIT_NS = 1000000000ull;
+__device__ DeviceHealth qb_device_health = {0u, 0u, DEFAULT_WAIT_LIMIT_NS};
 
 namespace qb {
 
@@ -30,7 +40,7 @@ uint32_t* device_status_ptr() {
     uint32_t* got = cache[dev].load(std::memory_order_acquire);
     if (got == nullptr) {
         void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, qb_device_status) != cudaSuccess) return nullptr;
+        if (cudaGetSymbolAddress(&p, qb_device_health) != cudaSuccess) return nullptr;
         got = static_cast<uint32_t*>(p);
         cache[dev].store(got, std::memory_order_release);
     }
@@ -59,7 +69,7 @@ __device__ uint32_t qb_status_taken;
 // Takes the status word and leaves 0 in one atomic step, so a bit that
 // another stream's kernel sets meanwhile is either taken here or stays.
 __global__ void status_exchange_kernel() {
-    qb_status_taken = atomicExch(&qb_device_status, 0u);
+    qb_status_taken = atomicExch(&qb_device_health.status, 0u);
 }
 }  // namespace
 
@@ -81,5 +91,21 @@ extern "C" int qb_kernel_status(int device, uint32_t* status_out) {
         return QB_ERR_CUDA;
     }
     *status_out = value;
+    return QB_OK;
+}
+
+extern "C" int qb_set_wait_limit(int device, uint64_t limit_ns) {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(device) != cudaSuccess) return qb::launch_status("qb_set_wait_limit: cudaSetDevice");
+    const uint64_t v = limit_ns ? limit_ns : DEFAULT_WAIT_LIMIT_NS;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess)
+        e = cudaMemcpyToSymbol(qb_device_health, &v, sizeof(v), offsetof(DeviceHealth, wait_limit_ns));
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) {
+        qb::set_error("qb_set_wait_limit: %s", cudaGetErrorString(e));
+        return QB_ERR_CUDA;
+    }
     return QB_OK;
 }

@@ -282,11 +282,7 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
             // last load issued on each stage
             for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j) {
                 const int s = j % STAGES;
-                if (!mbar_try_wait(smem_u32(&bars->full[s]), (uint32_t)(j / STAGES) & 1u)) {
-                    int flag = 0;
-                    mbar_wait(&bars->full[s], (uint32_t)(j / STAGES) & 1u, &flag, status,
-                              STATUS_GEMM_DRAIN);
-                }
+                mbar_drain(&bars->full[s], (uint32_t)(j / STAGES) & 1u, status, STATUS_GEMM_DRAIN);
             }
         }
     } else if (warp == 1) {
@@ -324,8 +320,7 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
             }
             // every MMA issued must finish before TMEM is freed
             mma_commit(&bars->drain);
-            int flag = 0;
-            mbar_wait(&bars->drain, 0, &flag, status, STATUS_GEMM_DRAIN);
+            mbar_drain(&bars->drain, 0, status, STATUS_GEMM_DRAIN);
         }
     } else if (warp == 2) {
         // ---------------- scale loader ----------------

@@ -11,9 +11,9 @@
 namespace qb {
 namespace tc {
 
-// a wait gives up after this long (the kernel then sets a status bit and
-// stops; the host reads QB_ERR_TIMEOUT)
-constexpr uint64_t TIMEOUT_NS = 1000000000ull;
+// Waits for copies and MMAs already in flight (the drains before a block
+// exits) give up after this long; they always end on their own well before.
+constexpr uint64_t DRAIN_LIMIT_NS = 1000000000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -51,22 +51,49 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
     return ok != 0;
 }
 
-// Waits for the phase with the given parity; false when it gave up (timeout
-// or another role aborted), after which the caller stops its loop.
+// The give-up limit of a kernel's own waits, in ns: the 64-bit word after
+// the status word (see DeviceHealth in capi.cu; one second unless
+// qb_set_wait_limit changed it).
+__device__ __forceinline__ uint64_t wait_limit_ns(const uint32_t* status) {
+    return *reinterpret_cast<const volatile uint64_t*>(status + 2);
+}
+
+// Waits for the phase with the given parity; false when it gave up (the
+// wait limit ran out, or another role aborted), after which the caller
+// stops its loop.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           uint32_t* status, uint32_t bit) {
     const uint32_t addr = smem_u32(bar);
     if (mbar_try_wait(addr, parity)) return true;
     const uint64_t start = globaltimer();
+    const uint64_t limit = wait_limit_ns(status);
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(addr, parity)) return true;
-        if ((it & 255u) == 0) {
+        // try_wait suspends for a while before it fails, so the clock is
+        // read after the first failed retry and then every 256
+        if (it == 1 || (it & 255u) == 0) {
             if (*abort_flag) return false;
-            if (globaltimer() - start > TIMEOUT_NS) {
+            if (globaltimer() - start > limit) {
                 atomicOr(status, bit);
                 *abort_flag = 1;
                 return false;
             }
+        }
+    }
+}
+
+// A drain: waits for copies or MMAs this block already issued, which end on
+// their own, so neither the abort flag nor the shortened limit applies.
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity, uint32_t* status,
+                                           uint32_t bit) {
+    const uint32_t addr = smem_u32(bar);
+    if (mbar_try_wait(addr, parity)) return true;
+    const uint64_t start = globaltimer();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(addr, parity)) return true;
+        if ((it & 255u) == 0 && globaltimer() - start > DRAIN_LIMIT_NS) {
+            atomicOr(status, bit);
+            return false;
         }
     }
 }

@@ -9,10 +9,14 @@ untimed warm-up join of one anchor precedes the timed one.
 
 ``--workload exists --outer N`` runs config 4's EXISTS variant instead: N
 outer rows (64-token shared prefix | 512-token context), each against its
-own 8 candidate documents of 4096-16384 tokens (pairs = 8 N), every
-candidate scored as the reference's join does (gate_group keeps an outer
-row with any TRUE answer; there is no early stop at the first TRUE). It
-reports outer rows/s and the EXISTS survivors as well.
+own 8 candidate documents of 4096-16384 tokens (pairs = 8 N). By default
+the scoring short-circuits per outer row on its first positive margin
+(``exists_stop``: the outer rows' candidate streams interleave one
+candidate per outer row per chunk, and the candidates of an outer row not
+yet launched when one answers TRUE are skipped); ``--no-stop`` scores every
+candidate as the reference's join does (gate_group keeps an outer row with
+any TRUE answer). It reports outer rows/s, the candidate pairs skipped and
+the EXISTS survivors as well.
 
 Prints one JSON line:
 
@@ -99,7 +103,8 @@ def exists_main(torch, args):
         partners.append([list(range(first, len(suffixes)))])
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    res = ex.join(anchors, [suffixes], budget=budget, partners=partners)
+    res = ex.join(anchors, [suffixes], budget=budget, partners=partners,
+                  exists_stop=not args.no_stop)
     wall = time.perf_counter() - t0
     pairs = len(suffixes)
     logical = sum(len(anchors[i]) * wl.n_candidates for i in range(len(anchors))) + sum(
@@ -109,14 +114,17 @@ def exists_main(torch, args):
         "metric": "EXISTS outer rows/s (Qwen3-4B FP8, config 4 EXISTS variant)",
         "unit": "outer rows/s", "value": len(outer) / res.gpu_s, "e2e": len(outer) / wall,
         "pairs_per_s": pairs / res.gpu_s, "outer_rows": len(outer), "pairs": pairs,
+        "pairs_skipped": res.skipped_pairs, "pairs_scored": pairs - res.skipped_pairs,
         "exists_survivors": len(survivors), "gpu_s": res.gpu_s, "wall_s": wall,
         "chunks": res.chunks, "logical_tokens": logical, "fresh_tokens": res.fresh_tokens,
         "borrowed_tokens": res.borrowed_tokens,
         "prefill_tokens_per_s": res.fresh_tokens / res.gpu_s,
         "h2d_bytes": res.h2d_bytes, "d2h_bytes": res.d2h_bytes,
         "config": {"workload": f"config4 EXISTS: outer rows 1..{len(outer)}, "
-                               f"{wl.n_candidates} candidates each, tree attention, every "
-                               f"candidate scored", "budget": budget or ex.budget},
+                               f"{wl.n_candidates} candidates each, tree attention, "
+                               + ("every candidate scored" if args.no_stop else
+                                  "short-circuit per outer row on the first TRUE"),
+                   "budget": budget or ex.budget},
         "data": "synthetic (seeded config-4 EXISTS shapes; random-init Qwen3-4B FP8 weights)",
     }
 
@@ -125,6 +133,8 @@ def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     p.add_argument("--workload", choices=["config2", "exists"], default="config2")
     p.add_argument("--outer", type=int, default=4, help="EXISTS outer rows timed")
+    p.add_argument("--no-stop", action="store_true",
+                   help="EXISTS: score every candidate (no short-circuit)")
     p.add_argument("--left", type=int, default=8, help="anchors (left rows) timed")
     p.add_argument("--right", type=int, default=500, help="partners (right rows)")
     p.add_argument("--pages", type=int, default=16384)

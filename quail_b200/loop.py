@@ -659,7 +659,7 @@ def run_filter(torch, arena, pipeline, async_ans, doc_ids, question_ids, budget,
 def run_join(torch, arena, pipeline, async_ans, anchor_prefixes, stage_suffixes, budget,
              stage_frames=None, anchor_keys=None, anchor_done=None, anchor_source=None,
              anchor_partners=None, anchor_batch=None, attention_mode=None, prefix_tree=None,
-             stats=None, device="cuda", on_chunk=None):
+             stats=None, device="cuda", on_chunk=None, stop_at_true=False, stream_step=None):
     """Stream partner lists against anchors, gating survivors between stages
     (Quail's run_join, loop.py:609-978; arguments as there).
 
@@ -670,6 +670,13 @@ def run_join(torch, arena, pipeline, async_ans, anchor_prefixes, stage_suffixes,
     picks the answer rows: None for 0/1 lists (AI joins), float32 arrays for
     AI.SCORE. With anchor_source (a FilterStream with hold_survivors), the
     filter's survivors stream in as resident anchors between join chunks.
+    With stop_at_true (an EXISTS join; the reference has no such stop and
+    scores every partner), an anchor's last-stage partners that are not yet
+    launched when one of its partners answers TRUE are skipped: its row
+    then ends after the launched ones, and which anchors have a TRUE is
+    unchanged. stream_step caps the partners one anchor launches per chunk,
+    so with a small step the anchors' streams interleave and a TRUE arrives
+    before most of its anchor's stream is packed.
 
     Returns:
         (answers, spans, tokens): answers[j][a] is anchor a's row over the
@@ -726,7 +733,8 @@ def run_join(torch, arena, pipeline, async_ans, anchor_prefixes, stage_suffixes,
         budget, arena.n_pages, arena.page_tokens, frame_tokens=[len(f) for f in frames],
         resident=resident, anchor_partners={a: partners_of(keys[a]) for a in range(len(keys))},
         temporary_suffix_pages=mode == "unified", answer_dtype=async_ans.dtype,
-        page_cost=arena.page_cost, tree=prefix_tree)
+        page_cost=arena.page_cost, tree=prefix_tree, stop_at_true=stop_at_true,
+        stream_step=stream_step)
     borrowing = sched.borrowing
     borrowing.can_borrow = borrow_check(arena, keys, borrowing)
     borrowers = borrowing.borrowers()
@@ -894,4 +902,5 @@ def run_join(torch, arena, pipeline, async_ans, anchor_prefixes, stage_suffixes,
         stats["borrowed_tokens"] = borrowing.borrowed_tokens
         stats["h2d_bytes"] = h2d[0]
         stats["chunks"] = h2d[1]
+        stats["skipped_partners"] = sched.skipped_partners
     return sched.answers, spans, tokens

@@ -278,8 +278,24 @@ class JoinAdmission:
     def __init__(self, prefix_tokens, stage_suffixes, chunk_budget, arena_pages, page_tokens,
                  frame_tokens=None, resident=None, anchor_partners=None,
                  temporary_suffix_pages=False, answer_dtype=None, canvas_tokens=0,
-                 page_cost=None, tree=None, can_borrow=None):
+                 page_cost=None, tree=None, can_borrow=None, stop_at_true=False,
+                 stream_step=None):
+        if stop_at_true and answer_dtype is not None:
+            raise ValueError("stop_at_true needs 0/1 answers (an EXISTS join), not scores")
+        if stream_step is not None and stream_step < 1:
+            raise ValueError("stream_step must be at least 1")
+        # at most this many partners of one anchor per chunk (None: as many
+        # as fit); with stop_at_true, a small step interleaves the anchors'
+        # streams so a TRUE answer arrives before most of a stream launches
+        self.stream_step = stream_step
         self.answer_dtype = answer_dtype
+        # EXISTS early stop (not in the reference, which scores every partner
+        # and gates afterwards, backend.py:231-240): once a last-stage
+        # partner of an anchor answers TRUE, its partners not launched yet
+        # are skipped; _cut[a] is the count its last-stage row stops at
+        self.stop_at_true = stop_at_true
+        self._cut = {}
+        self.skipped_partners = 0
         self.borrowing = Borrowing(len(prefix_tokens), tree, can_borrow)
         self.page_cost = page_cost or (lambda tokens, base=None: pages_for(tokens, page_tokens))
         self.chunk_budget = chunk_budget
@@ -339,6 +355,8 @@ class JoinAdmission:
     # ---- per-anchor costs ---------------------------------------------------
 
     def _count(self, a, j):
+        if j == len(self.stages) - 1 and a in self._cut:
+            return self._cut[a]
         lst = self._lists[a][j]
         return len(self.stages[j]) if lst is None else len(lst)
 
@@ -458,6 +476,8 @@ class JoinAdmission:
         cum = self._cum_of(a, j)
         frame = self.frame_rows[j] if i == 0 else 0
         end = bisect_right(cum, cum[i] + room - frame) - 1
+        if self.stream_step is not None:
+            end = min(end, i + self.stream_step)
         pages = 0
         if self.temporary_suffix_pages:
             costs = self._page_cums.get((a, j))
@@ -574,6 +594,13 @@ class JoinAdmission:
         if any(bits) if self.answer_dtype is None else np.any(bits):
             self._true[a][j] = True
         k = len(self.stages)
+        if (self.stop_at_true and j == k - 1 and self._true[a][j] and a not in self._cut
+                and self._next[a] < self._count(a, j)):
+            # the rest of the stream is decided: stop it where it was launched
+            self.skipped_partners += self._count(a, j) - self._next[a]
+            self._cut[a] = self._next[a]
+            if a in self.ready:
+                self.ready.remove(a)
         n_j = self._count(a, j)
         complete = end == n_j
         events = []

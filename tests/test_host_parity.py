@@ -249,6 +249,99 @@ def test_exists_workload_scores_each_candidate_once():
     assert max(sizes) <= budget
 
 
+def _exists_join(anchors, sufs, partners, budget, stop, true_rate, step=None):
+    """Single-stage join on the CPU; a partner answers TRUE when a hash of
+    its final row's token and position falls under true_rate."""
+    arena = KVArena(1, 4096, 16, 1, 8, device=None)
+    packed = []
+
+    class Rec(ModelPipeline):
+        tree_attention = True
+
+        def forward_chunk(self, chunk):
+            packed.append(chunk.host.tokens)
+            return chunk.host
+
+    class Ans:
+        dtype = None
+
+        def submit(self, host):
+            fin = host.final_indices
+            h = (host.input_ids[fin] * 2654435761 + host.positions[fin] * 40503) % 1000
+            return list((h < true_rate * 1000).astype(int))
+
+        def result(self, h):
+            return h
+
+    stats = {}
+    answers, _, tokens = loop.run_join(
+        torch, arena, Rec(), Ans(), anchors, [sufs], budget, attention_mode="tree",
+        prefix_tree=prefix_tree(anchors, 16), anchor_partners=lambda k: partners[k],
+        stats=stats, device="cpu", stop_at_true=stop, stream_step=step)
+    assert arena.free_pages == arena.n_pages, "every page returns to the free stack"
+    return answers[0], stats["skipped_partners"], tokens
+
+
+def _exists_case(true_rate, step):
+    """Full join vs early-stopped join of 9 outer rows x 16 candidates;
+    returns the candidates the stop skipped."""
+    from quail_b200.api import JoinResult
+    rng = np.random.default_rng(31)
+    prefix = rng.integers(100, 900, 64).tolist()
+    anchors = [prefix + rng.integers(100, 900, 96).tolist() for _ in range(9)]
+    sufs, partners = [], []
+    for _ in anchors:
+        first = len(sufs)
+        sufs.extend(rng.integers(100, 900, int(n)).tolist() + [7]
+                    for n in rng.integers(20, 100, 16))
+        partners.append([list(range(first, len(sufs)))])
+    full, skipped_full, tok_full = _exists_join(anchors, sufs, partners, 400, False, true_rate)
+    stop, skipped, tok_stop = _exists_join(anchors, sufs, partners, 400, True, true_rate, step)
+    assert skipped_full == 0
+    kw = dict(fresh_tokens=0, borrowed_tokens=0, chunks=0, h2d_bytes=0, d2h_bytes=0,
+              gpu_s=0.0, wall_s=0.0, n_anchors=len(anchors))
+    for sem in ("semi", "anti"):
+        assert (JoinResult(answers=[stop], **kw).survivors(sem)
+                == JoinResult(answers=[full], **kw).survivors(sem))
+    cut = 0
+    for a, row in full.items():
+        got = stop[a]
+        assert list(got) == list(row[:len(got)])
+        if len(got) < len(row):
+            assert any(got)
+            cut += len(row) - len(got)
+    assert cut == skipped
+    skipped_tokens = sum(len(sufs[i]) for a, row in full.items()
+                         for i in partners[a][0][len(stop[a]):])
+    assert tok_stop == tok_full - skipped_tokens
+    return skipped
+
+
+@pytest.mark.parametrize("step", [None, 1, 3])
+@pytest.mark.parametrize("true_rate", [0.05, 0.3, 0.9])
+def test_exists_early_stop_keeps_survivors(true_rate, step):
+    """EXISTS early stop: an outer row's candidates not yet launched when one
+    of its candidates answers TRUE are skipped. The EXISTS and NOT EXISTS
+    survivors equal those of the full join (the reference's any(row) gate,
+    backend.py:231-240), every stopped row is a prefix of the full row that
+    holds a TRUE, and the skipped candidates are never packed."""
+    skipped = _exists_case(true_rate, step)
+    if true_rate >= 0.3:
+        assert skipped > 0
+
+
+def test_interleaved_streams_skip_more():
+    """One candidate per outer row per chunk lets a TRUE stop its stream
+    before most of it is packed."""
+    assert _exists_case(0.3, 1) > _exists_case(0.3, None)
+
+
+def test_exists_stop_rejects_scores():
+    from quail_b200.pack import JoinAdmission
+    with pytest.raises(ValueError, match="0/1 answers"):
+        JoinAdmission([10], [[5]], 100, 64, 16, answer_dtype=np.float32, stop_at_true=True)
+
+
 def test_token_store_reads_reference_file():
     """The host input format: a token store file written by the reference's
     TokenStore opens here with the same documents and lengths, and (checked
