@@ -197,9 +197,10 @@ def qk_norm_rope(qkv, positions, cos_sin, q_w, k_w, eps, n_q, n_kv, head_dim=128
 # (an FFMA) rounded to bf16 before the PV product, row sums from the fp32 P,
 # the accumulator rescaled when m grows, out = acc * (1 / l) rounded to bf16,
 # lse = m * scale + ln(l). KEY_BLOCK is the key block of the sm_100a kernel.
-# Exact mode follows the kernel's thread layout for the row sums: thread tq
-# of a quad owns keys 8 nt + 2 tq + {0, 1} of each block, and the quad's four
-# sums combine as (l0 + l1) + (l2 + l3).
+# Exact mode follows the kernel: exp2 is its softmax exp2 (tc.exp2_soft),
+# and the row sum is eight partials (key j of a block goes to partial j % 8,
+# in key order, each partial rescaled by alpha per block) combined as
+# ((l0 + l1) + (l2 + l3)) + ((l4 + l5) + (l6 + l7)).
 KEY_BLOCK = 64
 LOG2E_F = 1.44269504088896341
 
@@ -221,9 +222,9 @@ def attend(q, k, v, scale, mask=None):
     if mask is not None:
         s = s.masked_fill(~mask, float("-inf"))
     m = torch.full((nq,), float("-inf"))
-    lq = torch.zeros(nq, 4)
+    lq = torch.zeros(nq, 8)
     acc = torch.zeros(nq, v.shape[1])
-    exp2 = tc.exp2 if exact else torch.exp2
+    exp2 = tc.exp2_soft if exact else torch.exp2
     for j0 in range(0, nk, KEY_BLOCK):
         sb = s[:, j0:j0 + KEY_BLOCK]
         nb = sb.shape[1]
@@ -237,12 +238,11 @@ def attend(q, k, v, scale, mask=None):
             p = exp2(tc.fma(sb, sl2.expand_as(sb), (-msl)[:, None].expand_as(sb)))
         else:
             p = exp2(sb * sl2 - msl[:, None])
-        # per-thread row sums: thread tq adds keys 8 nt + 2 tq + e in (nt, e) order
+        # eight row-sum partials: key 8 n + i of the block goes to partial i
         lq = lq * alpha[:, None]
-        pv = p.reshape(nq, 8, 4, 2)
-        for nt in range(8):
-            for e in range(2):
-                lq = lq + pv[:, nt, :, e]
+        pv = p.reshape(nq, 8, 8)
+        for n8 in range(8):
+            lq = lq + pv[:, n8, :]
         acc = acc * alpha[:, None]
         pb = bf16(p)
         vb = torch.zeros(KEY_BLOCK, v.shape[1], dtype=torch.bfloat16)
@@ -252,7 +252,8 @@ def attend(q, k, v, scale, mask=None):
         else:
             acc = acc + pb @ vb.to(torch.float32)
         m = m_new
-    l = (lq[:, 0] + lq[:, 1]) + (lq[:, 2] + lq[:, 3])
+    l = ((lq[:, 0] + lq[:, 1]) + (lq[:, 2] + lq[:, 3])) + \
+        ((lq[:, 4] + lq[:, 5]) + (lq[:, 6] + lq[:, 7]))
     out = acc * (1.0 / l)[:, None]
     if exact:
         lse = tc.fma(m, torch.full_like(m, scale), tc.ln(l))

@@ -23,7 +23,8 @@ def lib():
         L.qbm_gemm_fp8.argtypes = [_P, _P, _I, _P, _P, _P, _I, _I, _I]
         L.qbm_gemm_fp8_f32.argtypes = [_P, _P, _I, _P, _P, _P, _I, _I, _I]
         L.qbm_mma_bf16.argtypes = [_P, _P, _P, _P, _I, _I, _I]
-        for name in ("qbm_exp2f_array", "qbm_sigmoidf_array", "qbm_lnf_array"):
+        for name in ("qbm_exp2f_array", "qbm_exp2s_array", "qbm_sigmoidf_array",
+                     "qbm_lnf_array"):
             getattr(L, name).argtypes = [_P, _P, _I]
         L.qbm_fmaf_array.argtypes = [_P, _P, _P, _P, _I]
         L.qbm_sumsq_rows.argtypes = [_P, _I, _I, _P]
@@ -96,6 +97,11 @@ def _unary(name, x):
 
 def exp2(x):
     return _unary("qbm_exp2f_array", x)
+
+
+def exp2_soft(x):
+    """The attention softmax's exp2 (the kernel's qexp2s)."""
+    return _unary("qbm_exp2s_array", x)
 
 
 def sigmoid(x):

@@ -11,8 +11,9 @@
  *    normal exponent), truncates each term to a multiple of 2^(E - 25),
  *    sums exactly and rounds the sum toward zero to fp32.
  * 2. exp2 / ln: the FMA-only methods both sides implement (Taylor series
- *    of 2^f on [-1/2, 1/2] after n = rint(x); ln m = 2 atanh((m-1)/(m+1))
- *    on [sqrt(1/2), sqrt 2)), so CPU and GPU round identically.
+ *    of 2^f on [-1/2, 1/2] after n = rint(x), and the attention softmax's
+ *    degree-5 fit; ln m = 2 atanh((m-1)/(m+1)) on [sqrt(1/2), sqrt 2)), so
+ *    CPU and GPU round identically.
  * 3. Reduction orders of the kernels (8 values per thread with an FMA
  *    chain, xor-butterfly across a warp, warps summed in order).
  *
@@ -221,6 +222,29 @@ float qbm_exp2f(float x) {
     const int ni = (int)(f32_bits(t) - 0x4B400000u);
     if (ni >= -126) return p * f32_from_bits((uint32_t)(ni + 127) << 23);
     return (p * f32_from_bits((uint32_t)(ni + 126 + 127) << 23)) * f32_from_bits(1u << 23);
+}
+
+/* The attention softmax's exp2 (P and alpha), as the kernel's qexp2s:
+   n = rint(max(x, -127)), 2^f on [-1/2, 1/2] by a degree-5 polynomial
+   fitted for least relative error (max 2.1e-7), times 2^n; n = -127 gives
+   the scale 0, so x below -126.5 yields 0. For x <= 1, -inf and NaN. */
+static const float EXP2S_C[6] = {
+    1.0000001192092896f, 0.6931469440460205f, 0.24022120237350464f,
+    0.05550713464617729f, 0.009675541892647743f, 0.0013276466634124517f};
+
+float qbm_exp2s(float x) {
+    if (x != x) return f32_from_bits(0x7fffffffu);
+    const float xc = x < -127.0f ? -127.0f : x;
+    const float t = xc + 12582912.0f;
+    const float f = xc - (t - 12582912.0f);
+    float p = EXP2S_C[5];
+    for (int k = 4; k >= 0; --k) p = fmaf(p, f, EXP2S_C[k]);
+    const uint32_t sb = (f32_bits(t) << 23) + ((127u - 0x4B400000u) << 23);
+    return p * f32_from_bits(sb);
+}
+
+void qbm_exp2s_array(const float* x, float* y, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) y[i] = qbm_exp2s(x[i]);
 }
 
 static const float LOG2E_F = 1.44269504088896341f;

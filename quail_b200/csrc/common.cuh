@@ -335,6 +335,63 @@ __device__ __forceinline__ void qexp2f_x2_softmax(float& a, float& b, bool& rare
              a, b);
 }
 
+// The attention softmax's exp2 (P and the rescale factor alpha): 2^x for
+// x <= 1, -inf and NaN. n = rint(max(x, -127)), f = x - n in [-1/2, 1/2],
+// 2^f by a degree-5 polynomial fitted for least relative error on
+// [-1/2, 1/2] (weighted least squares with Lawson iterations; max relative
+// error 2.1e-7 in fp32 Horner, the accuracy class of the 2-ulp hardware
+// ex2.approx FlashAttention's softmax uses), times 2^n. n = -127 gives the
+// scale 0, so 2^x = 0 below -126.5 (FlashAttention's ex2 flushes subnormal
+// results to zero as well). Four FMA steps fewer than qexp2f and no
+// subnormal branch; the oracle's qbm_exp2s restates it bit for bit.
+#define QB_EXP2S_POLY(STEP)        \
+    STEP(0.009675541892647743f)    \
+    STEP(0.05550713464617729f)     \
+    STEP(0.24022120237350464f)     \
+    STEP(0.6931469440460205f)      \
+    STEP(1.0000001192092896f)
+constexpr float QB_EXP2S_C5 = 0.0013276466634124517f;
+
+__device__ __forceinline__ void qexp2s_x2(float& a, float& b) {
+    float ac, bc;
+    asm("max.NaN.f32 %0, %1, 0fC2FE0000;" : "=f"(ac) : "f"(a));  // -127
+    asm("max.NaN.f32 %0, %1, 0fC2FE0000;" : "=f"(bc) : "f"(b));
+    const uint64_t M = f2pack(12582912.0f, 12582912.0f);
+    const uint64_t x = f2pack(ac, bc);
+    const uint64_t t = f2add(x, M);
+    const uint64_t f = f2sub(x, f2sub(t, M));
+    uint64_t p = f2pack(QB_EXP2S_C5, QB_EXP2S_C5);
+#define QB_STEPS2(c) p = f2fma(p, f, f2pack(c, c));
+    QB_EXP2S_POLY(QB_STEPS2)
+#undef QB_STEPS2
+    float ta, tb;
+    f2unpack(t, ta, tb);
+    constexpr uint32_t K = (127u - 0x4B400000u) << 23;  // 2^n bits: (bits(t) << 23) + K
+    f2unpack(f2mul(p, f2pack(__uint_as_float((__float_as_uint(ta) << 23) + K),
+                             __uint_as_float((__float_as_uint(tb) << 23) + K))),
+             a, b);
+}
+
+__device__ __forceinline__ float qexp2s(float x) {
+    float xc;
+    asm("max.NaN.f32 %0, %1, 0fC2FE0000;" : "=f"(xc) : "f"(x));
+    const float t = __fadd_rn(xc, 12582912.0f);
+    const float f = __fsub_rn(xc, __fsub_rn(t, 12582912.0f));
+    float p = QB_EXP2S_C5;
+#define QB_STEPS(c) p = __fmaf_rn(p, f, c);
+    QB_EXP2S_POLY(QB_STEPS)
+#undef QB_STEPS
+    constexpr uint32_t K = (127u - 0x4B400000u) << 23;
+    return __fmul_rn(p, __uint_as_float((__float_as_uint(t) << 23) + K));
+}
+
+// max of three floats (NaN operands ignored, as fmaxf)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 // two sigmoidf_ref at once (same bits on each)
 __device__ __forceinline__ void sigmoidf_ref_x2(float& a, float& b) {
     float ea, eb;
