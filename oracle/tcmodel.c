@@ -226,11 +226,12 @@ float qbm_exp2f(float x) {
 
 /* The attention softmax's exp2 (P and alpha), as the kernel's qexp2s:
    n = rint(max(x, -127)), 2^f on [-1/2, 1/2] by a degree-5 polynomial
-   fitted for least relative error (max 2.1e-7), times 2^n; n = -127 gives
+   with constant term 1 fitted for least relative error (max 1.7e-7), times
+   2^n; n = -127 gives
    the scale 0, so x below -126.5 yields 0. For x <= 1, -inf and NaN. */
 static const float EXP2S_C[6] = {
-    1.0000001192092896f, 0.6931469440460205f, 0.24022120237350464f,
-    0.05550713464617729f, 0.009675541892647743f, 0.0013276466634124517f};
+    1.0f, 0.6931470036506653f, 0.24022242426872253f,
+    0.05550733581185341f, 0.009671512991189957f, 0.0013264724984765053f};
 
 float qbm_exp2s(float x) {
     if (x != x) return f32_from_bits(0x7fffffffu);

@@ -619,7 +619,9 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                     // keys [0, visible) exist for this row
                     const int visible = causal ? min(cl.key_end, qpos + 1) : cl.key_end;
                     float m = -INFINITY;
-                    float lp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    // eight row-sum partials (key j of a tile goes to partial
+                    // j % 8) as four f32x2 pairs: L[q] holds partials 2q, 2q + 1
+                    uint64_t L[4] = {0, 0, 0, 0};
                     for (int t = 0; t < cl.n_tiles; ++t, ++g) {
                         if (!mbar_wait(&aux->s_full[mt], (uint32_t)g & 1u, abort_flag, status,
                                        STATUS_ATTN_SOFTMAX)) {
@@ -628,16 +630,29 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         }
                         tc_fence_after();
                         const int lim = visible - t * KT;  // keys [0, lim) of the tile exist
+                        // warp-uniform: every lane sees the whole tile (no
+                        // masking), and how many 16-key chunks any lane sees
+                        // (later chunks are masked for the whole warp: skipped)
+                        const bool whole = __all_sync(0xffffffffu, lim >= KT);
+                        const int seen = __reduce_max_sync(0xffffffffu, (unsigned)max(lim, 0));
+                        const int chunks = min(KT / 16, (seen + 15) >> 4);
                         // pass 1: the masked row max
                         float mx = -INFINITY;
 #pragma unroll 1
-                        for (int c0 = 0; c0 < KT; c0 += 16) {
+                        for (int c0 = 0; c0 < chunks * 16; c0 += 16) {
                             uint32_t sr[16];
                             tmem_ld16_nowait(s_addr + (uint32_t)c0, sr);
                             tmem_wait_ld();
+                            if (whole) {
 #pragma unroll
-                            for (int k = 0; k < 16; ++k)
-                                mx = fmaxf(mx, c0 + k < lim ? __uint_as_float(sr[k]) : -INFINITY);
+                                for (int k = 0; k < 16; k += 2)
+                                    mx = fmax3(mx, __uint_as_float(sr[k]), __uint_as_float(sr[k + 1]));
+                            } else {
+#pragma unroll
+                                for (int k = 0; k < 16; k += 2)
+                                    mx = fmax3(mx, c0 + k < lim ? __uint_as_float(sr[k]) : -INFINITY,
+                                               c0 + k + 1 < lim ? __uint_as_float(sr[k + 1]) : -INFINITY);
+                            }
                         }
                         const float m_new = fmaxf(m, mx);
                         float alpha, msl;
@@ -645,12 +660,13 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                             alpha = 1.0f;
                             msl = 0.0f;
                         } else {
-                            alpha = qexp2f(__fmul_rn(__fsub_rn(m, m_new), sl2));
+                            alpha = qexp2s(__fmul_rn(__fsub_rn(m, m_new), sl2));
                             msl = __fmul_rn(m_new, sl2);
                         }
                         m = m_new;
+                        const uint64_t a2 = f2pack(alpha, alpha);
 #pragma unroll
-                        for (int k = 0; k < 4; ++k) lp[k] = __fmul_rn(lp[k], alpha);
+                        for (int q = 0; q < 4; ++q) L[q] = f2mul(L[q], a2);
                         // P buffer (g & 1) was last read by the P V two tiles back
                         if (g >= 2 && !mbar_wait(&aux->pv_done[g & 1][mt], (uint32_t)((g - 2) >> 1) & 1u,
                                                  abort_flag, status, STATUS_ATTN_SOFTMAX)) {
@@ -662,37 +678,28 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         // pass 2: p = exp2(s sl2 - m sl2), the row-sum partials, bf16 P
 #pragma unroll 1
                         for (int c0 = 0; c0 < KT; c0 += 16) {
-                            uint32_t sr[16];
-                            tmem_ld16_nowait(s_addr + (uint32_t)c0, sr);
-                            tmem_wait_ld();
-                            float pv[16];
-                            bool rare = false;
-#pragma unroll
-                            for (int k = 0; k < 16; k += 2) {
-                                const float s0 = c0 + k < lim ? __uint_as_float(sr[k]) : -INFINITY;
-                                const float s1 = c0 + k + 1 < lim ? __uint_as_float(sr[k + 1]) : -INFINITY;
-                                f2unpack(f2fma(f2pack(s0, s1), sl, nm), pv[k], pv[k + 1]);
-                                qexp2f_x2_softmax(pv[k], pv[k + 1], rare);
-                            }
-                            if (rare) {  // a subnormal p: the exact two-step scaling
+                            uint32_t pk[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                            if (c0 < chunks * 16) {
+                                uint32_t sr[16];
+                                tmem_ld16_nowait(s_addr + (uint32_t)c0, sr);
+                                tmem_wait_ld();
+                                float pv[16];
 #pragma unroll
                                 for (int k = 0; k < 16; k += 2) {
-                                    const float s0 = c0 + k < lim ? __uint_as_float(sr[k]) : -INFINITY;
-                                    const float s1 =
-                                        c0 + k + 1 < lim ? __uint_as_float(sr[k + 1]) : -INFINITY;
-                                    float a, b;
-                                    f2unpack(f2fma(f2pack(s0, s1), sl, nm), a, b);
-                                    qexp2f_x2(a, b);
-                                    pv[k] = a;
-                                    pv[k + 1] = b;
+                                    float s0 = __uint_as_float(sr[k]), s1 = __uint_as_float(sr[k + 1]);
+                                    if (!whole) {
+                                        s0 = c0 + k < lim ? s0 : -INFINITY;
+                                        s1 = c0 + k + 1 < lim ? s1 : -INFINITY;
+                                    }
+                                    f2unpack(f2fma(f2pack(s0, s1), sl, nm), pv[k], pv[k + 1]);
+                                    qexp2s_x2(pv[k], pv[k + 1]);
                                 }
-                            }
-                            uint32_t pk[8];
 #pragma unroll
-                            for (int k = 0; k < 16; k += 2) {
-                                // keys c0 + k, c0 + k + 1 belong to partial (k / 2) % 4 (c0 % 8 == 0)
-                                lp[(k >> 1) & 3] = __fadd_rn(__fadd_rn(lp[(k >> 1) & 3], pv[k]), pv[k + 1]);
-                                pk[k >> 1] = bf16x2_bits(pv[k], pv[k + 1]);
+                                for (int k = 0; k < 16; k += 2) {
+                                    // keys c0 + k, + 1 (c0 % 8 == 0): partials k % 8, k % 8 + 1
+                                    L[(k >> 1) & 3] = f2add(L[(k >> 1) & 3], f2pack(pv[k], pv[k + 1]));
+                                    pk[k >> 1] = bf16x2_bits(pv[k], pv[k + 1]);
+                                }
                             }
                             const int ch = c0 >> 3;  // 16-byte chunks ch, ch + 1 of the row
                             *reinterpret_cast<uint4*>(prow + ((ch ^ (i & 7)) << 4)) =
@@ -717,7 +724,11 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         break;
                     }
                     tc_fence_after();
-                    const float l = __fadd_rn(__fadd_rn(lp[0], lp[1]), __fadd_rn(lp[2], lp[3]));
+                    float lsum[8];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) f2unpack(L[q], lsum[2 * q], lsum[2 * q + 1]);
+                    const float l = __fadd_rn(__fadd_rn(__fadd_rn(lsum[0], lsum[1]), __fadd_rn(lsum[2], lsum[3])),
+                                              __fadd_rn(__fadd_rn(lsum[4], lsum[5]), __fadd_rn(lsum[6], lsum[7])));
                     const float inv = __frcp_rn(l);
                     if (cl.kind == CALL_READS) {
                         // normalised call-B output, bf16, for the rows of this read group

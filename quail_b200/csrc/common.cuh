@@ -337,20 +337,22 @@ __device__ __forceinline__ void qexp2f_x2_softmax(float& a, float& b, bool& rare
 
 // The attention softmax's exp2 (P and the rescale factor alpha): 2^x for
 // x <= 1, -inf and NaN. n = rint(max(x, -127)), f = x - n in [-1/2, 1/2],
-// 2^f by a degree-5 polynomial fitted for least relative error on
-// [-1/2, 1/2] (weighted least squares with Lawson iterations; max relative
-// error 2.1e-7 in fp32 Horner, the accuracy class of the 2-ulp hardware
-// ex2.approx FlashAttention's softmax uses), times 2^n. n = -127 gives the
+// 2^f by a degree-5 polynomial 1 + c1 f + ... + c5 f^5 fitted for least
+// relative error on [-1/2, 1/2] (weighted least squares with Lawson
+// iterations; max relative error 1.7e-7 in fp32 Horner, the accuracy class
+// of the 2-ulp hardware ex2.approx FlashAttention's softmax uses), times
+// 2^n. The constant term is exactly 1, so 2^0 = 1: a key tile that moves no
+// row max (alpha = 2^0) leaves the row sums and the output unscaled. n = -127 gives the
 // scale 0, so 2^x = 0 below -126.5 (FlashAttention's ex2 flushes subnormal
 // results to zero as well). Four FMA steps fewer than qexp2f and no
 // subnormal branch; the oracle's qbm_exp2s restates it bit for bit.
 #define QB_EXP2S_POLY(STEP)        \
-    STEP(0.009675541892647743f)    \
-    STEP(0.05550713464617729f)     \
-    STEP(0.24022120237350464f)     \
-    STEP(0.6931469440460205f)      \
-    STEP(1.0000001192092896f)
-constexpr float QB_EXP2S_C5 = 0.0013276466634124517f;
+    STEP(0.009671512991189957f)    \
+    STEP(0.05550733581185341f)     \
+    STEP(0.24022242426872253f)    \
+    STEP(0.6931470036506653f)     \
+    STEP(1.0f)
+constexpr float QB_EXP2S_C5 = 0.0013264724984765053f;
 
 __device__ __forceinline__ void qexp2s_x2(float& a, float& b) {
     float ac, bc;

@@ -10,16 +10,20 @@
 //      the positive NaNs)
 //   3  quant2_sat (+ the group bound and exact redo) vs quant2, e4m3 codes,
 //      on 64 group scales x 2^24 values of the group each
-//   4  qexp2f_x2_softmax (+ exact redo when rare) vs qexp2f, every x <= 1
-//      (every negative float, zeros, positives up to 1.0, -inf and NaNs)
+//   4  qexp2s_x2 (the attention softmax's packed exp2) vs qexp2s, every
+//      x <= 1 (every negative float, zeros, positives up to 1.0, -inf, NaNs)
+//   5  qexp2s against CUDA's exp2f, every x in [-125, 1]: a relative
+//      difference above 5e-7 counts (the polynomial's bound, 1.7e-7, plus
+//      exp2f's own maximum error of 2 ulp, 2.4e-7)
+// qbn_exp2s(x, y, n) evaluates qexp2s on the GPU for the oracle comparison.
 #include "common.cuh"
 
 using namespace qb;
 
 namespace {
 
-__device__ unsigned long long g_bad[5];
-__device__ unsigned int g_first[5];
+__device__ unsigned long long g_bad[6];
+__device__ unsigned int g_first[6];
 
 __device__ void record(int which, uint32_t bits) {
     atomicAdd(&g_bad[which], 1ull);
@@ -121,7 +125,7 @@ __global__ void check_quant(const float* amaxes) {
 
 // all bit patterns with sign 1 (negatives, -0, -inf, NaNs) and the
 // non-negative ones up to 1.0f
-__global__ void check_exp2_softmax() {
+__global__ void check_exp2s() {
     const uint64_t n = (1ull << 31) + 0x3F800001ull;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
          i += (uint64_t)gridDim.x * blockDim.x) {
@@ -132,30 +136,35 @@ __global__ void check_exp2_softmax() {
         const float xb = (__uint_as_float(bb) <= 1.0f || __uint_as_float(bb) != __uint_as_float(bb))
                              ? __uint_as_float(bb) : xa;
         float a = xa, b = xb;
-        bool rare = false;
-        qexp2f_x2_softmax(a, b, rare);
-        if (rare) {
-            a = xa;
-            b = xb;
-            qexp2f_x2(a, b);
-        }
-        const float wa = qexp2f(xa);
+        qexp2s_x2(a, b);
+        const float wa = qexp2s(xa);
         const bool nan_a = wa != wa;
         if (nan_a ? (a == a) : (__float_as_uint(a) != __float_as_uint(wa))) record(4, ba);
-        const float wb = qexp2f(xb);
+        const float wb = qexp2s(xb);
         const bool nan_b = wb != wb;
         if (nan_b ? (b == b) : (__float_as_uint(b) != __float_as_uint(wb)))
             record(4, __float_as_uint(xb));
+        if (xa >= -125.0f && xa <= 1.0f) {
+            const float e = exp2f(xa);
+            if (fabsf(wa - e) > 5e-7f * e) record(5, ba);
+        }
     }
+}
+
+__global__ void exp2s_kernel(const float* x, float* y, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        y[i] = qexp2s(x[i]);
 }
 
 }  // namespace
 
-// bad[5], first[5] (host): mismatch counts and the smallest mismatching
+// bad[6], first[6] (host): mismatch counts and the smallest mismatching
 // input bits of each check. Returns a cudaError_t.
 extern "C" int qbn_run_checks(unsigned long long* bad, unsigned int* first) {
-    unsigned long long zero[5] = {0, 0, 0, 0, 0};
-    unsigned int ones[5] = {0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu};
+    unsigned long long zero[6] = {0, 0, 0, 0, 0, 0};
+    unsigned int ones[6] = {0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu,
+                            0xFFFFFFFFu};
     cudaMemcpyToSymbol(g_bad, zero, sizeof(zero));
     cudaMemcpyToSymbol(g_first, ones, sizeof(ones));
     check_rcp<<<148 * 8, 256>>>(0x00800000u, 0x7E800000u);
@@ -172,11 +181,28 @@ extern "C" int qbn_run_checks(unsigned long long* bad, unsigned int* first) {
     cudaMalloc(&amax_dev, sizeof(amax_host));
     cudaMemcpy(amax_dev, amax_host, sizeof(amax_host), cudaMemcpyHostToDevice);
     check_quant<<<dim3(256, 64), 256>>>(amax_dev);
-    check_exp2_softmax<<<148 * 8, 256>>>();
+    check_exp2s<<<148 * 8, 256>>>();
     cudaError_t err = cudaDeviceSynchronize();
     cudaFree(amax_dev);
     if (err != cudaSuccess) return (int)err;
     cudaMemcpyFromSymbol(bad, g_bad, sizeof(zero));
     cudaMemcpyFromSymbol(first, g_first, sizeof(ones));
     return (int)cudaGetLastError();
+}
+
+// y[i] = qexp2s(x[i]) on the GPU (host arrays of n floats). Returns a
+// cudaError_t.
+extern "C" int qbn_exp2s(const float* x, float* y, int64_t n) {
+    float *dx = nullptr, *dy = nullptr;
+    cudaError_t err = cudaMalloc(&dx, n * sizeof(float));
+    if (err == cudaSuccess) err = cudaMalloc(&dy, n * sizeof(float));
+    if (err == cudaSuccess) err = cudaMemcpy(dx, x, n * sizeof(float), cudaMemcpyHostToDevice);
+    if (err == cudaSuccess) {
+        exp2s_kernel<<<148 * 4, 256>>>(dx, dy, n);
+        err = cudaDeviceSynchronize();
+    }
+    if (err == cudaSuccess) err = cudaMemcpy(y, dy, n * sizeof(float), cudaMemcpyDeviceToHost);
+    cudaFree(dx);
+    cudaFree(dy);
+    return (int)err;
 }

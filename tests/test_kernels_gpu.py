@@ -299,12 +299,25 @@ def test_qk_norm_rope_and_kv_append(dev):
     assert_status_clean()
 
 
-# GQA groups of 2 and 4 run the tcgen05 kernel (one and two 128-row M tiles),
-# an odd group the mma.sync kernel
+# GQA groups of 2 and 4 (one and two 128-row M tiles) and 8 (Qwen3-32B's
+# grouping: 64 query heads over 8 KV heads); the tcgen05 kernel takes even
+# groups only (every Qwen3 shape), an odd one is rejected before launch
 ATTN_CONFIGS = {"g2": TINY, "g4": dataclasses.replace(TINY, name="tiny-g4", n_q=8),
-                "g3": dataclasses.replace(TINY, name="tiny-g3", n_q=3, n_kv=1),
-                # Qwen3-32B's grouping (64 query heads over 8 KV heads)
                 "g8": dataclasses.replace(TINY, name="tiny-g8", n_q=16, n_kv=2)}
+
+
+def test_attention_rejects_odd_gqa_groups(dev):
+    cfg = dataclasses.replace(TINY, name="tiny-g3", n_q=3, n_kv=1)
+    _, arena, chunks = _attention_case("tree", dev, cfg=cfg)
+    eng = Engine(torch, arena, cfg)
+    chunk = chunks[0]
+    rows = chunk.tokens
+    q = torch.zeros(rows, cfg.n_q * cfg.head_dim, device=dev, dtype=torch.bfloat16)
+    kv = torch.zeros(rows, cfg.n_kv * cfg.head_dim, device=dev, dtype=torch.bfloat16)
+    chunk.meta["layer"] = 0
+    with pytest.raises(ValueError, match="query heads per KV head"):
+        eng.attention_tree(q, kv, kv, chunk.meta)
+    assert_status_clean()
 
 
 def _attention_case(mode, dev, seed=0, cfg=TINY, long=False):
