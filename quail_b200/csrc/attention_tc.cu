@@ -1,40 +1,53 @@
 // Tree and unified attention on tcgen05 tensor cores (sm_100a).
 //
-// Same results, bit for bit, as the mma.sync kernel of attention.cu (and the
-// CPU oracle): the B200's tcgen05 kind::f16 MMA accumulates exactly like
-// mma.sync m16n8k16 - per 16-deep step, every product and the accumulator
-// aligned to the largest exponent, truncated 25 bits below it, summed and
-// rounded toward zero (measured: tests/golden/tensorcore_probe.npz) - and
-// this kernel keeps that kernel's order of operations:
+// Bit for bit the CPU oracle's restatement (oracle/numerics.py attend): the
+// B200's tcgen05 kind::f16 MMA accumulates per 16-deep step with every
+// product and the accumulator aligned to the largest exponent, truncated 25
+// bits below it, summed and rounded toward zero (measured:
+// tests/golden/tensorcore_probe.npz), and the kernel fixes every other
+// rounding:
 //   S = Q K^T in eight 16-deep steps from zero; per 64-key tile the masked
 //   row max, alpha = exp2((m_old - m_new) sl2), O *= alpha before P V,
-//   P = bf16(exp2(s sl2 - m sl2)); the row sum in four partials (key
-//   8n + 2q + e goes to partial q, in key order) combined as
-//   (l0 + l1) + (l2 + l3); then the LSE merge with bf16 roundings and the
-//   per-head fp8 quantisation.
+//   P = bf16(exp2(s sl2 - m sl2)) with the softmax exp2 (qexp2s); the row
+//   sum in eight partials (key j of a tile goes to partial j % 8, in key
+//   order) combined as ((l0 + l1) + (l2 + l3)) + ((l4 + l5) + (l6 + l7));
+//   then the LSE merge with bf16 roundings and the per-head fp8
+//   quantisation.
 //
 // Block: 64 query rows of one cu_a segment x 4 query heads of one KV head
 // (2 when the GQA group is 2) as two M=128 tiles (rows 0-63 one head, rows
-// 64-127 the next) that share every K/V tile. 14 warps:
-//   warp 0       TMA loader: Q once, then K and V tiles of 64 keys into a
-//                2-stage ring - the segment's own keys as contiguous rows, the
-//                resident keys one box per page through the block table;
-//   warp 1       TMEM allocator and MMA issuer: S = Q K^T into TMEM, then
-//                O += P V with P from shared memory and V read MN-major; it
-//                also zeroes the V rows of a paged tile past the last key
-//                (pool rows there may hold anything, and 0 * NaN is NaN);
+// 64-127 the next) that share every K/V tile. 15 warps:
+//   warp 0       TMA loader: each item's call list, Q once, then K tiles of
+//                64 keys into a 2-stage ring - the segment's own keys as
+//                contiguous rows, the resident keys one box per page through
+//                the block table;
+//   warp 14      TMA loader of the V tiles, the same way, into a 3-stage ring
+//                (its own warp, so a V tile is requested as soon as its slot
+//                frees: the loads take several microseconds to land);
+//   warp 1       TMEM allocator and MMA issuer: S = Q K^T into one of two
+//                TMEM buffers per M tile, so the next tile's S runs while the
+//                softmax works on this one; then O += P V with P read from
+//                TMEM (the A operand) and V read MN-major from shared
+//                memory; it also zeroes the V rows of a paged tile past the
+//                last key (pool rows there may hold anything, and 0 * NaN is
+//                NaN);
 //   warps 2-9    softmax, one thread per row of an M tile: S from TMEM (read
-//                twice: the row max, then exp2), P to shared memory (128-byte
-//                swizzle, two buffers by tile parity), alpha likewise;
-//                after each call the same thread's epilogue: the normalised
-//                call-B output (bf16, kept in TMEM), or the merge, the
+//                twice: the row max, then exp2), bf16 P written back over the
+//                tile's S (tcgen05.st), alpha to shared memory; after each
+//                call the same thread's epilogue: the normalised call-B
+//                output (bf16, kept in shared memory), or the merge, the
 //                quantisation and the fp8 store;
 //   warps 10-13  correction, one thread per row of each M tile: O *= alpha in
 //                TMEM between P V steps.
-// TMEM (512 columns): O [2][128] | S [2][64] | call-B output bf16x2 [2][64].
+// TMEM (512 columns): O [2 M tiles][128] | S [2 M tiles][2 buffers][64], the
+// first 32 columns of an S buffer holding that tile's P once computed.
+// The K and V rings cost one MMA issue each per tile; a tcgen05.mma of
+// M=128, K=16 takes about 26 ns at N=64 and 35 ns at N=128 (measured), and
+// the issuing thread waits for each, so the S of the next tile is issued as
+// soon as its buffer frees rather than after the softmax of this one.
 // Every wait is bounded (about a second): a wait that gives up sets a status
 // bit and the abort flag, the other roles stop at their next wait, the MMA
-// issuer drains its MMAs and the loader its copies before TMEM is freed.
+// issuer drains its MMAs and the loaders their copies before TMEM is freed.
 #include "tc_common.cuh"
 
 namespace qb {
@@ -45,22 +58,25 @@ using namespace qb::tc;
 constexpr int D = 128;
 constexpr int QR = 64;  // query rows per block
 constexpr int KT = 64;  // keys per tile
-constexpr int KST = 3;  // K stages: a K tile is free once its S MMAs are done
-constexpr int VST = 2;  // V stages: a V tile is free once its P V MMAs are done
+constexpr int KST = 2;  // K stages: a K tile is free once its S MMAs are done
+constexpr int VST = 3;  // V stages: a V tile is free once its P V MMAs are done
 constexpr int MAX_CALLS = QR + 1;
-constexpr int FIRST_SOFT = 2, FIRST_CORR = 10;
-constexpr int NUM_THREADS = 14 * 32;
+constexpr int FIRST_SOFT = 2, FIRST_CORR = 10, V_WARP = 14;
+constexpr int NUM_THREADS = 15 * 32;
 
 constexpr int Q_BYTES = 2 * 2 * 128 * 128;  // [mt][half][128 rows][128 B]
 constexpr int KV_HALF = 64 * 128;           // [64 keys][64 dims]
 constexpr int KV_TILE = 2 * KV_HALF;        // K or V: two 64-dim halves
-constexpr int P_TILE = 128 * 128;           // [128 rows][64 keys]
+constexpr int OB_ROW = 256;                 // a row's call-B output: 128 bf16
 constexpr int OFF_K = Q_BYTES;
 constexpr int OFF_V = OFF_K + KST * KV_TILE;
-constexpr int OFF_P = OFF_V + VST * KV_TILE;
-constexpr int OFF_AUX = OFF_P + 4 * P_TILE;  // P: [buffer 2][mt 2]
+constexpr int OFF_OB = OFF_V + VST * KV_TILE;
+constexpr int OFF_AUX = OFF_OB + 2 * 128 * OB_ROW;  // OB: [mt 2][128 rows]
 
-constexpr uint32_t TM_O = 0, TM_S = 256, TM_OB = 384;
+// TMEM: O [mt][128 columns] at 0; S [mt][buffer][64 columns] at 256 + mt *
+// 128 + buffer * 64, its first 32 columns overwritten by the tile's bf16 P
+// (two keys a column), which the P V MMA reads as its A operand
+constexpr uint32_t TM_O = 0, TM_S = 256;
 
 // S: M=128, N=64; P V: M=128, N=128 with B (V) MN-major; bf16 in, f32 out
 constexpr uint32_t IDESC_S = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(KT >> 3) << 17) |
@@ -87,11 +103,11 @@ struct Aux {
     uint64_t q_full, q_empty;
     uint64_t info_full[2], info_empty[2];
     uint64_t k_full[KST], k_empty[KST], v_full[VST], v_empty[VST];
-    uint64_t s_full[2], s_empty[2], o_ready[2];
-    // per P buffer (tile parity) and M tile; phase = tile / 2, so a producer
+    uint64_t o_ready[2];
+    // per S/P buffer (tile parity) and M tile; phase = tile / 2, so a producer
     // can only complete a buffer's next phase after every waiter observed
     // the previous one (a parity wait needs that)
-    uint64_t p_full[2][2], pv_done[2][2];
+    uint64_t s_full[2][2], p_full[2][2], pv_done[2][2];
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
@@ -141,9 +157,6 @@ __device__ __forceinline__ uint64_t k_desc(uint32_t k_base, int ks) {
 __device__ __forceinline__ uint64_t v_desc(uint32_t v_base, int kk) {
     return sw128_mn_desc(v_base + (uint32_t)(kk * 16 * 128), KV_HALF, 1024);
 }
-__device__ __forceinline__ uint64_t p_desc(uint32_t p_base, int kk) {
-    return sw128_desc(p_base) + (uint64_t)(2 * kk);
-}
 
 template <bool UNIFIED>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -177,7 +190,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             mbar_init(&aux->info_full[b], 1);
             // released by the MMA warp, the active softmax warps and the
             // correction warps
-            mbar_init(&aux->info_empty[b], 1 + 4 * nmt + 4);
+            mbar_init(&aux->info_empty[b], 1 + 4 * nmt + 4 + 1);
         }
         for (int st = 0; st < KST; ++st) {
             mbar_init(&aux->k_full[st], 1);
@@ -188,8 +201,8 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             mbar_init(&aux->v_empty[st], 1);
         }
         for (int m = 0; m < 2; ++m) {
-            mbar_init(&aux->s_full[m], 1);
-            mbar_init(&aux->s_empty[m], 4);
+            mbar_init(&aux->s_full[0][m], 1);
+            mbar_init(&aux->s_full[1][m], 1);
             mbar_init(&aux->p_full[0][m], 4);
             mbar_init(&aux->p_full[1][m], 4);
             mbar_init(&aux->pv_done[0][m], 1);
@@ -319,15 +332,15 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                 for (int c = 0; c < nc && ok; ++c) {
                     const Call cl = inf->calls[c];
                     for (int t = 0; t < cl.n_tiles; ++t, ++g) {
-                        // K, then V: K may run KST tiles ahead of the S MMAs,
-                        // V VST tiles ahead of the P V MMAs
+                        // K may run KST tiles ahead of the S MMAs (the V tiles
+                        // have their own loader warp)
                         const int j0 = t * KT;
                         const int32_t* trow =
                             cl.kind == CALL_OWN
                                 ? nullptr
                                 : read_table +
                                       (int64_t)(cl.kind == CALL_UNIFIED ? seg : cl.group) * table_width;
-                        for (int kv = 0; kv < 2 && ok; ++kv) {
+                        for (int kv = 0; kv < 1 && ok; ++kv) {
                             const int n = kv == 0 ? nk : nv;
                             const int nst = kv == 0 ? KST : VST;
                             const int st = n % nst;
@@ -392,7 +405,6 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
         // next tile (possibly the next item's first) and P V of this tile, each
         // as soon as its inputs are ready ------
         const uint32_t q_base = smem_u32(smem);
-        const uint32_t p_base = smem_u32(smem + OFF_P);
         bool ok = true;
         // S cursor: item ks (local index), call cs, tile ts; gs = tiles issued;
         // jq = items with tiles whose Q the S cursor consumed
@@ -443,11 +455,12 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             tc_fence_after();
             if (lane == 0) {
                 for (int mt = 0; mt < nmt; ++mt) {
+                    const uint32_t s_tm = tmem + TM_S + (uint32_t)(mt * 128 + (gs & 1) * 64);
 #pragma unroll
                     for (int kk = 0; kk < D / 16; ++kk)
-                        mma_bf16_ss(tmem + TM_S + (uint32_t)(mt * 64), q_desc(q_base, mt, kk),
-                                    k_desc(k_base, kk), IDESC_S, kk > 0 ? 1u : 0u);
-                    mma_commit(&aux->s_full[mt]);
+                        mma_bf16_ss(s_tm, q_desc(q_base, mt, kk), k_desc(k_base, kk), IDESC_S,
+                                    kk > 0 ? 1u : 0u);
+                    mma_commit(&aux->s_full[gs & 1][mt]);
                 }
                 mma_commit(&aux->k_empty[st]);  // the K tile is free once these are done
             }
@@ -462,24 +475,27 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             if (c >= inf->n_calls && lane == 0) mma_commit(&aux->q_empty);
             __syncwarp();
         };
-        // S of the cursor's tile can go: its item's Q, its K tile, the S buffers
+        // S of the cursor's tile can go: its item's Q, its K tile, and its S
+        // buffer (gs & 1), free once the P V two tiles back, which read the P
+        // written over it, is done
         auto s_ready = [&]() -> bool {
             int r = 1;
             if (lane == 0) {
                 if (ts == 0 && cs == 0)  // the item's first S: its Q
-                    r = mbar_try_wait(smem_u32(&aux->q_full), (uint32_t)jq & 1u);
-                if (r) r = mbar_try_wait(smem_u32(&aux->k_full[gs % KST]), (uint32_t)(gs / KST) & 1u);
-                for (int mt = 0; mt < nmt && r && gs > 0; ++mt)
-                    r = mbar_try_wait(smem_u32(&aux->s_empty[mt]), (uint32_t)(gs - 1) & 1u);
+                    r = mbar_test_wait(smem_u32(&aux->q_full), (uint32_t)jq & 1u);
+                if (r) r = mbar_test_wait(smem_u32(&aux->k_full[gs % KST]), (uint32_t)(gs / KST) & 1u);
+                for (int mt = 0; mt < nmt && r && gs > 1; ++mt)
+                    r = mbar_test_wait(smem_u32(&aux->pv_done[gs & 1][mt]),
+                                       (uint32_t)((gs - 2) >> 1) & 1u);
             }
             return __shfl_sync(0xffffffffu, r, 0) != 0;
         };
         auto pv_ready = [&](int g, int mt) -> bool {
             int r = 0;
             if (lane == 0)
-                r = mbar_try_wait(smem_u32(&aux->v_full[g % VST]), (uint32_t)(g / VST) & 1u) &&
-                    mbar_try_wait(smem_u32(&aux->p_full[g & 1][mt]), (uint32_t)(g >> 1) & 1u) &&
-                    mbar_try_wait(smem_u32(&aux->o_ready[mt]), (uint32_t)g & 1u);
+                r = mbar_test_wait(smem_u32(&aux->v_full[g % VST]), (uint32_t)(g / VST) & 1u) &&
+                    mbar_test_wait(smem_u32(&aux->p_full[g & 1][mt]), (uint32_t)(g >> 1) & 1u) &&
+                    mbar_test_wait(smem_u32(&aux->o_ready[mt]), (uint32_t)g & 1u);
             return __shfl_sync(0xffffffffu, r, 0) != 0;
         };
         // issues the S cursor's tile when ready; returns false on give-up
@@ -543,10 +559,11 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                             zeroed = true;
                             tc_fence_after();
                             if (lane == 0) {
+                                // A = P (bf16, two keys a column) in TMEM over S
+                                const uint32_t p_tm = tmem + TM_S + (uint32_t)(mt * 128 + (g & 1) * 64);
 #pragma unroll
                                 for (int kk = 0; kk < KT / 16; ++kk)
-                                    mma_bf16_ss(tmem + TM_O + (uint32_t)(mt * 128),
-                                                p_desc(p_base + (uint32_t)(((g & 1) * 2 + mt) * P_TILE), kk),
+                                    mma_bf16_ts(tmem + TM_O + (uint32_t)(mt * 128), p_tm + (uint32_t)(kk * 8),
                                                 v_desc(v_base, kk), IDESC_PV,
                                                 (t > 0 || kk > 0) ? 1u : 0u);
                                 mma_commit(&aux->pv_done[g & 1][mt]);
@@ -588,6 +605,68 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
         if (lane == 0) mma_commit(&aux->drain);
         __syncwarp();
         mbar_drain(&aux->drain, 0, status, STATUS_ATTN_MMA);
+    } else if (warp == V_WARP) {
+        // ---------------- V loader: the V tiles of every item's calls, up to
+        // VST tiles ahead of the P V MMAs (the K loader runs on its own) ----------------
+        if (lane == 0) {
+            int nv = 0;
+            bool ok = true;
+            for (int item = blockIdx.x, k = 0; item < n_items && ok; item += gridDim.x, ++k) {
+                const int slot = k & 1;
+                if (!mbar_wait(&aux->info_full[slot], (uint32_t)(k >> 1) & 1u, abort_flag, status,
+                               STATUS_ATTN_LOAD))
+                    break;
+                const Info* inf = &aux->info[slot];
+                const int hk = inf->hk, seg = inf->seg, seg_start = inf->seg_start;
+                for (int c = 0; c < inf->n_calls && ok; ++c) {
+                    const Call cl = inf->calls[c];
+                    const int32_t* trow =
+                        cl.kind == CALL_OWN
+                            ? nullptr
+                            : read_table + (int64_t)(cl.kind == CALL_UNIFIED ? seg : cl.group) * table_width;
+                    for (int t = 0; t < cl.n_tiles; ++t, ++nv) {
+                        const int st = nv % VST;
+                        if (!mbar_wait(&aux->v_empty[st], ((uint32_t)(nv / VST) & 1u) ^ 1u, abort_flag,
+                                       status, STATUS_ATTN_LOAD)) {
+                            ok = false;
+                            break;
+                        }
+                        uint8_t* dst = smem + OFF_V + st * KV_TILE;
+                        uint64_t* full = &aux->v_full[st];
+                        mbar_arrive_expect_tx(full, KV_TILE);
+                        const int j0 = t * KT;
+                        if (cl.kind == CALL_OWN) {
+                            for (int half = 0; half < 2; ++half)
+                                tma_load_2d(smem_u32(dst + half * KV_HALF), &map_v, hk * D + half * 64,
+                                            seg_start + j0, full);
+                        } else {
+                            for (int pg = 0; pg < KT / page_tokens; ++pg) {
+                                const int key = j0 + pg * page_tokens;
+                                int64_t page = 0;  // keys past the last one: any valid page
+                                if (key < cl.n_keys) {
+                                    page = trow[key / page_tokens];
+                                    if (page < 0 || page >= n_pages) {
+                                        atomicOr(status, STATUS_BAD_INDEX);
+                                        page = 0;
+                                    }
+                                }
+                                const int y = (int)(page * page_tokens);
+                                const int off = pg * page_tokens * 128;
+                                for (int half = 0; half < 2; ++half)
+                                    tma_load_2d(smem_u32(dst + half * KV_HALF + off), &map_vp,
+                                                hk * D + half * 64, y, full);
+                            }
+                        }
+                    }
+                }
+                if (!ok) break;
+                mbar_arrive(&aux->info_empty[slot]);
+            }
+            // no copy may still be landing when the block exits
+            for (int j = (nv > VST ? nv - VST : 0); j < nv; ++j)
+                mbar_drain(&aux->v_full[j % VST], (uint32_t)(j / VST) & 1u, status,
+                           STATUS_ATTN_LOAD);
+        }
     } else if (warp < FIRST_CORR) {
         // ------- softmax, then each call's epilogue: one thread per row of an M tile -------
         const int mt = (warp - FIRST_SOFT) >> 2;
@@ -596,9 +675,9 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             const int i = q4 * 32 + lane;
             const int qi = i & (QR - 1);
             const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-            const uint32_t s_addr = tmem + lane_off + TM_S + (uint32_t)(mt * 64);
             const uint32_t o_addr = tmem + lane_off + TM_O + (uint32_t)(mt * 128);
-            const uint32_t ob_addr = tmem + lane_off + TM_OB + (uint32_t)(mt * 64);
+            // this row's call-B output (bf16): 16-byte chunk j at (j ^ i % 16) * 16
+            uint8_t* obrow = smem + OFF_OB + (mt * 128 + i) * OB_ROW;
             const float sl2 = __fmul_rn(scale, 1.44269504088896341f);
             const uint64_t sl = f2pack(sl2, sl2);
             int g = 0;
@@ -623,8 +702,11 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                     // j % 8) as four f32x2 pairs: L[q] holds partials 2q, 2q + 1
                     uint64_t L[4] = {0, 0, 0, 0};
                     for (int t = 0; t < cl.n_tiles; ++t, ++g) {
-                        if (!mbar_wait(&aux->s_full[mt], (uint32_t)g & 1u, abort_flag, status,
-                                       STATUS_ATTN_SOFTMAX)) {
+                        // S of this tile in buffer g & 1; its P goes over it
+                        const uint32_t s_addr =
+                            tmem + lane_off + TM_S + (uint32_t)(mt * 128 + (g & 1) * 64);
+                        if (!mbar_wait(&aux->s_full[g & 1][mt], (uint32_t)(g >> 1) & 1u, abort_flag,
+                                       status, STATUS_ATTN_SOFTMAX)) {
                             ok = false;
                             break;
                         }
@@ -667,13 +749,6 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         const uint64_t a2 = f2pack(alpha, alpha);
 #pragma unroll
                         for (int q = 0; q < 4; ++q) L[q] = f2mul(L[q], a2);
-                        // P buffer (g & 1) was last read by the P V two tiles back
-                        if (g >= 2 && !mbar_wait(&aux->pv_done[g & 1][mt], (uint32_t)((g - 2) >> 1) & 1u,
-                                                 abort_flag, status, STATUS_ATTN_SOFTMAX)) {
-                            ok = false;
-                            break;
-                        }
-                        uint8_t* prow = smem + OFF_P + ((g & 1) * 2 + mt) * P_TILE + i * 128;
                         const uint64_t nm = f2pack(-msl, -msl);
                         // pass 2: p = exp2(s sl2 - m sl2), the row-sum partials, bf16 P
 #pragma unroll 1
@@ -701,20 +776,15 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                                     pk[k >> 1] = bf16x2_bits(pv[k], pv[k + 1]);
                                 }
                             }
-                            const int ch = c0 >> 3;  // 16-byte chunks ch, ch + 1 of the row
-                            *reinterpret_cast<uint4*>(prow + ((ch ^ (i & 7)) << 4)) =
-                                make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                            *reinterpret_cast<uint4*>(prow + (((ch + 1) ^ (i & 7)) << 4)) =
-                                make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                            // keys c0 .. c0 + 15 as 8 bf16 pairs over S columns c0 / 2 ..
+                            // (already read: this chunk's S is in registers)
+                            tmem_st8(s_addr + (uint32_t)(c0 >> 1), pk);
                         }
+                        tmem_wait_st();
                         tc_fence_before();
                         aux->alpha[g & 1][mt][i] = alpha;
-                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                         __syncwarp();
-                        if (lane == 0) {
-                            mbar_arrive(&aux->s_empty[mt]);
-                            mbar_arrive(&aux->p_full[g & 1][mt]);
-                        }
+                        if (lane == 0) mbar_arrive(&aux->p_full[g & 1][mt]);
                     }
                     if (!ok) break;
                     // ---- epilogue of call c for this row: the last P V must be done ----
@@ -731,24 +801,31 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                                               __fadd_rn(__fadd_rn(lsum[4], lsum[5]), __fadd_rn(lsum[6], lsum[7])));
                     const float inv = __frcp_rn(l);
                     if (cl.kind == CALL_READS) {
-                        // normalised call-B output, bf16, for the rows of this read group
+                        // normalised call-B output, bf16, for the rows of this read
+                        // group (other rows keep what an earlier read group left)
                         const bool member = inf->s_grp[qi] == cl.group;
                         if (member) lse_b = __fmaf_rn(m, scale, qlnf(l));
+                        if (__any_sync(0xffffffffu, member)) {
 #pragma unroll 1
-                        for (int c0 = 0; c0 < D; c0 += 32) {
-                            uint32_t r[32], ob[16];
-                            tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
-                            tmem_ld16_nowait(ob_addr + (uint32_t)(c0 >> 1), ob);
-                            tmem_wait_ld();
+                            for (int c0 = 0; c0 < D; c0 += 32) {
+                                uint32_t r[32];
+                                tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
+                                tmem_wait_ld();
+                                uint32_t ob[16];
 #pragma unroll
-                            for (int j = 0; j < 16; ++j) {
-                                const uint32_t v = bf16x2_bits(__fmul_rn(__uint_as_float(r[2 * j]), inv),
-                                                               __fmul_rn(__uint_as_float(r[2 * j + 1]), inv));
-                                if (member) ob[j] = v;
+                                for (int j = 0; j < 16; ++j)
+                                    ob[j] = bf16x2_bits(__fmul_rn(__uint_as_float(r[2 * j]), inv),
+                                                        __fmul_rn(__uint_as_float(r[2 * j + 1]), inv));
+                                if (member) {
+#pragma unroll
+                                    for (int u = 0; u < 4; ++u) {
+                                        const int j = (c0 >> 3) + u;
+                                        *reinterpret_cast<uint4*>(obrow + ((j ^ (i & 15)) << 4)) =
+                                            make_uint4(ob[4 * u], ob[4 * u + 1], ob[4 * u + 2], ob[4 * u + 3]);
+                                    }
+                                }
                             }
-                            tmem_st16(ob_addr + (uint32_t)(c0 >> 1), ob);
                         }
-                        tmem_wait_st();
                     } else {
                         // merge with call B, per-head fp8 quantisation, store
                         const float lse_a = __fmaf_rn(m, scale, qlnf(l));
@@ -756,18 +833,29 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         float w = 0.0f;
                         if (has_b) w = bf16_round(sigmoidf_ref(__fsub_rn(lse_b, lse_a)));
                         const uint64_t inv2 = f2pack(inv, inv), w2 = f2pack(w, w);
-                        // pass 1: the merged row (bf16) into this M tile's two P
-                        // buffers (free: its last P V finished) and its amax; pass 2:
-                        // from there, quantised and stored. A row's 16-byte chunk j
-                        // sits at (j ^ i % 16) * 16 of its 256 bytes: conflict-free.
-                        // rows 0-63 in P[0][mt], rows 64-127 in P[1][mt]
-                        uint8_t* yrow = smem + OFF_P + ((i >> 6) * 2 + mt) * P_TILE + (i & 63) * 256;
+                        // pass 1: the merged row (bf16) over the row's call-B output
+                        // (each chunk read before it is overwritten) and its amax;
+                        // pass 2: from there, quantised and stored
+                        uint8_t* yrow = obrow;
                         float amax = 0.0f;
 #pragma unroll 1
                         for (int c0 = 0; c0 < D; c0 += 32) {
                             uint32_t r[32], ob[16];
                             tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
-                            tmem_ld16_nowait(ob_addr + (uint32_t)(c0 >> 1), ob);
+                            if (has_b) {
+#pragma unroll
+                                for (int u = 0; u < 4; ++u) {
+                                    const int j = (c0 >> 3) + u;
+                                    const uint4 b4 = *reinterpret_cast<const uint4*>(obrow + ((j ^ (i & 15)) << 4));
+                                    ob[4 * u] = b4.x;
+                                    ob[4 * u + 1] = b4.y;
+                                    ob[4 * u + 2] = b4.z;
+                                    ob[4 * u + 3] = b4.w;
+                                }
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < 16; ++j) ob[j] = 0;
+                            }
                             tmem_wait_ld();
                             uint32_t yv[16];
 #pragma unroll
