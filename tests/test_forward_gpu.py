@@ -104,6 +104,84 @@ def test_qwen3_4b_shaped_rows_match_oracle():
     run_and_compare(cfg, weights, docs, questions, budget=4096, n_pages=200, mode="tree")
 
 
+def test_full_budget_config1_chunk_rows_match_oracle():
+    """A full config-1 chunk (the 110,376-token budget, about 450 rows with
+    suffixes lognormal(5.3, 0.6) clipped to [32, 2048], one of them past
+    1,500 tokens) through a 2-layer model of Qwen3-4B's width: the
+    persistent GEMMs' multi-wave tile walk at M near 110k, many-tile causal
+    segments and the shared prefix read by every row. A row's margin
+    depends only on its own tokens and the shared prefix (every kernel is
+    per row or per segment), so the oracle replays two rows of the chunk -
+    the prefix-tree root that computes the shared 64 tokens and the longest
+    row, which borrows them - as a chunk of their own, and their margins must
+    equal the GPU's bit for bit. (About two minutes of exact-mode oracle
+    time on 16 host cores for the two replayed rows.)"""
+    import dataclasses
+    from quail_b200.workload import config1
+    cfg = dataclasses.replace(QWEN3_4B, name="qwen3-4b-2l", n_layers=2)
+    wl = config1()
+    lengths = wl.docs.lengths
+    long_row = int(np.flatnonzero(lengths >= 1500)[0])
+    picked = list(range(470)) + [long_row]
+    docs = [wl.docs[i] for i in picked]
+    budget = QWEN3_4B.max_chunk_tokens
+    dev = torch.device("cuda")
+    weights = random_weights(cfg, seed=0, device=dev)
+    arena = KVArena(cfg.n_layers, 8192, 16, cfg.n_kv, cfg.head_dim, device=dev)
+    arena.pools.zero_()
+    pipe = Qwen3Pipeline(torch, weights, arena)
+    ans = AsyncAnswers(torch, AnswerRows(torch, weights), keep_margins=True)
+    hosts = []
+    loop.run_filter(torch, arena, pipe, ans, docs, wl.questions, budget, arena_writes=True,
+                    attention_mode="tree", prefix_tree=prefix_tree(docs, 16), device=dev,
+                    on_chunk=lambda host, groups: hosts.append(host))
+    torch.cuda.synchronize()
+    assert nat.kernel_status(torch.cuda.current_device()) == 0
+    first = hosts[0]
+    assert first.tokens > 100_000
+    got = {}
+    for host, margins in zip(hosts, ans.margins):
+        for (doc, _), m in zip(host.layout, margins):
+            got[doc] = m
+    tree = prefix_tree(docs, 16)
+    root = int(tree.order[0])
+    first_docs = [doc for doc, _ in first.layout]
+    assert root in first_docs and len(picked) - 1 in first_docs, "the long row is in chunk 1"
+    check = [root, len(picked) - 1]
+    sub = [docs[d] for d in check]
+    sub_tree = prefix_tree(sub, 16)
+    assert int(sub_tree.order[0]) == 0, "the same row computes the shared prefix"
+    cpu_w = weights.to("cpu")
+    cpu_arena = of.CpuArena(cfg.n_layers, 64 * 16 * 16, cfg.n_kv, cfg.head_dim)
+    sub_arena = KVArena(1, 1024, 16, 1, 8, device=None)
+    _, ans_w, tc, fc = cpu_w.answer_rows()
+    want = {}
+
+    class Oracle:
+        tree_attention = True
+
+        def forward_chunk(self, chunk):
+            return chunk.host
+
+    class Answers:
+        def submit(self, host):
+            normed = of.forward_chunk(cpu_w, host, cpu_arena)
+            margin, _ = nx.answer_margin(normed, ans_w, tc, fc)
+            for (doc, _), m in zip(host.layout, margin.numpy()):
+                want[check[doc]] = m
+            return [1] * len(host.layout)
+
+        def result(self, h):
+            return h
+
+    loop.run_filter(torch, sub_arena, Oracle(), Answers(), sub, wl.questions, budget,
+                    arena_writes=True, attention_mode="tree", prefix_tree=sub_tree,
+                    device="cpu")
+    for d in check:
+        assert np.float32(got[d]).view(np.int32) == np.float32(want[d]).view(np.int32), \
+            (d, got[d], want[d])
+
+
 def test_qwen3_32b_width_rows_match_oracle():
     """Qwen3-32B's layer shapes (hidden 5120, 64 query / 8 KV heads, inter
     25600), two layers, on a few config-3-shaped rows."""
