@@ -19,6 +19,7 @@ import numpy as np
 
 from quail_b200 import loop
 from quail_b200.arena import KVArena
+from quail_b200.loop import InputStaging
 from quail_b200.model import random_weights
 from quail_b200.pipeline import build_pipeline
 from quail_b200.readout import AnswerRows, AsyncAnswers, AsyncScores
@@ -86,6 +87,8 @@ class B200Executor:
         self.pipeline = build_pipeline(torch, self.weights, self.arena)
         self.answer_rows = AnswerRows(torch, self.weights)
         self.budget = cfg.max_chunk_tokens
+        # pinned host / device input buffers reused by every chunk upload
+        self.staging = InputStaging(torch, self.device)
 
     def reset_arena(self):
         """Free every page (the pools stay allocated)."""
@@ -114,7 +117,7 @@ class B200Executor:
             [list(q) for q in question_ids], budget or self.budget, timing=timing,
             limit=limit, arena_writes=arena_writes, attention_mode=attention,
             document_done=done, prefix_tree=tree, stats=stats, device=self.device,
-            on_chunk=on_chunk)
+            on_chunk=on_chunk, staging=self.staging)
         for groups, margins in zip(order, ans.margins):
             for (doc, _stage), m in zip(groups, margins):
                 last_margin[doc] = float(m)
@@ -141,7 +144,7 @@ class B200Executor:
             stage_frames=stage_frames, attention_mode=attention, prefix_tree=tree,
             anchor_partners=None if partners is None else (lambda key: partners[key]),
             stats=stats, device=self.device, stop_at_true=stop_at_true,
-            stream_step=stream_step)
+            stream_step=stream_step, staging=self.staging)
         torch.cuda.synchronize(self.device)
         wall = time.perf_counter() - t0
         gpu_s = sum(a.elapsed_time(b) for _, a, b in spans if a is not None) / 1000.0

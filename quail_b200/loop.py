@@ -60,6 +60,52 @@ def attention_tiles(cu) -> np.ndarray:
     return np.stack([seg[order], rows[order]], axis=1).astype(np.int32)
 
 
+class InputStaging:
+    """Reused pinned host and device buffers for chunk uploads, one pair per
+    array name (Quail's InputStaging, quail/backends/quail/executor/loop.py:
+    66-133).
+
+    A chunk's arrays are copied into the pinned host buffer of their name
+    (grown when too small) and sent with one asynchronous copy on the
+    current stream into the device buffer of that name. The host buffer is
+    reused once the event recorded after its last copy has passed, so the
+    CPU never overwrites data a transfer still reads; the device buffer is
+    reused in stream order, after the kernels of the chunk before. The
+    device tensors of an upload are therefore valid until the next upload
+    of the same name has run: callers that keep several chunks' inputs
+    resident at once (bench.py's prepacked chunks) upload without staging.
+    """
+
+    def __init__(self, torch, device="cuda"):
+        self.torch = torch
+        self.device = device
+        self.buffers = {}   # name -> (pinned host, device, event)
+        self.h2d_bytes = 0
+
+    def copy(self, name, array, dtype):
+        torch = self.torch
+        src = torch.from_numpy(np.ascontiguousarray(array).reshape(-1))
+        n = src.numel()
+        held = self.buffers.get(name)
+        if held is not None:
+            held[2].synchronize()   # the last transfer from this host buffer is done
+        if held is None or held[0].numel() < n or held[0].dtype != dtype:
+            size = max(n, 1)
+            if held is not None:
+                size = max(size, 2 * held[0].numel())
+            held = (torch.empty(size, dtype=dtype, pin_memory=True),
+                    torch.empty(size, dtype=dtype, device=self.device),
+                    torch.cuda.Event())
+            self.buffers[name] = held
+        host, dev, event = held
+        host[:n].copy_(src)
+        dev[:n].copy_(host[:n], non_blocking=True)
+        event.record()
+        self.h2d_bytes += n * host.element_size()
+        shape = np.shape(array)
+        return dev[:n].view(shape) if len(shape) > 1 else dev[:n]
+
+
 @dataclass
 class Chunk:
     """One packed forward pass (device tensors), Quail's Chunk contract."""
@@ -91,13 +137,20 @@ class HostChunk:
     fresh_keys: tuple = ()
     h2d_bytes: int = field(default=0)
 
-    def upload(self, torch, device="cuda") -> Chunk:
-        """Copy every array to the device (pinned, non-blocking)."""
+    def upload(self, torch, device="cuda", staging=None) -> Chunk:
+        """Copy every array to the device (non-blocking): through the reused
+        pinned buffers of an InputStaging, or, without one, through fresh
+        pinned copies that the chunk owns."""
         nbytes = [0]
 
-        def dev(a, dtype):
+        def dev(name, a, dtype):
             if a is None:
                 return None
+            if staging is not None and str(device) != "cpu":
+                before = staging.h2d_bytes
+                out = staging.copy(name, np.asarray(a), dtype)
+                nbytes[0] += staging.h2d_bytes - before
+                return out
             t = torch.from_numpy(np.ascontiguousarray(a))
             if t.dtype != dtype:
                 t = t.to(dtype)
@@ -107,30 +160,33 @@ class HostChunk:
             return t.pin_memory().to(device, non_blocking=True)
 
         m = self.meta
-        meta = dict(layer=0, kv_src=dev(m["kv_src"], torch.int64),
-                    kv_dst=dev(m["kv_dst"], torch.int64), reads=None, unified=None,
-                    canvas=None, cu_a=dev(m["cu_a"], torch.int32), max_a=m["max_a"])
+        i64, i32 = torch.int64, torch.int32
+        meta = dict(layer=0, kv_src=dev("kv_src", m["kv_src"], i64),
+                    kv_dst=dev("kv_dst", m["kv_dst"], i64), reads=None, unified=None,
+                    canvas=None, cu_a=dev("cu_a", m["cu_a"], i32), max_a=m["max_a"])
         if self.attention_mode == "tree":
-            meta["tiles"] = dev(attention_tiles(m["cu_a"]), torch.int32)
+            meta["tiles"] = dev("tiles", attention_tiles(m["cu_a"]), i32)
         if m["reads"] is not None:
             r = m["reads"]
             meta["reads"] = dict(
-                rows=dev(r["rows"], torch.int64), cu_q=dev(r["cu_q"], torch.int32),
-                max_q=r["max_q"], used=dev(r["used"], torch.int32), max_used=r["max_used"],
-                table=dev(r["table"], torch.int32), source=dev(r["source"], torch.int32))
+                rows=dev("reads.rows", r["rows"], i64), cu_q=dev("reads.cu_q", r["cu_q"], i32),
+                max_q=r["max_q"], used=dev("reads.used", r["used"], i32),
+                max_used=r["max_used"], table=dev("reads.table", r["table"], i32),
+                source=dev("reads.source", r["source"], i32))
         if m["unified"] is not None:
             u = m["unified"]
             meta["unified"] = dict(
-                src=dev(u["src"], torch.int64), dst=dev(u["dst"], torch.int64),
-                tail_src=dev(u["tail_src"], torch.int64),
-                tail_dst=dev(u["tail_dst"], torch.int64),
-                used=dev(u["used"], torch.int32), table=dev(u["table"], torch.int32),
-                max_used=u["max_used"], cu_q=dev(u["cu_q"], torch.int32), max_q=u["max_q"],
-                tiles=dev(attention_tiles(u["cu_q"]), torch.int32))
+                src=dev("unified.src", u["src"], i64), dst=dev("unified.dst", u["dst"], i64),
+                tail_src=dev("unified.tail_src", u["tail_src"], i64),
+                tail_dst=dev("unified.tail_dst", u["tail_dst"], i64),
+                used=dev("unified.used", u["used"], i32),
+                table=dev("unified.table", u["table"], i32),
+                max_used=u["max_used"], cu_q=dev("unified.cu_q", u["cu_q"], i32),
+                max_q=u["max_q"], tiles=dev("unified.tiles", attention_tiles(u["cu_q"]), i32))
         chunk = Chunk(
-            input_ids=dev(self.input_ids, torch.int64),
-            positions=dev(self.positions, torch.int64),
-            final_indices=dev(self.final_indices, torch.int64),
+            input_ids=dev("input_ids", self.input_ids, i64),
+            positions=dev("positions", self.positions, i64),
+            final_indices=dev("final_indices", self.final_indices, i64),
             meta=meta, attention_mode=self.attention_mode, tokens=self.tokens,
             layout=self.layout, temporary_keys=self.temporary_keys,
             fresh_keys=self.fresh_keys, host=self)
@@ -412,13 +468,16 @@ class FilterStream:
         prefix_tree: PrefixTree over doc_ids, or None.
         limit: stop admitting after this many survivors.
         device: where chunks are uploaded ("cuda" or "cpu" for host tests).
+        staging: an InputStaging whose pinned buffers the uploads reuse, or
+            None for fresh pinned copies per chunk (needed when the caller
+            keeps several chunks' device inputs at once).
     """
 
     def __init__(self, torch, arena, pipeline, async_ans, doc_ids, question_ids, budget,
                  timing=None, limit=None, *, arena_writes, arena_keys=None,
                  hold_survivors=False, hold_extra_tokens=0,
                  attention_mode=None, document_done=None, prefix_tree=None,
-                 device="cuda", on_chunk=None):
+                 device="cuda", on_chunk=None, staging=None):
         p = _shared_preamble_tokens(question_ids)
         keys = range(len(doc_ids)) if arena_keys is None else arena_keys
         if len(keys) != len(doc_ids):
@@ -472,6 +531,7 @@ class FilterStream:
         self.capacity_extra = capacity_extra
         self.tails = tails
         self.device = device
+        self.staging = staging
         self.on_chunk = on_chunk
         self.spans = []
         self.tokens = 0
@@ -605,7 +665,7 @@ class FilterStream:
             parent = sched.borrowing.tree_parent[doc]
             if parent is not None:
                 arena.release(self.keys[parent])
-        chunk = host.upload(self.torch, self.device)
+        chunk = host.upload(self.torch, self.device, self.staging)
         self.h2d_bytes += host.h2d_bytes
         if self.on_chunk is not None:
             self.on_chunk(host, groups)
@@ -635,7 +695,7 @@ class FilterStream:
 def run_filter(torch, arena, pipeline, async_ans, doc_ids, question_ids, budget, timing=None,
                limit=None, *, arena_writes, arena_keys=None, attention_mode=None,
                document_done=None, prefix_tree=None, stats=None, device="cuda",
-               on_chunk=None):
+               on_chunk=None, staging=None):
     """The filter chain run to the end; see FilterStream for the arguments.
 
     Returns:
@@ -646,7 +706,7 @@ def run_filter(torch, arena, pipeline, async_ans, doc_ids, question_ids, budget,
                           timing=timing, limit=limit, arena_writes=arena_writes,
                           arena_keys=arena_keys, attention_mode=attention_mode,
                           document_done=document_done, prefix_tree=prefix_tree,
-                          device=device, on_chunk=on_chunk)
+                          device=device, on_chunk=on_chunk, staging=staging)
     while not stream.done:
         stream.next()
     if stats is not None:
@@ -659,7 +719,8 @@ def run_filter(torch, arena, pipeline, async_ans, doc_ids, question_ids, budget,
 def run_join(torch, arena, pipeline, async_ans, anchor_prefixes, stage_suffixes, budget,
              stage_frames=None, anchor_keys=None, anchor_done=None, anchor_source=None,
              anchor_partners=None, anchor_batch=None, attention_mode=None, prefix_tree=None,
-             stats=None, device="cuda", on_chunk=None, stop_at_true=False, stream_step=None):
+             stats=None, device="cuda", on_chunk=None, stop_at_true=False, stream_step=None,
+             staging=None):
     """Stream partner lists against anchors, gating survivors between stages
     (Quail's run_join, loop.py:609-978; arguments as there).
 
@@ -828,7 +889,7 @@ def run_join(torch, arena, pipeline, async_ans, anchor_prefixes, stage_suffixes,
     def run_one(part):
         nonlocal tokens
         host = build(part)
-        chunk = host.upload(torch, device)
+        chunk = host.upload(torch, device, staging)
         h2d[0] += host.h2d_bytes
         h2d[1] += 1
         if on_chunk is not None:
