@@ -20,7 +20,10 @@ Measurements (one JSON line on rank 0):
   launch over CUDA-event launch time, against 2x the measured sustained
   bf16 dense peak (B200's FP8:bf16 dense ratio);
 - cpu_baseline: the CPU oracle (a restatement of the reference's torch
-  path) on a bounded sample of the same rows on the host cores.
+  path) on a bounded sample of the same rows on the host cores;
+- other_scales: the same timed chunks in the other scale mode (--scales:
+  ue8m0 by default, the power-of-two scales vLLM's DeepGEMM path uses and
+  the block-scaled MMA applies; fp32 keeps the loaded block scales).
 
 --impl reference runs the reference arm: the reference's computation
 restated on the host CPU (the oracle), timed per step on a bounded sample.
@@ -43,6 +46,10 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "AI.IF rows/sec (Qwen3-4B FP8 filter, config 1)"
 UNIT = "rows/s"
+SCALES_UE8M0 = ("ue8m0: power-of-two activation and weight block scales (weights "
+                "re-quantised at load), block-scaled MMA; the mode vLLM selects for "
+                "DeepGEMM (is_deep_gemm_e8m0_used), the only one its sm_100 GEMM takes")
+SCALES_FP32 = "fp32: activation and weight block scales as computed / loaded"
 
 
 # DRAM bytes (read + write) per GEMM launch, averaged over the 144 launches
@@ -74,6 +81,12 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--budget", type=int, default=0)
+    p.add_argument("--scales", default="ue8m0", choices=["ue8m0", "fp32"],
+                   help="quantiser / GEMM scale mode: ue8m0 (power-of-two scales on the "
+                        "block-scaled MMA; DeepGEMM's mode on sm_100) or fp32")
+    p.add_argument("--other-steps", type=int, default=6,
+                   help="timed chunks of the other scale mode, reported beside the "
+                        "headline (0: skip)")
     return p.parse_args()
 
 
@@ -218,7 +231,7 @@ def prepack(torch, arena, wl, lo, hi, budget, n_chunks, device):
         n_rows = min(hi - lo, 2 * n_rows)
 
 
-def cpu_baseline(torch, weights, wl, rows, page_tokens=16):
+def cpu_baseline(torch, weights, wl, rows, page_tokens=16, ue8m0=False):
     """The CPU oracle over a bounded sample (rows 0..rows-1 of the workload)."""
     from oracle import forward as of
     from oracle import numerics as nx
@@ -231,6 +244,7 @@ def cpu_baseline(torch, weights, wl, rows, page_tokens=16):
     # the baseline times the reference's algorithm at BLAS speed (the
     # oracle's fast mode), not the bit-exact tensor-core model
     nx.MODE["exact"] = False
+    nx.MODE["ue8m0"] = ue8m0
     cpu_w = weights.to("cpu")
     docs = [wl.docs[i] for i in range(rows)]
     arena = KVArena(1, 4096, page_tokens, 1, 8, device=None)
@@ -276,7 +290,17 @@ def reference_arm(args):
 
     wl = config1()
     weights = random_weights(QWEN3_4B, seed=0, device="cpu")
-    run_once, cores, rows, tokens = cpu_baseline(torch, weights, wl, args.ref_rows)
+    ue8m0 = args.scales == "ue8m0"
+    if ue8m0:
+        # vLLM's load-time re-quantisation to power-of-two block scales
+        from oracle import numerics as nx
+        from quail_b200.model import LINEARS
+        for layer in weights.layers:
+            for wn, sn in LINEARS:
+                q, sc = nx.requant_weight_ue8m0(getattr(layer, wn), getattr(layer, sn))
+                setattr(layer, wn, q)
+                setattr(layer, sn, sc)
+    run_once, cores, rows, tokens = cpu_baseline(torch, weights, wl, args.ref_rows, ue8m0=ue8m0)
     for _ in range(args.warmup):
         run_once()
     t0 = time.perf_counter()
@@ -292,7 +316,7 @@ def reference_arm(args):
         "vs_baseline": None, "dtype": "f32 (fp8 codes dequantised on the CPU)",
         "data": "synthetic (seeded, config-1 shapes)",
         "config": {"workload": "config1: Qwen3-4B FP8 AI.IF filter, host CPU oracle sample",
-                   "sample_rows": rows, "sample_tokens": tokens},
+                   "sample_rows": rows, "sample_tokens": tokens, "scales": args.scales},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -321,7 +345,7 @@ def main():
     cfg = QWEN3_4B
     wl = config1()
     budget = args.budget or cfg.max_chunk_tokens
-    ex = B200Executor(torch, cfg, args.pages, device=dev, seed=0)
+    ex = B200Executor(torch, cfg, args.pages, device=dev, seed=0, scales=args.scales)
     lo, hi = token_shard(wl.row_tokens(), rank, world)
 
     # ---- device-resident timing: chunks packed and uploaded beforehand ----
@@ -380,6 +404,46 @@ def main():
         rows_all, tokens_all = float(rows_timed), float(tokens_timed)
     del outs
 
+    # ---- the other scale mode on the same chunks (fresh seed-0 weights) ----
+    other = None
+    n_other = min(args.other_steps, args.steps)
+    if n_other > 0:
+        from quail_b200.model import random_weights, requant_ue8m0
+        from quail_b200.pipeline import build_pipeline
+        o_ue8m0 = args.scales != "ue8m0"
+        w_other = random_weights(cfg, seed=0, device=dev)
+        if o_ue8m0:
+            requant_ue8m0(w_other)
+        pipe_other = build_pipeline(torch, w_other, ex.arena, ue8m0=o_ue8m0)
+        pipe_other.forward_chunk(chunks[0])
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        pipe_other.engine.gemm_events = []
+        o0 = torch.cuda.Event(enable_timing=True)
+        o1 = torch.cuda.Event(enable_timing=True)
+        o0.record()
+        for chunk in timed[:n_other]:
+            pipe_other.forward_chunk(chunk)
+        o1.record()
+        torch.cuda.synchronize()
+        o_ms = o0.elapsed_time(o1)
+        o_gemm = pipe_other.engine.gemm_events
+        o_gemm_ms = sum(a.elapsed_time(b) for a, b, _, _ in o_gemm)
+        o_flops = sum(f for _, _, f, _ in o_gemm)
+        o_rows = sum(len(c.layout) for c in timed[:n_other])
+        ov = torch.tensor([o_ms, o_rows, o_gemm_ms, o_flops], dtype=torch.float64, device=dev)
+        if world > 1:
+            omx = ov.clone()
+            dist.all_reduce(omx, op=dist.ReduceOp.MAX)
+            osm = ov.clone()
+            dist.all_reduce(osm, op=dist.ReduceOp.SUM)
+            o_ms, o_rows = float(omx[0]), float(osm[1])
+        other = {"scales": "ue8m0" if o_ue8m0 else "fp32", "steps": n_other,
+                 "value": o_rows / (o_ms / 1000.0), "ms_per_step": o_ms / n_other,
+                 "gemm_tflops": o_flops / (o_gemm_ms / 1000.0) / 1e12 if o_gemm_ms else None}
+        del pipe_other, w_other, o_gemm
+
     # ---- end to end through the public API, host inputs ----
     e2e = None
     if not args.no_e2e:
@@ -419,7 +483,8 @@ def main():
     # ---- CPU baseline (rank 0, N=1) ----
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        run_once, cores, rows, tokens = cpu_baseline(torch, ex.weights, wl, args.cpu_rows)
+        run_once, cores, rows, tokens = cpu_baseline(torch, ex.weights, wl, args.cpu_rows,
+                                                     ue8m0=args.scales == "ue8m0")
         t0 = time.perf_counter()
         run_once()
         dt = time.perf_counter() - t0
@@ -427,6 +492,7 @@ def main():
                "sample": f"rows 0..{rows - 1} of config 1 ({tokens} tokens, one tree chunk) "
                          f"through the CPU oracle, {dt:.1f} s"}
 
+    ue8m0 = args.scales == "ue8m0"
     if rank == 0:
         peaks, src = measured_peaks()
         peak = 2.0 * peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
@@ -435,11 +501,15 @@ def main():
             "metric": METRIC, "value": rows_all / (ms / 1000.0), "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "fp8-e4m3 GEMMs, bf16 activations, fp32 accumulate",
+            "vs_baseline": None,
+            "dtype": ("fp8-e4m3 GEMMs with UE8M0 (power-of-two) block scales" if ue8m0 else
+                      "fp8-e4m3 GEMMs with fp32 block scales")
+                     + ", bf16 activations, fp32 accumulate",
             "data": "synthetic (seeded config-1 rows; random-init Qwen3-4B FP8 weights)",
             "config": {"workload": "config1: Qwen3-4B FP8 AI.IF filter, tree attention",
+                       "scales": (SCALES_UE8M0 if ue8m0 else SCALES_FP32),
                        "rows_per_rank_timed": rows_timed, "chunk_budget_tokens": budget,
-                       "parallelism": f"dp{world} (contiguous row slices)",
+                       "parallelism": f"dp{world} (token-balanced contiguous row slices)",
                        "prefill_tokens_per_s": tokens_all / (ms / 1000.0),
                        "l2": "inputs larger than L2 (>=0.5 GB activations per chunk)",
                        "status_word": status},
@@ -455,7 +525,7 @@ def main():
                          "launches": len(gemm), "gemm_ms": gemm_ms,
                          "gemm_share_of_step": gemm_ms / ms if ms else None},
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-            "clocks": clocks,
+            "clocks": clocks, "other_scales": other,
         }
         print(json.dumps(line))
     if world > 1:

@@ -14,7 +14,14 @@
  *     uint8_t, and every "scale" array holds one float per 128-column group
  *     of a row, laid out group-major: scale[g * scale_ld + row]
  *     (the column-major (rows, width/128) layout of
- *     quail/backends/quail/executor/attention.py:153-156).
+ *     quail/backends/quail/executor/attention.py:153-156);
+ *   - `ue8m0` selects the reference's UE8M0 scale mode (Engine.use_ue8m0,
+ *     vLLM's is_deep_gemm_e8m0_used; quail/backends/quail/executor/
+ *     attention.py:115, 151, 315-316, 350-351, 467-468): a quantiser's
+ *     scale becomes exp2(ceil(log2(max(amax, 1e-10) / 448))), the least
+ *     power of two at or above the fp32 scale (taken exactly from its
+ *     bits), and the GEMMs take power-of-two scales on the block-scaled
+ *     MMA path. 0 keeps the fp32 scales.
  *
  * Each function names the reference interface it replaces
  * (paths inside the animysore/quail repository).
@@ -33,6 +40,13 @@ extern "C" {
 #define QB_ERR_CUDA 2      /* a CUDA runtime or driver call failed */
 #define QB_ERR_DEVICE 3    /* the device is not sm_100 or lacks a feature */
 #define QB_ERR_TIMEOUT 4   /* a kernel's bounded wait ran out (see qb_kernel_status) */
+
+/* Bits of the device status word (qb_kernel_status). */
+#define QB_STATUS_WAIT_GEMM 0x0Fu    /* a GEMM role's bounded wait gave up */
+#define QB_STATUS_WAIT_ATTN 0xF0u    /* an attention role's bounded wait gave up */
+#define QB_STATUS_BAD_TOKEN 0x100u   /* a token id outside [0, vocab) */
+#define QB_STATUS_BAD_INDEX 0x200u   /* a page, row or segment index out of range */
+#define QB_STATUS_BAD_SCALE 0x400u   /* a UE8M0-mode scale that is not a power of two */
 
 /* Library version, (major << 16) | (minor << 8) | patch. */
 int qb_version(void);
@@ -70,7 +84,8 @@ int qb_set_wait_limit(int device, uint64_t limit_ns);
 int qb_embed_rmsnorm_quant(const int64_t* ids, int64_t rows, const void* embed,
                            int64_t vocab, int64_t hidden, const void* norm_w,
                            float eps, void* residual_out, void* q_out,
-                           float* scale_out, int64_t scale_ld, void* stream);
+                           float* scale_out, int64_t scale_ld, int ue8m0,
+                           void* stream);
 
 /*
  * Fused residual add + RMSNorm + 1x128 fp8 quantisation:
@@ -84,7 +99,7 @@ int qb_embed_rmsnorm_quant(const int64_t* ids, int64_t rows, const void* embed,
  */
 int qb_add_rmsnorm_quant(const void* hidden, void* residual, const void* w,
                          float eps, int64_t rows, int64_t hidden_dim, void* q_out,
-                         float* scale_out, int64_t scale_ld, void* stream);
+                         float* scale_out, int64_t scale_ld, int ue8m0, void* stream);
 
 /*
  * FP8 e4m3 GEMM with 1x128 activation scales and 128x128 weight scales on
@@ -96,10 +111,15 @@ int qb_add_rmsnorm_quant(const void* hidden, void* residual, const void* w,
  * a: fp8 [m, k] row-major; a_scale: f32 [k/128, a_scale_ld];
  * w: fp8 [n, k] row-major; w_scale: f32 [n/128, k/128]; out: bf16 [m, n].
  * Requires k % 128 == 0, n % 128 == 0, a and w 16-byte aligned.
+ * ue8m0 != 0 (fp8_gemm_nt's is_deep_gemm_e8m0_used): every scale is a power
+ * of two, applied by the block-scaled MMA (tcgen05 kind::mxf8f6f4) and
+ * accumulated over the whole K in fp32:
+ * out[m, n] = bf16( sum_k a[m,k] w[n,k] a_scale[k/128, m] w_scale[n/128, k/128] );
+ * n % 256 == 0; a scale that is not a power of two sets QB_STATUS_BAD_SCALE.
  */
 int qb_gemm_fp8_bs(const void* a, const float* a_scale, int64_t a_scale_ld,
                    const void* w, const float* w_scale, void* out, int64_t m,
-                   int64_t n, int64_t k, void* stream);
+                   int64_t n, int64_t k, int ue8m0, void* stream);
 
 /*
  * Per-head RMSNorm of q and k, neox rotary from cos_sin[pos] (cos in the
@@ -144,7 +164,7 @@ int qb_gemm_fp8_qknorm_rope(const void* a, const float* a_scale,
                             float eps, int n_q, int n_kv, int head_dim,
                             void* q_out, void* k_out, void* v_out,
                             const int64_t* row_dst, void* k_pool, void* v_pool,
-                            int64_t pool_rows, void* stream);
+                            int64_t pool_rows, int ue8m0, void* stream);
 
 /*
  * Builds the per-row destination map the fused KV append reads:
@@ -194,7 +214,8 @@ int qb_tree_attention(const void* q, const void* k, const void* v, int64_t rows,
                       int64_t table_width, const int32_t* source,
                       const void* k_pool, const void* v_pool, int64_t n_pages,
                       int page_tokens, float softmax_scale, void* q_out,
-                      float* scale_out, int64_t scale_ld, void* stream);
+                      float* scale_out, int64_t scale_ld, int ue8m0,
+                      void* stream);
 
 /*
  * The unified attention path: one causal paged call in which query
@@ -214,7 +235,7 @@ int qb_unified_attention(const void* q, int64_t rows, int n_q, int n_kv,
                          int64_t table_width, const void* k_pool,
                          const void* v_pool, int64_t n_pages, int page_tokens,
                          float softmax_scale, void* q_out, float* scale_out,
-                         int64_t scale_ld, void* stream);
+                         int64_t scale_ld, int ue8m0, void* stream);
 
 /*
  * Host helper for qb_tree_attention: the (segment, first row) pairs of the
@@ -235,7 +256,7 @@ int qb_tree_attention_tiles(const int32_t* cu_a_host, int64_t n_seg,
  */
 int qb_silu_mul_quant(const void* gate_up, int64_t rows, int64_t inter,
                       void* q_out, float* scale_out, int64_t scale_ld,
-                      void* stream);
+                      int ue8m0, void* stream);
 
 /*
  * The MLP's gate_up projection and its SiLU-gated quantisation in one
@@ -254,7 +275,21 @@ int qb_gemm_fp8_silu_quant(const void* a, const float* a_scale,
                            int64_t a_scale_ld, const void* w,
                            const float* w_scale, void* q_out, float* scale_out,
                            int64_t scale_ld, int64_t m, int64_t inter,
-                           int64_t k, void* stream);
+                           int64_t k, int ue8m0, void* stream);
+
+/*
+ * Re-quantises a block-scaled fp8 weight to power-of-two block scales, in
+ * place, for the UE8M0 mode: per 128 x 128 block x = w * w_scale (fp32),
+ * s = max(amax(|x|), 1e-4) / 448 raised to the least power of two at or
+ * above it, w = e4m3(x / s), w_scale = s. Replaces vLLM's
+ * requant_weight_ue8m0_inplace, which Quail's model load runs when
+ * DeepGEMM uses UE8M0 scales (vllm/model_executor/layers/quantization/
+ * utils/fp8_utils.py; the mode quail/backends/quail/executor/attention.py:
+ * 115 reads). w: fp8 [n, k] row-major, 16-byte aligned; w_scale: f32
+ * [n/128, k/128]. n, k multiples of 128.
+ */
+int qb_requant_weight_ue8m0(void* w, float* w_scale, int64_t n, int64_t k,
+                            void* stream);
 
 /*
  * Final norm over the answer rows only: for each final row f,

@@ -13,6 +13,10 @@ Two modes (MODE["exact"]):
   oracle/tcmodel.c). Agrees with the kernels bit for bit.
 - fast (the CPU baseline): the same algorithm with torch's own reductions,
   fp32 BLAS GEMMs and exp; agrees to the last bits, runs at BLAS speed.
+
+MODE["ue8m0"] selects the reference's UE8M0 scale mode (Engine.use_ue8m0,
+quail/backends/quail/executor/attention.py:115): power-of-two quantiser
+scales and the GEMMs' whole-K accumulation of the block-scaled MMA.
 """
 
 import numpy as np
@@ -22,7 +26,7 @@ from oracle import tc
 
 GROUP = 128
 FP8_MAX = 448.0
-MODE = {"exact": True}
+MODE = {"exact": True, "ue8m0": False}
 
 
 def _to_bf16(x):
@@ -69,6 +73,20 @@ def fma(a, b, c):
     return tc.fma(a, b, c)
 
 
+def ue8m0_scale(scale):
+    """The UE8M0 mode's scale: exp2(ceil(log2(scale))) for fp32 scale > 0,
+    taken exactly as the least power of two >= scale (from the bits: a
+    power of two, inf and NaN stay). The reference computes it through
+    log2 (attention.py:315-316, 350-351, 467-468; vLLM's
+    per_token_group_quant_fp8 with use_ue8m0); a float log2 can round to
+    an integer for a scale a few ulps above a power of two, which the exact
+    form does not."""
+    b = scale.to(torch.float32).contiguous().view(torch.int32)
+    up = (b & 0x7F800000) + 0x800000
+    keep = ((b & 0x7FFFFF) == 0) | (b >= 0x7F800000)
+    return torch.where(keep, b, up).view(torch.float32)
+
+
 def quant_groups(y):
     """1x128 fp8 quantisation of fp32 rows.
 
@@ -82,6 +100,8 @@ def quant_groups(y):
     g = y.reshape(rows, width // GROUP, GROUP)
     amax = g.abs().amax(dim=2)
     scale = torch.clamp(amax, min=1e-10) / FP8_MAX
+    if MODE["ue8m0"]:
+        scale = ue8m0_scale(scale)
     q = torch.clamp(g / scale[:, :, None], -FP8_MAX, FP8_MAX)
     return to_fp8(q.reshape(rows, width)), scale.t().contiguous()
 
@@ -148,6 +168,8 @@ def gemm_fp8_bs(a_codes, a_scales, w_codes, w_scales):
     order (DeepGEMM's promotion), bf16 output. a_scales is group-major
     (K/128, M). Exact mode: the partials follow the tensor cores'
     accumulation (tcmodel.c); fast mode: fp32 BLAS partials."""
+    if MODE["ue8m0"]:
+        return gemm_fp8_mx(a_codes, a_scales, w_codes, w_scales)
     if MODE["exact"]:
         return tc.gemm_fp8(a_codes, a_scales, w_codes, w_scales)
     m, k = a_codes.shape
@@ -160,6 +182,39 @@ def gemm_fp8_bs(a_codes, a_scales, w_codes, w_scales):
     for b in range(kb):
         acc = acc + (a[b] @ w[b]) * (a_scales[b][:, None] * ws[:, b][None, :])
     return to_bf16(acc)
+
+
+def gemm_fp8_mx(a_codes, a_scales, w_codes, w_scales):
+    """fp8_gemm_nt in the UE8M0 mode on sm_100 (DeepGEMM's block-scaled
+    kernels): every scale a power of two, applied to the products, one fp32
+    accumulation over the whole K, bf16 output. Exact mode: the tensor
+    cores' accumulation per K=32 step (tcmodel.c gemm_mx); fast mode: the
+    exactly scaled operands through an fp32 BLAS GEMM."""
+    if MODE["exact"]:
+        return tc.gemm_mx(a_codes, a_scales, w_codes, w_scales)
+    m, k = a_codes.shape
+    n = w_codes.shape[0]
+    a = dequant(a_codes, a_scales)
+    ws = w_scales.to(torch.float32).repeat_interleave(GROUP, 0).repeat_interleave(GROUP, 1)
+    w = w_codes.to(torch.float32) * ws[:n, :k]
+    return to_bf16(a @ w.t())
+
+
+def requant_weight_ue8m0(w_codes, w_scales):
+    """A block-scaled fp8 weight re-quantised to power-of-two block scales,
+    as vLLM does at load time when DeepGEMM uses UE8M0 (vllm 0.22,
+    model_executor/layers/quantization/utils/fp8_utils.py
+    requant_weight_ue8m0_inplace, through deep_gemm.py per_block_cast_to_fp8):
+    x = code * scale (fp32) per 128 x 128 block; s = max(amax, 1e-4) / 448
+    raised to a power of two; codes = e4m3(x / s). Returns (codes, scales)."""
+    n, k = w_codes.shape
+    nb, kb = n // GROUP, k // GROUP
+    x = (w_codes.to(torch.float32).reshape(nb, GROUP, kb, GROUP)
+         * w_scales.to(torch.float32)[:, None, :, None])
+    amax = x.abs().amax(dim=(1, 3)).clamp(min=1e-4)
+    s = ue8m0_scale(amax / FP8_MAX)
+    q = to_fp8(x / s[:, None, :, None]).reshape(n, k)
+    return q, s
 
 
 def qk_norm_rope(qkv, positions, cos_sin, q_w, k_w, eps, n_q, n_kv, head_dim=128):

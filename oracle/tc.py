@@ -22,6 +22,8 @@ def lib():
         L = ctypes.CDLL(str(path))
         L.qbm_gemm_fp8.argtypes = [_P, _P, _I, _P, _P, _P, _I, _I, _I]
         L.qbm_gemm_fp8_f32.argtypes = [_P, _P, _I, _P, _P, _P, _I, _I, _I]
+        L.qbm_gemm_mx.argtypes = [_P, _P, _I, _P, _P, _P, _I, _I, _I]
+        L.qbm_gemm_mx_f32.argtypes = [_P, _P, _I, _P, _P, _P, _I, _I, _I]
         L.qbm_mma_bf16.argtypes = [_P, _P, _P, _P, _I, _I, _I]
         for name in ("qbm_exp2f_array", "qbm_exp2s_array", "qbm_sigmoidf_array",
                      "qbm_lnf_array"):
@@ -72,6 +74,24 @@ def gemm_fp8_f32(a_codes, a_scales, w_codes, w_scales):
     out = torch.empty(m, n, dtype=torch.float32)
     lib().qbm_gemm_fp8_f32(_p(a), _p(as_), as_.shape[1], _p(w), _p(ws), _p(out), m, n, k)
     return out
+
+
+def gemm_mx(a_codes, a_scales, w_codes, w_scales, f32=False):
+    """The kernel's UE8M0-mode GEMM (block-scaled MMA over the whole K),
+    bit for bit: bf16 [M, N] (f32: the accumulator before rounding)."""
+    a = _c(a_codes).view(torch.uint8)
+    w = _c(w_codes).view(torch.uint8)
+    as_ = _c(a_scales, torch.float32)
+    ws = _c(w_scales, torch.float32)
+    m, k = a.shape
+    n = w.shape[0]
+    if f32:
+        out = torch.empty(m, n, dtype=torch.float32)
+        lib().qbm_gemm_mx_f32(_p(a), _p(as_), as_.shape[1], _p(w), _p(ws), _p(out), m, n, k)
+        return out
+    out = torch.empty(m, n, dtype=torch.int16)
+    lib().qbm_gemm_mx(_p(a), _p(as_), as_.shape[1], _p(w), _p(ws), _p(out), m, n, k)
+    return out.view(torch.bfloat16)
 
 
 def mma_bf16(a, b, c0=None):

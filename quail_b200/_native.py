@@ -32,23 +32,24 @@ SIGNATURES = {
     "qb_last_error": [],
     "qb_kernel_status": [_I32, _P],
     "qb_set_wait_limit": [_I32, ctypes.c_uint64],
-    "qb_embed_rmsnorm_quant": [_P, _I64, _P, _I64, _I64, _P, _F32, _P, _P, _P, _I64, _P],
-    "qb_add_rmsnorm_quant": [_P, _P, _P, _F32, _I64, _I64, _P, _P, _I64, _P],
-    "qb_gemm_fp8_bs": [_P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _P],
+    "qb_embed_rmsnorm_quant": [_P, _I64, _P, _I64, _I64, _P, _F32, _P, _P, _P, _I64, _I32, _P],
+    "qb_add_rmsnorm_quant": [_P, _P, _P, _F32, _I64, _I64, _P, _P, _I64, _I32, _P],
+    "qb_gemm_fp8_bs": [_P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I32, _P],
     "qb_qknorm_rope": [_P, _I64, _P, _P, _I64, _P, _P, _F32, _I64, _I32, _I32, _I32,
                        _P, _P, _P, _P, _P, _P, _I64, _P],
     "qb_kv_row_map": [_P, _P, _I64, _I64, _I64, _P, _P],
     "qb_kv_scatter": [_P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _I64, _P],
     "qb_tree_attention": [_P, _P, _P, _I64, _I32, _I32, _I32, _P, _I64, _P, _I64,
                           _P, _P, _P, _I64, _I64, _P, _P, _P, _I64, _I32, _F32,
-                          _P, _P, _I64, _P],
+                          _P, _P, _I64, _I32, _P],
     "qb_tree_attention_tiles": [_P, _I64, _P, _I64, _P],
     "qb_unified_attention": [_P, _I64, _I32, _I32, _I32, _P, _I64, _P, _I64, _P, _P, _I64,
-                             _P, _P, _I64, _I32, _F32, _P, _P, _I64, _P],
-    "qb_silu_mul_quant": [_P, _I64, _I64, _P, _P, _I64, _P],
-    "qb_gemm_fp8_silu_quant": [_P, _P, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P],
+                             _P, _P, _I64, _I32, _F32, _P, _P, _I64, _I32, _P],
+    "qb_silu_mul_quant": [_P, _I64, _I64, _P, _P, _I64, _I32, _P],
+    "qb_gemm_fp8_silu_quant": [_P, _P, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _P],
     "qb_gemm_fp8_qknorm_rope": [_P, _P, _I64, _P, _P, _I64, _I64, _P, _P, _I64, _P, _P, _F32,
-                                _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _I64, _P],
+                                _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _I64, _I32, _P],
+    "qb_requant_weight_ue8m0": [_P, _P, _I64, _I64, _P],
     "qb_final_norm": [_P, _P, _I64, _I64, _P, _I64, _P, _F32, _P, _P],
     "qb_answer_margin": [_P, _I64, _I64, _P, _I32, _P, _I32, _P, _I32, _P, _P, _P],
     "qb_answer_score": [_P, _I64, _I64, _P, _I32, _P, _I32, _P, _I32, _P, _P],

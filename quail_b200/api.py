@@ -20,7 +20,7 @@ import numpy as np
 from quail_b200 import loop
 from quail_b200.arena import KVArena
 from quail_b200.loop import InputStaging
-from quail_b200.model import random_weights
+from quail_b200.model import random_weights, requant_ue8m0, scales_are_ue8m0
 from quail_b200.pipeline import build_pipeline
 from quail_b200.readout import AnswerRows, AsyncAnswers, AsyncScores
 from quail_b200.tokens import prefix_tree
@@ -75,16 +75,28 @@ class B200Executor:
         n_pages: KV arena pages (16 tokens each).
         weights: loaded Weights, or None for seeded random-init weights.
         device: the CUDA device.
+        scales: "fp32" (block scales as loaded) or "ue8m0" (the reference's
+            UE8M0 mode, DeepGEMM's on sm_100: power-of-two scales, the
+            block-scaled MMA; weights whose scales are not all powers of two
+            are re-quantised in place first, as vLLM does at load).
     """
 
-    def __init__(self, torch, cfg, n_pages, weights=None, device="cuda", seed=0):
+    def __init__(self, torch, cfg, n_pages, weights=None, device="cuda", seed=0,
+                 scales="fp32"):
+        if scales not in ("fp32", "ue8m0"):
+            raise ValueError(f"scales {scales!r}: fp32 or ue8m0")
         self.torch = torch
         self.cfg = cfg
         self.device = torch.device(device)
+        self.scales = scales
         self.weights = weights or random_weights(cfg, seed=seed, device=self.device)
+        if scales == "ue8m0" and not scales_are_ue8m0(self.weights):
+            with torch.cuda.device(self.device):
+                requant_ue8m0(self.weights)
         self.arena = KVArena(cfg.n_layers, n_pages, 16, cfg.n_kv, cfg.head_dim,
                              device=self.device)
-        self.pipeline = build_pipeline(torch, self.weights, self.arena)
+        self.pipeline = build_pipeline(torch, self.weights, self.arena,
+                                       ue8m0=scales == "ue8m0")
         self.answer_rows = AnswerRows(torch, self.weights)
         self.budget = cfg.max_chunk_tokens
         # pinned host / device input buffers reused by every chunk upload

@@ -14,7 +14,7 @@ int launch_attention_tc(bool unified, const char* who, const void* q, const void
                         int64_t table_width, const int32_t* source, const void* k_pool,
                         const void* v_pool, int64_t n_pages, int page_tokens,
                         float softmax_scale, void* q_out, float* scale_out, int64_t scale_ld,
-                        void* stream);
+                        bool ue8m0, void* stream);
 }  // namespace qb
 
 namespace {
@@ -72,7 +72,7 @@ extern "C" int qb_tree_attention(const void* q, const void* k, const void* v, in
                                  int64_t table_width, const int32_t* source, const void* k_pool,
                                  const void* v_pool, int64_t n_pages, int page_tokens,
                                  float softmax_scale, void* q_out, float* scale_out,
-                                 int64_t scale_ld, void* stream) {
+                                 int64_t scale_ld, int ue8m0, void* stream) {
     const char* who = "qb_tree_attention";
     int st = check_common(who, rows, n_q, n_kv, head_dim, n_seg, n_tiles, scale_ld, q_out,
                           scale_out);
@@ -89,7 +89,7 @@ extern "C" int qb_tree_attention(const void* q, const void* k, const void* v, in
     st = qb::launch_attention_tc(false, who, q, k, v, rows, n_q, n_kv, cu_a, tiles, n_tiles,
                                  read_cu_q, read_used, read_table, n_reads, table_width, source,
                                  k_pool, v_pool, n_pages, page_tokens, softmax_scale, q_out,
-                                 scale_out, scale_ld, stream);
+                                 scale_out, scale_ld, ue8m0 != 0, stream);
     if (st == -1)
         return invalid("qb_tree_attention: query heads per KV head must be 2, 4 or a multiple "
                        "of 4, and page_tokens a divisor of 64 of at least 8");
@@ -102,7 +102,7 @@ extern "C" int qb_unified_attention(const void* q, int64_t rows, int n_q, int n_
                                     int64_t table_width, const void* k_pool, const void* v_pool,
                                     int64_t n_pages, int page_tokens, float softmax_scale,
                                     void* q_out, float* scale_out, int64_t scale_ld,
-                                    void* stream) {
+                                    int ue8m0, void* stream) {
     const char* who = "qb_unified_attention";
     int st = check_common(who, rows, n_q, n_kv, head_dim, n_seq, n_tiles, scale_ld, q_out,
                           scale_out);
@@ -117,7 +117,7 @@ extern "C" int qb_unified_attention(const void* q, int64_t rows, int n_q, int n_
     st = qb::launch_attention_tc(true, who, q, nullptr, nullptr, rows, n_q, n_kv, cu_q, tiles,
                                  n_tiles, nullptr, used, table, 0, table_width, nullptr, k_pool,
                                  v_pool, n_pages, page_tokens, softmax_scale, q_out, scale_out,
-                                 scale_ld, stream);
+                                 scale_ld, ue8m0 != 0, stream);
     if (st == -1)
         return invalid("qb_unified_attention: query heads per KV head must be 2, 4 or a "
                        "multiple of 4, and page_tokens a divisor of 64 of at least 8");

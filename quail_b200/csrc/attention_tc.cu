@@ -158,7 +158,9 @@ __device__ __forceinline__ uint64_t v_desc(uint32_t v_base, int kk) {
     return sw128_mn_desc(v_base + (uint32_t)(kk * 16 * 128), KV_HALF, 1024);
 }
 
-template <bool UNIFIED>
+// UE8M0: the output's per-head scales are powers of two (the reference's
+// use_ue8m0 mode of merge_attn_quant and the unified path's quant).
+template <bool UNIFIED, bool UE8M0>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                     const __grid_constant__ CUtensorMap map_k,
@@ -873,9 +875,10 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         }
                         const int row = row0 + qi;
                         const int h = h0 + 2 * mt + (i >> 6);
-                        const float sc = group_scale(amax);
+                        const float sc = UE8M0 ? ue8m0_scale(amax) : group_scale(amax);
                         const GroupDivider dv(sc);
                         const bool big = !(amax < 0x1p+100f);  // the quotient range bound
+                        const float inv = ue8m0_inverse(sc);
                         uint8_t* out = q_out + ((int64_t)(row < seg_end ? row : row0) * n_q + h) * D;
 #pragma unroll 1
                         for (int c0 = 0; c0 < D; c0 += 32) {
@@ -890,12 +893,18 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                                 yv[4 * u + 3] = v4.w;
                             }
                             float qv[32];
-                            bool rare = big;
+                            bool rare = UE8M0 ? false : big;
 #pragma unroll
                             for (int j = 0; j < 16; ++j) {
                                 qv[2 * j] = __uint_as_float(yv[j] << 16);
                                 qv[2 * j + 1] = __uint_as_float(yv[j] & 0xFFFF0000u);
-                                dv.quant2_sat(qv[2 * j], qv[2 * j + 1], rare);
+                                if (UE8M0) {  // y * 2^-e, exact
+                                    f2unpack(f2mul(f2pack(qv[2 * j], qv[2 * j + 1]),
+                                                   f2pack(inv, inv)),
+                                             qv[2 * j], qv[2 * j + 1]);
+                                } else {
+                                    dv.quant2_sat(qv[2 * j], qv[2 * j + 1], rare);
+                                }
                             }
                             if (rare) {  // a zero, tiny or non-finite value: the exact path
 #pragma unroll
@@ -1017,7 +1026,7 @@ int launch_attention_tc(bool unified, const char* who, const void* q, const void
                         int64_t table_width, const int32_t* source, const void* k_pool,
                         const void* v_pool, int64_t n_pages, int page_tokens,
                         float softmax_scale, void* q_out, float* scale_out, int64_t scale_ld,
-                        void* stream) {
+                        bool ue8m0, void* stream) {
     using namespace attn_tc;
     const int group = n_q / n_kv;
     if (group % 2 != 0) return -1;
@@ -1053,9 +1062,10 @@ int launch_attention_tc(bool unified, const char* who, const void* q, const void
         mkp = mk;
         mvp = mv;
     }
-    auto kernel = unified ? attention_tc_kernel<true> : attention_tc_kernel<false>;
-    static std::atomic<bool> attr[2][MAX_DEVICES];
-    if (!set_smem_once(attr[unified], kernel, (int)SMEM_BYTES)) return launch_status(who);
+    auto kernel = unified ? (ue8m0 ? attention_tc_kernel<true, true> : attention_tc_kernel<true, false>)
+                          : (ue8m0 ? attention_tc_kernel<false, true> : attention_tc_kernel<false, false>);
+    static std::atomic<bool> attr[2][2][MAX_DEVICES];
+    if (!set_smem_once(attr[unified][ue8m0], kernel, (int)SMEM_BYTES)) return launch_status(who);
     // persistent: one block per SM walks the items (query tile x head group,
     // head groups of a tile adjacent so they share K/V in L2)
     const int64_t items = n_tiles * (int64_t)(n_kv * (group / hp));

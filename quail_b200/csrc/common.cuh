@@ -48,6 +48,7 @@ enum : uint32_t {
     STATUS_ATTN_CORRECTION = 1u << 7,
     STATUS_BAD_TOKEN = 1u << 8,     // a token id outside [0, vocab)
     STATUS_BAD_INDEX = 1u << 9,     // a page, row or segment index out of range
+    STATUS_BAD_SCALE = 1u << 10,    // a UE8M0-mode scale that is not a power of two
 };
 
 inline int invalid(const char* what) {
@@ -101,6 +102,26 @@ __device__ __forceinline__ float group_scale(float amax) {
     return a < INFINITY ? __fmaf_rn(e, r, q0) : q0;  // inf: e would be NaN
 }
 
+// The UE8M0 mode of the same quantisers (use_ue8m0: scale =
+// exp2(ceil(log2(max(amax, 1e-10) / 448)))): the least power of two >= the
+// fp32 scale above, taken exactly from its bits. q = y / scale is then the
+// exact product y * 2^-e, rounded once by the e4m3 conversion.
+__device__ __forceinline__ float ue8m0_scale(float amax) {
+    const float s = group_scale(amax);
+    const uint32_t b = __float_as_uint(s);
+    if ((b & 0x7FFFFFu) == 0 || b >= 0x7F800000u) return s;  // a power of two, inf or NaN
+    return __uint_as_float((b & 0x7F800000u) + 0x800000u);
+}
+
+// 1 / s for a UE8M0 scale s = 2^k (k in [-43, 127]; 0 for an infinite s,
+// NaN for NaN), exactly
+__device__ __forceinline__ float ue8m0_inverse(float s) {
+    const uint32_t b = __float_as_uint(s);
+    if (b >= 0x7F800000u) return b == 0x7F800000u ? 0.0f : s;
+    if (b >= 0x7F000000u) return __uint_as_float(0x00400000u >> ((b >> 23) - 254u));  // 2^-127
+    return __uint_as_float(0x7F000000u - b);
+}
+
 // y / scale for many y of one group: the correctly rounded quotient from
 // one reciprocal per group by Markstein's correction (P. Markstein, IBM J.
 // Res. Dev. 34(1), 1990): r = RN(1/s), q0 = RN(y r), e = y - s q0 (exact by
@@ -138,6 +159,12 @@ struct GroupDivider {
     // values with quant2.
     __device__ __forceinline__ void quant2_sat(float& a, float& b, bool& rare) const;
 };
+
+// e4m3 byte -> its value (exact through half precision)
+__device__ __forceinline__ float fp8_to_float(uint8_t c) {
+    const __half_raw h = __nv_cvt_fp8_to_halfraw(c, __NV_E4M3);
+    return __half2float(__half(h));
+}
 
 // two floats -> two e4m3 bytes (low byte = first value)
 __device__ __forceinline__ uint16_t fp8x2(float a, float b) {

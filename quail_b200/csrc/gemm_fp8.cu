@@ -61,15 +61,26 @@ constexpr int SCALE_SLOTS = 8;
 // stores (one 32 x 64 box per epilogue warp) instead of per-thread row
 // stores, so the epilogue returns to the next tile at once.
 template <int BN, int NST = MAX_STAGES, bool TSTORE = false, bool SILU = false,
-          bool ROPE = false>
+          bool ROPE = false, bool MX = false>
 struct Cfg {
     static constexpr int STAGES = NST;
     static_assert(NST >= 2 && NST <= MAX_STAGES, "stages");
+    static_assert(!MX || BN == 256, "UE8M0 tiles are 256 wide");
     static constexpr int A_BYTES = BM * BK;
     static constexpr int B_BYTES = BN * BK;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int NBUF = 512 / BN;       // accumulator buffers in TMEM
-    static constexpr int TMEM_COLS = NBUF * BN;  // all 512 columns
+    // accumulator buffers in TMEM: 512 / BN K-block partials; MX one
+    // whole-K accumulator in columns 0-255 and the stages' scale factors
+    // from column TM_SF (12 columns a stage: SFA 4, SFB 8)
+    static constexpr int NBUF = MX ? 1 : 512 / BN;
+    static constexpr int TMEM_COLS = 512;
+    static constexpr int TM_SF = 256;
+    static_assert(!MX || TM_SF + 12 * NST <= TMEM_COLS, "scale-factor columns");
+    // MX: raw fp32 scales land by cp.async RAW_SLOTS - 1 K blocks ahead of
+    // their conversion into the SF ring (tcgen05.cp source layout)
+    static constexpr int RAW_SLOTS = MX ? (ROPE ? 4 : 8) : SCALE_SLOTS;
+    static constexpr int SF_SLOTS = MX ? 4 : 1;  // (1: keeps the MX-only code well formed)
+    static constexpr int SF_BYTES = 1536;  // SFA 32 x 16 B, SFB 2 x 32 x 16 B
     static constexpr int SLICE = BN / 4;      // columns per epilogue warp
     static_assert(!TSTORE || SLICE == 64, "TMA-store staging rows are 128 bytes");
     // TSTORE: one 32 x 64 bf16 staging box per epilogue warp; ROPE: the same
@@ -82,10 +93,11 @@ struct Cfg {
     static constexpr int SCALE_OFF = STAGES * STAGE_BYTES + OUT_BYTES;
     static_assert(!SILU || (BN == 256 && !TSTORE), "SILU tiles are 128 gate + 128 up columns");
     static_assert(!ROPE || (BN == 256 && !TSTORE && !SILU), "ROPE tiles are two heads");
+    static constexpr int SF_OFF = SCALE_OFF + RAW_SLOTS * 528;
     // SILU: per-row group max partials, [2 tile parities][4 slices][BM rows];
     // ROPE: the q and k norm weights (2 x 128 bf16), then each epilogue
     // warp's 32 rows of (position, KV destination)
-    static constexpr int RED_OFF = SCALE_OFF + SCALE_SLOTS * 528;
+    static constexpr int RED_OFF = SF_OFF + (MX ? SF_SLOTS * SF_BYTES : 0);
     static constexpr int RED_BYTES = SILU ? 2 * 4 * BM * 4 : ROPE ? 512 + EPI_WARPS * 32 * 16 : 0;
     static constexpr int BAR_OFF = RED_OFF + RED_BYTES;
     static constexpr int BAR_BYTES = 512;
@@ -93,6 +105,11 @@ struct Cfg {
     // instruction descriptor: D f32, A/B e4m3, both K-major, N, M=128
     static constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) |
                                       ((uint32_t)(BM >> 4) << 24);
+    // block-scaled (kind::mxf8f6f4): A/B e4m3, both K-major, dense K=32,
+    // N, UE8M0 scale factors (bit 23), M=128, scale-factor ids 0
+    static constexpr uint32_t IDESC_MX = ((uint32_t)(BN >> 3) << 17) | (1u << 23) |
+                                         ((uint32_t)(BM >> 4) << 24);
+    static_assert(SMEM <= 232448, "shared memory per block");
 };
 
 // one K block's scales: a[r] for tile row r (0 past the last row), w[j] for
@@ -118,6 +135,9 @@ struct Barriers {
     // ROPE: per warp pair (the two column halves of a head's rows): both
     // have read each other's partials
     uint64_t pair[8];
+    // MX: a K block's scale factors are in the SF ring / have been copied
+    uint64_t sf_full[4];
+    uint64_t sf_empty[4];
     uint32_t tmem_base;
     int abort;
 };
@@ -155,6 +175,29 @@ __device__ __forceinline__ void mma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t
         : "memory");
 }
 
+// D (+)= sum_k a[m,k] w[n,k] 2^(sfa[m] - 127) 2^(sfb[n] - 127) over K=32:
+// the block-scaled MMA with UE8M0 scale factors read from TMEM (sfa: 4
+// columns for the 128 rows, sfb: 8 columns for the 256 columns)
+__device__ __forceinline__ void mma_mx(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t sfa, uint32_t sfb,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], "
+        "p;\n\t}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+        : "memory");
+}
+
+// The UE8M0 byte of a power-of-two fp32 scale (its biased exponent; 0 for
+// a zero scale, which only rows past M carry). bad: not a power of two.
+__device__ __forceinline__ uint32_t ue8m0_byte(float s, bool& bad) {
+    const uint32_t b = __float_as_uint(s);
+    bad |= b != 0u && ((b & 0x807FFFFFu) != 0u || (b >> 23) == 255u);
+    return (b >> 23) & 0xFFu;
+}
+
 // acc[0..1] = fma(v[0..1], s, acc[0..1]): two IEEE fp32 FMAs in one
 // instruction (fma.rn.f32x2), each rounded exactly as fmaf would.
 __device__ __forceinline__ void fma2(float* acc, const uint32_t* v, float s) {
@@ -171,8 +214,11 @@ __device__ __forceinline__ void fma2(float* acc, const uint32_t* v, float s) {
 // q_scale[j * q_scale_ld + row]).
 // map_c is read only when TSTORE (bf16 out, box 64 x 32, 128-byte swizzle)
 // or SILU (fp8 out, box 32 x 32, 32-byte swizzle).
+// MX (the UE8M0 mode): power-of-two scales applied by the block-scaled MMA,
+// one accumulator over the whole K, and UE8M0 quantisation in the SILU
+// epilogue.
 template <int BN, typename OutT = bf16, int NST = MAX_STAGES, bool TSTORE = false,
-          bool SILU = false, bool ROPE = false>
+          bool SILU = false, bool ROPE = false, bool MX = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                    const __grid_constant__ CUtensorMap map_b,
@@ -180,7 +226,7 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                    int64_t a_scale_ld, const float* __restrict__ w_scale, OutT* __restrict__ out,
                    float* __restrict__ q_scale, int64_t q_scale_ld, int M, int N, int K,
                    uint32_t* status, const __grid_constant__ RopeArgs rope) {
-    using C = Cfg<BN, NST, TSTORE, SILU, ROPE>;
+    using C = Cfg<BN, NST, TSTORE, SILU, ROPE, MX>;
     constexpr int STAGES = C::STAGES;
     static_assert(!TSTORE || sizeof(OutT) == 2, "TMA stores write bf16");
     static_assert(!SILU || sizeof(OutT) == 1, "SILU writes fp8");
@@ -220,6 +266,10 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
             mbar_init(&bars->quad[1][q], 4);
         }
         for (int q = 0; q < 8; ++q) mbar_init(&bars->pair[q], 2);
+        for (int q = 0; q < 4; ++q) {
+            mbar_init(&bars->sf_full[q], 1);
+            mbar_init(&bars->sf_empty[q], 1);
+        }
         bars->abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -288,15 +338,52 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            int it = 0, acc_it = 0;
+            int it = 0, acc_it = 0, tcount = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++tcount) {
                 for (int kb = 0; kb < n_kb; ++kb, ++it, ++acc_it) {
                     const int s = it % STAGES;
                     if (!mbar_wait(&bars->full[s], (uint32_t)(it / STAGES) & 1u, abort_flag,
                                    status, STATUS_GEMM_MMA)) {
                         ok = false;
                         break;
+                    }
+                    if constexpr (MX) {
+                        // the tile's accumulator is free once the epilogue
+                        // has loaded the previous tile
+                        if (kb == 0 && !mbar_wait(&bars->tmem_empty[0],
+                                                  ((uint32_t)tcount & 1u) ^ 1u, abort_flag, status,
+                                                  STATUS_GEMM_MMA)) {
+                            ok = false;
+                            break;
+                        }
+                        const int slot = it % C::SF_SLOTS;
+                        if (!mbar_wait(&bars->sf_full[slot], (uint32_t)(it / C::SF_SLOTS) & 1u,
+                                       abort_flag, status, STATUS_GEMM_MMA)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        // stage s's scale-factor columns: the MMAs of the K
+                        // block that used them last completed before this
+                        // stage's operands could be loaded again
+                        const uint32_t sfa = tmem_base + (uint32_t)(C::TM_SF + 12 * s);
+                        const uint32_t sfb = sfa + 4u;
+                        const uint32_t src = smem_u32(smem + C::SF_OFF + slot * C::SF_BYTES);
+                        tmem_cp_32x128b_x4(sfa, rows16_desc(src));
+                        tmem_cp_32x128b_x4(sfb, rows16_desc(src + 512));
+                        tmem_cp_32x128b_x4(sfb + 4u, rows16_desc(src + 1024));
+                        const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+                        const uint64_t adesc = sw128_desc(sa);
+                        const uint64_t bdesc = sw128_desc(sa + C::A_BYTES);
+#pragma unroll
+                        for (int k = 0; k < BK / 32; ++k)
+                            mma_mx(tmem_base, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k),
+                                   C::IDESC_MX, sfa, sfb, (kb > 0 || k > 0) ? 1u : 0u);
+                        mma_commit(&bars->empty[s]);
+                        mma_commit(&bars->sf_empty[slot]);
+                        if (kb == n_kb - 1) mma_commit(&bars->tmem_full[0]);
+                        continue;
                     }
                     const int buf = acc_it % C::NBUF;
                     const uint32_t use = (uint32_t)(acc_it / C::NBUF);
@@ -322,6 +409,72 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
             mma_commit(&bars->drain);
             mbar_drain(&bars->drain, 0, status, STATUS_GEMM_DRAIN);
         }
+    } else if (warp == 2 && MX) {
+        // ---------------- scale-factor loader (UE8M0) ----------------
+        // A K block's 128 activation scales and the tile's two weight block
+        // scales land by cp.async in the raw ring; LAG K blocks later their
+        // exponent bytes are written in the layout tcgen05.cp 32x128b takes
+        // (row r: the words of tile rows r, 32 + r, 64 + r, 96 + r; for the
+        // weights columns likewise, one block scale in each 128) and handed
+        // to the MMA thread.
+        constexpr int LAG = C::RAW_SLOTS - 1;
+        constexpr int NB = BN / 128;
+        auto sf_convert = [&](int j) -> bool {
+            const int slot = j % C::SF_SLOTS;
+            if (!mbar_wait(&bars->sf_empty[slot], ((uint32_t)(j / C::SF_SLOTS) & 1u) ^ 1u,
+                           abort_flag, status, STATUS_GEMM_EPILOGUE))
+                return false;
+            __syncwarp();  // every lane's copies of block j have landed
+            const ScaleSlot* raw = scales + j % C::RAW_SLOTS;
+            bool bad = false;
+            uint4 a4;
+            a4.x = ue8m0_byte(raw->a[lane], bad);
+            a4.y = ue8m0_byte(raw->a[32 + lane], bad);
+            a4.z = ue8m0_byte(raw->a[64 + lane], bad);
+            a4.w = ue8m0_byte(raw->a[96 + lane], bad);
+            const uint32_t w0 = ue8m0_byte(raw->w[0], bad), w1 = ue8m0_byte(raw->w[1], bad);
+            uint8_t* sf = smem + C::SF_OFF + slot * C::SF_BYTES;
+            *reinterpret_cast<uint4*>(sf + lane * 16) = a4;
+            *reinterpret_cast<uint4*>(sf + 512 + lane * 16) = make_uint4(w0, w0, w0, w0);
+            *reinterpret_cast<uint4*>(sf + 1024 + lane * 16) = make_uint4(w1, w1, w1, w1);
+            if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(status, STATUS_BAD_SCALE);
+            // the copies read shared memory through the async proxy
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->sf_full[slot]);
+            return true;
+        };
+        int it = 0, done = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+            const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
+            for (int kb = 0; kb < n_kb; ++kb) {
+                ScaleSlot* sl = scales + it % C::RAW_SLOTS;
+                const float* col = a_scale + (int64_t)kb * a_scale_ld;
+#pragma unroll
+                for (int j = 0; j < BM / 32; ++j) {
+                    const int r = j * 32 + lane;
+                    const bool valid = m0 + r < M;
+                    cp_async4(smem_u32(&sl->a[r]), valid ? col + m0 + r : a_scale,
+                              valid ? 4u : 0u);
+                }
+                if (lane < NB) {
+                    const int wb = SILU ? (tile % num_n) + lane * (N / 256) : n0 / 128 + lane;
+                    cp_async4(smem_u32(&sl->w[lane]), w_scale + (int64_t)wb * n_kb + kb, 4u);
+                }
+                asm volatile("cp.async.commit_group;" ::: "memory");
+                ++it;
+                if (it > LAG) {
+                    asm volatile("cp.async.wait_group %0;" ::"n"(LAG) : "memory");
+                    if (!sf_convert(done++)) {
+                        ok = false;
+                        break;
+                    }
+                }
+            }
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        while (ok && done < it) ok = sf_convert(done++);
     } else if (warp == 2) {
         // ---------------- scale loader ----------------
         int it = 0;
@@ -390,9 +543,34 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                 }
             }
             float acc[C::SLICE];
+            if constexpr (MX) {
+                // the whole-K accumulator: load this warp's columns, hand
+                // the buffer back to the MMA thread for the next tile
+                if (!mbar_wait(&bars->tmem_full[0], (uint32_t)tcount & 1u, abort_flag, status,
+                               STATUS_GEMM_EPILOGUE)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t taddr = tmem_base + lane_addr + (uint32_t)col0;
 #pragma unroll
-            for (int j = 0; j < C::SLICE; ++j) acc[j] = 0.0f;
-            for (int kb = 0; kb < n_kb; ++kb, ++acc_it) {
+                for (int c = 0; c < C::SLICE; c += 32) {
+                    uint32_t v[32];
+                    const uint32_t cc = (SILU && c > 0) ? 128u : (ROPE && c > 0) ? 64u : (uint32_t)c;
+                    tmem_ld16_nowait(taddr + cc, v);
+                    tmem_ld16_nowait(taddr + cc + 16u, v + 16);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) acc[c + j] = __uint_as_float(v[j]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->tmem_empty[0]);
+            }
+#pragma unroll
+            for (int j = 0; j < C::SLICE; ++j)
+                if (!MX) acc[j] = 0.0f;
+            for (int kb = 0; kb < (MX ? 0 : n_kb); ++kb, ++acc_it) {
                 const int slot = acc_it % SCALE_SLOTS;
                 if (!mbar_wait(&bars->scale_full[slot], (uint32_t)(acc_it / SCALE_SLOTS) & 1u,
                                abort_flag, status, STATUS_GEMM_EPILOGUE)) {
@@ -471,12 +649,24 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                 }
                 amax = fmaxf(fmaxf(red[row_in_tile], red[BM + row_in_tile]),
                              fmaxf(red[2 * BM + row_in_tile], red[3 * BM + row_in_tile]));
-                const float scale = group_scale(amax);
+                const float scale = MX ? ue8m0_scale(amax) : group_scale(amax);
                 const GroupDivider dv(scale);
                 const bool big = !(amax < 0x1p+100f);
                 uint32_t pk[8];
+                if constexpr (MX) {
+                    // q = y * 2^-e exactly, rounded once by the conversion
+                    const float inv = ue8m0_inverse(scale);
+                    const uint64_t inv2 = f2pack(inv, inv);
 #pragma unroll
-                for (int i = 0; i < 32; i += 4) {
+                    for (int i = 0; i < 32; i += 4) {
+                        float a, b, c, d;
+                        f2unpack(f2mul(f2pack(acc[i], acc[i + 1]), inv2), a, b);
+                        f2unpack(f2mul(f2pack(acc[i + 2], acc[i + 3]), inv2), c, d);
+                        pk[i >> 2] = (uint32_t)fp8x2(a, b) | ((uint32_t)fp8x2(c, d) << 16);
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < (MX ? 0 : 32); i += 4) {
                     float a = acc[i], b = acc[i + 1], c = acc[i + 2], d = acc[i + 3];
                     bool rare = big;
                     dv.quant2_sat(a, b, rare);
@@ -866,11 +1056,11 @@ int make_out_map(CUtensorMap* map, void* base, int64_t rows, int64_t n) {
 
 // SILU: n = 2 * inter weight rows, out fp8 [m, inter], q_scale [inter / 128, q_scale_ld]
 template <int BN, int NST = MAX_STAGES, bool TSTORE = false, bool SILU = false,
-          bool ROPE = false>
+          bool ROPE = false, bool MX = false>
 int launch(const void* a, const float* a_scale, int64_t a_scale_ld, const void* w,
            const float* w_scale, void* out, int64_t m, int64_t n, int64_t k, cudaStream_t stream,
            float* q_scale = nullptr, int64_t q_scale_ld = 0, const RopeArgs* rope = nullptr) {
-    using C = Cfg<BN, NST, TSTORE, SILU, ROPE>;
+    using C = Cfg<BN, NST, TSTORE, SILU, ROPE, MX>;
     using OutT = typename std::conditional<SILU, uint8_t, bf16>::type;
     CUtensorMap map_a, map_b, map_c;
     memset(&map_c, 0, sizeof(map_c));
@@ -886,7 +1076,7 @@ int launch(const void* a, const float* a_scale, int64_t a_scale_ld, const void* 
         st = make_fp8_box32_map(&map_c, out, m, n / 2);
         if (st) return st;
     }
-    auto kernel = gemm_fp8_bs_kernel<BN, OutT, NST, TSTORE, SILU, ROPE>;
+    auto kernel = gemm_fp8_bs_kernel<BN, OutT, NST, TSTORE, SILU, ROPE, MX>;
     static std::atomic<bool> attr[MAX_DEVICES];
     if (!set_smem_once(attr, kernel, C::SMEM))
         return launch_status("qb_gemm_fp8_bs: smem attribute");
@@ -909,10 +1099,11 @@ int launch(const void* a, const float* a_scale, int64_t a_scale_ld, const void* 
 
 extern "C" int qb_gemm_fp8_bs(const void* a, const float* a_scale, int64_t a_scale_ld,
                               const void* w, const float* w_scale, void* out, int64_t m, int64_t n,
-                              int64_t k, void* stream) {
+                              int64_t k, int ue8m0, void* stream) {
     if (m < 0 || n <= 0 || k <= 0) return invalid("qb_gemm_fp8_bs: bad sizes");
     if (k % BK != 0) return invalid("qb_gemm_fp8_bs: k must be a multiple of 128");
     if (n % 128 != 0) return invalid("qb_gemm_fp8_bs: n must be a multiple of 128");
+    if (ue8m0 && n % 256 != 0) return invalid("qb_gemm_fp8_bs: ue8m0 needs n a multiple of 256");
     if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL)
         return invalid("qb_gemm_fp8_bs: sizes exceed int32");
     if (a_scale_ld < m) return invalid("qb_gemm_fp8_bs: a_scale_ld < m");
@@ -921,6 +1112,10 @@ extern "C" int qb_gemm_fp8_bs(const void* a, const float* a_scale, int64_t a_sca
     if (!a_scale || !w_scale) return invalid("qb_gemm_fp8_bs: NULL scales");
     if (m == 0) return QB_OK;
     cudaStream_t s = (cudaStream_t)stream;
+    // UE8M0: the block-scaled MMA applies the power-of-two scales
+    if (ue8m0)
+        return launch<256, 3, true, false, false, true>(a, a_scale, a_scale_ld, w, w_scale, out, m,
+                                                        n, k, s);
     // The TMA-store epilogue (3 stages, the tile staged in shared memory)
     // beats 4 stages with per-thread row stores on every 4B shape (measured on
     // B200: qkv 2,144 vs 1,815, o 2,200 vs 1,989, gate_up 1,973 vs 1,694,
@@ -933,7 +1128,7 @@ extern "C" int qb_gemm_fp8_bs(const void* a, const float* a_scale, int64_t a_sca
 extern "C" int qb_gemm_fp8_silu_quant(const void* a, const float* a_scale, int64_t a_scale_ld,
                                       const void* w, const float* w_scale, void* q_out,
                                       float* scale_out, int64_t scale_ld, int64_t m,
-                                      int64_t inter, int64_t k, void* stream) {
+                                      int64_t inter, int64_t k, int ue8m0, void* stream) {
     if (m < 0 || inter <= 0 || k <= 0) return invalid("qb_gemm_fp8_silu_quant: bad sizes");
     if (k % BK != 0) return invalid("qb_gemm_fp8_silu_quant: k must be a multiple of 128");
     if (inter % 128 != 0)
@@ -947,6 +1142,10 @@ extern "C" int qb_gemm_fp8_silu_quant(const void* a, const float* a_scale, int64
     if (!a_scale || !w_scale || !scale_out)
         return invalid("qb_gemm_fp8_silu_quant: NULL scales");
     if (m == 0) return QB_OK;
+    if (ue8m0)
+        return launch<256, 4, false, true, false, true>(a, a_scale, a_scale_ld, w, w_scale, q_out,
+                                                        m, 2 * inter, k, (cudaStream_t)stream,
+                                                        scale_out, scale_ld);
     return launch<256, 4, false, true>(a, a_scale, a_scale_ld, w, w_scale, q_out, m, 2 * inter,
                                        k, (cudaStream_t)stream, scale_out, scale_ld);
 }
@@ -956,7 +1155,7 @@ extern "C" int qb_gemm_fp8_qknorm_rope(
     int64_t m, int64_t k, const int64_t* positions, const void* cos_sin, int64_t max_pos,
     const void* q_w, const void* k_w, float eps, int n_q, int n_kv, int head_dim, void* q_out,
     void* k_out, void* v_out, const int64_t* row_dst, void* k_pool, void* v_pool,
-    int64_t pool_rows, void* stream) {
+    int64_t pool_rows, int ue8m0, void* stream) {
     if (head_dim != 128) return invalid("qb_gemm_fp8_qknorm_rope: head_dim must be 128");
     if (m < 0 || k <= 0 || n_q <= 0 || n_kv <= 0 || n_q % n_kv != 0)
         return invalid("qb_gemm_fp8_qknorm_rope: bad sizes or head counts");
@@ -1004,6 +1203,10 @@ extern "C" int qb_gemm_fp8_qknorm_rope(
     r.k_pool = (bf16*)k_pool;
     r.v_pool = (bf16*)v_pool;
     r.pool_rows = pool_rows;
+    if (ue8m0)
+        return launch<256, 3, false, false, true, true>(a, a_scale, a_scale_ld, w, w_scale, nullptr,
+                                                        m, n, k, (cudaStream_t)stream, nullptr, 0,
+                                                        &r);
     return launch<256, 3, false, false, true>(a, a_scale, a_scale_ld, w, w_scale, nullptr, m, n,
                                               k, (cudaStream_t)stream, nullptr, 0, &r);
 }

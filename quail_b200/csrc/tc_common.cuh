@@ -137,6 +137,25 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
+// Shared-memory matrix descriptor without swizzle for rows of 16 bytes:
+// 8-row x 16-byte core matrices, consecutive 8-row groups 128 bytes apart
+// (SBO; LBO the same, with one 16-byte column it strides nothing), version
+// 1, base offset 0. Row r of the matrix sits at saddr + 16 r: the source of
+// a tcgen05.cp 32x128b copy.
+__device__ __forceinline__ uint64_t rows16_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128 >> 4) << 16) |
+           ((uint64_t)(128 >> 4) << 32) | ((uint64_t)1 << 46);
+}
+
+// 32 rows x 128 bits of shared memory (rows16_desc) into TMEM columns
+// taddr .. taddr + 3 of lanes 0-31, copied to the other three lane quarters
+// as well (warpx4). Asynchronous; ordered before a later tcgen05.mma of the
+// same thread and tracked by its tcgen05.commit.
+__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+                 : "memory");
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile(
         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(

@@ -32,12 +32,18 @@ class Engine:
         torch: the torch module.
         arena: KVArena the attention reads and the KV append writes.
         cfg: ModelConfig of the loaded weights.
+        ue8m0: the reference's UE8M0 scale mode (Engine.use_ue8m0, from
+            vLLM's is_deep_gemm_e8m0_used; quail/backends/quail/executor/
+            attention.py:115): power-of-two activation scales from every
+            quantiser, and GEMMs on the block-scaled MMA. The weights'
+            scales must then be powers of two (model.requant_ue8m0).
     """
 
-    def __init__(self, torch, arena, cfg):
+    def __init__(self, torch, arena, cfg, ue8m0=False):
         self.torch = torch
         self.arena = arena
         self.cfg = cfg
+        self.use_ue8m0 = bool(ue8m0)
         self.num_q_heads = cfg.n_q
         self.num_kv_heads = cfg.n_kv
         self.head_dim = cfg.head_dim
@@ -67,7 +73,7 @@ class Engine:
         out = self._quant_buffers(rows, h)
         nat.call("qb_embed_rmsnorm_quant", nat.ptr(ids), rows, nat.ptr(embed), embed.shape[0],
                  h, nat.ptr(norm_w), self.cfg.eps, nat.ptr(residual), nat.ptr(out.q),
-                 nat.ptr(out.scale), out.ld, self._stream())
+                 nat.ptr(out.scale), out.ld, int(self.use_ue8m0), self._stream())
         return residual, out
 
     def norm_quant(self, hidden, norm_w, residual):
@@ -76,7 +82,7 @@ class Engine:
         out = self._quant_buffers(rows, h)
         nat.call("qb_add_rmsnorm_quant", nat.ptr(hidden), nat.ptr(residual), nat.ptr(norm_w),
                  self.cfg.eps, rows, h, nat.ptr(out.q), nat.ptr(out.scale), out.ld,
-                 self._stream())
+                 int(self.use_ue8m0), self._stream())
         return out
 
     def activation_quant(self, gate_up):
@@ -84,7 +90,7 @@ class Engine:
         rows, two_i = gate_up.shape
         out = self._quant_buffers(rows, two_i // 2)
         nat.call("qb_silu_mul_quant", nat.ptr(gate_up), rows, two_i // 2, nat.ptr(out.q),
-                 nat.ptr(out.scale), out.ld, self._stream())
+                 nat.ptr(out.scale), out.ld, int(self.use_ue8m0), self._stream())
         return out
 
     # ---- GEMM ------------------------------------------------------------------
@@ -99,7 +105,8 @@ class Engine:
             start, end = t.cuda.Event(enable_timing=True), t.cuda.Event(enable_timing=True)
             start.record()
         nat.call("qb_gemm_fp8_bs", nat.ptr(x.q), nat.ptr(x.scale), x.ld, nat.ptr(weight),
-                 nat.ptr(weight_scale), nat.ptr(out), m, n, k, self._stream())
+                 nat.ptr(weight_scale), nat.ptr(out), m, n, k, int(self.use_ue8m0),
+                 self._stream())
         if timed:
             end.record()
             # algorithmic bytes: A and W once, C once, both scale arrays
@@ -120,7 +127,7 @@ class Engine:
             start.record()
         nat.call("qb_gemm_fp8_silu_quant", nat.ptr(x.q), nat.ptr(x.scale), x.ld,
                  nat.ptr(weight), nat.ptr(weight_scale), nat.ptr(out.q), nat.ptr(out.scale),
-                 out.ld, m, inter, k, self._stream())
+                 out.ld, m, inter, k, int(self.use_ue8m0), self._stream())
         if timed:
             end.record()
             n = 2 * inter
@@ -179,7 +186,7 @@ class Engine:
                  nat.ptr(weight_scale), m, k_dim, nat.ptr(positions), nat.ptr(cos_sin),
                  cos_sin.shape[0], nat.ptr(q_w), nat.ptr(k_w), cfg.eps, cfg.n_q, cfg.n_kv,
                  cfg.head_dim, nat.ptr(q), nat.ptr(k), nat.ptr(v), nat.ptr(row_dst), nat.ptr(kp),
-                 nat.ptr(vp), self.arena.pool_rows, self._stream())
+                 nat.ptr(vp), self.arena.pool_rows, int(self.use_ue8m0), self._stream())
         if timed:
             end.record()
             n = weight.shape[0]
@@ -217,7 +224,8 @@ class Engine:
                  cfg.n_kv, cfg.head_dim, nat.ptr(meta["cu_a"]), meta["cu_a"].shape[0] - 1,
                  nat.ptr(tiles), tiles.shape[0], *args, nat.ptr(kp), nat.ptr(vp),
                  self.arena.n_pages, self.arena.page_tokens, self.softmax_scale,
-                 nat.ptr(out.q), nat.ptr(out.scale), out.ld, self._stream())
+                 nat.ptr(out.q), nat.ptr(out.scale), out.ld, int(self.use_ue8m0),
+                 self._stream())
         meta["layer"] += 1
         return out
 
@@ -241,7 +249,8 @@ class Engine:
                  nat.ptr(u["cu_q"]), u["cu_q"].shape[0] - 1, nat.ptr(tiles), tiles.shape[0],
                  nat.ptr(u["used"]), nat.ptr(table), table.shape[1], nat.ptr(kp), nat.ptr(vp),
                  self.arena.n_pages, self.arena.page_tokens, self.softmax_scale,
-                 nat.ptr(out.q), nat.ptr(out.scale), out.ld, self._stream())
+                 nat.ptr(out.q), nat.ptr(out.scale), out.ld, int(self.use_ue8m0),
+                 self._stream())
         meta["layer"] += 1
         return out
 

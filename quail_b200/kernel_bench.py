@@ -34,6 +34,9 @@ from quail_b200 import _native as nat
 
 ROOT = Path(__file__).resolve().parent.parent
 
+# --ue8m0: the UE8M0 scale mode (power-of-two scales, block-scaled MMA)
+UE8M0 = 0
+
 
 def peaks():
     """(HBM GB/s, FP8 dense TFLOP/s, source) from MEASURED_PEAKS.json."""
@@ -59,15 +62,19 @@ def time_launches(torch, launch, warmup, iters):
     return start.elapsed_time(end) / max(iters, 1)
 
 
+def _pow2(torch, x):
+    return torch.exp2(torch.ceil(torch.log2(x))) if UE8M0 else x
+
+
 def fp8_rows(torch, rows, k):
     q = (torch.randn(rows, k, device="cuda") * 2).to(torch.float8_e4m3fn)
-    scale = torch.rand(k // 128, rows, device="cuda") * 0.01 + 0.001
+    scale = _pow2(torch, torch.rand(k // 128, rows, device="cuda") * 0.01 + 0.001)
     return q, scale
 
 
 def fp8_weight(torch, n, k):
     w = torch.randn(n, k, device="cuda").to(torch.float8_e4m3fn)
-    s = torch.rand(n // 128, k // 128, device="cuda") * 0.02 + 0.001
+    s = _pow2(torch, torch.rand(n // 128, k // 128, device="cuda") * 0.02 + 0.001)
     return w, s
 
 
@@ -78,7 +85,7 @@ def gemm_launcher(torch, m, n, k):
 
     def launch():
         nat.call("qb_gemm_fp8_bs", nat.ptr(a), nat.ptr(a_s), m, nat.ptr(w), nat.ptr(w_s),
-                 nat.ptr(out), m, n, k, nat.stream_handle(torch))
+                 nat.ptr(out), m, n, k, UE8M0, nat.stream_handle(torch))
     return launch
 
 
@@ -101,13 +108,14 @@ def op_gate_up(torch, args):
 
     def fused():
         nat.call("qb_gemm_fp8_silu_quant", nat.ptr(a), nat.ptr(a_s), m, nat.ptr(w),
-                 nat.ptr(w_s), nat.ptr(q), nat.ptr(s), m, m, inter, k, nat.stream_handle(torch))
+                 nat.ptr(w_s), nat.ptr(q), nat.ptr(s), m, m, inter, k, UE8M0,
+                 nat.stream_handle(torch))
 
     def unfused():
         nat.call("qb_gemm_fp8_bs", nat.ptr(a), nat.ptr(a_s), m, nat.ptr(w), nat.ptr(w_s),
-                 nat.ptr(gu), m, 2 * inter, k, nat.stream_handle(torch))
+                 nat.ptr(gu), m, 2 * inter, k, UE8M0, nat.stream_handle(torch))
         nat.call("qb_silu_mul_quant", nat.ptr(gu), m, inter, nat.ptr(q), nat.ptr(s), m,
-                 nat.stream_handle(torch))
+                 UE8M0, nat.stream_handle(torch))
     ms = time_launches(torch, fused, args.warmup, args.iters)
     ms_unfused = time_launches(torch, unfused, args.warmup, args.iters)
     flops = 2.0 * m * 2 * inter * k
@@ -137,11 +145,11 @@ def op_qkv_rope(torch, args):
         nat.call("qb_gemm_fp8_qknorm_rope", nat.ptr(a), nat.ptr(a_s), m, nat.ptr(w), nat.ptr(w_s),
                  m, k, nat.ptr(pos), nat.ptr(cos_sin), cos_sin.shape[0], nat.ptr(qw), nat.ptr(qw),
                  1e-6, cfg.n_q, cfg.n_kv, cfg.head_dim, nat.ptr(q), nat.ptr(kk), nat.ptr(v),
-                 nat.ptr(row_dst), nat.ptr(kp), nat.ptr(vp), m, st)
+                 nat.ptr(row_dst), nat.ptr(kp), nat.ptr(vp), m, UE8M0, st)
 
     def unfused():
         nat.call("qb_gemm_fp8_bs", nat.ptr(a), nat.ptr(a_s), m, nat.ptr(w), nat.ptr(w_s),
-                 nat.ptr(qkv), m, n, k, st)
+                 nat.ptr(qkv), m, n, k, UE8M0, st)
         nat.call("qb_qknorm_rope", nat.ptr(qkv), n, nat.ptr(pos), nat.ptr(cos_sin),
                  cos_sin.shape[0], nat.ptr(qw), nat.ptr(qw), 1e-6, m, cfg.n_q, cfg.n_kv,
                  cfg.head_dim, nat.ptr(q), nat.ptr(kk), nat.ptr(v), nat.ptr(row_dst), nat.ptr(kp),
@@ -178,7 +186,7 @@ def op_silu(torch, args):
 
     def launch():
         nat.call("qb_silu_mul_quant", nat.ptr(gate_up), rows, inter, nat.ptr(q), nat.ptr(s),
-                 rows, nat.stream_handle(torch))
+                 rows, UE8M0, nat.stream_handle(torch))
     ms = time_launches(torch, launch, args.warmup, args.iters)
     nbytes = rows * (4 * inter + inter + 4 * (inter // 128))
     return {"shape": [rows, inter], "ms": ms, "gbs": nbytes / ms / 1e6, "bound": "hbm",
@@ -195,7 +203,7 @@ def op_norm(torch, args):
 
     def launch():
         nat.call("qb_add_rmsnorm_quant", nat.ptr(hidden), nat.ptr(residual), nat.ptr(w), 1e-6,
-                 rows, h, nat.ptr(q), nat.ptr(s), rows, nat.stream_handle(torch))
+                 rows, h, nat.ptr(q), nat.ptr(s), rows, UE8M0, nat.stream_handle(torch))
     ms = time_launches(torch, launch, args.warmup, args.iters)
     nbytes = rows * (2 * h + 2 * h + 2 * h + h + 4 * (h // 128))
     return {"shape": [rows, h], "ms": ms, "gbs": nbytes / ms / 1e6, "bound": "hbm",
@@ -275,7 +283,7 @@ def op_attention(torch, args):
     q = torch.randn(rows, cfg.n_q * d, device="cuda").to(torch.bfloat16)
     k = torch.randn(rows, cfg.n_kv * d, device="cuda").to(torch.bfloat16)
     v = torch.randn(rows, cfg.n_kv * d, device="cuda").to(torch.bfloat16)
-    eng = Engine(torch, arena, cfg)
+    eng = Engine(torch, arena, cfg, ue8m0=UE8M0)
 
     def launch():
         meta["layer"] = 0
@@ -309,7 +317,11 @@ def main(argv=None):
     p.add_argument("--pages", type=int, default=16384)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--ue8m0", action="store_true",
+                   help="UE8M0 scale mode: power-of-two scales, block-scaled MMA")
     args = p.parse_args(argv)
+    global UE8M0
+    UE8M0 = int(args.ue8m0)
     import torch
     torch.manual_seed(0)
     result = globals()["op_" + args.op](torch, args)

@@ -135,6 +135,38 @@ def _torch():
     return torch
 
 
+#: the fp8 linears of a Layer: (weight attribute, block-scale attribute)
+LINEARS = (("qkv_w", "qkv_s"), ("o_w", "o_s"), ("gate_up_w", "gate_up_s"),
+           ("down_w", "down_s"))
+
+
+def scales_are_ue8m0(weights) -> bool:
+    """True when every block scale of every linear is a power of two."""
+    torch = _torch()
+    for layer in weights.layers:
+        for _, sn in LINEARS:
+            bits = getattr(layer, sn).contiguous().view(torch.int32)
+            if bool(((bits & 0x807FFFFF) != 0).any()):
+                return False
+    return True
+
+
+def requant_ue8m0(weights):
+    """Re-quantise every linear to power-of-two block scales in place (the
+    UE8M0 mode's load-time step: vLLM's requant_weight_ue8m0_inplace, here
+    qb_requant_weight_ue8m0 on the weights' GPU). Returns weights."""
+    from quail_b200 import _native as nat
+    torch = _torch()
+    for layer in weights.layers:
+        for wn, sn in LINEARS:
+            w, sc = getattr(layer, wn), getattr(layer, sn)
+            if not (w.is_contiguous() and sc.is_contiguous()):
+                raise ValueError(f"{wn}/{sn}: contiguous tensors needed")
+            nat.call("qb_requant_weight_ue8m0", nat.ptr(w), nat.ptr(sc), w.shape[0],
+                     w.shape[1], nat.stream_handle(torch))
+    return weights
+
+
 def rotary_cache(cfg: ModelConfig, device="cpu"):
     """vLLM's neox rotary cache: cos | sin of pos * theta^(-2i/d), cast to bf16.
 

@@ -40,12 +40,14 @@ class ModelPipeline:
 class Qwen3Pipeline(ModelPipeline):
     """Qwen3 FP8 forward passes on sm_100a kernels."""
 
-    def __init__(self, torch, weights, arena):
+    def __init__(self, torch, weights, arena, ue8m0=False):
         self.torch = torch
         self.weights = weights
         self.cfg = weights.config
         self.arena = arena
-        self.engine = Engine(torch, arena, self.cfg)
+        # ue8m0: the UE8M0 scale mode (Engine.use_ue8m0); the weights' block
+        # scales must be powers of two (model.requant_ue8m0)
+        self.engine = Engine(torch, arena, self.cfg, ue8m0=ue8m0)
         self.tree_attention = True
         self.max_chunk_tokens = self.cfg.max_chunk_tokens
         self.layers = weights.layers
@@ -116,6 +118,6 @@ class Qwen3Pipeline(ModelPipeline):
         return eng.final_norm(hidden, residual, chunk.final_indices, w.final_norm)
 
 
-def build_pipeline(torch, weights, arena):
+def build_pipeline(torch, weights, arena, ue8m0=False):
     """The pipeline for weights.config (Quail's build_pipeline seam)."""
-    return Qwen3Pipeline(torch, weights, arena)
+    return Qwen3Pipeline(torch, weights, arena, ue8m0=ue8m0)

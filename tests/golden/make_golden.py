@@ -22,7 +22,11 @@ Two kinds of fixtures:
 - kernels.npz: seeded inputs and outputs of the reference's fused Triton
   kernels (add_rms_norm_quant, qk_norm_rope, silu_mul_quant,
   merge_attn_quant, kv_row_scatter; attention.py:293-642) run on CPU
-  tensors under TRITON_INTERPRET=1. The oracle must reproduce them.
+  tensors under TRITON_INTERPRET=1, the quantisers in both scale modes
+  (UE8M0=False and True). The oracle must reproduce them.
+- requant_ue8m0.npz: block-scaled fp8 weights and their re-quantisation to
+  power-of-two scales by vLLM's requant_weight_ue8m0_inplace (the installed
+  vllm package, on CPU tensors), the load-time step of the UE8M0 mode.
 
 The reference imports sqlglot at package import; only the SQL frontend
 uses it, so an empty stand-in module is installed for the import.
@@ -467,11 +471,18 @@ def make_kernel_vectors():
     r = torch.randn(n, h, generator=g).to(torch.bfloat16)
     w = (1 + 0.1 * torch.randn(h, generator=g)).to(torch.bfloat16)
     out.update(norm_x=x, norm_r_in=r.clone(), norm_w=w)
+    r8 = r.clone()
     q = torch.empty(n, h, dtype=torch.float8_e4m3fn)
     s = torch.empty(h // 128, n, dtype=torch.float32).t()
     k["norm"][(n,)](x, r, w, q, s, x.stride(0), r.stride(0), q.stride(0), s.stride(1),
                     s.stride(0), 1e-6, H=h, BLOCK=512, GROUP_C=128, NG=h // 128, UE8M0=False)
     out.update(norm_r_out=r, norm_q=q.view(torch.uint8), norm_s=s.t().contiguous())
+    # the same inputs in the UE8M0 scale mode
+    q = torch.empty(n, h, dtype=torch.float8_e4m3fn)
+    s = torch.empty(h // 128, n, dtype=torch.float32).t()
+    k["norm"][(n,)](x, r8, w, q, s, x.stride(0), r8.stride(0), q.stride(0), s.stride(1),
+                    s.stride(0), 1e-6, H=h, BLOCK=512, GROUP_C=128, NG=h // 128, UE8M0=True)
+    out.update(norm_q_ue8m0=q.view(torch.uint8), norm_s_ue8m0=s.t().contiguous())
 
     # qk_norm_rope: 4 q heads, 2 kv heads, head 128
     n, qh, kh, d = 5, 4, 2, 128
@@ -498,6 +509,11 @@ def make_kernel_vectors():
     k["silu"][(n, half // 512)](gu, q, s, gu.stride(0), q.stride(0), s.stride(1), s.stride(0),
                                 HALF=half, GROUP_C=128, GPB=4, UE8M0=False)
     out.update(silu_gu=gu, silu_q=q.view(torch.uint8), silu_s=s.t().contiguous())
+    q = torch.empty(n, half, dtype=torch.float8_e4m3fn)
+    s = torch.empty(half // 128, n, dtype=torch.float32).t()
+    k["silu"][(n, half // 512)](gu, q, s, gu.stride(0), q.stride(0), s.stride(1), s.stride(0),
+                                HALF=half, GROUP_C=128, GPB=4, UE8M0=True)
+    out.update(silu_q_ue8m0=q.view(torch.uint8), silu_s_ue8m0=s.t().contiguous())
 
     # merge_attn_quant: 6 rows, 4 heads x 128; rows 1 and 4 read nothing
     n, heads, d = 6, 4, 128
@@ -514,6 +530,13 @@ def make_kernel_vectors():
         s.stride(0), D=d, GPB=4, UE8M0=False)
     out.update(merge_a=a, merge_b=b, merge_la=la.contiguous(), merge_lb=lb.contiguous(),
                merge_src=src, merge_q=q.view(torch.uint8), merge_s=s.t().contiguous())
+    q = torch.empty(n, heads * d, dtype=torch.float8_e4m3fn)
+    s = torch.empty(heads, n, dtype=torch.float32).t()
+    k["merge_quant"][(n, heads // 4)](
+        a, b, la, lb, src, q, s, a.stride(0), a.stride(1), b.stride(0), b.stride(1),
+        la.stride(0), la.stride(1), lb.stride(0), lb.stride(1), q.stride(0), s.stride(1),
+        s.stride(0), D=d, GPB=4, UE8M0=True)
+    out.update(merge_q_ue8m0=q.view(torch.uint8), merge_s_ue8m0=s.t().contiguous())
 
     # kv_row_scatter: 3 rows into a 10-row pool of 2 x 128
     kk = torch.randn(4, 2, 128, generator=g).to(torch.bfloat16)
@@ -533,6 +556,31 @@ def make_kernel_vectors():
         else:
             arrays[name] = val.contiguous().numpy()
     np.savez_compressed(HERE / "kernels.npz", **arrays)
+
+
+def make_requant_vectors():
+    os.environ["TORCHDYNAMO_DISABLE"] = "1"
+    from vllm.model_executor.layers.quantization.utils.fp8_utils import (
+        requant_weight_ue8m0_inplace,
+    )
+
+    g = torch.Generator().manual_seed(11)
+    out = {}
+    n, k = 384, 512
+    # config-1 weights: e4m3(N(0, 1)) codes, lognormal(ln 0.02, 0.3) scales;
+    # block (0, 1) all zeros (amax clamped to 1e-4), block (1, 2) holding a
+    # +-448 code, block (2, 3) tiny codes only
+    w = torch.randn(n, k, generator=g).to(torch.float8_e4m3fn)
+    w[0:128, 128:256] = 0
+    w[128, 300] = 448.0
+    w[256:384, 384:512] = (torch.randn(128, 128, generator=g) * 0.01).to(torch.float8_e4m3fn)
+    s = torch.exp(np.log(0.02) + 0.3 * torch.randn(n // 128, k // 128, generator=g))
+    s[2, 0] = 2.0 ** -20
+    w2, s2 = w.clone(), s.clone()
+    requant_weight_ue8m0_inplace(w2, s2, (128, 128))
+    out.update(w=w.view(torch.uint8), s=s, w_ue8m0=w2.view(torch.uint8), s_ue8m0=s2)
+    np.savez_compressed(HERE / "requant_ue8m0.npz",
+                        **{name: val.contiguous().numpy() for name, val in out.items()})
 
 
 def main():
@@ -559,6 +607,9 @@ def main():
     if not only or "token_store" in only:
         make_token_store()
         print("token_store.arrow written")
+    if not only or "requant" in only:
+        make_requant_vectors()
+        print("requant_ue8m0.npz written")
     if only and "kernels" not in only:
         return
     make_kernel_vectors()

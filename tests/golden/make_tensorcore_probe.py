@@ -6,6 +6,10 @@ launch) and records, for seeded operands with a wide exponent spread:
 
 - gemm_s{3,6}_*: e4m3 codes a [64, 128], w [64, 128] and the fp32
   accumulator of one 128-deep block (four tcgen05 K=32 MMAs, unit scales);
+- mx_s{3,6}_*: the UE8M0 mode's block-scaled MMA (kind::mxf8f6f4): codes
+  a [64, 512], w [64, 512], power-of-two scales with random exponents
+  (a_scale [4, 64], w_scale [1, 4]) and the fp32 accumulator of the whole
+  K (sixteen K=32 steps);
 - mma_*: bf16 A [16, 16], B [16, 8], fp32 C and the fp32 D = C + A B of one
   mma.sync;
 - tcf16_m{0,1}_r*: tcgen05 kind::f16 (bf16) chains of four K=16 MMAs in the
@@ -15,10 +19,12 @@ launch) and records, for seeded operands with a wide exponent spread:
 
 tests/test_oracle_model.py checks that oracle/tcmodel.c reproduces every
 output bit for bit. Run: python tests/golden/make_tensorcore_probe.py
+[output .npz, default tests/golden/tensorcore_probe.npz]
 """
 
 import ctypes
 import subprocess
+import sys
 import tempfile
 from pathlib import Path
 
@@ -127,7 +133,28 @@ def main():
                 out[key + "_b"] = tb.view(torch.int16).numpy()
                 out[key + "_c"] = c if use_c else np.full((1,), np.nan, np.float32)
                 out[key + "_d"] = dd.cpu().numpy()
-    np.savez_compressed(HERE / "tensorcore_probe.npz", **out)
+        # separate stream: the entries above keep their operands
+        rng_mx = np.random.default_rng(1)
+        for spread in (3, 6):
+            a = torch.from_numpy(operands(rng_mx, (128, 512), spread)).to(torch.float8_e4m3fn)
+            w = torch.from_numpy(operands(rng_mx, (256, 512), spread)).to(torch.float8_e4m3fn)
+            a_s = np.exp2(rng_mx.integers(-12, 5, (4, 128))).astype(np.float32)
+            w_s = np.exp2(rng_mx.integers(-12, 5, (2, 4))).astype(np.float32)
+            A, W = a.to(dev), w.to(dev)
+            AS, WS = torch.from_numpy(a_s).to(dev), torch.from_numpy(w_s).to(dev)
+            res = torch.zeros(128, 256, device=dev)
+            assert lib.probe_gemm_mx_f32(P(A.data_ptr()), P(AS.data_ptr()), ctypes.c_int64(128),
+                                         P(W.data_ptr()), P(WS.data_ptr()), P(res.data_ptr()),
+                                         ctypes.c_int64(128), ctypes.c_int64(256),
+                                         ctypes.c_int64(512), stream) == 0
+            torch.cuda.synchronize()
+            out[f"mx_s{spread}_a"] = a.view(torch.uint8).numpy()[:64]
+            out[f"mx_s{spread}_w"] = w.view(torch.uint8).numpy()[:64]
+            out[f"mx_s{spread}_as"] = np.ascontiguousarray(a_s[:, :64])
+            out[f"mx_s{spread}_ws"] = w_s[:1]
+            out[f"mx_s{spread}_out"] = res.cpu().numpy()[:64, :64]
+    dest = Path(sys.argv[1]) if len(sys.argv) > 1 else HERE / "tensorcore_probe.npz"
+    np.savez_compressed(dest, **out)
 
 
 if __name__ == "__main__":

@@ -1,23 +1,40 @@
 // Tensor-core numerics probes for tests/golden/make_tensorcore_probe.py (test
-// infrastructure, not part of the library): tcgen05 f8f6f4 partials in fp32
-// and one mma.sync m16n8k16 bf16. Bounds: every index below is within the
+// infrastructure, not part of the library): tcgen05 f8f6f4 partials and the
+// block-scaled (UE8M0) accumulator in fp32, and one mma.sync m16n8k16 bf16. Bounds: every index below is within the
 // buffers the host allocates (checked in probe.py).
 #include "../../quail_b200/csrc/gemm_fp8.cu"
+
+// The library's GEMM kernel with an fp32 output (the accumulator before
+// the bf16 rounding): MX = false, the promoted 128-deep partials; MX = true,
+// the UE8M0 mode's whole-K block-scaled accumulator. n % 256 == 0.
+template <bool MX>
+static int probe_f32(const void* a, const float* as, int64_t ld, const void* w, const float* ws,
+                     float* out, int64_t m, int64_t n, int64_t k, void* stream) {
+    using C = Cfg<256, MAX_STAGES, false, false, false, MX>;
+    CUtensorMap ma, mb, mc;
+    memset(&mc, 0, sizeof(mc));  // no TMA store on the fp32 path
+    if (make_map(&ma, a, m, k, BM) || make_map(&mb, w, n, k, 256)) return 1;
+    auto kern = gemm_fp8_bs_kernel<256, float, MAX_STAGES, false, false, false, MX>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    uint32_t* status = device_status_ptr();
+    RopeArgs none;
+    memset(&none, 0, sizeof(none));
+    const int64_t tiles = ((m + BM - 1) / BM) * (n / 256);
+    kern<<<(int)(tiles < 148 ? tiles : 148), NUM_THREADS, C::SMEM, (cudaStream_t)stream>>>(
+        ma, mb, mc, as, ld, ws, out, nullptr, 0, (int)m, (int)n, (int)k, status, none);
+    return cudaGetLastError() != cudaSuccess;
+}
 
 extern "C" int probe_gemm_f32(const void* a, const float* as, int64_t ld, const void* w,
                               const float* ws, float* out, int64_t m, int64_t n, int64_t k,
                               void* stream) {
-    CUtensorMap ma, mb, mc;
-    memset(&mc, 0, sizeof(mc));  // no TMA store on the fp32 path
-    if (make_map(&ma, a, m, k, BM) || make_map(&mb, w, n, k, 256)) return 1;
-    cudaFuncSetAttribute(gemm_fp8_bs_kernel<256, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         Cfg<256>::SMEM);
-    uint32_t* status = device_status_ptr();
-    int64_t tiles = ((m + BM - 1) / BM) * (n / 256);
-    gemm_fp8_bs_kernel<256, float><<<(int)(tiles < 148 ? tiles : 148), NUM_THREADS, Cfg<256>::SMEM,
-                                     (cudaStream_t)stream>>>(ma, mb, mc, as, ld, ws, out, (int)m, (int)n,
-                                                             (int)k, status);
-    return cudaGetLastError() != cudaSuccess;
+    return probe_f32<false>(a, as, ld, w, ws, out, m, n, k, stream);
+}
+
+extern "C" int probe_gemm_mx_f32(const void* a, const float* as, int64_t ld, const void* w,
+                                 const float* ws, float* out, int64_t m, int64_t n, int64_t k,
+                                 void* stream) {
+    return probe_f32<true>(a, as, ld, w, ws, out, m, n, k, stream);
 }
 
 // one warp: D[16x8] = A[16x16] B[16x8] + C, fragments in the PTX layout

@@ -26,11 +26,20 @@ def interpreter_bf16(x):
 
 
 def interpreter_fp8(x):
-    """fp32 -> e4m3 as the Triton interpreter does it: nearest even, except
-    that the carry of a round-up into the next binade is ORed into the
-    exponent: when the pre-carry biased exponent is odd the carry is lost
-    and the result is half the correctly rounded power of two."""
-    rne = x.to(torch.float8_e4m3fn)
+    """fp32 -> e4m3 as the Triton interpreter does it: nearest, ties away
+    from zero (the compiled cvt.rn rounds ties to even; ties are frequent
+    in the UE8M0 mode, where q = y * 2^-e is exact), except that the carry
+    of a round-up into the next binade is ORed into the exponent: when the
+    pre-carry biased exponent is odd the carry is lost and the result is
+    half the correctly rounded power of two."""
+    xd = x.to(torch.float64)
+    a = xd.abs()
+    _, e2 = torch.frexp(a)
+    quantum = torch.exp2(torch.clamp(e2 - 1, min=-6).to(torch.float64) - 3)
+    k = a / quantum
+    tie = (k - torch.floor(k)) == 0.5
+    away = (torch.sign(xd) * (torch.floor(k) + 1) * quantum).to(torch.float32)
+    rne = torch.where(tie, away, x.to(torch.float32)).to(torch.float8_e4m3fn)
     code = rne.view(torch.uint8)
     r = rne.to(torch.float32)
     mantissa_zero = (code & 0x7) == 0
@@ -113,6 +122,45 @@ def test_merge_attn_quant(vec, interpreter_rounding):
                                vec["merge_src"], 4)
     fp8_codes_close(q, vec["merge_q"])
     torch.testing.assert_close(s, vec["merge_s"], rtol=2e-7, atol=0)
+
+
+@pytest.fixture
+def ue8m0_mode():
+    nx.MODE["ue8m0"] = True
+    yield
+    nx.MODE["ue8m0"] = False
+
+
+def test_add_rmsnorm_quant_ue8m0(vec, interpreter_rounding, ue8m0_mode):
+    """UE8M0=True: the scales are powers of two, equal to the reference's."""
+    _, q, s = nx.add_rmsnorm_quant(vec["norm_x"], vec["norm_r_in"], vec["norm_w"], 1e-6)
+    assert torch.equal(s, vec["norm_s_ue8m0"])
+    fp8_codes_close(q, vec["norm_q_ue8m0"])
+
+
+def test_silu_mul_quant_ue8m0(vec, interpreter_rounding, ue8m0_mode):
+    q, s = nx.silu_mul_quant(vec["silu_gu"])
+    assert torch.equal(s, vec["silu_s_ue8m0"])
+    fp8_codes_close(q, vec["silu_q_ue8m0"])
+
+
+def test_merge_attn_quant_ue8m0(vec, interpreter_rounding, ue8m0_mode):
+    q, s = nx.merge_attn_quant(vec["merge_a"].reshape(6, 512), vec["merge_la"],
+                               vec["merge_b"].reshape(4, 512), vec["merge_lb"],
+                               vec["merge_src"], 4)
+    assert torch.equal(s, vec["merge_s_ue8m0"])
+    fp8_codes_close(q, vec["merge_q_ue8m0"])
+
+
+def test_requant_weight_ue8m0_matches_vllm():
+    """The oracle's load-time re-quantisation against vLLM's own
+    requant_weight_ue8m0_inplace (tests/golden/requant_ue8m0.npz), zero,
+    full-range and tiny blocks included: codes and scales bit for bit."""
+    d = np.load(GOLDEN.parent / "requant_ue8m0.npz")
+    w = torch.from_numpy(d["w"]).view(torch.float8_e4m3fn)
+    q, s = nx.requant_weight_ue8m0(w, torch.from_numpy(d["s"]))
+    assert torch.equal(s, torch.from_numpy(d["s_ue8m0"]))
+    assert torch.equal(q.view(torch.uint8), torch.from_numpy(d["w_ue8m0"]))
 
 
 def test_kv_row_scatter(vec):

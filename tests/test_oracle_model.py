@@ -32,6 +32,22 @@ def test_fp8_mma_model_reproduces_measured_accumulators():
         assert np.array_equal(got.numpy().view(np.int32), want.view(np.int32))
 
 
+def test_mx_mma_model_reproduces_measured_accumulators():
+    """The UE8M0 mode's block-scaled MMA (kind::mxf8f6f4, power-of-two
+    scale factors): every K=32 step is a model step whose products carry
+    the scale exponents, chained over the whole K from C = 0."""
+    d = np.load(PROBE)
+    if "mx_s3_out" not in d.files:
+        pytest.skip("probe fixture predates the block-scaled measurements")
+    for spread in (3, 6):
+        a = torch.from_numpy(d[f"mx_s{spread}_a"]).view(torch.float8_e4m3fn)
+        w = torch.from_numpy(d[f"mx_s{spread}_w"]).view(torch.float8_e4m3fn)
+        got = tc.gemm_mx(a, torch.from_numpy(d[f"mx_s{spread}_as"]), w,
+                         torch.from_numpy(d[f"mx_s{spread}_ws"]), f32=True)
+        want = d[f"mx_s{spread}_out"]
+        assert np.array_equal(got.numpy().view(np.int32), want.view(np.int32))
+
+
 def test_bf16_mma_model_reproduces_measured_accumulators():
     d = np.load(PROBE)
     A, B, C, D = d["mma_A"], d["mma_B"], d["mma_C"], d["mma_D"]

@@ -13,6 +13,10 @@ Two steps, so the CPU half runs off the GPU box:
     python tests/tolerance_config1.py gpu --rows 64 --out margins.npz
     python tests/tolerance_config1.py cpu --gpu margins.npz --out summary.json
 
+--depths 1,2,4,8,16,36 repeats both steps on the model cut to its first L
+layers (the same weights), which shows how the difference grows with
+depth.
+
 ``gpu`` runs B200Executor.filter over config-1 rows 0..N-1 (seeded
 random-init weights, tree attention, the bench's chunk budget) and saves
 the margins; ``cpu`` packs the same rows through the same host loop, runs
@@ -41,12 +45,45 @@ def gpu(args):
     from quail_b200.model import QWEN3_4B
     from quail_b200.workload import config1
 
+    from quail_b200.model import random_weights
+
     wl = config1()
-    ex = B200Executor(torch, QWEN3_4B, 4096, seed=0)
     docs = [wl.docs[i] for i in range(args.rows)]
-    res = ex.filter(docs, wl.questions)
-    np.savez(args.out, margins=res.margins, bits=res.bits, rows=np.arange(args.rows))
-    print(json.dumps({"rows": args.rows, "chunks": res.chunks, "out": args.out}))
+    # generated on the CPU and copied, so both steps hold the same weights
+    # (the CPU and CUDA generators give different numbers)
+    full = random_weights(QWEN3_4B, seed=0, device="cpu").to(torch.device("cuda"))
+    if args.scales == "ue8m0":
+        from quail_b200.model import requant_ue8m0
+        requant_ue8m0(full)
+    out = {"rows": np.arange(args.rows)}
+    for depth in depths(args):
+        cfg, weights = truncated(QWEN3_4B, full, depth)
+        ex = B200Executor(torch, cfg, 4096, weights=weights, scales=args.scales)
+        res = ex.filter(docs, wl.questions, budget=QWEN3_4B.max_chunk_tokens)
+        out[f"margins_L{depth}"] = res.margins
+        del ex
+    if len(depths(args)) == 1:
+        out["margins"] = out[f"margins_L{depths(args)[0]}"]
+    np.savez(args.out, **out)
+    print(json.dumps({"rows": args.rows, "depths": depths(args), "out": args.out}))
+
+
+def depths(args):
+    return [int(d) for d in args.depths.split(",")] if args.depths else [36]
+
+
+def truncated(cfg, weights, depth):
+    """(config, Weights) of the first `depth` layers, tensors shared."""
+    import dataclasses
+
+    from quail_b200.model import Weights
+
+    if depth == cfg.n_layers:
+        return cfg, weights
+    c = dataclasses.replace(cfg, name=f"{cfg.name}-L{depth}", n_layers=depth)
+    w = Weights(c, weights.embed, weights.final_norm, weights.cos_sin)
+    w.layers = weights.layers[:depth]
+    return c, w
 
 
 def cpu(args):
@@ -66,7 +103,30 @@ def cpu(args):
     nx.MODE["exact"] = False
     wl = config1()
     docs = [wl.docs[i] for i in range(n)]
-    weights = random_weights(QWEN3_4B, seed=0, device="cpu")
+    full = random_weights(QWEN3_4B, seed=0, device="cpu")
+    if args.scales == "ue8m0":
+        from quail_b200.model import LINEARS
+        nx.MODE["ue8m0"] = True
+        for layer in full.layers:
+            for wn, sn in LINEARS:
+                q, sc = nx.requant_weight_ue8m0(getattr(layer, wn), getattr(layer, sn))
+                setattr(layer, wn, q)
+                setattr(layer, sn, sc)
+    summaries = []
+    for depth in depths(args):
+        cfg, weights = truncated(QWEN3_4B, full, depth)
+        summaries.append(compare(torch, of, nx, loop, KVArena, prefix_tree, wl, docs, weights,
+                                 got[f"margins_L{depth}"] if f"margins_L{depth}" in got.files
+                                 else got["margins"]))
+    text = json.dumps(summaries if len(summaries) > 1 else summaries[0], indent=1)
+    Path(args.out).write_text(text + "\n")
+    print(text)
+
+
+def compare(torch, of, nx, loop, KVArena, prefix_tree, wl, docs, weights, m_gpu):
+    from quail_b200.model import QWEN3_4B
+
+    n = len(docs)
     cfg = weights.config
     _, ans_w, tc, fc = weights.answer_rows()
     arena = KVArena(1, 4096, 16, 1, 8, device=None)
@@ -94,15 +154,16 @@ def cpu(args):
     loop.run_filter(torch, arena, Oracle(), Answers(), docs, wl.questions,
                     QWEN3_4B.max_chunk_tokens, arena_writes=True, attention_mode="tree",
                     prefix_tree=prefix_tree(docs, 16), device="cpu")
-    m_gpu = got["margins"].astype(np.float64)
+    m_gpu = m_gpu.astype(np.float64)
     m_ref = want.astype(np.float64)
     d = np.abs(m_gpu - m_ref)
     sure = np.abs(m_ref) > 0.1
     summary = {
-        "what": "|margin(B200 kernels) - margin(oracle fast mode: fp32 BLAS K-block "
-                "partials, torch exp2)|, Qwen3-4B FP8 (36 layers, seeded random-init "
-                "weights), config-1 rows 0..%d, tree attention" % (n - 1),
-        "rows": n,
+        "what": "|margin(B200 kernels) - margin(oracle fast mode: fp32 BLAS GEMMs, torch "
+                "exp2 and reductions)|, Qwen3-4B FP8 (first %d layers, seeded random-init "
+                "weights), config-1 rows 0..%d, tree attention, %s scales"
+                % (cfg.n_layers, n - 1, "ue8m0" if nx.MODE["ue8m0"] else "fp32"),
+        "layers": cfg.n_layers, "rows": n,
         "max_abs_diff": float(d.max()), "mean_abs_diff": float(d.mean()),
         "median_abs_diff": float(np.median(d)), "p90_abs_diff": float(np.quantile(d, 0.9)),
         "within_0.05": float(np.mean(d <= 0.05)),
@@ -113,8 +174,7 @@ def cpu(args):
         "decision_agreement_all": float(np.mean((m_gpu > 0) == (m_ref > 0))),
         "cpu_seconds": time.perf_counter() - t0,
     }
-    Path(args.out).write_text(json.dumps(summary, indent=1) + "\n")
-    print(json.dumps(summary))
+    return summary
 
 
 def main():
@@ -123,6 +183,9 @@ def main():
     p.add_argument("--rows", type=int, default=64)
     p.add_argument("--gpu", default="margins.npz")
     p.add_argument("--out", default="out")
+    p.add_argument("--scales", default="fp32", choices=["fp32", "ue8m0"])
+    p.add_argument("--depths", default="",
+                   help="comma-separated layer counts (default: the full 36)")
     args = p.parse_args()
     (gpu if args.step == "gpu" else cpu)(args)
 
