@@ -79,7 +79,11 @@ struct Cfg {
     // MX: raw fp32 scales land by cp.async RAW_SLOTS - 1 K blocks ahead of
     // their conversion into the SF ring (tcgen05.cp source layout)
     static constexpr int RAW_SLOTS = MX ? (ROPE ? 4 : 8) : SCALE_SLOTS;
-    static constexpr int SF_SLOTS = MX ? 4 : 1;  // (1: keeps the MX-only code well formed)
+    // MX: one SF slot per stage, filled and released with the stage (its
+    // full barrier takes the scale loader's arrival besides the TMA bytes,
+    // its empty barrier frees both), so the MMA thread waits and commits
+    // once per K block
+    static constexpr int SF_SLOTS = MX ? NST : 1;  // (1: keeps the MX-only code well formed)
     static constexpr int SF_BYTES = 1536;  // SFA 32 x 16 B, SFB 2 x 32 x 16 B
     static constexpr int SLICE = BN / 4;      // columns per epilogue warp
     static_assert(!TSTORE || SLICE == 64, "TMA-store staging rows are 128 bytes");
@@ -135,9 +139,6 @@ struct Barriers {
     // ROPE: per warp pair (the two column halves of a head's rows): both
     // have read each other's partials
     uint64_t pair[8];
-    // MX: a K block's scale factors are in the SF ring / have been copied
-    uint64_t sf_full[4];
-    uint64_t sf_empty[4];
     uint32_t tmem_base;
     int abort;
 };
@@ -246,7 +247,7 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&bars->full[s], 1);
+            mbar_init(&bars->full[s], MX ? 2 : 1);  // MX: + the scale loader's arrival
             mbar_init(&bars->empty[s], 1);
         }
         for (int b = 0; b < C::NBUF; ++b) {
@@ -266,10 +267,6 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
             mbar_init(&bars->quad[1][q], 4);
         }
         for (int q = 0; q < 8; ++q) mbar_init(&bars->pair[q], 2);
-        for (int q = 0; q < 4; ++q) {
-            mbar_init(&bars->sf_full[q], 1);
-            mbar_init(&bars->sf_empty[q], 1);
-        }
         bars->abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -357,19 +354,13 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                             ok = false;
                             break;
                         }
-                        const int slot = it % C::SF_SLOTS;
-                        if (!mbar_wait(&bars->sf_full[slot], (uint32_t)(it / C::SF_SLOTS) & 1u,
-                                       abort_flag, status, STATUS_GEMM_MMA)) {
-                            ok = false;
-                            break;
-                        }
                         tc_fence_after();
                         // stage s's scale-factor columns: the MMAs of the K
                         // block that used them last completed before this
                         // stage's operands could be loaded again
                         const uint32_t sfa = tmem_base + (uint32_t)(C::TM_SF + 12 * s);
                         const uint32_t sfb = sfa + 4u;
-                        const uint32_t src = smem_u32(smem + C::SF_OFF + slot * C::SF_BYTES);
+                        const uint32_t src = smem_u32(smem + C::SF_OFF + s * C::SF_BYTES);
                         tmem_cp_32x128b_x4(sfa, rows16_desc(src));
                         tmem_cp_32x128b_x4(sfb, rows16_desc(src + 512));
                         tmem_cp_32x128b_x4(sfb + 4u, rows16_desc(src + 1024));
@@ -381,7 +372,6 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                             mma_mx(tmem_base, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k),
                                    C::IDESC_MX, sfa, sfb, (kb > 0 || k > 0) ? 1u : 0u);
                         mma_commit(&bars->empty[s]);
-                        mma_commit(&bars->sf_empty[slot]);
                         if (kb == n_kb - 1) mma_commit(&bars->tmem_full[0]);
                         continue;
                     }
@@ -420,8 +410,10 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
         constexpr int LAG = C::RAW_SLOTS - 1;
         constexpr int NB = BN / 128;
         auto sf_convert = [&](int j) -> bool {
-            const int slot = j % C::SF_SLOTS;
-            if (!mbar_wait(&bars->sf_empty[slot], ((uint32_t)(j / C::SF_SLOTS) & 1u) ^ 1u,
+            // stage slot's SF area is free once its previous MMAs (and
+            // their scale-factor copies) completed: the stage's empty phase
+            const int slot = j % STAGES;
+            if (!mbar_wait(&bars->empty[slot], ((uint32_t)(j / STAGES) & 1u) ^ 1u,
                            abort_flag, status, STATUS_GEMM_EPILOGUE))
                 return false;
             __syncwarp();  // every lane's copies of block j have landed
@@ -441,7 +433,7 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
             // the copies read shared memory through the async proxy
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->sf_full[slot]);
+            if (lane == 0) mbar_arrive(&bars->full[slot]);
             return true;
         };
         int it = 0, done = 0;
