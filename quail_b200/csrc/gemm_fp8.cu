@@ -91,9 +91,13 @@ struct Cfg {
     // 4 KB per warp holds the pair's sum-of-squares partials, then the two
     // 32 x 32 output boxes (64-byte swizzle)
     // SILU: one 32 x 32 fp8 box (1 KB) per epilogue warp
-    static constexpr int OUT_BYTES = (TSTORE || ROPE) ? EPI_WARPS * 32 * SLICE * 2
-                                     : SILU           ? EPI_WARPS * 32 * 32
-                                                      : 0;
+    // TSTORE with MX: the bf16 tile leaves in 32 x 16 boxes (32-byte
+    // swizzle) through 1 KB per warp, so four operand stages fit
+    static constexpr bool SMALL_OUT = TSTORE && MX;
+    static constexpr int OUT_BYTES = SMALL_OUT           ? EPI_WARPS * 1024
+                                     : (TSTORE || ROPE) ? EPI_WARPS * 32 * SLICE * 2
+                                     : SILU             ? EPI_WARPS * 32 * 32
+                                                        : 0;
     static constexpr int SCALE_OFF = STAGES * STAGE_BYTES + OUT_BYTES;
     static_assert(!SILU || (BN == 256 && !TSTORE), "SILU tiles are 128 gate + 128 up columns");
     static_assert(!ROPE || (BN == 256 && !TSTORE && !SILU), "ROPE tiles are two heads");
@@ -910,6 +914,29 @@ gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
                     }
                     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                 }
+            } else if constexpr (C::SMALL_OUT) {
+                // this warp's 32 rows x 64 columns as four 32 x 16 boxes
+                // through one 1 KB area: row r's 16-byte half j at r * 32 +
+                // (j ^ (r / 4) % 2) * 16 (the 32-byte swizzle of map_c)
+                uint8_t* stage = smem + STAGES * C::STAGE_BYTES + ew * 1024;
+                const int sw = (lane >> 2) & 1;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                    __syncwarp();
+                    *reinterpret_cast<uint4*>(stage + lane * 32 + (sw << 4)) =
+                        float_to_bf16x8(acc + 16 * q);
+                    *reinterpret_cast<uint4*>(stage + lane * 32 + ((sw ^ 1) << 4)) =
+                        float_to_bf16x8(acc + 16 * q + 8);
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    // rows past M are clipped by the tensor map's bounds
+                    if (lane == 0 && m0 + quarter * 32 < M) {
+                        tma_store_2d(&map_c, smem_u32(stage), n0 + col0 + 16 * q,
+                                     m0 + quarter * 32);
+                        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                    }
+                }
             } else if constexpr (TSTORE) {
                 // this warp's 32 rows x 64 columns, row r's 16-byte chunk j at
                 // r * 128 + (j ^ r % 8) * 16: the 128-byte swizzle of map_c,
@@ -1026,7 +1053,8 @@ int make_fp8_box32_map(CUtensorMap* map, void* base, int64_t rows, int64_t n) {
 }
 
 // bf16 output map: rows x n, box 32 rows x 64 columns, 128-byte swizzle
-int make_out_map(CUtensorMap* map, void* base, int64_t rows, int64_t n) {
+// (small: box 32 rows x 16 columns, 32-byte swizzle)
+int make_out_map(CUtensorMap* map, void* base, int64_t rows, int64_t n, bool small = false) {
     PFN_cuTensorMapEncodeTiled_v12000 enc = get_encoder();
     if (!enc) {
         set_error("qb_gemm_fp8_bs: cuTensorMapEncodeTiled unavailable");
@@ -1034,10 +1062,11 @@ int make_out_map(CUtensorMap* map, void* base, int64_t rows, int64_t n) {
     }
     cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)n * 2};
-    cuuint32_t box[2] = {64, 32};
+    cuuint32_t box[2] = {small ? 16u : 64u, 32};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     small ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         set_error("qb_gemm_fp8_bs: cuTensorMapEncodeTiled (out) failed (%d)", (int)r);
@@ -1061,7 +1090,7 @@ int launch(const void* a, const float* a_scale, int64_t a_scale_ld, const void* 
     st = make_map(&map_b, w, n, k, SILU ? 128 : BN);
     if (st) return st;
     if (TSTORE) {
-        st = make_out_map(&map_c, out, m, n);
+        st = make_out_map(&map_c, out, m, n, C::SMALL_OUT);
         if (st) return st;
     }
     if (SILU) {
@@ -1106,7 +1135,7 @@ extern "C" int qb_gemm_fp8_bs(const void* a, const float* a_scale, int64_t a_sca
     cudaStream_t s = (cudaStream_t)stream;
     // UE8M0: the block-scaled MMA applies the power-of-two scales
     if (ue8m0)
-        return launch<256, 3, true, false, false, true>(a, a_scale, a_scale_ld, w, w_scale, out, m,
+        return launch<256, 4, true, false, false, true>(a, a_scale, a_scale_ld, w, w_scale, out, m,
                                                         n, k, s);
     // The TMA-store epilogue (3 stages, the tile staged in shared memory)
     // beats 4 stages with per-thread row stores on every 4B shape (measured on
