@@ -107,8 +107,14 @@ class B200Executor:
         self.arena.reset()
 
     def filter(self, documents, question_ids, *, budget=None, attention="tree",
-               share_prefixes=True, arena_writes=True, limit=None) -> FilterResult:
-        """Run one AI.IF filter over documents; returns answers and margins."""
+               share_prefixes=True, arena_writes=True, limit=None, keys=None,
+               retain_survivors=()) -> FilterResult:
+        """Run one AI.IF filter over documents; returns answers and margins.
+
+        keys: the documents' arena keys ((alias, document) pairs to retain
+        them); retain_survivors: True or document positions whose KV stays
+        resident after a TRUE for a later operator (quail_b200.retention
+        manages it between operators)."""
         torch = self.torch
         t0 = time.perf_counter()
         tree = prefix_tree(documents, self.arena.page_tokens) if share_prefixes else None
@@ -127,7 +133,8 @@ class B200Executor:
         answers, spans, tokens = loop.run_filter(
             torch, self.arena, self.pipeline, ans, documents,
             [list(q) for q in question_ids], budget or self.budget, timing=timing,
-            limit=limit, arena_writes=arena_writes, attention_mode=attention,
+            limit=limit, arena_writes=arena_writes, arena_keys=keys,
+            retain_survivors=retain_survivors, attention_mode=attention,
             document_done=done, prefix_tree=tree, stats=stats, device=self.device,
             on_chunk=on_chunk, staging=self.staging)
         for groups, margins in zip(order, ans.margins):
@@ -145,7 +152,8 @@ class B200Executor:
                             d2h_bytes=ans.d2h_bytes, gpu_s=gpu_s, wall_s=wall, timing=timing)
 
     def _join(self, readout, anchors, stage_suffixes, stage_frames, budget, attention,
-              share_prefixes, partners, stop_at_true=False, stream_step=None):
+              share_prefixes, partners, stop_at_true=False, stream_step=None,
+              anchor_keys=None, anchor_done=None):
         torch = self.torch
         t0 = time.perf_counter()
         tree = prefix_tree(anchors, self.arena.page_tokens) if share_prefixes else None
@@ -156,7 +164,8 @@ class B200Executor:
             stage_frames=stage_frames, attention_mode=attention, prefix_tree=tree,
             anchor_partners=None if partners is None else (lambda key: partners[key]),
             stats=stats, device=self.device, stop_at_true=stop_at_true,
-            stream_step=stream_step, staging=self.staging)
+            stream_step=stream_step, staging=self.staging, anchor_keys=anchor_keys,
+            anchor_done=anchor_done)
         torch.cuda.synchronize(self.device)
         wall = time.perf_counter() - t0
         gpu_s = sum(a.elapsed_time(b) for _, a, b in spans if a is not None) / 1000.0
@@ -169,18 +178,22 @@ class B200Executor:
 
     def join(self, anchors, stage_suffixes, *, stage_frames=None, budget=None,
              attention="tree", share_prefixes=True, partners=None,
-             exists_stop=False) -> JoinResult:
+             exists_stop=False, anchor_keys=None, anchor_done=None) -> JoinResult:
         """Run one AI join: every anchor against its partners, stage by stage
         (an anchor continues to stage j + 1 once a stage-j partner answered
         TRUE). partners: per anchor, per stage, partner indices or None.
         exists_stop: for an EXISTS (semi) or NOT EXISTS (anti) join, stop an
         anchor's last-stage stream at its first TRUE answer (partners not yet
         launched are skipped; survivors are unchanged), with the anchors'
-        streams interleaved one partner per anchor per chunk."""
+        streams interleaved one partner per anchor per chunk. anchor_keys:
+        the anchors' arena keys (a retained key's KV is reused as a resident
+        anchor); anchor_done(a, row): the finished anchor's free or retain
+        decision (retention.retain_after_join), else it is freed."""
         ans = AsyncAnswers(self.torch, self.answer_rows)
         return self._join(ans, anchors, stage_suffixes, stage_frames, budget, attention,
                           share_prefixes, partners, stop_at_true=exists_stop,
-                          stream_step=1 if exists_stop else None)
+                          stream_step=1 if exists_stop else None, anchor_keys=anchor_keys,
+                          anchor_done=anchor_done)
 
     def score(self, anchors, suffixes, *, budget=None, attention="tree",
               share_prefixes=True, partners=None) -> JoinResult:

@@ -14,10 +14,16 @@ HBM layout: one allocation of shape (n_layers, 2, n_pages * page_tokens,
 n_kv, head_dim) bf16; ``layer_kv(l)`` views its K and V halves as the flat
 (rows, n_kv, head_dim) pools the kernels index by row.
 
-Not built here (outside the AI.IF prefill path): sliding-window pools
-(Gemma only) and cross-operator retention; the methods the filter loop
-calls for them are no-ops.
+Cross-operator retention (arena.py:153-226, 556-620): a filter survivor
+or a finished join anchor can stay resident for a later operator, rewound
+to its prefix; retained keys are evicted lowest planned-reuse priority
+first (a heap of (priority, version, key, pages, tokens), stale entries
+skipped by version) when admission is short of pages or the retained
+pages pass the cap. Not built here (Gemma only): sliding-window pools;
+the methods the filter loop calls for them are no-ops.
 """
+
+import heapq
 
 import numpy as np
 
@@ -34,9 +40,23 @@ class PageArena:
         self.holds = [0] * n_pages
         self.tokens = {}
         self.pinned = set()
+        # retention: key -> prefix tokens kept, key -> pages its eviction
+        # frees (when retained), the priority heap and entry versions
+        self.retained = {}
+        self.retained_sizes = {}
+        self.retained_pages = 0
+        self.retention_heap = []
+        self.retention_versions = {}
+        self.retention_counter = 0
+        self.retention_policy = None
+        self.retention_cap_pages = None
 
     def pages_needed(self, tokens: int) -> int:
         return -(-tokens // self.page_tokens)
+
+    @property
+    def retained_prefix_tokens(self) -> int:
+        return sum(self.tokens[key] for key in self.retained)
 
     @property
     def free_pages(self) -> int:
@@ -96,12 +116,97 @@ class PageArena:
         borrowed = self.borrowed.pop(key)
         self.tokens.pop(key)
         self.pinned.discard(key)
+        self._unretain(key)
         return self.release_pages(borrowed + pages)
 
     def pin(self, key) -> None:
         if key not in self.owned:
             raise KeyError(key)
+        self._unretain(key)
         self.pinned.add(key)
+
+    # ---- retention --------------------------------------------------------
+
+    def _unretain(self, key) -> None:
+        # a heap entry stays behind; its version no longer matches
+        self.retained_pages -= self.retained_sizes.pop(key, 0)
+        self.retained.pop(key, None)
+        self.retention_versions.pop(key, None)
+
+    def retain(self, key, priority=None) -> None:
+        """Make a resident key evictable once its current use ends.
+
+        The pages counted are the ones evicting it would free now (those it
+        alone holds); priority defaults to the policy's, else tokens per
+        page."""
+        if key not in self.owned:
+            raise KeyError(key)
+        self.pinned.discard(key)
+        tokens = self.tokens[key]
+        self._unretain(key)
+        pages = sum(1 for page in self.table_pages(key) if self.holds[page] == 1)
+        self.retained[key] = tokens
+        self.retained_sizes[key] = pages
+        self.retained_pages += pages
+        self.retention_counter += 1
+        version = self.retention_counter
+        self.retention_versions[key] = version
+        if priority is None:
+            if self.retention_policy is not None:
+                priority = self.retention_policy.priority(key, tokens, max(1, pages))
+            else:
+                priority = (tokens / max(1, pages),)
+        heapq.heappush(self.retention_heap, (priority, version, key, pages, tokens))
+
+    def configure_retention(self, policy, cap_pages: int) -> None:
+        """A new priority rule and retained-page cap: every retained key is
+        re-entered under it (active keys stay unevictable)."""
+        if not 0 <= cap_pages <= self.n_pages:
+            raise ValueError("retention capacity must fit inside the arena")
+        self.retention_policy = policy
+        self.retention_cap_pages = cap_pages
+        self.retention_heap = []
+        for key in list(self.retained):
+            self.retain(key)
+
+    def pop_retained_victim(self, keep=frozenset()):
+        """(key, pages, tokens) of the lowest-priority retained key, no longer
+        retained; keys in keep are passed over. None when there is none."""
+        passed, victim = [], None
+        while self.retention_heap:
+            entry = heapq.heappop(self.retention_heap)
+            _, version, key, pages, tokens = entry
+            if self.retention_versions.get(key) != version:
+                continue
+            if key in keep:
+                passed.append(entry)
+                continue
+            self._unretain(key)
+            victim = (key, pages, tokens)
+            break
+        for entry in passed:
+            heapq.heappush(self.retention_heap, entry)
+        return victim
+
+    def borrowed_tokens(self, key) -> int:
+        return len(self.borrowed[key]) * self.page_tokens
+
+    def rewind(self, key, tokens: int) -> int:
+        """Keep the key's first tokens; its trailing unused pages go back."""
+        if key not in self.owned:
+            raise KeyError(key)
+        borrowed = self.borrowed_tokens(key)
+        capacity = borrowed + len(self.owned[key]) * self.page_tokens
+        if tokens < borrowed or tokens > capacity:
+            raise ValueError("rewind tokens leave the resident capacity")
+        keep = self.pages_needed(tokens) - len(self.borrowed[key])
+        released = self.owned[key][keep:]
+        self.owned[key] = self.owned[key][:keep]
+        self.tokens[key] = tokens
+        freed = self.release_pages(released)
+        if key in self.retained:
+            self.retain(key)
+        return freed
 
     def grow(self, key, capacity_tokens: int):
         if key not in self.owned:
@@ -144,15 +249,21 @@ class KVArena:
         self._capacity_rows = {}
         self._holds = {}
         self._deferred = set()
-        self.retention_cap_pages = None
+        self.reset_stats()
 
     def reset(self) -> None:
-        """Forget every key and hold (the pools stay allocated)."""
+        """Forget every key, hold and retention (the pools stay allocated)."""
         self.accounting = PageArena(self.accounting.n_pages, self.accounting.page_tokens)
         self._capacity_rows = {}
         self._holds = {}
         self._deferred = set()
-        self.retention_cap_pages = None
+        self.reset_stats()
+
+    def reset_stats(self) -> None:
+        """Zero the eviction counters."""
+        self.evicted_keys = 0
+        self.evicted_pages = 0
+        self.evicted_prefix_tokens = 0
 
     # ---- geometry ---------------------------------------------------------
 
@@ -178,7 +289,27 @@ class KVArena:
 
     @property
     def retained_pages(self) -> int:
-        return 0
+        return self.accounting.retained_pages
+
+    @property
+    def retained_prefix_tokens(self) -> int:
+        return self.accounting.retained_prefix_tokens
+
+    @property
+    def retention_cap_pages(self):
+        return self.accounting.retention_cap_pages
+
+    @retention_cap_pages.setter
+    def retention_cap_pages(self, pages) -> None:
+        self.accounting.retention_cap_pages = pages
+
+    def configure_retention(self, policy, cap_pages: int) -> None:
+        """Set the eviction priority rule and the retained-page cap."""
+        self.accounting.configure_retention(policy, cap_pages)
+
+    def retained_keys(self) -> list:
+        """Every key whose KV is kept for a later operator."""
+        return list(self.accounting.retained)
 
     def pages_needed(self, tokens: int) -> int:
         return self.accounting.pages_needed(tokens)
@@ -272,15 +403,52 @@ class KVArena:
         self._capacity_rows.pop(key)
         return self.accounting.free_key(key)
 
-    # sliding windows and retention are outside this path
+    # ---- retention (arena.py:541-620) ------------------------------------------
+
+    def retain(self, key, tokens: int, priority=None) -> int:
+        """Rewind a key to its first tokens and keep it for a later
+        operator; returns the pages that came free (the rewind's, and any
+        eviction the cap forces). Keys are (alias, document) pairs."""
+        if not (isinstance(key, tuple) and len(key) == 2):
+            raise TypeError(f"retained keys are (alias, document) pairs, got {key!r}")
+        acct = self.accounting
+        before = self.free_pages
+        acct.rewind(key, tokens)
+        self._set_rows(key)
+        acct.retain(key, priority)
+        if acct.retention_cap_pages is not None:
+            self.evict_retained(max(0, acct.retained_pages - acct.retention_cap_pages))
+        return self.free_pages - before
+
+    def evict_retained(self, pages_needed: int) -> tuple:
+        """Evict retained keys, lowest priority first, until pages_needed
+        pages have come free; keys held for queued borrowers stay. Returns
+        the evicted keys."""
+        start = self.free_pages
+        evicted = []
+        while self.free_pages - start < pages_needed:
+            victim = self.accounting.pop_retained_victim(keep=self._holds)
+            if victim is None:
+                break
+            evicted.append(victim[0])
+            self.evict_key(victim[0])
+        return tuple(evicted)
+
+    def evict_key(self, key) -> int:
+        """Free one retained key and count the KV lost."""
+        tokens = self.accounting.tokens[key]
+        pages = self.free_key(key)
+        self.evicted_keys += 1
+        self.evicted_pages += pages
+        self.evicted_prefix_tokens += tokens
+        return pages
+
+    # the sliding window is outside this path
     def keep_window(self, key, shared: int) -> None:
         return None
 
     def trim_window(self, key) -> int:
         return 0
-
-    def evict_retained(self, pages_needed: int) -> tuple:
-        return ()
 
     # ---- residency ----------------------------------------------------------
 

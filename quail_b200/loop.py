@@ -475,20 +475,27 @@ class FilterStream:
 
     def __init__(self, torch, arena, pipeline, async_ans, doc_ids, question_ids, budget,
                  timing=None, limit=None, *, arena_writes, arena_keys=None,
-                 hold_survivors=False, hold_extra_tokens=0,
+                 retain_survivors=(), hold_survivors=False, hold_extra_tokens=0,
                  attention_mode=None, document_done=None, prefix_tree=None,
                  device="cuda", on_chunk=None, staging=None):
         p = _shared_preamble_tokens(question_ids)
         keys = range(len(doc_ids)) if arena_keys is None else arena_keys
         if len(keys) != len(doc_ids):
             raise ValueError("arena_keys must match doc_ids")
+        # retain_survivors: True, or the document positions whose KV stays
+        # resident (rewound to the document) after a last-stage TRUE
+        retain_all = retain_survivors is True
+        retain = set() if retain_all else set(retain_survivors)
+        if hold_survivors and (retain_all or retain):
+            raise ValueError("held survivors are pinned, not retained")
         stage_tokens = [len(question_ids[0])] + [len(q) - p for q in question_ids[1:]]
         tails = [list(question_ids[0])] + [list(q[p:]) for q in question_ids[1:]]
         for i, tail in enumerate(tails):
             if not tail:
                 raise ValueError(f"stage {i} question has no tokens beyond the shared "
                                  f"preamble ({p} tokens)")
-        if not arena_writes and (len(question_ids) > 1 or hold_survivors):
+        if not arena_writes and (len(question_ids) > 1 or retain_all or retain
+                                 or hold_survivors):
             raise ValueError("arena_writes=False needs a single stage")
         self.attention_mode = attention_path(pipeline, attention_mode)
         unified = self.attention_mode == "unified"
@@ -526,6 +533,8 @@ class FilterStream:
         self.timing = timing
         self.arena_writes = arena_writes
         self.hold = hold_survivors
+        self.retain_all = retain_all
+        self.retain = retain
         self.reserve_pages = 0  # pages a join consumer needs free for its partners
         self.preamble = p
         self.capacity_extra = capacity_extra
@@ -590,10 +599,15 @@ class FilterStream:
         finished = []
         for (doc, stage, _fresh), bit in zip(groups, bits):
             passed = bool(bit)
-            # a held survivor keeps its pages: the join consumer frees them
-            hold = passed and stage == last_stage and self.hold
-            for d in self.sched.report(doc, stage, passed, release=not hold):
+            last = stage == last_stage
+            # a retained survivor stays resident for a later operator; a
+            # held one keeps its pages for the join consumer, which frees them
+            keep = passed and last and (self.retain_all or doc in self.retain)
+            hold = passed and last and self.hold
+            for d in self.sched.report(doc, stage, passed, release=not (keep or hold)):
                 self.arena.free_key(self.keys[d])
+            if keep:
+                self.arena.retain(self.keys[doc], len(self.doc_ids[doc]))
             if hold:
                 items.append((self.keys[doc], self.doc_ids[doc]))
             if not passed or stage == last_stage:
@@ -693,9 +707,9 @@ class FilterStream:
 
 
 def run_filter(torch, arena, pipeline, async_ans, doc_ids, question_ids, budget, timing=None,
-               limit=None, *, arena_writes, arena_keys=None, attention_mode=None,
-               document_done=None, prefix_tree=None, stats=None, device="cuda",
-               on_chunk=None, staging=None):
+               limit=None, *, arena_writes, arena_keys=None, retain_survivors=(),
+               attention_mode=None, document_done=None, prefix_tree=None, stats=None,
+               device="cuda", on_chunk=None, staging=None):
     """The filter chain run to the end; see FilterStream for the arguments.
 
     Returns:
@@ -704,9 +718,10 @@ def run_filter(torch, arena, pipeline, async_ans, doc_ids, question_ids, budget,
     """
     stream = FilterStream(torch, arena, pipeline, async_ans, doc_ids, question_ids, budget,
                           timing=timing, limit=limit, arena_writes=arena_writes,
-                          arena_keys=arena_keys, attention_mode=attention_mode,
-                          document_done=document_done, prefix_tree=prefix_tree,
-                          device=device, on_chunk=on_chunk, staging=staging)
+                          arena_keys=arena_keys, retain_survivors=retain_survivors,
+                          attention_mode=attention_mode, document_done=document_done,
+                          prefix_tree=prefix_tree, device=device, on_chunk=on_chunk,
+                          staging=staging)
     while not stream.done:
         stream.next()
     if stats is not None:

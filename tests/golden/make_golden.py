@@ -407,6 +407,105 @@ def run_reference_feed(name):
     return summary
 
 
+# ---- retention between operators (arena.py:153-226, 541-620; retention.py) ----
+
+RETAIN_SCENARIOS = ("retain_tree", "retain_unified")
+
+
+def retention_inputs(name):
+    """(docs, question, frame, partners, budget, n_pages, attention, config,
+    uses, after): a filter whose survivors stay resident, a boundary that
+    frees and evicts some, and a join over every survivor whose finished
+    matching anchors are retained again."""
+    rng = np.random.default_rng(21)
+    instr = rng.integers(1000, 150000, 48).tolist()
+    docs = [instr + rng.integers(1000, 150000, int(rng.integers(20, 120))).tolist()
+            for _ in range(18)]
+    question = [int(rng.integers(1000, 150000)), 7]
+    frame = rng.integers(1000, 150000, 4).tolist()
+    partners = [rng.integers(1000, 150000, int(rng.integers(6, 30))).tolist()
+                for _ in range(7)]
+    attention = "unified" if name.endswith("unified") else "tree"
+    config = {"linear_seconds": 1e-6, "pair_seconds": 3e-9, "cap_pages": 24}
+    return (docs, question, frame, partners, 400, 64, attention, config,
+            {"d": (0.75, 2)}, {"d": (0.5, 3)})
+
+
+def arena_state(arena):
+    return dict(retained=sorted([list(k) for k in arena.retained_keys()]),
+                resident=sorted([list(k) for k in arena.resident_keys()
+                                 if isinstance(k, tuple)]),
+                retained_pages=int(arena.retained_pages), free_pages=int(arena.free_pages),
+                evicted_keys=int(arena.evicted_keys), evicted_pages=int(arena.evicted_pages),
+                evicted_prefix_tokens=int(arena.evicted_prefix_tokens))
+
+
+def run_reference_retention(name):
+    from quail.backends.quail.executor import loop
+    from quail.backends.quail.executor.arena import KVArena
+    from quail.backends.quail.executor.models.base import ModelPipeline
+    from quail.backends.quail.retention import apply_retention, retain_after_join
+    from quail.execution.tokens import prefix_tree
+
+    _cpu_staging(loop)
+    (docs, question, frame, partners, budget, pages, attention, config, uses,
+     after) = retention_inputs(name)
+    arena = KVArena(1, pages, 16, 1, 8, dtype=torch.bfloat16, device="cpu")
+    arena.reset_stats()
+    arrays, entries = {}, []
+
+    class Recorder(ModelPipeline):
+        tree_attention = True
+
+        def forward_chunk(self, chunk):
+            entries.append(chunk_record(chunk, arrays, len(entries)))
+            return chunk
+
+    class Answers:
+        dtype = None
+
+        def submit(self, chunk):
+            return answer_bits(chunk.input_ids, chunk.positions, chunk.final_indices)
+
+        def result(self, handle):
+            return handle
+
+    keys = [("d", i) for i in range(len(docs))]
+    f_answers, _, f_tokens = loop.run_filter(
+        _Torch(), arena, Recorder(), Answers(), docs, [question], budget, pinned=False,
+        arena_writes=True, arena_keys=keys, retain_survivors=True, attention_mode=attention,
+        prefix_tree=prefix_tree(docs, 16))
+    n_filter_chunks = len(entries)
+    after_filter = arena_state(arena)
+    survivors = sorted(d for d, row in f_answers.items() if row and row[-1])
+    apply_retention(arena, config, uses, survivors={"d": survivors[:-2]})
+    after_boundary = arena_state(arena)
+    anchors = [docs[d] for d in survivors]
+    akeys = [keys[d] for d in survivors]
+
+    def anchor_done(a, row):
+        if any(row):
+            retain_after_join(arena, akeys[a], len(anchors[a]), config, after)
+        else:
+            arena.free_key(akeys[a])
+
+    j_answers, _, j_tokens = loop.run_join(
+        _Torch(), arena, Recorder(), Answers(), anchors, [partners], budget,
+        stage_frames=[frame], anchor_keys=akeys, anchor_done=anchor_done,
+        attention_mode=attention)
+    summary = dict(name=name, chunks=entries, n_filter_chunks=n_filter_chunks,
+                   filter_tokens=int(f_tokens), join_tokens=int(j_tokens),
+                   filter_answers={str(k): v for k, v in sorted(f_answers.items())},
+                   survivors=survivors,
+                   join_answers=[{str(a): [float(x) for x in row] for a, row in sorted(st.items())}
+                                 for st in j_answers],
+                   after_filter=after_filter, after_boundary=after_boundary,
+                   after_join=arena_state(arena))
+    np.savez_compressed(HERE / f"host_{name}.npz", **arrays)
+    (HERE / f"host_{name}.json").write_text(json.dumps(summary, separators=(",", ":")))
+    return summary
+
+
 # ---- token store (quail/execution/tokens.py:180-359) ---------------------------
 
 def make_token_store():
@@ -604,6 +703,11 @@ def main():
             continue
         summary = run_reference_feed(name)
         print(name, "chunks", len(summary["chunks"]), "anchors", len(summary["keys"]))
+    for name in RETAIN_SCENARIOS:
+        if only and name not in only:
+            continue
+        summary = run_reference_retention(name)
+        print(name, "chunks", len(summary["chunks"]), "after join", summary["after_join"])
     if not only or "token_store" in only:
         make_token_store()
         print("token_store.arrow written")

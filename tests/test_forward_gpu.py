@@ -375,3 +375,33 @@ def test_tiny_filter_feeding_join_matches_oracle():
         g = next(got[kind])
         assert np.array_equal(g.view(np.int32), want.astype(np.float32).view(np.int32)), kind
     assert not arena.accounting.owned
+
+
+def test_retained_survivors_feed_a_join_like_fresh_anchors():
+    """Retention between operators on the GPU: a filter keeps its survivors'
+    KV (retain_survivors), and a join over them reads that resident KV
+    instead of recomputing the prefixes. The join's answers equal a join
+    whose anchors are computed fresh, with fewer fresh tokens."""
+    from quail_b200.api import B200Executor
+    from quail_b200.retention import apply_retention
+
+    cfg = TINY
+    docs, questions = rows_with_prefix(9, 24, 48, 16, 120, 16, cfg.vocab)
+    partners = [list(np.random.default_rng(4).integers(16, cfg.vocab, n)) for n in (9, 17, 12)]
+    ex = B200Executor(torch, cfg, 600, seed=1)
+    keys = [("d", i) for i in range(len(docs))]
+    res = ex.filter(docs, questions, keys=keys, retain_survivors=True, budget=1200)
+    survivors = [d for d in range(len(docs)) if res.bits[d]]
+    assert survivors and set(k[1] for k in ex.arena.retained_keys()) <= set(survivors)
+    config = {"linear_seconds": 1e-6, "pair_seconds": 1e-9, "cap_pages": ex.arena.n_pages}
+    apply_retention(ex.arena, config, {"d": (1.0, 1)}, survivors={"d": survivors})
+    resident = [d for d in survivors if ex.arena.is_resident(keys[d])]
+    assert resident
+    anchors = [docs[d] for d in survivors]
+    warm = ex.join(anchors, [partners], budget=1200, anchor_keys=[keys[d] for d in survivors],
+                   share_prefixes=False)
+    ex.reset_arena()
+    cold = ex.join(anchors, [partners], budget=1200, share_prefixes=False)
+    assert warm.answers == cold.answers
+    assert warm.fresh_tokens < cold.fresh_tokens
+    assert nat.kernel_status(torch.cuda.current_device()) == 0

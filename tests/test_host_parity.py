@@ -442,3 +442,104 @@ def test_filter_feeding_join_matches_reference(name):
     assert tokens == want["tokens"] and source.tokens == want["source_tokens"]
     assert arena.free_pages == want["free_pages_after"]
 
+
+
+@pytest.mark.parametrize("name", mg.RETAIN_SCENARIOS)
+def test_retention_between_operators_matches_reference(name):
+    """KV retention across operators (arena retention, FilterStream
+    retain_survivors, quail_b200.retention): a filter whose survivors stay
+    resident (evicted past the cap in priority order), a boundary that frees
+    the survivors no later operator reads and re-prioritises the rest, and a
+    join over every survivor (the retained ones resident, so their prefixes
+    are not recomputed; admission evicting retained KV when short of pages)
+    whose matching anchors are retained again. Chunks of both loops, the
+    answers and the arena's retained keys, free pages and eviction counters
+    after each phase equal the reference's."""
+    from quail_b200.retention import apply_retention, retain_after_join
+
+    (docs, question, frame, partners, budget, pages, attention, config, uses,
+     after) = mg.retention_inputs(name)
+    want = json.loads((GOLDEN / f"host_{name}.json").read_text())
+    want_arrays = np.load(GOLDEN / f"host_{name}.npz")
+    arena = KVArena(1, pages, 16, 1, 8, device=None)
+    arrays, entries = {}, []
+
+    class Recorder(ModelPipeline):
+        tree_attention = True
+
+        def forward_chunk(self, chunk):
+            entries.append(mg.chunk_record(chunk.host, arrays, len(entries)))
+            return chunk.host
+
+    class Answers:
+        dtype = None
+
+        def submit(self, host):
+            return mg.answer_bits(host.input_ids, host.positions, host.final_indices)
+
+        def result(self, handle):
+            return handle
+
+    keys = [("d", i) for i in range(len(docs))]
+    f_answers, _, f_tokens = loop.run_filter(
+        torch, arena, Recorder(), Answers(), docs, [question], budget, arena_writes=True,
+        arena_keys=keys, retain_survivors=True, attention_mode=attention,
+        prefix_tree=prefix_tree(docs, 16), device="cpu")
+    assert len(entries) == want["n_filter_chunks"]
+    assert mg.arena_state(arena) == want["after_filter"]
+    survivors = sorted(d for d, row in f_answers.items() if row and row[-1])
+    assert survivors == want["survivors"]
+    apply_retention(arena, config, uses, survivors={"d": survivors[:-2]})
+    assert mg.arena_state(arena) == want["after_boundary"]
+    anchors = [docs[d] for d in survivors]
+    akeys = [keys[d] for d in survivors]
+
+    def anchor_done(a, row):
+        if any(row):
+            retain_after_join(arena, akeys[a], len(anchors[a]), config, after)
+        else:
+            arena.free_key(akeys[a])
+
+    j_answers, _, j_tokens = loop.run_join(
+        torch, arena, Recorder(), Answers(), anchors, [partners], budget,
+        stage_frames=[frame], anchor_keys=akeys, anchor_done=anchor_done,
+        attention_mode=attention, device="cpu")
+    assert entries == want["chunks"]
+    assert sorted(arrays) == sorted(want_arrays.files)
+    for key in want_arrays.files:
+        assert np.array_equal(arrays[key].astype(np.int64), want_arrays[key].astype(np.int64)), key
+    assert {str(k): v for k, v in sorted(f_answers.items())} == want["filter_answers"]
+    assert [{str(a): [float(x) for x in row] for a, row in sorted(st.items())}
+            for st in j_answers] == want["join_answers"]
+    assert (f_tokens, j_tokens) == (want["filter_tokens"], want["join_tokens"])
+    assert mg.arena_state(arena) == want["after_join"]
+
+
+def test_retention_priority_and_rewind():
+    """Unit checks of the retention rules on the accounting alone: a
+    retained key rewinds to its prefix, eviction takes the lowest priority
+    first, a held key is passed over, pinning withdraws a key and the cap
+    evicts on retain."""
+    from quail_b200.retention import RetentionPolicy, causal_pairs
+
+    assert causal_pairs(4) == 10 and causal_pairs(10, 4) == 4 * 10 - 6
+    arena = KVArena(1, 20, 16, 1, 8, device=None)
+    for i, n in enumerate((40, 64, 20)):
+        assert arena.activate(("d", i), n, capacity_tokens=n + 30) is not None
+    free0 = arena.free_pages
+    assert arena.retain(("d", 0), 40) == 2  # 70 capacity tokens: 5 pages; 40 tokens: 3
+    arena.retain(("d", 1), 64)
+    arena.retain(("d", 2), 20)
+    assert arena.free_pages > free0
+    assert sorted(arena.retained_keys()) == [("d", 0), ("d", 1), ("d", 2)]
+    # tokens per page: d0 40/3, d1 64/4, d2 20/2 -> d2 goes first, then d0
+    arena.hold(("d", 2), 1)
+    assert arena.evict_retained(1) == (("d", 0),)
+    arena.drop_holds([("d", 2)])
+    arena.pin(("d", 1))
+    assert arena.retained_keys() == [("d", 2)]
+    arena.configure_retention(RetentionPolicy(1e-6, 1e-9, {"d": (1.0, 1)}), 0)
+    assert arena.evict_retained(arena.retained_pages) == (("d", 2),)
+    assert arena.evicted_keys == 2 and arena.retained_pages == 0
+    with pytest.raises(TypeError):
+        arena.retain(7, 10)
