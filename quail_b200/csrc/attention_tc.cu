@@ -16,12 +16,12 @@
 //
 // Block: 64 query rows of one cu_a segment x 4 query heads of one KV head
 // (2 when the GQA group is 2) as two M=128 tiles (rows 0-63 one head, rows
-// 64-127 the next) that share every K/V tile. 15 warps:
+// 64-127 the next) that share every K/V tile. 11 warps:
 //   warp 0       TMA loader: each item's call list, Q once, then K tiles of
 //                64 keys into a 2-stage ring - the segment's own keys as
 //                contiguous rows, the resident keys one box per page through
 //                the block table;
-//   warp 14      TMA loader of the V tiles, the same way, into a 3-stage ring
+//   warp 10      TMA loader of the V tiles, the same way, into a 3-stage ring
 //                (its own warp, so a V tile is requested as soon as its slot
 //                frees: the loads take several microseconds to land);
 //   warp 1       TMEM allocator and MMA issuer: S = Q K^T into one of two
@@ -33,12 +33,13 @@
 //                NaN);
 //   warps 2-9    softmax, one thread per row of an M tile: S from TMEM (read
 //                twice: the row max, then exp2), bf16 P written back over the
-//                tile's S (tcgen05.st), alpha to shared memory; after each
-//                call the same thread's epilogue: the normalised call-B
-//                output (bf16, kept in shared memory), or the merge, the
-//                quantisation and the fp8 store;
-//   warps 10-13  correction, one thread per row of each M tile: O *= alpha in
-//                TMEM between P V steps.
+//                tile's S (tcgen05.st), then the row's O *= alpha in TMEM
+//                once the previous P V is done (the thread's own rescale: a
+//                separate correction warp set, handling both M tiles in turn
+//                behind a barrier per tile, held each P V about 2.6 us after
+//                its P was ready); after each call the same thread's
+//                epilogue: the normalised call-B output (bf16, kept in shared
+//                memory), or the merge, the quantisation and the fp8 store.
 // TMEM (512 columns): O [2 M tiles][128] | S [2 M tiles][2 buffers][64], the
 // first 32 columns of an S buffer holding that tile's P once computed.
 // The K and V rings cost one MMA issue each per tile; a tcgen05.mma of
@@ -61,8 +62,8 @@ constexpr int KT = 64;  // keys per tile
 constexpr int KST = 2;  // K stages: a K tile is free once its S MMAs are done
 constexpr int VST = 3;  // V stages: a V tile is free once its P V MMAs are done
 constexpr int MAX_CALLS = QR + 1;
-constexpr int FIRST_SOFT = 2, FIRST_CORR = 10, V_WARP = 14;
-constexpr int NUM_THREADS = 15 * 32;
+constexpr int FIRST_SOFT = 2, V_WARP = 10;
+constexpr int NUM_THREADS = 11 * 32;
 
 constexpr int Q_BYTES = 2 * 2 * 128 * 128;  // [mt][half][128 rows][128 B]
 constexpr int KV_HALF = 64 * 128;           // [64 keys][64 dims]
@@ -103,7 +104,6 @@ struct Aux {
     uint64_t q_full, q_empty;
     uint64_t info_full[2], info_empty[2];
     uint64_t k_full[KST], k_empty[KST], v_full[VST], v_empty[VST];
-    uint64_t o_ready[2];
     // per S/P buffer (tile parity) and M tile; phase = tile / 2, so a producer
     // can only complete a buffer's next phase after every waiter observed
     // the previous one (a parity wait needs that)
@@ -111,7 +111,6 @@ struct Aux {
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
-    float alpha[2][2][128];  // [buffer][mt][row]
     Info info[2];
 };
 
@@ -190,9 +189,9 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
         mbar_init(&aux->q_empty, 1);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&aux->info_full[b], 1);
-            // released by the MMA warp, the active softmax warps and the
-            // correction warps
-            mbar_init(&aux->info_empty[b], 1 + 4 * nmt + 4 + 1);
+            // released by the MMA warp, the active softmax warps and the V
+            // loader
+            mbar_init(&aux->info_empty[b], 1 + 4 * nmt + 1);
         }
         for (int st = 0; st < KST; ++st) {
             mbar_init(&aux->k_full[st], 1);
@@ -209,7 +208,6 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             mbar_init(&aux->p_full[1][m], 4);
             mbar_init(&aux->pv_done[0][m], 1);
             mbar_init(&aux->pv_done[1][m], 1);
-            mbar_init(&aux->o_ready[m], 4);
         }
         mbar_init(&aux->drain, 1);
         aux->abort = 0;
@@ -496,8 +494,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             int r = 0;
             if (lane == 0)
                 r = mbar_test_wait(smem_u32(&aux->v_full[g % VST]), (uint32_t)(g / VST) & 1u) &&
-                    mbar_test_wait(smem_u32(&aux->p_full[g & 1][mt]), (uint32_t)(g >> 1) & 1u) &&
-                    mbar_test_wait(smem_u32(&aux->o_ready[mt]), (uint32_t)g & 1u);
+                    mbar_test_wait(smem_u32(&aux->p_full[g & 1][mt]), (uint32_t)(g >> 1) & 1u);
             return __shfl_sync(0xffffffffu, r, 0) != 0;
         };
         // issues the S cursor's tile when ready; returns false on give-up
@@ -669,7 +666,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                 mbar_drain(&aux->v_full[j % VST], (uint32_t)(j / VST) & 1u, status,
                            STATUS_ATTN_LOAD);
         }
-    } else if (warp < FIRST_CORR) {
+    } else {
         // ------- softmax, then each call's epilogue: one thread per row of an M tile -------
         const int mt = (warp - FIRST_SOFT) >> 2;
         if (mt < nmt) {
@@ -782,9 +779,41 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                             // (already read: this chunk's S is in registers)
                             tmem_st8(s_addr + (uint32_t)(c0 >> 1), pk);
                         }
+                        if (t > 0) {
+                            // O *= alpha before this tile's P V, once the P V
+                            // before it (the last to write O) is done
+                            if (!mbar_wait(&aux->pv_done[(g - 1) & 1][mt],
+                                           (uint32_t)((g - 1) >> 1) & 1u, abort_flag, status,
+                                           STATUS_ATTN_SOFTMAX)) {
+                                tmem_wait_st();
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+                                const uint64_t a2 = f2pack(alpha, alpha);
+#pragma unroll 1
+                                for (int c0 = 0; c0 < D; c0 += 32) {
+                                    uint32_t r[32];
+                                    tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
+                                    tmem_wait_ld();
+#pragma unroll
+                                    for (int j = 0; j < 32; j += 2) {
+                                        float x, y;
+                                        f2unpack(f2mul(f2pack(__uint_as_float(r[j]),
+                                                              __uint_as_float(r[j + 1])),
+                                                       a2),
+                                                 x, y);
+                                        r[j] = __float_as_uint(x);
+                                        r[j + 1] = __float_as_uint(y);
+                                    }
+                                    tmem_st32(o_addr + (uint32_t)c0, r);
+                                }
+                            }
+                        }
+                        // P (and O rescaled) stored before the P V reads them
                         tmem_wait_st();
                         tc_fence_before();
-                        aux->alpha[g & 1][mt][i] = alpha;
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&aux->p_full[g & 1][mt]);
                     }
@@ -936,72 +965,6 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&aux->info_empty[slot]);
             }
-        }
-    } else {
-        // ---------------- correction: O *= alpha between P V steps ----------------
-        const int q4 = warp & 3;
-        const int i = q4 * 32 + lane;
-        const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-        int g = 0;
-        bool ok = true;
-        for (int item = blockIdx.x, k = 0; item < n_items && ok; item += gridDim.x, ++k) {
-            const int slot = k & 1;
-            if (!mbar_wait(&aux->info_full[slot], (uint32_t)(k >> 1) & 1u, abort_flag, status,
-                           STATUS_ATTN_CORRECTION))
-                break;
-            const Info* inf = &aux->info[slot];
-            const int n_calls = inf->n_calls;
-            for (int c = 0; c < n_calls && ok; ++c) {
-                const int n_t = inf->calls[c].n_tiles;
-                for (int t = 0; t < n_t && ok; ++t, ++g) {
-                    for (int mt = 0; mt < nmt; ++mt) {
-                        // every p_full phase is waited for (a parity wait is only
-                        // sound when the waiter is at most one phase behind)
-                        if (!mbar_wait(&aux->p_full[g & 1][mt], (uint32_t)(g >> 1) & 1u, abort_flag,
-                                       status, STATUS_ATTN_CORRECTION)) {
-                            ok = false;
-                            break;
-                        }
-                        if (t > 0) {
-                            if (!mbar_wait(&aux->pv_done[(g - 1) & 1][mt],
-                                           (uint32_t)((g - 1) >> 1) & 1u, abort_flag, status,
-                                           STATUS_ATTN_CORRECTION)) {
-                                ok = false;
-                                break;
-                            }
-                            tc_fence_after();
-                            const float a = aux->alpha[g & 1][mt][i];
-                            if (__any_sync(0xffffffffu, a != 1.0f)) {
-                                const uint64_t a2 = f2pack(a, a);
-                                const uint32_t o_addr = tmem + lane_off + TM_O + (uint32_t)(mt * 128);
-#pragma unroll 1
-                                for (int c0 = 0; c0 < D; c0 += 32) {
-                                    uint32_t r[32];
-                                    tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
-                                    tmem_wait_ld();
-#pragma unroll
-                                    for (int j = 0; j < 32; j += 2) {
-                                        float x, y;
-                                        f2unpack(f2mul(f2pack(__uint_as_float(r[j]),
-                                                              __uint_as_float(r[j + 1])),
-                                                       a2),
-                                                 x, y);
-                                        r[j] = __float_as_uint(x);
-                                        r[j + 1] = __float_as_uint(y);
-                                    }
-                                    tmem_st32(o_addr + (uint32_t)c0, r);
-                                }
-                                tmem_wait_st();
-                            }
-                        }
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&aux->o_ready[mt]);
-                    }
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&aux->info_empty[slot]);
         }
     }
 
