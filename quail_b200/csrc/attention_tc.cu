@@ -16,7 +16,7 @@
 //
 // Block: 64 query rows of one cu_a segment x 4 query heads of one KV head
 // (2 when the GQA group is 2) as two M=128 tiles (rows 0-63 one head, rows
-// 64-127 the next) that share every K/V tile. 11 warps:
+// 64-127 the next) that share every K/V tile. 12 warps:
 //   warp 0       TMA loader: each item's call list, Q once, then K tiles of
 //                64 keys into a 2-stage ring - the segment's own keys as
 //                contiguous rows, the resident keys one box per page through
@@ -24,13 +24,18 @@
 //   warp 10      TMA loader of the V tiles, the same way, into a 3-stage ring
 //                (its own warp, so a V tile is requested as soon as its slot
 //                frees: the loads take several microseconds to land);
-//   warp 1       TMEM allocator and MMA issuer: S = Q K^T into one of two
+//   warp 1       TMEM allocator and S issuer: S = Q K^T into one of two
 //                TMEM buffers per M tile, so the next tile's S runs while the
-//                softmax works on this one; then O += P V with P read from
-//                TMEM (the A operand) and V read MN-major from shared
-//                memory; it also zeroes the V rows of a paged tile past the
-//                last key (pool rows there may hold anything, and 0 * NaN is
-//                NaN);
+//                softmax works on this one;
+//   warp 11      P V issuer: O += P V with P read from TMEM (the A operand)
+//                and V read MN-major from shared memory, as soon as an M
+//                tile's P is written; it also zeroes the V rows of a paged
+//                tile past the last key (pool rows there may hold anything,
+//                and 0 * NaN is NaN). Two issuers, each waiting on one
+//                barrier at a time: one thread polling both kinds of work
+//                took 300-600 cycles a step and sat about 2,000 cycles in
+//                each tile's 16 S issues, so each P V went out 2-4k cycles
+//                after its P;
 //   warps 2-9    softmax, one thread per row of an M tile: S from TMEM (read
 //                twice: the row max, then exp2), bf16 P written back over the
 //                tile's S (tcgen05.st), then the row's O *= alpha in TMEM
@@ -42,13 +47,13 @@
 //                memory), or the merge, the quantisation and the fp8 store.
 // TMEM (512 columns): O [2 M tiles][128] | S [2 M tiles][2 buffers][64], the
 // first 32 columns of an S buffer holding that tile's P once computed.
-// The K and V rings cost one MMA issue each per tile; a tcgen05.mma of
-// M=128, K=16 takes about 26 ns at N=64 and 35 ns at N=128 (measured), and
-// the issuing thread waits for each, so the S of the next tile is issued as
-// soon as its buffer frees rather than after the softmax of this one.
+// A tcgen05.mma of M=128, K=16 takes about 26 ns at N=64 and 35 ns at
+// N=128 on an idle SM (measured), and the issuing thread waits for each, so
+// the S of the next tile is issued as soon as its buffer frees rather than
+// after the softmax of this one.
 // Every wait is bounded (about a second): a wait that gives up sets a status
 // bit and the abort flag, the other roles stop at their next wait, the MMA
-// issuer drains its MMAs and the loaders their copies before TMEM is freed.
+// issuers drain their MMAs and the loaders their copies before TMEM is freed.
 #include "tc_common.cuh"
 
 namespace qb {
@@ -62,8 +67,8 @@ constexpr int KT = 64;  // keys per tile
 constexpr int KST = 2;  // K stages: a K tile is free once its S MMAs are done
 constexpr int VST = 3;  // V stages: a V tile is free once its P V MMAs are done
 constexpr int MAX_CALLS = QR + 1;
-constexpr int FIRST_SOFT = 2, V_WARP = 10;
-constexpr int NUM_THREADS = 11 * 32;
+constexpr int FIRST_SOFT = 2, V_WARP = 10, PV_WARP = 11;
+constexpr int NUM_THREADS = 12 * 32;
 
 constexpr int Q_BYTES = 2 * 2 * 128 * 128;  // [mt][half][128 rows][128 B]
 constexpr int KV_HALF = 64 * 128;           // [64 keys][64 dims]
@@ -108,7 +113,7 @@ struct Aux {
     // can only complete a buffer's next phase after every waiter observed
     // the previous one (a parity wait needs that)
     uint64_t s_full[2][2], p_full[2][2], pv_done[2][2];
-    uint64_t drain;
+    uint64_t drain[2];  // [S issuer, P V issuer]
     uint32_t tmem_base;
     int abort;
     Info info[2];
@@ -189,9 +194,9 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
         mbar_init(&aux->q_empty, 1);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&aux->info_full[b], 1);
-            // released by the MMA warp, the active softmax warps and the V
-            // loader
-            mbar_init(&aux->info_empty[b], 1 + 4 * nmt + 1);
+            // released by the S issuer, the active softmax warps, the V
+            // loader and the P V issuer
+            mbar_init(&aux->info_empty[b], 1 + 4 * nmt + 1 + 1);
         }
         for (int st = 0; st < KST; ++st) {
             mbar_init(&aux->k_full[st], 1);
@@ -209,7 +214,8 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             mbar_init(&aux->pv_done[0][m], 1);
             mbar_init(&aux->pv_done[1][m], 1);
         }
-        mbar_init(&aux->drain, 1);
+        mbar_init(&aux->drain[0], 1);
+        mbar_init(&aux->drain[1], 1);
         aux->abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -401,209 +407,128 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                            STATUS_ATTN_LOAD);
         }
     } else if (warp == 1) {
-        // ------ MMA issuer (lane 0 issues; the warp zeroes V tails): S of the
-        // next tile (possibly the next item's first) and P V of this tile, each
-        // as soon as its inputs are ready ------
+        // ------ S issuer (lane 0): S = Q K^T of each tile in order, into
+        // the tile's S buffer (g & 1) once the P V two tiles back, which
+        // read the P written over it, is done ------
         const uint32_t q_base = smem_u32(smem);
-        bool ok = true;
-        // S cursor: item ks (local index), call cs, tile ts; gs = tiles issued;
-        // jq = items with tiles whose Q the S cursor consumed
-        int s_item = blockIdx.x, ks = 0, cs = 0, ts = 0, gs = 0, jq = 0;
-        bool s_have_info = false;  // the S cursor's item info is acquired
-        // moves the S cursor to its next tile; false when the items are done
-        // or a wait gave up. Blocking only when told so.
-        auto s_seek = [&](bool block, bool& ready) -> bool {
-            ready = false;
-            while (s_item < n_items) {
-                const int slot = ks & 1;
-                if (!s_have_info) {
-                    int r = 1;
-                    if (lane == 0) {
-                        if (block)
-                            r = mbar_wait(&aux->info_full[slot], (uint32_t)(ks >> 1) & 1u,
-                                          abort_flag, status, STATUS_ATTN_MMA) ? 1 : -1;
-                        else
-                            r = mbar_try_wait(smem_u32(&aux->info_full[slot]),
-                                              (uint32_t)(ks >> 1) & 1u) ? 1 : 0;
-                    }
-                    r = __shfl_sync(0xffffffffu, r, 0);
-                    if (r < 0) return false;
-                    if (r == 0) return true;  // not yet: try again later
-                    s_have_info = true;
-                    cs = 0;
-                    ts = 0;
-                }
+        if (lane == 0) {
+            int gs = 0, jq = 0;
+            bool ok = true;
+            for (int item = blockIdx.x, k = 0; item < n_items && ok; item += gridDim.x, ++k) {
+                const int slot = k & 1;
+                if (!mbar_wait(&aux->info_full[slot], (uint32_t)(k >> 1) & 1u, abort_flag, status,
+                               STATUS_ATTN_MMA))
+                    break;
                 const Info* inf = &aux->info[slot];
-                while (cs < inf->n_calls && ts >= inf->calls[cs].n_tiles) {
-                    ++cs;
-                    ts = 0;
-                }
-                if (cs < inf->n_calls) {
-                    ready = true;
-                    return true;
-                }
-                s_item += gridDim.x;
-                ++ks;
-                s_have_info = false;
-            }
-            return true;
-        };
-        auto s_issue = [&]() {
-            const Info* inf = &aux->info[ks & 1];
-            const int st = gs % KST;
-            const uint32_t k_base = smem_u32(smem + OFF_K + st * KV_TILE);
-            tc_fence_after();
-            if (lane == 0) {
-                for (int mt = 0; mt < nmt; ++mt) {
-                    const uint32_t s_tm = tmem + TM_S + (uint32_t)(mt * 128 + (gs & 1) * 64);
+                const int n_calls = inf->n_calls, total = inf->total_tiles;
+                for (int c = 0, j = 0; c < n_calls && ok; ++c) {
+                    const int n_t = inf->calls[c].n_tiles;
+                    for (int t = 0; t < n_t; ++t, ++gs, ++j) {
+                        // the item's Q, the tile's K, and its S buffer
+                        if (j == 0)
+                            ok = mbar_wait(&aux->q_full, (uint32_t)(jq++) & 1u, abort_flag, status,
+                                           STATUS_ATTN_MMA);
+                        if (ok)
+                            ok = mbar_wait(&aux->k_full[gs % KST], (uint32_t)(gs / KST) & 1u,
+                                           abort_flag, status, STATUS_ATTN_MMA);
+                        for (int mt = 0; mt < nmt && ok && gs > 1; ++mt)
+                            ok = mbar_wait(&aux->pv_done[gs & 1][mt], (uint32_t)((gs - 2) >> 1) & 1u,
+                                           abort_flag, status, STATUS_ATTN_MMA);
+                        if (!ok) break;
+                        tc_fence_after();
+                        const uint32_t k_base = smem_u32(smem + OFF_K + (gs % KST) * KV_TILE);
+                        for (int mt = 0; mt < nmt; ++mt) {
+                            const uint32_t s_tm = tmem + TM_S + (uint32_t)(mt * 128 + (gs & 1) * 64);
 #pragma unroll
-                    for (int kk = 0; kk < D / 16; ++kk)
-                        mma_bf16_ss(s_tm, q_desc(q_base, mt, kk), k_desc(k_base, kk), IDESC_S,
-                                    kk > 0 ? 1u : 0u);
-                    mma_commit(&aux->s_full[gs & 1][mt]);
+                            for (int kk = 0; kk < D / 16; ++kk)
+                                mma_bf16_ss(s_tm, q_desc(q_base, mt, kk), k_desc(k_base, kk), IDESC_S,
+                                            kk > 0 ? 1u : 0u);
+                            mma_commit(&aux->s_full[gs & 1][mt]);
+                        }
+                        mma_commit(&aux->k_empty[gs % KST]);  // the K tile is free once these are done
+                        // the item's last S: Q may be reloaded once these are done
+                        if (j == total - 1) mma_commit(&aux->q_empty);
+                    }
                 }
-                mma_commit(&aux->k_empty[st]);  // the K tile is free once these are done
+                // done with the item's info (its S MMAs are all issued)
+                mbar_arrive(&aux->info_empty[slot]);
             }
-            ++gs;
-            ++ts;
-            // the item's last S: Q may be reloaded once these MMAs are done
-            int c = cs, t = ts;
-            while (c < inf->n_calls && t >= inf->calls[c].n_tiles) {
-                ++c;
-                t = 0;
-            }
-            if (c >= inf->n_calls && lane == 0) mma_commit(&aux->q_empty);
-            __syncwarp();
-        };
-        // S of the cursor's tile can go: its item's Q, its K tile, and its S
-        // buffer (gs & 1), free once the P V two tiles back, which read the P
-        // written over it, is done
-        auto s_ready = [&]() -> bool {
-            int r = 1;
-            if (lane == 0) {
-                if (ts == 0 && cs == 0)  // the item's first S: its Q
-                    r = mbar_test_wait(smem_u32(&aux->q_full), (uint32_t)jq & 1u);
-                if (r) r = mbar_test_wait(smem_u32(&aux->k_full[gs % KST]), (uint32_t)(gs / KST) & 1u);
-                for (int mt = 0; mt < nmt && r && gs > 1; ++mt)
-                    r = mbar_test_wait(smem_u32(&aux->pv_done[gs & 1][mt]),
-                                       (uint32_t)((gs - 2) >> 1) & 1u);
-            }
-            return __shfl_sync(0xffffffffu, r, 0) != 0;
-        };
-        auto pv_ready = [&](int g, int mt) -> bool {
+            // every MMA issued must finish before TMEM is freed
+            mma_commit(&aux->drain[0]);
+            mbar_drain(&aux->drain[0], 0, status, STATUS_ATTN_MMA);
+        }
+    } else if (warp == PV_WARP) {
+        // ------ P V issuer (lane 0 issues; the warp zeroes V tails): O += P V
+        // of each tile and M tile in order, with P read from TMEM (the A
+        // operand, bf16 over the tile's S) and V MN-major from shared
+        // memory, as soon as that M tile's P is written ------
+        // lane 0 waits, the warp follows its verdict
+        auto wait0 = [&](uint64_t* bar, uint32_t parity) -> bool {
             int r = 0;
-            if (lane == 0)
-                r = mbar_test_wait(smem_u32(&aux->v_full[g % VST]), (uint32_t)(g / VST) & 1u) &&
-                    mbar_test_wait(smem_u32(&aux->p_full[g & 1][mt]), (uint32_t)(g >> 1) & 1u);
+            if (lane == 0) r = mbar_wait(bar, parity, abort_flag, status, STATUS_ATTN_MMA) ? 1 : 0;
             return __shfl_sync(0xffffffffu, r, 0) != 0;
-        };
-        // issues the S cursor's tile when ready; returns false on give-up
-        auto try_s = [&](bool block, bool& issued) -> bool {
-            issued = false;
-            bool ready;
-            if (!s_seek(block, ready)) return false;
-            if (!ready || !s_ready()) return true;
-            if (ts == 0 && cs == 0) ++jq;
-            s_issue();
-            issued = true;
-            return true;
         };
         int g = 0;
+        bool ok = true;
         for (int item = blockIdx.x, k = 0; item < n_items && ok; item += gridDim.x, ++k) {
             const int slot = k & 1;
-            if (!mbar_wait(&aux->info_full[slot], (uint32_t)(k >> 1) & 1u, abort_flag, status,
-                           STATUS_ATTN_MMA)) {
-                ok = false;
-                break;
-            }
+            if (!wait0(&aux->info_full[slot], (uint32_t)(k >> 1) & 1u)) break;
             const Info* inf = &aux->info[slot];
             const int n_calls = inf->n_calls;
             for (int c = 0; c < n_calls && ok; ++c) {
                 const Call cl = inf->calls[c];
-                for (int t = 0; t < cl.n_tiles; ++t, ++g) {
+                for (int t = 0; t < cl.n_tiles && ok; ++t, ++g) {
                     const int st = g % VST;
                     uint8_t* vd = smem + OFF_V + st * KV_TILE;
                     const uint32_t v_base = smem_u32(vd);
-                    bool pv_issued[2] = {nmt < 1, nmt < 2};
-                    bool zeroed = false;
-                    uint64_t t0 = 0;
-                    for (uint32_t spins = 0; !(pv_issued[0] && pv_issued[1]); ++spins) {
-                        bool progress = false;
-                        // S runs at most one tile ahead of P V: S(g) first, then S(g + 1)
-                        if (gs <= g + 1) {
-                            bool issued;
-                            if (!try_s(gs <= g, issued)) {
-                                ok = false;
-                                break;
-                            }
-                            progress |= issued;
+                    if (!wait0(&aux->v_full[st], (uint32_t)(g / VST) & 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    const int valid = cl.n_keys - t * KT;
+                    if (cl.kind != CALL_OWN && valid < KT) {
+                        // the V rows past the last key: zeros (pool rows there
+                        // may hold anything, and 0 * NaN is NaN)
+                        const int first = valid < 0 ? 0 : valid;
+                        for (int idx = first * 8 + lane; idx < KT * 8; idx += 32) {
+                            const int r = idx >> 3, ch = idx & 7;
+                            *reinterpret_cast<uint4*>(vd + r * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+                            *reinterpret_cast<uint4*>(vd + KV_HALF + r * 128 + ch * 16) =
+                                make_uint4(0, 0, 0, 0);
                         }
-                        for (int mt = 0; mt < nmt && gs > g; ++mt) {
-                            if (pv_issued[mt] || !pv_ready(g, mt)) continue;
-                            const int valid = cl.n_keys - t * KT;
-                            if (!zeroed && cl.kind != CALL_OWN && valid < KT) {
-                                // the V rows past the last key: zeros (the tile
-                                // landed: pv_ready waited for it)
-                                const int first = valid < 0 ? 0 : valid;
-                                for (int idx = first * 8 + lane; idx < KT * 8; idx += 32) {
-                                    const int r = idx >> 3, ch = idx & 7;
-                                    *reinterpret_cast<uint4*>(vd + r * 128 + ch * 16) =
-                                        make_uint4(0, 0, 0, 0);
-                                    *reinterpret_cast<uint4*>(vd + KV_HALF + r * 128 + ch * 16) =
-                                        make_uint4(0, 0, 0, 0);
-                                }
-                                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                                __syncwarp();
-                            }
-                            zeroed = true;
-                            tc_fence_after();
-                            if (lane == 0) {
-                                // A = P (bf16, two keys a column) in TMEM over S
-                                const uint32_t p_tm = tmem + TM_S + (uint32_t)(mt * 128 + (g & 1) * 64);
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        __syncwarp();
+                    }
+                    for (int mt = 0; mt < nmt; ++mt) {
+                        if (!wait0(&aux->p_full[g & 1][mt], (uint32_t)(g >> 1) & 1u)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        if (lane == 0) {
+                            // A = P (bf16, two keys a column) in TMEM over S
+                            const uint32_t p_tm = tmem + TM_S + (uint32_t)(mt * 128 + (g & 1) * 64);
 #pragma unroll
-                                for (int kk = 0; kk < KT / 16; ++kk)
-                                    mma_bf16_ts(tmem + TM_O + (uint32_t)(mt * 128), p_tm + (uint32_t)(kk * 8),
-                                                v_desc(v_base, kk), IDESC_PV,
-                                                (t > 0 || kk > 0) ? 1u : 0u);
-                                mma_commit(&aux->pv_done[g & 1][mt]);
-                            }
-                            __syncwarp();
-                            pv_issued[mt] = true;
-                            progress = true;
+                            for (int kk = 0; kk < KT / 16; ++kk)
+                                mma_bf16_ts(tmem + TM_O + (uint32_t)(mt * 128), p_tm + (uint32_t)(kk * 8),
+                                            v_desc(v_base, kk), IDESC_PV, (t > 0 || kk > 0) ? 1u : 0u);
+                            mma_commit(&aux->pv_done[g & 1][mt]);
                         }
-                        if (!progress && (spins & 255u) == 255u) {
-                            // bounded: give up after the timeout or when another role did
-                            int stop = 0;
-                            if (lane == 0) {
-                                const uint64_t now = globaltimer();
-                                if (t0 == 0) t0 = now;
-                                if (*abort_flag) {
-                                    stop = 1;
-                                } else if (now - t0 > wait_limit_ns(status)) {
-                                    atomicOr(status, STATUS_ATTN_MMA);
-                                    *abort_flag = 1;
-                                    stop = 1;
-                                }
-                            }
-                            if (__shfl_sync(0xffffffffu, stop, 0)) {
-                                ok = false;
-                                break;
-                            }
-                        }
+                        __syncwarp();
                     }
                     if (!ok) break;
                     if (lane == 0) mma_commit(&aux->v_empty[st]);
                     __syncwarp();
                 }
             }
-            // done with the item's info (its S and P V are all issued)
+            // done with the item's info (its P V are all issued)
             if (lane == 0) mbar_arrive(&aux->info_empty[slot]);
             __syncwarp();
         }
         // every MMA issued must finish before TMEM is freed
-        if (lane == 0) mma_commit(&aux->drain);
+        if (lane == 0) mma_commit(&aux->drain[1]);
         __syncwarp();
-        mbar_drain(&aux->drain, 0, status, STATUS_ATTN_MMA);
+        mbar_drain(&aux->drain[1], 0, status, STATUS_ATTN_MMA);
     } else if (warp == V_WARP) {
         // ---------------- V loader: the V tiles of every item's calls, up to
         // VST tiles ahead of the P V MMAs (the K loader runs on its own) ----------------
