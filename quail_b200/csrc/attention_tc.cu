@@ -16,14 +16,14 @@
 //
 // Block: 64 query rows of one cu_a segment x 4 query heads of one KV head
 // (2 when the GQA group is 2) as two M=128 tiles (rows 0-63 one head, rows
-// 64-127 the next) that share every K/V tile. 12 warps:
+// 64-127 the next) that share every K/V tile. 16 warps:
 //   warp 0       TMA loader: each item's call list, Q once, then K tiles of
 //                64 keys into a 2-stage ring - the segment's own keys as
 //                contiguous rows, the resident keys one box per page through
 //                the block table;
 //   warp 10      TMA loader of the V tiles, the same way, into a 3-stage ring
 //                (its own warp, so a V tile is requested as soon as its slot
-//                frees: the loads take several microseconds to land);
+//                frees);
 //   warp 1       TMEM allocator and S issuer: S = Q K^T into one of two
 //                TMEM buffers per M tile, so the next tile's S runs while the
 //                softmax works on this one;
@@ -44,7 +44,12 @@
 //                behind a barrier per tile, held each P V about 2.6 us after
 //                its P was ready); after each call the same thread's
 //                epilogue: the normalised call-B output (bf16, kept in shared
-//                memory), or the merge, the quantisation and the fp8 store.
+//                memory), or the merge with it (bf16, over it) and the row's
+//                absolute max;
+//   warps 12-15  store warps, one thread per row of each M tile: the merged
+//                row quantised per head to fp8 and stored, while the softmax
+//                warps go on with the next item (whose first epilogue waits
+//                for its row's shared memory to be free again).
 // TMEM (512 columns): O [2 M tiles][128] | S [2 M tiles][2 buffers][64], the
 // first 32 columns of an S buffer holding that tile's P once computed.
 // A tcgen05.mma of M=128, K=16 takes about 26 ns at N=64 and 35 ns at
@@ -67,8 +72,8 @@ constexpr int KT = 64;  // keys per tile
 constexpr int KST = 2;  // K stages: a K tile is free once its S MMAs are done
 constexpr int VST = 3;  // V stages: a V tile is free once its P V MMAs are done
 constexpr int MAX_CALLS = QR + 1;
-constexpr int FIRST_SOFT = 2, V_WARP = 10, PV_WARP = 11;
-constexpr int NUM_THREADS = 12 * 32;
+constexpr int FIRST_SOFT = 2, V_WARP = 10, PV_WARP = 11, FIRST_STORE = 12;
+constexpr int NUM_THREADS = 16 * 32;
 
 constexpr int Q_BYTES = 2 * 2 * 128 * 128;  // [mt][half][128 rows][128 B]
 constexpr int KV_HALF = 64 * 128;           // [64 keys][64 dims]
@@ -114,8 +119,12 @@ struct Aux {
     // the previous one (a parity wait needs that)
     uint64_t s_full[2][2], p_full[2][2], pv_done[2][2];
     uint64_t drain[2];  // [S issuer, P V issuer]
+    // per M tile: an item's merged rows are in shared memory (softmax ->
+    // store warps) / stored, the rows free again (store warps -> softmax)
+    uint64_t y_full[2], y_empty[2];
     uint32_t tmem_base;
     int abort;
+    float ep_amax[2][128];  // [mt][row] the merged row's absolute max
     Info info[2];
 };
 
@@ -195,8 +204,8 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
         for (int b = 0; b < 2; ++b) {
             mbar_init(&aux->info_full[b], 1);
             // released by the S issuer, the active softmax warps, the V
-            // loader and the P V issuer
-            mbar_init(&aux->info_empty[b], 1 + 4 * nmt + 1 + 1);
+            // loader, the P V issuer and the store warps
+            mbar_init(&aux->info_empty[b], 1 + 4 * nmt + 1 + 1 + 4);
         }
         for (int st = 0; st < KST; ++st) {
             mbar_init(&aux->k_full[st], 1);
@@ -215,6 +224,10 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             mbar_init(&aux->pv_done[1][m], 1);
         }
         mbar_init(&aux->drain[0], 1);
+        for (int m = 0; m < 2; ++m) {
+            mbar_init(&aux->y_full[m], 4);
+            mbar_init(&aux->y_empty[m], 4);
+        }
         mbar_init(&aux->drain[1], 1);
         aux->abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -591,6 +604,94 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                 mbar_drain(&aux->v_full[j % VST], (uint32_t)(j / VST) & 1u, status,
                            STATUS_ATTN_LOAD);
         }
+    } else if (warp >= FIRST_STORE) {
+        // ------- store warps: pass 2 of an item's call-A epilogue, one thread
+        // per row of each M tile: the merged row (bf16, in shared memory)
+        // quantised per head to fp8 and stored -------
+        const int q4 = warp & 3;
+        const int i = q4 * 32 + lane;
+        const int qi = i & (QR - 1);
+        int ea = 0;
+        bool ok = true;
+        for (int item = blockIdx.x, k = 0; item < n_items && ok; item += gridDim.x, ++k) {
+            const int slot = k & 1;
+            if (!mbar_wait(&aux->info_full[slot], (uint32_t)(k >> 1) & 1u, abort_flag, status,
+                           STATUS_ATTN_SOFTMAX))
+                break;
+            const Info* inf = &aux->info[slot];
+            if (inf->n_calls > 0) {  // every item with calls ends in a call-A epilogue
+                const int row0 = inf->row0, seg_end = inf->seg_end, h0 = inf->h0;
+                for (int mt = 0; mt < nmt && ok; ++mt) {
+                    if (!mbar_wait(&aux->y_full[mt], (uint32_t)ea & 1u, abort_flag, status,
+                                   STATUS_ATTN_SOFTMAX)) {
+                        ok = false;
+                        break;
+                    }
+                    const float amax = aux->ep_amax[mt][i];
+                    const uint8_t* yrow = smem + OFF_OB + (mt * 128 + i) * OB_ROW;
+                        const int row = row0 + qi;
+                        const int h = h0 + 2 * mt + (i >> 6);
+                        const float sc = UE8M0 ? ue8m0_scale(amax) : group_scale(amax);
+                        const GroupDivider dv(sc);
+                        const bool big = !(amax < 0x1p+100f);  // the quotient range bound
+                        const float inv = ue8m0_inverse(sc);
+                        uint8_t* out = q_out + ((int64_t)(row < seg_end ? row : row0) * n_q + h) * D;
+#pragma unroll 1
+                        for (int c0 = 0; c0 < D; c0 += 32) {
+                            uint32_t yv[16];
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                const int j = (c0 >> 3) + u;
+                                const uint4 v4 = *reinterpret_cast<const uint4*>(yrow + ((j ^ (i & 15)) << 4));
+                                yv[4 * u] = v4.x;
+                                yv[4 * u + 1] = v4.y;
+                                yv[4 * u + 2] = v4.z;
+                                yv[4 * u + 3] = v4.w;
+                            }
+                            float qv[32];
+                            bool rare = UE8M0 ? false : big;
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                qv[2 * j] = __uint_as_float(yv[j] << 16);
+                                qv[2 * j + 1] = __uint_as_float(yv[j] & 0xFFFF0000u);
+                                if (UE8M0) {  // y * 2^-e, exact
+                                    f2unpack(f2mul(f2pack(qv[2 * j], qv[2 * j + 1]),
+                                                   f2pack(inv, inv)),
+                                             qv[2 * j], qv[2 * j + 1]);
+                                } else {
+                                    dv.quant2_sat(qv[2 * j], qv[2 * j + 1], rare);
+                                }
+                            }
+                            if (rare) {  // a zero, tiny or non-finite value: the exact path
+#pragma unroll
+                                for (int j = 0; j < 16; ++j) {
+                                    float a = __uint_as_float(yv[j] << 16);
+                                    float b = __uint_as_float(yv[j] & 0xFFFF0000u);
+                                    dv.quant2(a, b);
+                                    qv[2 * j] = a;
+                                    qv[2 * j + 1] = b;
+                                }
+                            }
+                            uint32_t packed[8];
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4)
+                                packed[j >> 2] = (uint32_t)fp8x2(qv[j], qv[j + 1]) |
+                                                 ((uint32_t)fp8x2(qv[j + 2], qv[j + 3]) << 16);
+                            if (row < seg_end) {
+                                uint4* o4 = reinterpret_cast<uint4*>(out + c0);
+                                o4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                                o4[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                            }
+                        }
+                        if (row < seg_end) scale_out[(int64_t)h * scale_ld + row] = sc;
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&aux->y_empty[mt]);
+                }
+                ++ea;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&aux->info_empty[slot]);
+        }
     } else {
         // ------- softmax, then each call's epilogue: one thread per row of an M tile -------
         const int mt = (warp - FIRST_SOFT) >> 2;
@@ -604,7 +705,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             uint8_t* obrow = smem + OFF_OB + (mt * 128 + i) * OB_ROW;
             const float sl2 = __fmul_rn(scale, 1.44269504088896341f);
             const uint64_t sl = f2pack(sl2, sl2);
-            int g = 0;
+            int g = 0, ea = 0;  // tiles, call-A epilogues handed to the store warps
             bool ok = true;
             for (int item = blockIdx.x, k = 0; item < n_items && ok; item += gridDim.x, ++k) {
                 const int slot = k & 1;
@@ -749,6 +850,14 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         ok = false;
                         break;
                     }
+                    // the item's first epilogue writes this row's shared-memory
+                    // output once the store warps are done with the last item's
+                    if (c == 0 && ea > 0 &&
+                        !mbar_wait(&aux->y_empty[mt], (uint32_t)(ea - 1) & 1u, abort_flag, status,
+                                   STATUS_ATTN_SOFTMAX)) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
                     float lsum[8];
 #pragma unroll
@@ -827,61 +936,11 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                                     make_uint4(yv[4 * u], yv[4 * u + 1], yv[4 * u + 2], yv[4 * u + 3]);
                             }
                         }
-                        const int row = row0 + qi;
-                        const int h = h0 + 2 * mt + (i >> 6);
-                        const float sc = UE8M0 ? ue8m0_scale(amax) : group_scale(amax);
-                        const GroupDivider dv(sc);
-                        const bool big = !(amax < 0x1p+100f);  // the quotient range bound
-                        const float inv = ue8m0_inverse(sc);
-                        uint8_t* out = q_out + ((int64_t)(row < seg_end ? row : row0) * n_q + h) * D;
-#pragma unroll 1
-                        for (int c0 = 0; c0 < D; c0 += 32) {
-                            uint32_t yv[16];
-#pragma unroll
-                            for (int u = 0; u < 4; ++u) {
-                                const int j = (c0 >> 3) + u;
-                                const uint4 v4 = *reinterpret_cast<const uint4*>(yrow + ((j ^ (i & 15)) << 4));
-                                yv[4 * u] = v4.x;
-                                yv[4 * u + 1] = v4.y;
-                                yv[4 * u + 2] = v4.z;
-                                yv[4 * u + 3] = v4.w;
-                            }
-                            float qv[32];
-                            bool rare = UE8M0 ? false : big;
-#pragma unroll
-                            for (int j = 0; j < 16; ++j) {
-                                qv[2 * j] = __uint_as_float(yv[j] << 16);
-                                qv[2 * j + 1] = __uint_as_float(yv[j] & 0xFFFF0000u);
-                                if (UE8M0) {  // y * 2^-e, exact
-                                    f2unpack(f2mul(f2pack(qv[2 * j], qv[2 * j + 1]),
-                                                   f2pack(inv, inv)),
-                                             qv[2 * j], qv[2 * j + 1]);
-                                } else {
-                                    dv.quant2_sat(qv[2 * j], qv[2 * j + 1], rare);
-                                }
-                            }
-                            if (rare) {  // a zero, tiny or non-finite value: the exact path
-#pragma unroll
-                                for (int j = 0; j < 16; ++j) {
-                                    float a = __uint_as_float(yv[j] << 16);
-                                    float b = __uint_as_float(yv[j] & 0xFFFF0000u);
-                                    dv.quant2(a, b);
-                                    qv[2 * j] = a;
-                                    qv[2 * j + 1] = b;
-                                }
-                            }
-                            uint32_t packed[8];
-#pragma unroll
-                            for (int j = 0; j < 32; j += 4)
-                                packed[j >> 2] = (uint32_t)fp8x2(qv[j], qv[j + 1]) |
-                                                 ((uint32_t)fp8x2(qv[j + 2], qv[j + 3]) << 16);
-                            if (row < seg_end) {
-                                uint4* o4 = reinterpret_cast<uint4*>(out + c0);
-                                o4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                                o4[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-                            }
-                        }
-                        if (row < seg_end) scale_out[(int64_t)h * scale_ld + row] = sc;
+                        // pass 2 (quantisation and store) goes to the store warps
+                        aux->ep_amax[mt][i] = amax;
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&aux->y_full[mt]);
+                        ++ea;
                     }
                     // O (and the call-B output) read before the next call's first P V
                     tc_fence_before();
