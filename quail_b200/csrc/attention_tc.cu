@@ -42,14 +42,16 @@
 //                once the previous P V is done (the thread's own rescale: a
 //                separate correction warp set, handling both M tiles in turn
 //                behind a barrier per tile, held each P V about 2.6 us after
-//                its P was ready); after each call the same thread's
-//                epilogue: the normalised call-B output (bf16, kept in shared
-//                memory), or the merge with it (bf16, over it) and the row's
-//                absolute max;
-//   warps 12-15  store warps, one thread per row of each M tile: the merged
-//                row quantised per head to fp8 and stored, while the softmax
-//                warps go on with the next item (whose first epilogue waits
-//                for its row's shared memory to be free again).
+//                its P was ready); after a call B its normaliser goes to the
+//                store warps, after call A the same thread merges with the
+//                call-B output (bf16, over it) and takes the row's absolute
+//                max;
+//   warps 12-15  store warps, one thread per row of each M tile: a call B's
+//                O normalised to bf16 into shared memory once its last P V is
+//                done (the next call's first P V waits for that read), and
+//                the merged row quantised per head to fp8 and stored, while
+//                the softmax warps go on (a call-A epilogue waits for the
+//                row's shared memory to be free again).
 // TMEM (512 columns): O [2 M tiles][128] | S [2 M tiles][2 buffers][64], the
 // first 32 columns of an S buffer holding that tile's P once computed.
 // A tcgen05.mma of M=128, K=16 takes about 26 ns at N=64 and 35 ns at
@@ -122,9 +124,14 @@ struct Aux {
     // per M tile: an item's merged rows are in shared memory (softmax ->
     // store warps) / stored, the rows free again (store warps -> softmax)
     uint64_t y_full[2], y_empty[2];
+    // per M tile: a call's normaliser is written (softmax -> store warps) /
+    // its O read and its bf16 output in shared memory (store warps -> P V
+    // issuer and softmax)
+    uint64_t b_full[2], o_free[2];
     uint32_t tmem_base;
     int abort;
     float ep_amax[2][128];  // [mt][row] the merged row's absolute max
+    float ep_inv[2][128];   // [mt][row] 1 / l of a call-B output
     Info info[2];
 };
 
@@ -227,6 +234,8 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
         for (int m = 0; m < 2; ++m) {
             mbar_init(&aux->y_full[m], 4);
             mbar_init(&aux->y_empty[m], 4);
+            mbar_init(&aux->b_full[m], 4);
+            mbar_init(&aux->o_free[m], 4);
         }
         mbar_init(&aux->drain[1], 1);
         aux->abort = 0;
@@ -481,7 +490,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             if (lane == 0) r = mbar_wait(bar, parity, abort_flag, status, STATUS_ATTN_MMA) ? 1 : 0;
             return __shfl_sync(0xffffffffu, r, 0) != 0;
         };
-        int g = 0;
+        int g = 0, eb = 0;  // tiles; call-B outputs the store warps took from O
         bool ok = true;
         for (int item = blockIdx.x, k = 0; item < n_items && ok; item += gridDim.x, ++k) {
             const int slot = k & 1;
@@ -512,8 +521,12 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                         __syncwarp();
                     }
+                    // a call's first P V overwrites O: after a call B, once the
+                    // store warps have read it
+                    const bool after_b = t == 0 && c > 0 && inf->calls[c - 1].kind == CALL_READS;
                     for (int mt = 0; mt < nmt; ++mt) {
-                        if (!wait0(&aux->p_full[g & 1][mt], (uint32_t)(g >> 1) & 1u)) {
+                        if (!wait0(&aux->p_full[g & 1][mt], (uint32_t)(g >> 1) & 1u) ||
+                            (after_b && !wait0(&aux->o_free[mt], (uint32_t)eb & 1u))) {
                             ok = false;
                             break;
                         }
@@ -530,6 +543,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         __syncwarp();
                     }
                     if (!ok) break;
+                    if (after_b) ++eb;
                     if (lane == 0) mma_commit(&aux->v_empty[st]);
                     __syncwarp();
                 }
@@ -611,7 +625,8 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
         const int q4 = warp & 3;
         const int i = q4 * 32 + lane;
         const int qi = i & (QR - 1);
-        int ea = 0;
+        const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+        int g = 0, ea = 0, eb = 0;  // tiles; call-A and call-B epilogues done
         bool ok = true;
         for (int item = blockIdx.x, k = 0; item < n_items && ok; item += gridDim.x, ++k) {
             const int slot = k & 1;
@@ -619,7 +634,55 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                            STATUS_ATTN_SOFTMAX))
                 break;
             const Info* inf = &aux->info[slot];
-            if (inf->n_calls > 0) {  // every item with calls ends in a call-A epilogue
+            const int n_calls = inf->n_calls;
+            // each call B's output: once its last P V is done, O normalised
+            // (bf16) into the shared-memory rows of the read group's members
+            for (int c = 0; c < n_calls && ok; ++c) {
+                const Call cl = inf->calls[c];
+                g += cl.n_tiles;
+                if (cl.kind != CALL_READS) continue;
+                const bool member = inf->s_grp[qi] == cl.group;
+                for (int mt = 0; mt < nmt && ok; ++mt) {
+                    if (!mbar_wait(&aux->b_full[mt], (uint32_t)eb & 1u, abort_flag, status,
+                                   STATUS_ATTN_SOFTMAX) ||
+                        !mbar_wait(&aux->pv_done[(g - 1) & 1][mt], (uint32_t)((g - 1) >> 1) & 1u,
+                                   abort_flag, status, STATUS_ATTN_SOFTMAX)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const float inv = aux->ep_inv[mt][i];
+                    const uint32_t o_addr = tmem + lane_off + TM_O + (uint32_t)(mt * 128);
+                    uint8_t* obrow = smem + OFF_OB + (mt * 128 + i) * OB_ROW;
+                    if (__any_sync(0xffffffffu, member)) {
+#pragma unroll 1
+                        for (int c0 = 0; c0 < D; c0 += 32) {
+                            uint32_t r[32];
+                            tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
+                            tmem_wait_ld();
+                            uint32_t ob[16];
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                ob[j] = bf16x2_bits(__fmul_rn(__uint_as_float(r[2 * j]), inv),
+                                                    __fmul_rn(__uint_as_float(r[2 * j + 1]), inv));
+                            if (member) {
+#pragma unroll
+                                for (int u = 0; u < 4; ++u) {
+                                    const int j = (c0 >> 3) + u;
+                                    *reinterpret_cast<uint4*>(obrow + ((j ^ (i & 15)) << 4)) =
+                                        make_uint4(ob[4 * u], ob[4 * u + 1], ob[4 * u + 2], ob[4 * u + 3]);
+                                }
+                            }
+                        }
+                    }
+                    // O read before the next call's first P V
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&aux->o_free[mt]);
+                }
+                ++eb;
+            }
+            if (ok && n_calls > 0) {  // every item with calls ends in a call-A epilogue
                 const int row0 = inf->row0, seg_end = inf->seg_end, h0 = inf->h0;
                 for (int mt = 0; mt < nmt && ok; ++mt) {
                     if (!mbar_wait(&aux->y_full[mt], (uint32_t)ea & 1u, abort_flag, status,
@@ -705,7 +768,9 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
             uint8_t* obrow = smem + OFF_OB + (mt * 128 + i) * OB_ROW;
             const float sl2 = __fmul_rn(scale, 1.44269504088896341f);
             const uint64_t sl = f2pack(sl2, sl2);
-            int g = 0, ea = 0;  // tiles, call-A epilogues handed to the store warps
+            // tiles; call-A and call-B epilogues handed to the store warps,
+            // and the call-B ones seen through
+            int g = 0, ea = 0, eb = 0, ebw = 0;
             bool ok = true;
             for (int item = blockIdx.x, k = 0; item < n_items && ok; item += gridDim.x, ++k) {
                 const int slot = k & 1;
@@ -714,7 +779,6 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                     break;
                 const Info* inf = &aux->info[slot];
                 const int n_calls = inf->n_calls;
-                const int row0 = inf->row0, seg_end = inf->seg_end, h0 = inf->h0;
                 float lse_b = 0.0f;  // this row's call-B log-sum-exp
                 for (int c = 0; c < n_calls && ok; ++c) {
                     const Call cl = inf->calls[c];
@@ -844,21 +908,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         if (lane == 0) mbar_arrive(&aux->p_full[g & 1][mt]);
                     }
                     if (!ok) break;
-                    // ---- epilogue of call c for this row: the last P V must be done ----
-                    if (!mbar_wait(&aux->pv_done[(g - 1) & 1][mt], (uint32_t)((g - 1) >> 1) & 1u,
-                                   abort_flag, status, STATUS_ATTN_SOFTMAX)) {
-                        ok = false;
-                        break;
-                    }
-                    // the item's first epilogue writes this row's shared-memory
-                    // output once the store warps are done with the last item's
-                    if (c == 0 && ea > 0 &&
-                        !mbar_wait(&aux->y_empty[mt], (uint32_t)(ea - 1) & 1u, abort_flag, status,
-                                   STATUS_ATTN_SOFTMAX)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
+                    // ---- epilogue of call c for this row ----
                     float lsum[8];
 #pragma unroll
                     for (int q = 0; q < 4; ++q) f2unpack(L[q], lsum[2 * q], lsum[2 * q + 1]);
@@ -866,32 +916,32 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                                               __fadd_rn(__fadd_rn(lsum[4], lsum[5]), __fadd_rn(lsum[6], lsum[7])));
                     const float inv = __frcp_rn(l);
                     if (cl.kind == CALL_READS) {
-                        // normalised call-B output, bf16, for the rows of this read
-                        // group (other rows keep what an earlier read group left)
-                        const bool member = inf->s_grp[qi] == cl.group;
-                        if (member) lse_b = __fmaf_rn(m, scale, qlnf(l));
-                        if (__any_sync(0xffffffffu, member)) {
-#pragma unroll 1
-                            for (int c0 = 0; c0 < D; c0 += 32) {
-                                uint32_t r[32];
-                                tmem_ld32_nowait(o_addr + (uint32_t)c0, r);
-                                tmem_wait_ld();
-                                uint32_t ob[16];
-#pragma unroll
-                                for (int j = 0; j < 16; ++j)
-                                    ob[j] = bf16x2_bits(__fmul_rn(__uint_as_float(r[2 * j]), inv),
-                                                        __fmul_rn(__uint_as_float(r[2 * j + 1]), inv));
-                                if (member) {
-#pragma unroll
-                                    for (int u = 0; u < 4; ++u) {
-                                        const int j = (c0 >> 3) + u;
-                                        *reinterpret_cast<uint4*>(obrow + ((j ^ (i & 15)) << 4)) =
-                                            make_uint4(ob[4 * u], ob[4 * u + 1], ob[4 * u + 2], ob[4 * u + 3]);
-                                    }
-                                }
-                            }
-                        }
-                    } else {
+                        // the normalised call-B output (bf16, for the rows of this
+                        // read group) is the store warps' work: they wait for the
+                        // call's last P V, read O and leave it in shared memory
+                        if (inf->s_grp[qi] == cl.group) lse_b = __fmaf_rn(m, scale, qlnf(l));
+                        aux->ep_inv[mt][i] = inv;
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&aux->b_full[mt]);
+                        ++eb;
+                        continue;
+                    }
+                    // call A: its last P V done, the store warps through with the
+                    // last item's rows and with this item's call-B outputs
+                    bool got = mbar_wait(&aux->pv_done[(g - 1) & 1][mt], (uint32_t)((g - 1) >> 1) & 1u,
+                                         abort_flag, status, STATUS_ATTN_SOFTMAX);
+                    if (got && ea > 0)
+                        got = mbar_wait(&aux->y_empty[mt], (uint32_t)(ea - 1) & 1u, abort_flag, status,
+                                        STATUS_ATTN_SOFTMAX);
+                    for (; got && ebw < eb; ++ebw)
+                        got = mbar_wait(&aux->o_free[mt], (uint32_t)ebw & 1u, abort_flag, status,
+                                        STATUS_ATTN_SOFTMAX);
+                    if (!got) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    {
                         // merge with call B, per-head fp8 quantisation, store
                         const float lse_a = __fmaf_rn(m, scale, qlnf(l));
                         const bool has_b = !UNIFIED && inf->s_grp[qi] >= 0;
