@@ -429,11 +429,13 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                            STATUS_ATTN_LOAD);
         }
     } else if (warp == 1) {
-        // ------ S issuer (lane 0): S = Q K^T of each tile in order, into
-        // the tile's S buffer (g & 1) once the P V two tiles back, which
-        // read the P written over it, is done ------
+        // ------ S issuer: S = Q K^T of each tile in order, into the tile's
+        // S buffer (g & 1) once the P V two tiles back, which read the P
+        // written over it, is done. The whole warp runs the loop and waits,
+        // lane 0 issues: with lane 0 looping alone while the other lanes
+        // sat at a block barrier, the attention ran 5% slower ------
         const uint32_t q_base = smem_u32(smem);
-        if (lane == 0) {
+        {
             int gs = 0, jq = 0;
             bool ok = true;
             for (int item = blockIdx.x, k = 0; item < n_items && ok; item += gridDim.x, ++k) {
@@ -459,6 +461,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         if (!ok) break;
                         tc_fence_after();
                         const uint32_t k_base = smem_u32(smem + OFF_K + (gs % KST) * KV_TILE);
+                        if (lane == 0) {
                         for (int mt = 0; mt < nmt; ++mt) {
                             const uint32_t s_tm = tmem + TM_S + (uint32_t)(mt * 128 + (gs & 1) * 64);
 #pragma unroll
@@ -470,25 +473,28 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         mma_commit(&aux->k_empty[gs % KST]);  // the K tile is free once these are done
                         // the item's last S: Q may be reloaded once these are done
                         if (j == total - 1) mma_commit(&aux->q_empty);
+                        }
+                        __syncwarp();
                     }
                 }
                 // done with the item's info (its S MMAs are all issued)
-                mbar_arrive(&aux->info_empty[slot]);
+                if (lane == 0) mbar_arrive(&aux->info_empty[slot]);
+                __syncwarp();
             }
             // every MMA issued must finish before TMEM is freed
-            mma_commit(&aux->drain[0]);
+            if (lane == 0) mma_commit(&aux->drain[0]);
+            __syncwarp();
             mbar_drain(&aux->drain[0], 0, status, STATUS_ATTN_MMA);
         }
     } else if (warp == PV_WARP) {
-        // ------ P V issuer (lane 0 issues; the warp zeroes V tails): O += P V
+        // ------ P V issuer (the warp waits, lane 0 issues, the warp zeroes
+        // V tails; waits by lane 0 alone with the verdict broadcast were
+        // slower): O += P V
         // of each tile and M tile in order, with P read from TMEM (the A
         // operand, bf16 over the tile's S) and V MN-major from shared
         // memory, as soon as that M tile's P is written ------
-        // lane 0 waits, the warp follows its verdict
         auto wait0 = [&](uint64_t* bar, uint32_t parity) -> bool {
-            int r = 0;
-            if (lane == 0) r = mbar_wait(bar, parity, abort_flag, status, STATUS_ATTN_MMA) ? 1 : 0;
-            return __shfl_sync(0xffffffffu, r, 0) != 0;
+            return mbar_wait(bar, parity, abort_flag, status, STATUS_ATTN_MMA);
         };
         int g = 0, eb = 0;  // tiles; call-B outputs the store warps took from O
         bool ok = true;
