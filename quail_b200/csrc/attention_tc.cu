@@ -20,7 +20,8 @@
 //   warp 0       TMA loader: each item's call list, Q once, then K tiles of
 //                64 keys into a 2-stage ring - the segment's own keys as
 //                contiguous rows, the resident keys one box per page through
-//                the block table;
+//                the block table (the warp runs the load loops and waits,
+//                lane 0 issues, as in every issuing warp here);
 //   warp 10      TMA loader of the V tiles, the same way, into a 3-stage ring
 //                (its own warp, so a V tile is requested as soon as its slot
 //                frees);
@@ -341,19 +342,27 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                 inf->n_calls = nc;
                 inf->total_tiles = total;
                 mbar_arrive(&aux->info_full[slot]);
+            }
+            // the Q and K loads: the warp runs the loops and waits, lane 0 issues
+            __syncwarp();
+            const int nc = inf->n_calls, total = inf->total_tiles;
+            {
                 if (total > 0) {
                     // Q of the item's heads, once the previous item's S MMAs are done
                     if (jq > 0 && !mbar_wait(&aux->q_empty, (uint32_t)(jq - 1) & 1u, abort_flag,
                                              status, STATUS_ATTN_LOAD)) {
                         ok = false;
                     } else {
-                        mbar_arrive_expect_tx(&aux->q_full, (uint32_t)(nmt * 32768));
-                        for (int mt = 0; mt < nmt; ++mt)
-                            for (int hh = 0; hh < 2; ++hh)
-                                for (int half = 0; half < 2; ++half)
-                                    tma_load_2d(smem_u32(smem + mt * 32768 + half * 16384 + hh * 8192),
-                                                &map_q, (h0 + 2 * mt + hh) * D + half * 64, row0,
-                                                &aux->q_full);
+                        if (lane == 0) {
+                            mbar_arrive_expect_tx(&aux->q_full, (uint32_t)(nmt * 32768));
+                            for (int mt = 0; mt < nmt; ++mt)
+                                for (int hh = 0; hh < 2; ++hh)
+                                    for (int half = 0; half < 2; ++half)
+                                        tma_load_2d(smem_u32(smem + mt * 32768 + half * 16384 + hh * 8192),
+                                                    &map_q, (h0 + 2 * mt + hh) * D + half * 64, row0,
+                                                    &aux->q_full);
+                        }
+                        __syncwarp();
                         ++jq;
                     }
                 }
@@ -382,6 +391,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                             uint8_t* dst = smem + (kv == 0 ? OFF_K : OFF_V) + st * KV_TILE;
                             const CUtensorMap* own_map = kv == 0 ? &map_k : &map_v;
                             const CUtensorMap* page_map = kv == 0 ? &map_kp : &map_vp;
+                            if (lane == 0) {
                             mbar_arrive_expect_tx(full, KV_TILE);
                             if (cl.kind == CALL_OWN) {
                                 const int y = seg_start + j0;
@@ -406,17 +416,14 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                                                     hk * D + half * 64, y, full);
                                 }
                             }
+                            }
+                            __syncwarp();
                             if (kv == 0) ++nk; else ++nv;
                         }
                         if (!ok) break;
                     }
                 }
             }
-            ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
-            g = __shfl_sync(0xffffffffu, g, 0);
-            nk = __shfl_sync(0xffffffffu, nk, 0);
-            nv = __shfl_sync(0xffffffffu, nv, 0);
-            jq = __shfl_sync(0xffffffffu, jq, 0);
         }
         // no copy may still be landing when the block exits
         if (lane == 0) {
@@ -564,8 +571,9 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
         mbar_drain(&aux->drain[1], 0, status, STATUS_ATTN_MMA);
     } else if (warp == V_WARP) {
         // ---------------- V loader: the V tiles of every item's calls, up to
-        // VST tiles ahead of the P V MMAs (the K loader runs on its own) ----------------
-        if (lane == 0) {
+        // VST tiles ahead of the P V MMAs (the K loader runs on its own); the
+        // warp runs the loop and waits, lane 0 issues ----------------
+        {
             int nv = 0;
             bool ok = true;
             for (int item = blockIdx.x, k = 0; item < n_items && ok; item += gridDim.x, ++k) {
@@ -590,6 +598,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         }
                         uint8_t* dst = smem + OFF_V + st * KV_TILE;
                         uint64_t* full = &aux->v_full[st];
+                        if (lane == 0) {
                         mbar_arrive_expect_tx(full, KV_TILE);
                         const int j0 = t * KT;
                         if (cl.kind == CALL_OWN) {
@@ -614,10 +623,13 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                                                 hk * D + half * 64, y, full);
                             }
                         }
+                        }
+                        __syncwarp();
                     }
                 }
                 if (!ok) break;
-                mbar_arrive(&aux->info_empty[slot]);
+                if (lane == 0) mbar_arrive(&aux->info_empty[slot]);
+                __syncwarp();
             }
             // no copy may still be landing when the block exits
             for (int j = (nv > VST ? nv - VST : 0); j < nv; ++j)
