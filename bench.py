@@ -58,7 +58,7 @@ SCALES_FP32 = "fp32: activation and weight block scales as computed / loaded"
 # x 36 layers). A profile constant, not measured in this run: ncu's
 # dram__bytes_read.sum + dram__bytes_write.sum over the launch list of this
 # bench's own workload (one pass per launch).
-GEMM_DRAM_BYTES_PER_LAUNCH = 1.7120e9
+GEMM_DRAM_BYTES_PER_LAUNCH = 1.7174e9
 GEMM_TRAFFIC_SOURCE = ("profile constant: ncu dram__bytes_read.sum + dram__bytes_write.sum, "
                        "mean over the GEMM launches of one config-1 chunk")
 
